@@ -1,0 +1,156 @@
+/*
+ * sketchpad_b200.h -- C ABI of the B200-native (sm_100a) diffusion-denoiser kernels.
+ *
+ * Drop-in boundary for the GPU operator surface of rhi-zone/sketchpad
+ * (crates/sketchpad-cubecl): fused flash attention, fused GroupNorm(+SiLU), Q8_0 and FP8
+ * quantized linears.  Conventions shared by every entry point:
+ *   - all pointers are device pointers unless the name ends in _host;
+ *   - every launch is asynchronous on `stream` (a cudaStream_t; NULL = legacy default);
+ *   - outputs are allocated by the caller (the reference allocates them inside the op and
+ *     hands them to the caller; here the caller owns both sides);
+ *   - the return value is a status code (SP_OK = 0, negative = error) and the library never
+ *     aborts; sp_last_error() returns a message for the calling thread's last failure;
+ *   - strides are in ELEMENTS, dimension order as in the reference tensor's shape.
+ */
+#ifndef SKETCHPAD_B200_H
+#define SKETCHPAD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SP_ABI_VERSION 1
+
+typedef enum sp_status {
+  SP_OK = 0,
+  SP_ERR_INVALID_ARG = -1, /* null pointer, non-positive size, bad enum */
+  SP_ERR_SHAPE = -2,       /* inconsistent or unsupported shape (e.g. C % groups != 0) */
+  SP_ERR_DTYPE = -3,       /* dtype combination not supported */
+  SP_ERR_ALIGN = -4,       /* pointer/stride alignment the kernel cannot use */
+  SP_ERR_LAUNCH = -5,      /* CUDA launch / driver call failed */
+  SP_ERR_WORKSPACE = -6,   /* workspace missing or too small */
+  SP_ERR_DEVICE = -7       /* device is not sm_100 */
+} sp_status;
+
+typedef enum sp_dtype { SP_F32 = 0, SP_F16 = 1, SP_BF16 = 2 } sp_dtype;
+
+typedef enum sp_act { SP_ACT_NONE = 0, SP_ACT_SILU = 1 } sp_act;
+
+/* Library ABI version (SP_ABI_VERSION). */
+int sp_abi_version(void);
+/* Message describing the calling thread's most recent failed call ("" if none). */
+const char* sp_last_error(void);
+/* Reads and clears the device watchdog word of the current device: 0 when no bounded
+ * device-side wait has expired since the last call, else the code of the first expiry.
+ * Synchronizes `stream`. */
+int sp_watchdog_read_and_clear(void* stream, int* code_out);
+
+/* ------------------------------------------------------------------------------------
+ * Flash attention forward.
+ * Replaces sketchpad_cubecl::flash_attention / flash_attention_masked
+ *   (crates/sketchpad-cubecl/src/attention.rs:97, :119, impl :130-178).
+ * out = softmax(Q K^T * scale [+ mask] [causal]) V with an f32 accumulator.
+ *   q [B,H,Sq,D], k [B,H,Skv,D], v [B,H,Skv,Dv], out [B,H,Sq,Dv], any element strides
+ *   whose innermost stride is 1 and whose other strides are multiples of 8 elements.
+ *   dtype_in: SP_BF16 or SP_F16 (q, k, v share it); dtype_out: SP_BF16, SP_F16 or SP_F32.
+ *   D, Dv: multiples of 8 in [8, 128].
+ *   mask: NULL or an additive f32 mask [Sq, Skv] (row stride mask_row_stride), shared by
+ *         every batch and head (the reference's Tensor<B,2> mask).
+ *   causal: key j > query i is excluded (FlashAttentionOptions::causal, :40-68).
+ *   scale <= 0 selects 1/sqrt(D).
+ * ------------------------------------------------------------------------------------ */
+int sp_flash_attn_fwd(const void* q, const void* k, const void* v, const float* mask,
+                      int64_t mask_row_stride, void* out, int64_t B, int64_t H, int64_t Sq,
+                      int64_t Skv, int64_t D, int64_t Dv, const int64_t q_strides[4],
+                      const int64_t k_strides[4], const int64_t v_strides[4],
+                      const int64_t o_strides[4], int dtype_in, int dtype_out, int causal,
+                      float scale, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * GroupNorm (+ SiLU), single pass over HBM.
+ * Replaces sketchpad_cubecl::groupnorm_silu / groupnorm
+ *   (crates/sketchpad-cubecl/src/groupnorm_silu.rs:232, :323; GroupNormSiLuOptions :22-46)
+ * with the semantics of the CPU path crates/sketchpad-core/src/groupnorm.rs:62-102
+ * (clamp +-65000, f32 statistics, biased variance, clamp after the affine).
+ *   x [B,C,H,W] with element strides x_strides (NULL = contiguous); y contiguous [B,C,H,W].
+ *   gamma, beta [C]; x, y, gamma, beta all of `dtype` (SP_F32, SP_F16, SP_BF16).
+ *   act: SP_ACT_SILU (groupnorm_silu) or SP_ACT_NONE (groupnorm).
+ *   Returns SP_ERR_SHAPE when C % groups != 0 (the reference panics there).
+ * workspace: strided inputs and groups larger than one thread-block cluster can hold on
+ *   chip use a two-kernel path that needs device workspace; sp_groupnorm_act_workspace_size()
+ *   returns its size, or 0 when x and y are 16-byte aligned and the single-pass path applies
+ *   (workspace may then be NULL).
+ * ------------------------------------------------------------------------------------ */
+size_t sp_groupnorm_act_workspace_size(int64_t B, int64_t C, int64_t H, int64_t W,
+                                       const int64_t x_strides[4], int64_t groups, int dtype);
+int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y, int64_t B,
+                     int64_t C, int64_t H, int64_t W, const int64_t x_strides[4], int64_t groups,
+                     float eps, int act, int dtype, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Q8_0 (GGUF) weights.
+ * A Q8_0 row of in_f values is in_f/32 blocks of 34 bytes: f16 LE scale + 32 int8.
+ * The GPU layout is planar: q [out_f, in_f] int8 and scale [out_f, in_f/32] f16 bits;
+ * the repack is lossless, so decode stays bit-exact.
+ * ------------------------------------------------------------------------------------ */
+/* Host repack of GGUF bytes (replaces the upload in GpuQuantizedLinear::from_bytes,
+ * crates/sketchpad-cubecl/src/quantized_matmul.rs:670-702). */
+int sp_q8_0_repack_host(const uint8_t* gguf_host, size_t nbytes, int64_t out_f, int64_t in_f,
+                        int8_t* q_host, uint16_t* scale_host);
+/* Device repack of GGUF bytes already in device memory. */
+int sp_q8_0_repack(const void* gguf, size_t nbytes, int64_t out_f, int64_t in_f, void* q,
+                   void* scale, void* stream);
+/* Dequantize to [out_f, in_f] (replaces dequantize_q8_0, quantized_matmul.rs:376-408 and
+ * GpuQuantizedLinear::dequantize :705).  out_dtype SP_F32 gives f32(scale)*q exactly as
+ * crates/sketchpad-convert/src/gguf.rs:643-656 does (subnormal scales included). */
+int sp_q8_0_dequant(const void* q, const void* scale, int64_t out_f, int64_t in_f, void* out,
+                    int out_dtype, void* stream);
+/* y[M,N] = x[M,K] . dequant(W)[N,K]^T (+ bias[N]); the dequantization happens inside the
+ * GEMM mainloop (replaces GpuQuantizedLinear::forward, quantized_matmul.rs:752-766).
+ * x, y, bias: SP_BF16.  K % 64 == 0, N % 16 == 0.  bias may be NULL. */
+int sp_q8_0_linear(const void* x, const void* q, const void* scale, const void* bias, void* y,
+                   int64_t M, int64_t N, int64_t K, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * FP8 (e4m3) weights with f32 scales (per output channel, or one per tensor).
+ * The reference simulates FP8 in f32 (crates/sketchpad-core/src/quantization.rs:422-615);
+ * here the weights are real e4m3 bytes.
+ * ------------------------------------------------------------------------------------ */
+/* quantize_fp8 with the E4M3 config (quantization.rs:495-577): w f32 [N,K] ->
+ * e4m3 bytes [N,K] + scale (N floats per channel, else 1).  Rounds like
+ * quantize_fp8_scalar (:451-492) -- nearest, ties away from zero -- for every value the
+ * e4m3 grid can hold; scaled magnitudes below 2^-6 go to the nearest e4m3 subnormal. */
+typedef enum sp_fp8_scale_mode {
+  SP_FP8_PER_TENSOR = 0,  /* scale[0] = max|w| / 448 (1 if w == 0), computed here */
+  SP_FP8_PER_CHANNEL = 1, /* scale[n] = max|w[n,:]| / 448, computed here */
+  SP_FP8_GIVEN_SCALE = 2  /* scale[0] supplied by the caller (Fp8Config::with_scale) */
+} sp_fp8_scale_mode;
+int sp_fp8_quantize(const float* w, int64_t N, int64_t K, int scale_mode, void* w_e4m3,
+                    float* scale, void* stream);
+/* Fp8Tensor::dequantize (quantization.rs:435-447): out[n,k] = e4m3(w[n,k]) * scale[n or 0]. */
+int sp_fp8_dequant(const void* w_e4m3, const float* scale, int64_t nscale, int64_t N, int64_t K,
+                   void* out, int out_dtype, void* stream);
+/* Fp8Linear::forward (quantization.rs:601-609): y = x . dequant(W)^T + bias with the e4m3
+ * decode in the GEMM mainloop and the scale in the epilogue.  x, y, bias: SP_BF16.
+ * K % 64 == 0, N % 16 == 0. */
+int sp_fp8_linear(const void* x, const void* w_e4m3, const float* scale, int64_t nscale,
+                  const void* bias, void* y, int64_t M, int64_t N, int64_t K, int dtype,
+                  void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * LayerNorm over the last dimension (crates/sketchpad-core/src/layernorm.rs:63-73), which
+ * uses burn's unbiased (n-1) variance; unbiased = 0 gives the biased form.
+ * x, y [rows, n] contiguous; gamma, beta [n]; all of `dtype`.
+ * ------------------------------------------------------------------------------------ */
+int sp_layernorm(const void* x, const void* gamma, const void* beta, void* y, int64_t rows,
+                 int64_t n, float eps, int unbiased, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SKETCHPAD_B200_H */

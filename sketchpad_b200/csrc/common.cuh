@@ -1,0 +1,44 @@
+// common.cuh -- host-side helpers shared by the C-ABI entry points: status/error reporting,
+// dtype sizes, the TMA descriptor encoder (fetched from the driver at run time), and
+// launch checking.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/sketchpad_b200.h"
+
+namespace sp {
+
+// Records a printf-style message for sp_last_error() and returns `status`.
+int set_error(int status, const char* fmt, ...);
+void clear_error();
+
+inline int dtype_size(int dt) {
+  switch (dt) {
+    case SP_F32: return 4;
+    case SP_F16: return 2;
+    case SP_BF16: return 2;
+    default: return 0;
+  }
+}
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Checks cudaGetLastError after a launch; returns SP_OK or SP_ERR_LAUNCH with a message.
+int check_launch(const char* what);
+
+// Returns SP_OK if the current device is sm_100 (B200/GB200 class), else SP_ERR_DEVICE.
+int require_sm100();
+
+// SM count of the current device (cached per device).
+int num_sms();
+
+// cuTensorMapEncodeTiled obtained through cudaGetDriverEntryPoint (no libcuda link).
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, const void* base,
+                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                 CUtensorMapSwizzle swizzle);
+
+}  // namespace sp

@@ -1,0 +1,494 @@
+// groupnorm_act.cu -- fused GroupNorm (+SiLU) for NCHW activations on sm_100a.
+//
+// Semantics: crates/sketchpad-core/src/groupnorm.rs:62-102 + crates/sketchpad-core/src/silu.rs:5-7
+//   x <- clamp(x, +-65000); per (batch, group): mean, BIASED variance (f32 statistics);
+//   y <- clamp((x - mean) / sqrt(var + eps) * gamma[c] + beta[c], +-65000); y <- y*sigmoid(y).
+// Replaces the reference's two-kernel GPU path (groupnorm_silu.rs:64-211), whose statistics
+// kernel runs one thread per (batch, group).
+//
+// Fast path (contiguous x): ONE read and ONE write of HBM.  A (batch, group) is split over a
+// thread-block cluster of CS CTAs (CS <= 16); each CTA keeps its slice in registers (16-byte
+// vector loads), the cluster reduces the sum and then the centred sum of squares through
+// distributed shared memory, and every CTA normalises its slice straight from registers.
+//
+// General path (strided x, or a group larger than a 16-CTA cluster holds): two kernels.
+// Pass 1 writes per-chunk (count, mean, M2) partials to a caller workspace; pass 2 merges
+// its group's partials (Chan et al.'s pairwise update) and normalises (x is read twice).
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace sp {
+namespace {
+
+constexpr int kGnThreads = 256;
+constexpr int kMaxCluster = 16;
+constexpr float kClamp = 65000.0f;
+
+template <typename T>
+struct VecTraits;
+template <>
+struct VecTraits<float> {
+  static constexpr int kElems = 4;
+};
+template <>
+struct VecTraits<__half> {
+  static constexpr int kElems = 8;
+};
+template <>
+struct VecTraits<__nv_bfloat16> {
+  static constexpr int kElems = 8;
+};
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// Unpack a 16-byte vector into f32 lanes.
+template <typename T>
+__device__ __forceinline__ void unpack(const uint4& u, float* f) {
+  if constexpr (sizeof(T) == 4) {
+    f[0] = __uint_as_float(u.x);
+    f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z);
+    f[3] = __uint_as_float(u.w);
+  } else {
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = to_f32(h[i]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack(const float* f) {
+  uint4 u;
+  if constexpr (sizeof(T) == 4) {
+    u.x = __float_as_uint(f[0]);
+    u.y = __float_as_uint(f[1]);
+    u.z = __float_as_uint(f[2]);
+    u.w = __float_as_uint(f[3]);
+  } else {
+    T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = from_f32<T>(f[i]);
+  }
+  return u;
+}
+
+__device__ __forceinline__ float clamp65k(float v) { return fminf(fmaxf(v, -kClamp), kClamp); }
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  v = clamp65k(v);
+  if (act == SP_ACT_SILU) v = v / (1.0f + __expf(-v));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide sum over kGnThreads threads; result valid in every thread.
+__device__ __forceinline__ float block_sum(float v, float* scratch /* >= 32 floats */) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();  // scratch may still be read from a previous call
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float t = lane < (kGnThreads / 32) ? scratch[lane] : 0.f;
+  return warp_sum(t);
+}
+
+struct GnParams {
+  const void* x;
+  const void* gamma;
+  const void* beta;
+  void* y;
+  int64_t C, HW, G, cg;       // channels, H*W, groups, channels per group
+  int64_t n;                   // elements per group = cg * HW
+  int64_t chunk_vecs;          // 16-byte vectors per CTA slice
+  float eps;
+  int act;
+};
+
+// grid = (CS, B*G), cluster = (CS, 1, 1); x and y contiguous, n % vec == 0, 16-B aligned.
+template <typename T, int VPT>
+__global__ void __launch_bounds__(kGnThreads, 2) gn_cluster_kernel(GnParams p) {
+  constexpr int VE = VecTraits<T>::kElems;
+  __shared__ float red[2];          // this CTA's partial (sum, centred sum of squares)
+  __shared__ float scratch[32];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int cs = (int)cluster.num_blocks();
+
+  const int64_t bg = blockIdx.y;  // b * G + g
+  const int64_t g = bg % p.G;
+  const int64_t base = bg * p.n;  // contiguous NCHW: a group is one contiguous range
+  const uint4* xv = reinterpret_cast<const uint4*>(static_cast<const T*>(p.x) + base);
+  uint4* yv = reinterpret_cast<uint4*>(static_cast<T*>(p.y) + base);
+  const int64_t nvec = p.n / VE;
+  const int64_t v0 = (int64_t)rank * p.chunk_vecs;
+  const int64_t v1 = min(nvec, v0 + p.chunk_vecs);
+
+  uint4 buf[VPT];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = v0 + threadIdx.x + (int64_t)j * kGnThreads;
+    if (vi < v1) buf[j] = __ldg(xv + vi);
+  }
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = v0 + threadIdx.x + (int64_t)j * kGnThreads;
+    if (vi < v1) {
+      float f[VE];
+      unpack<T>(buf[j], f);
+#pragma unroll
+      for (int e = 0; e < VE; ++e) s += clamp65k(f[e]);
+    }
+  }
+  s = block_sum(s, scratch);
+  if (threadIdx.x == 0) red[0] = s;
+  cluster.sync();
+  float tot = 0.f;
+  for (int r = 0; r < cs; ++r) tot += *cluster.map_shared_rank(&red[0], r);
+  const float mean = tot / (float)p.n;
+
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = v0 + threadIdx.x + (int64_t)j * kGnThreads;
+    if (vi < v1) {
+      float f[VE];
+      unpack<T>(buf[j], f);
+#pragma unroll
+      for (int e = 0; e < VE; ++e) {
+        const float d = clamp65k(f[e]) - mean;
+        ss += d * d;
+      }
+    }
+  }
+  ss = block_sum(ss, scratch);
+  if (threadIdx.x == 0) red[1] = ss;
+  cluster.sync();
+  float tss = 0.f;
+  for (int r = 0; r < cs; ++r) tss += *cluster.map_shared_rank(&red[1], r);
+  // Every remote read of this CTA's `red` is done once all CTAs pass this arrive; the
+  // matching wait sits at the end so the normalisation overlaps it.
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  const float var = tss / (float)p.n;
+  const float rstd = rsqrtf(var + p.eps);
+
+  const T* gam = static_cast<const T*>(p.gamma);
+  const T* bet = static_cast<const T*>(p.beta);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = v0 + threadIdx.x + (int64_t)j * kGnThreads;
+    if (vi < v1) {
+      float f[VE];
+      unpack<T>(buf[j], f);
+      // HW % VE == 0 on this path, so one vector never straddles two channels.
+      const int c = (int)g * (int)p.cg + (int)((uint32_t)(vi * VE) / (uint32_t)p.HW);
+      const float w = to_f32(gam[c]) * rstd;
+      const float b = to_f32(bet[c]);
+#pragma unroll
+      for (int e = 0; e < VE; ++e) f[e] = apply_act((clamp65k(f[e]) - mean) * w + b, p.act);
+      yv[vi] = pack<T>(f);
+    }
+  }
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// General path: strided input, or groups beyond one cluster's capacity.
+// ---------------------------------------------------------------------------------------
+struct GnGeneralParams {
+  const void* x;
+  const void* gamma;
+  const void* beta;
+  void* y;
+  int64_t B, C, H, W, G, cg, n;
+  int64_t sb, sc, sh, sw;  // element strides of x
+  int64_t chunk;           // elements per chunk
+  int64_t nchunks;         // chunks per group
+  float* part;             // [B*G, nchunks, 3] : count, mean, M2
+  float eps;
+  int act;
+};
+
+__device__ __forceinline__ int64_t gn_offset(const GnGeneralParams& p, int64_t b, int64_t g,
+                                             int64_t e) {
+  const int64_t cl = e / (p.H * p.W);
+  const int64_t hw = e - cl * p.H * p.W;
+  const int64_t h = hw / p.W, w = hw - h * p.W;
+  return b * p.sb + (g * p.cg + cl) * p.sc + h * p.sh + w * p.sw;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(GnGeneralParams p) {
+  __shared__ float scratch[32];
+  const int64_t bg = blockIdx.y, b = bg / p.G, g = bg % p.G;
+  const int64_t e0 = (int64_t)blockIdx.x * p.chunk;
+  const int64_t e1 = min(p.n, e0 + p.chunk);
+  const T* x = static_cast<const T*>(p.x);
+  float s = 0.f;
+  for (int64_t e = e0 + threadIdx.x; e < e1; e += kGnThreads) s += clamp65k(to_f32(x[gn_offset(p, b, g, e)]));
+  s = block_sum(s, scratch);
+  const float cnt = (float)(e1 - e0);
+  const float m = s / cnt;
+  float ss = 0.f;
+  for (int64_t e = e0 + threadIdx.x; e < e1; e += kGnThreads) {
+    const float d = clamp65k(to_f32(x[gn_offset(p, b, g, e)])) - m;
+    ss += d * d;
+  }
+  ss = block_sum(ss, scratch);
+  if (threadIdx.x == 0) {
+    float* o = p.part + (bg * p.nchunks + blockIdx.x) * 3;
+    o[0] = cnt;
+    o[1] = m;
+    o[2] = ss;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GnGeneralParams p) {
+  __shared__ float stats[2];
+  const int64_t bg = blockIdx.y, b = bg / p.G, g = bg % p.G;
+  if (threadIdx.x == 0) {
+    // Chan's pairwise merge of (count, mean, M2), in chunk order.
+    const float* q = p.part + bg * p.nchunks * 3;
+    double n = 0.0, mean = 0.0, m2 = 0.0;
+    for (int64_t i = 0; i < p.nchunks; ++i) {
+      const double nb = q[3 * i], mb = q[3 * i + 1], m2b = q[3 * i + 2];
+      const double nn = n + nb, d = mb - mean;
+      mean += d * nb / nn;
+      m2 += m2b + d * d * n * nb / nn;
+      n = nn;
+    }
+    stats[0] = (float)mean;
+    stats[1] = rsqrtf((float)(m2 / n) + p.eps);
+  }
+  __syncthreads();
+  const float mean = stats[0], rstd = stats[1];
+  const int64_t e0 = (int64_t)blockIdx.x * p.chunk;
+  const int64_t e1 = min(p.n, e0 + p.chunk);
+  const T* x = static_cast<const T*>(p.x);
+  const T* gam = static_cast<const T*>(p.gamma);
+  const T* bet = static_cast<const T*>(p.beta);
+  T* y = static_cast<T*>(p.y) + bg * p.n;  // output is contiguous
+  for (int64_t e = e0 + threadIdx.x; e < e1; e += kGnThreads) {
+    const int64_t c = g * p.cg + e / (p.H * p.W);
+    const float v = (clamp65k(to_f32(x[gn_offset(p, b, g, e)])) - mean) * rstd;
+    y[e] = from_f32<T>(apply_act(v * to_f32(gam[c]) + to_f32(bet[c]), p.act));
+  }
+}
+
+constexpr int64_t kGeneralChunk = 16384;
+
+struct GnPlan {
+  bool cluster_path;
+  int cs;      // cluster size
+  int vpt;     // vectors per thread
+  int64_t chunk_vecs;
+  int64_t nchunks;  // general path
+};
+
+GnPlan plan_gn(int64_t B, int64_t G, int64_t n, bool contiguous, bool vec_ok, int vec_elems) {
+  GnPlan pl{};
+  const int64_t nvec = n / vec_elems;
+  // 16 vectors (64 f32) per thread for f32, 8 vectors (64 halves) for 16-bit types: both
+  // stay within the 128 registers that two resident CTAs per SM allow.
+  const int max_vpt = vec_elems == 4 ? 16 : 8;
+  if (contiguous && vec_ok && n < (1LL << 31)) {
+    static const int kVpts[] = {1, 2, 4, 8, 16};
+    int best_cs = 0, best_vpt = 0;
+    // smallest cluster whose slices fit max_vpt vectors per thread
+    for (int cs = 1; cs <= kMaxCluster; cs *= 2) {
+      const int64_t per = (nvec + cs - 1) / cs;
+      if (per <= (int64_t)kGnThreads * max_vpt) {
+        best_cs = cs;
+        break;
+      }
+    }
+    if (best_cs) {
+      // widen the cluster while the grid is small and the slices stay >= 2 vectors/thread
+      const int64_t target_ctas = 2LL * num_sms();
+      while (best_cs < kMaxCluster && B * G * best_cs < target_ctas &&
+             (nvec + 2 * best_cs - 1) / (2 * best_cs) >= (int64_t)kGnThreads * 2)
+        best_cs *= 2;
+      const int64_t per = (nvec + best_cs - 1) / best_cs;
+      for (int v : kVpts)
+        if ((int64_t)v * kGnThreads >= per) {
+          best_vpt = v;
+          break;
+        }
+      pl.cluster_path = true;
+      pl.cs = best_cs;
+      pl.vpt = best_vpt;
+      pl.chunk_vecs = per;
+      return pl;
+    }
+  }
+  pl.cluster_path = false;
+  pl.nchunks = (n + kGeneralChunk - 1) / kGeneralChunk;
+  return pl;
+}
+
+template <typename T, int VPT>
+int launch_cluster(const GnParams& p, int cs, int64_t BG, cudaStream_t stream) {
+  auto kern = gn_cluster_kernel<T, VPT>;
+  if (cs > 8) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess)
+      return set_error(SP_ERR_LAUNCH, "groupnorm: cluster size %d not allowed: %s", cs,
+                       cudaGetErrorString(e));
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)cs, (unsigned)BG, 1);
+  cfg.blockDim = dim3(kGnThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  if (e != cudaSuccess)
+    return set_error(SP_ERR_LAUNCH, "groupnorm cluster launch (cs=%d, vpt=%d) failed: %s", cs,
+                     VPT, cudaGetErrorString(e));
+  return SP_OK;
+}
+
+template <typename T>
+int launch_cluster_vpt(const GnParams& p, int cs, int vpt, int64_t BG, cudaStream_t s) {
+  switch (vpt) {
+    case 1: return launch_cluster<T, 1>(p, cs, BG, s);
+    case 2: return launch_cluster<T, 2>(p, cs, BG, s);
+    case 4: return launch_cluster<T, 4>(p, cs, BG, s);
+    case 8: return launch_cluster<T, 8>(p, cs, BG, s);
+    default:
+      if constexpr (sizeof(T) == 4) return launch_cluster<T, 16>(p, cs, BG, s);
+      return set_error(SP_ERR_SHAPE, "groupnorm: internal plan error (vpt %d)", vpt);
+  }
+}
+
+template <typename T>
+int launch_general(const GnGeneralParams& p, int64_t BG, cudaStream_t s) {
+  dim3 grid((unsigned)p.nchunks, (unsigned)BG, 1);
+  gn_partial_kernel<T><<<grid, kGnThreads, 0, s>>>(p);
+  int rc = check_launch("groupnorm partial");
+  if (rc) return rc;
+  gn_apply_kernel<T><<<grid, kGnThreads, 0, s>>>(p);
+  return check_launch("groupnorm apply");
+}
+
+}  // namespace
+}  // namespace sp
+
+extern "C" {
+
+namespace sp {
+namespace {
+size_t general_workspace_bytes(int64_t B, int64_t C, int64_t H, int64_t W, int64_t groups) {
+  const int64_t n = C / groups * H * W;
+  const int64_t nchunks = (n + kGeneralChunk - 1) / kGeneralChunk;
+  return (size_t)(B * groups * nchunks * 3 * sizeof(float));
+}
+bool is_contiguous_nchw(int64_t B, int64_t C, int64_t H, int64_t W, const int64_t* st) {
+  if (!st) return true;
+  const int64_t want[4] = {C * H * W, H * W, W, 1};
+  const int64_t dims[4] = {B, C, H, W};
+  for (int i = 0; i < 4; ++i)
+    if (dims[i] > 1 && st[i] != want[i]) return false;
+  return true;
+}
+}  // namespace
+}  // namespace sp
+
+size_t sp_groupnorm_act_workspace_size(int64_t B, int64_t C, int64_t H, int64_t W,
+                                       const int64_t x_strides[4], int64_t groups, int dtype) {
+  const int es = sp::dtype_size(dtype);
+  if (!es || B <= 0 || C <= 0 || H <= 0 || W <= 0 || groups <= 0 || C % groups) return 0;
+  const bool contiguous = sp::is_contiguous_nchw(B, C, H, W, x_strides);
+  const int vec = 16 / es;
+  const sp::GnPlan pl = sp::plan_gn(B, groups, C / groups * H * W, contiguous,
+                                    contiguous && (H * W) % vec == 0, vec);
+  return pl.cluster_path ? 0 : sp::general_workspace_bytes(B, C, H, W, groups);
+}
+
+int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y, int64_t B,
+                     int64_t C, int64_t H, int64_t W, const int64_t x_strides[4], int64_t groups,
+                     float eps, int act, int dtype, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  using namespace sp;
+  clear_error();
+  if (!x || !gamma || !beta || !y)
+    return set_error(SP_ERR_INVALID_ARG, "groupnorm: null tensor pointer");
+  if (B <= 0 || C <= 0 || H <= 0 || W <= 0 || groups <= 0)
+    return set_error(SP_ERR_INVALID_ARG, "groupnorm: non-positive dimension");
+  if (C % groups != 0)
+    return set_error(SP_ERR_SHAPE, "channels (%lld) must be divisible by num_groups (%lld)",
+                     (long long)C, (long long)groups);
+  if (act != SP_ACT_NONE && act != SP_ACT_SILU)
+    return set_error(SP_ERR_INVALID_ARG, "groupnorm: unknown activation %d", act);
+  const int es = dtype_size(dtype);
+  if (!es) return set_error(SP_ERR_DTYPE, "groupnorm: unknown dtype %d", dtype);
+  if (B * groups > 65535)
+    return set_error(SP_ERR_SHAPE, "groupnorm: batch*groups (%lld) exceeds 65535",
+                     (long long)(B * groups));
+  if (int rc = require_sm100()) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  const int64_t HW = H * W, cg = C / groups, n = cg * HW;
+  int64_t st[4] = {C * HW, HW, W, 1};
+  const bool contiguous = is_contiguous_nchw(B, C, H, W, x_strides);
+  if (!contiguous)
+    for (int i = 0; i < 4; ++i) st[i] = x_strides[i];
+  const int vec_elems = 16 / es;
+  const bool vec_ok = contiguous && (HW % vec_elems == 0) && aligned(x, 16) && aligned(y, 16);
+  const GnPlan pl = plan_gn(B, groups, n, contiguous, vec_ok, vec_elems);
+
+  if (pl.cluster_path) {
+    GnParams p{x, gamma, beta, y, C, HW, groups, cg, n, pl.chunk_vecs, eps, act};
+    switch (dtype) {
+      case SP_F32: return launch_cluster_vpt<float>(p, pl.cs, pl.vpt, B * groups, s);
+      case SP_F16: return launch_cluster_vpt<__half>(p, pl.cs, pl.vpt, B * groups, s);
+      default: return launch_cluster_vpt<__nv_bfloat16>(p, pl.cs, pl.vpt, B * groups, s);
+    }
+  }
+  const size_t need = general_workspace_bytes(B, C, H, W, groups);
+  if (!workspace || workspace_bytes < need)
+    return set_error(SP_ERR_WORKSPACE,
+                     "groupnorm: this shape/layout takes the two-pass path and needs %zu bytes "
+                     "of workspace (got %zu)",
+                     need, workspace_bytes);
+  if (!aligned(workspace, 4)) return set_error(SP_ERR_ALIGN, "groupnorm: workspace misaligned");
+  GnGeneralParams p{x,  gamma, beta,  y,     B,     C,     H, W, groups, cg, n,
+                    st[0], st[1], st[2], st[3], kGeneralChunk, pl.nchunks,
+                    static_cast<float*>(workspace), eps, act};
+  switch (dtype) {
+    case SP_F32: return launch_general<float>(p, B * groups, s);
+    case SP_F16: return launch_general<__half>(p, B * groups, s);
+    default: return launch_general<__nv_bfloat16>(p, B * groups, s);
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,338 @@
+// quant_linear.cu -- y = x . dequant(W)^T (+ bias) with the weight decode fused into the
+// mainloop of a tcgen05 GEMM (sm_100a).
+//
+// Replaces GpuQuantizedLinear::forward (crates/sketchpad-cubecl/src/quantized_matmul.rs:752-766),
+// which materialises the whole dequantized matrix and then runs a separate matmul, and
+// Fp8Linear::forward (crates/sketchpad-core/src/quantization.rs:601-609).
+//
+// CTA tile: 128 rows of x (UMMA M) x 256 weight rows (UMMA N), K in steps of 64.
+//   warp 0      TMA: x tile (bf16, 128B swizzle) + raw 8-bit weight tile, RAW_STAGES deep.
+//   warp 1      TMEM owner + MMA issuer: acc[128 x 256 f32] += x_tile . wtile^T.
+//   warps 2..5  decoders: raw 8-bit tile -> bf16 tile in the UMMA K-major 128B-swizzled
+//               layout (Q8_0: f16 block scale * int8; FP8: exact e4m3 -> bf16), CVT_STAGES
+//               deep; then the epilogue (TMEM -> per-channel scale, bias -> bf16 -> HBM).
+#include "common.cuh"
+#include "quant_codec.cuh"
+#include "tc.cuh"
+
+namespace sp {
+namespace {
+
+constexpr int kQBM = 128, kQBN = 256, kQBK = 64;
+constexpr int kQThreads = 192;
+constexpr int kRawStages = 4, kCvtStages = 2;
+constexpr int kXBytes = kQBM * kQBK * 2;    // 16 KB
+constexpr int kWRawBytes = kQBN * kQBK;     // 16 KB
+constexpr int kWCvtBytes = kQBN * kQBK * 2; // 32 KB
+
+enum WFormat : int { W_Q8_0 = 0, W_FP8 = 1 };
+
+struct QlSmem {
+  static constexpr int kX = 0;
+  static constexpr int kWRaw = kX + kRawStages * kXBytes;
+  static constexpr int kWCvt = kWRaw + kRawStages * kWRawBytes;
+  static constexpr int kBar = kWCvt + kCvtStages * kWCvtBytes;
+  static constexpr int kNumBars = 2 * kRawStages + 2 * kCvtStages + 1 + 1;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kAlloc = kMisc + 16 + 1024;
+};
+
+struct QlParams {
+  int64_t M, N, K;
+  const uint16_t* q8_scale;  // Q8_0: [N, K/32] f16 bits
+  const float* fp8_scale;    // FP8: [N] or [1]
+  int64_t nscale;
+  const __nv_bfloat16* bias;  // [N] or null
+  __nv_bfloat16* y;           // [M, N]
+};
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// 4 int8 (one u32) * f32 scale -> 2 x bf16x2 (exact int8 -> f32 via the 2^23 magic number).
+__device__ __forceinline__ void q8x4_to_bf16(uint32_t w, float s, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;  // int8 -> biased uint8 (q + 128)
+  const float kMagic = 8388736.0f;     // 2^23 + 128
+  const float f0 = __uint_as_float(prmt(u, 0x4B000000u, 0x7650)) - kMagic;
+  const float f1 = __uint_as_float(prmt(u, 0x4B000000u, 0x7651)) - kMagic;
+  const float f2 = __uint_as_float(prmt(u, 0x4B000000u, 0x7652)) - kMagic;
+  const float f3 = __uint_as_float(prmt(u, 0x4B000000u, 0x7653)) - kMagic;
+  lo = pack_bf16x2(f0 * s, f1 * s);
+  hi = pack_bf16x2(f2 * s, f3 * s);
+}
+
+// 4 e4m3 bytes -> 2 x bf16x2, exact: the e4m3 bit pattern is placed in bf16 position
+// (exponent bias 7 instead of 127) and multiplied by 2^120; e4m3 subnormals land on bf16
+// subnormals and are scaled exactly as well.
+__device__ __forceinline__ void e4m3x4_to_bf16(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t a = prmt(w, 0u, 0x4140);  // b0 | b1 << 16
+  const uint32_t b = prmt(w, 0u, 0x4342);  // b2 | b3 << 16
+  const uint32_t ta = ((a & 0x007F007Fu) << 4) | ((a & 0x00800080u) << 8);
+  const uint32_t tb = ((b & 0x007F007Fu) << 4) | ((b & 0x00800080u) << 8);
+  const uint32_t k2p120 = 0x7B807B80u;  // bf16x2 {2^120, 2^120}
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(lo) : "r"(ta), "r"(k2p120));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(hi) : "r"(tb), "r"(k2p120));
+}
+
+template <int WF>
+__global__ void __launch_bounds__(kQThreads, 1)
+    qlinear_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
+                   const QlParams p) {
+  using L = QlSmem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = raw_full + kRawStages;
+  uint64_t* cvt_full = raw_empty + kRawStages;
+  uint64_t* cvt_empty = cvt_full + kCvtStages;
+  uint64_t* acc_full = cvt_empty + kCvtStages;
+  uint64_t* drain = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kQBM;
+  const int n0 = blockIdx.y * kQBN;
+  const int ktiles = (int)(p.K / kQBK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRawStages; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 1 + 128);  // MMA commit (x consumed) + 128 decoders (raw W)
+    }
+    for (int s = 0; s < kCvtStages; ++s) {
+      mbar_init(&cvt_full[s], 128);
+      mbar_init(&cvt_empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmx);
+      tma_prefetch_desc(&tmw);
+      int issued = 0;
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int st = kt % kRawStages;
+        const uint32_t ph = (kt / kRawStages) & 1;
+        if (kt >= kRawStages && !mbar_wait(&raw_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) break;
+        mbar_arrive_expect_tx(&raw_full[st], kXBytes + kWRawBytes);
+        tma_load_2d(smem + L::kX + st * kXBytes, &tmx, &raw_full[st], kt * kQBK, m0);
+        tma_load_2d(smem + L::kWRaw + st * kWRawBytes, &tmw, &raw_full[st], kt * kQBK, n0);
+        issued = kt + 1;
+      }
+      if (*abort_flag)
+        for (int kt = max(0, issued - kRawStages); kt < issued; ++kt)
+          mbar_wait(&raw_full[kt % kRawStages], (kt / kRawStages) & 1, nullptr, WD_TMA_WAIT);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(kQBM, kQBN, 1u, 0, 0);
+      bool ok = true;
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int rs = kt % kRawStages, cs = kt % kCvtStages;
+        if (!mbar_wait(&raw_full[rs], (kt / kRawStages) & 1, abort_flag, WD_MMA_WAIT) ||
+            !mbar_wait(&cvt_full[cs], (kt / kCvtStages) & 1, abort_flag, WD_MMA_WAIT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t xa = smem_u32(smem + L::kX + rs * kXBytes);
+        const uint32_t wb = smem_u32(smem + L::kWCvt + cs * kWCvtBytes);
+#pragma unroll
+        for (int kk = 0; kk < kQBK / 16; ++kk) {
+          const uint64_t a = make_smem_desc(xa + kk * 32, 16, 1024, LAYOUT_SW128);
+          const uint64_t b = make_smem_desc(wb + kk * 32, 16, 1024, LAYOUT_SW128);
+          umma_ss(tmem, a, b, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&raw_empty[rs]);
+        umma_commit(&cvt_empty[cs]);
+      }
+      if (ok) umma_commit(acc_full);
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, WD_MMA_WAIT);
+    }
+  } else {
+    // ------------------------------------------------------------ decoders
+    const int t = threadIdx.x - 64;  // 0..127
+    bool ok = true;
+    for (int kt = 0; kt < ktiles; ++kt) {
+      const int rs = kt % kRawStages, cs = kt % kCvtStages;
+      if (!mbar_wait(&raw_full[rs], (kt / kRawStages) & 1, abort_flag, WD_CONVERT_WAIT)) {
+        ok = false;
+        break;
+      }
+      if (kt >= kCvtStages &&
+          !mbar_wait(&cvt_empty[cs], ((kt / kCvtStages) - 1) & 1, abort_flag, WD_CONVERT_WAIT)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* raw = smem + L::kWRaw + rs * kWRawBytes;
+      uint8_t* cvt = smem + L::kWCvt + cs * kWCvtBytes;
+#pragma unroll 2
+      for (int it = 0; it < (kQBN * 4) / 128; ++it) {
+        const int task = t + it * 128;
+        const int row = task >> 2, ch = task & 3;  // 16 weights: k = 16*ch .. 16*ch+15
+        const uint4 w = *reinterpret_cast<const uint4*>(raw + row * 64 + ch * 16);
+        uint32_t o[8];
+        if constexpr (WF == W_Q8_0) {
+          const int64_t n = n0 + row;
+          float s = 0.f;
+          if (n < p.N)
+            s = __half2float(__ushort_as_half(
+                p.q8_scale[n * (p.K / 32) + (int64_t)kt * 2 + (ch >> 1)]));
+          q8x4_to_bf16(w.x, s, o[0], o[1]);
+          q8x4_to_bf16(w.y, s, o[2], o[3]);
+          q8x4_to_bf16(w.z, s, o[4], o[5]);
+          q8x4_to_bf16(w.w, s, o[6], o[7]);
+        } else {
+          e4m3x4_to_bf16(w.x, o[0], o[1]);
+          e4m3x4_to_bf16(w.y, o[2], o[3]);
+          e4m3x4_to_bf16(w.z, o[4], o[5]);
+          e4m3x4_to_bf16(w.w, o[6], o[7]);
+        }
+        // bf16 row of 64 = eight 16-byte chunks; this task fills chunks 2*ch and 2*ch+1
+        uint8_t* rowp = cvt + row * 128;
+        *reinterpret_cast<uint4*>(rowp + (((2 * ch) ^ (row & 7)) << 4)) =
+            make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(rowp + (((2 * ch + 1) ^ (row & 7)) << 4)) =
+            make_uint4(o[4], o[5], o[6], o[7]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&raw_empty[rs]);
+      mbar_arrive(&cvt_full[cs]);
+    }
+
+    // ------------------------------------------------------------ epilogue
+    if (ok && mbar_wait(acc_full, 0, abort_flag, WD_EPILOGUE_WAIT)) {
+      tc_fence_after();
+      const int quarter = warp & 3;
+      const int row = quarter * 32 + lane;
+      const int64_t m = m0 + row;
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+      for (int c = 0; c < kQBN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        tmem_wait_ld();
+        if (m >= p.M) continue;
+        const int64_t nb = n0 + c;
+        if (nb >= p.N) continue;
+        __nv_bfloat16* dst = p.y + m * p.N + nb;
+#pragma unroll
+        for (int g = 0; g < 32; g += 8) {
+          if (nb + g >= p.N) break;  // N % 16 == 0, so groups of 8 are whole
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int64_t n = nb + g + e;
+            float a = __uint_as_float(r[g + e]);
+            if constexpr (WF == W_FP8) a *= p.fp8_scale[p.nscale == 1 ? 0 : n];
+            if (p.bias) a += __bfloat162float(p.bias[n]);
+            v[e] = a;
+          }
+          *reinterpret_cast<uint4*>(dst + g) =
+              make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                         pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+template <int WF>
+int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_t s) {
+  if (!aligned(x, 16) || !aligned(w8, 16) || !aligned(p.y, 16))
+    return set_error(SP_ERR_ALIGN, "quantized linear: x, weights and y must be 16-byte aligned");
+  CUtensorMap mx, mw;
+  {
+    const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
+    const uint64_t strides[1] = {(uint64_t)p.K * 2};
+    const uint32_t box[2] = {kQBK, kQBM};
+    if (int rc = encode_tiled(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
+    const uint64_t strides[1] = {(uint64_t)p.K};
+    const uint32_t box[2] = {kQBK, kQBN};
+    if (int rc = encode_tiled(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w8, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+  }
+  auto kern = qlinear_kernel<WF>;
+  static_assert(QlSmem::kAlloc <= 232448, "quantized linear smem budget");
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, QlSmem::kAlloc);
+  if (e != cudaSuccess)
+    return set_error(SP_ERR_LAUNCH, "quantized linear: smem attribute failed: %s", cudaGetErrorString(e));
+  dim3 grid((unsigned)((p.M + kQBM - 1) / kQBM), (unsigned)((p.N + kQBN - 1) / kQBN));
+  kern<<<grid, kQThreads, QlSmem::kAlloc, s>>>(mx, mw, p);
+  return check_launch("quantized linear");
+}
+
+int check_ql_shape(int64_t M, int64_t N, int64_t K, int dtype) {
+  if (M <= 0 || N <= 0 || K <= 0) return set_error(SP_ERR_INVALID_ARG, "quantized linear: bad shape");
+  if (K % kQBK) return set_error(SP_ERR_SHAPE, "quantized linear: K=%lld must be a multiple of 64", (long long)K);
+  if (N % 16) return set_error(SP_ERR_SHAPE, "quantized linear: N=%lld must be a multiple of 16", (long long)N);
+  if (dtype != SP_BF16) return set_error(SP_ERR_DTYPE, "quantized linear: activations must be bf16");
+  if (M > 65535LL * kQBM || N > 65535LL * kQBN || K > (1LL << 31))
+    return set_error(SP_ERR_SHAPE, "quantized linear: shape too large");
+  return SP_OK;
+}
+
+}  // namespace
+}  // namespace sp
+
+extern "C" {
+
+int sp_q8_0_linear(const void* x, const void* q, const void* scale, const void* bias, void* y, int64_t M,
+                   int64_t N, int64_t K, int dtype, void* stream) {
+  using namespace sp;
+  clear_error();
+  if (!x || !q || !scale || !y) return set_error(SP_ERR_INVALID_ARG, "q8_0 linear: null pointer");
+  if (int rc = check_ql_shape(M, N, K, dtype)) return rc;
+  if (int rc = require_sm100()) return rc;
+  QlParams p{M, N, K, static_cast<const uint16_t*>(scale), nullptr, 0,
+             static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y)};
+  return launch_qlinear<W_Q8_0>(x, q, p, static_cast<cudaStream_t>(stream));
+}
+
+int sp_fp8_linear(const void* x, const void* w_e4m3, const float* scale, int64_t nscale, const void* bias,
+                  void* y, int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
+  using namespace sp;
+  clear_error();
+  if (!x || !w_e4m3 || !scale || !y) return set_error(SP_ERR_INVALID_ARG, "fp8 linear: null pointer");
+  if (nscale != 1 && nscale != N)
+    return set_error(SP_ERR_SHAPE, "fp8 linear: scale count %lld must be 1 or N", (long long)nscale);
+  if (int rc = check_ql_shape(M, N, K, dtype)) return rc;
+  if (int rc = require_sm100()) return rc;
+  QlParams p{M, N, K, nullptr, scale, nscale, static_cast<const __nv_bfloat16*>(bias),
+             static_cast<__nv_bfloat16*>(y)};
+  return launch_qlinear<W_FP8>(x, w_e4m3, p, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

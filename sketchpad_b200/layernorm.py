@@ -1,0 +1,45 @@
+"""LayerNorm with the reference's unbiased variance (crates/sketchpad-core/src/layernorm.rs:63-73).
+
+burn's `var` divides by n - 1, so this is NOT torch.nn.LayerNorm; the UNet and DiT blocks of
+the reference normalise this way and the step harness needs the same numbers.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._torch import dtype_code, ptr, require_cuda, stream_ptr
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5,
+               unbiased: bool = True, out=None) -> torch.Tensor:
+    dev = require_cuda(x, weight, bias, out)
+    n = x.shape[-1]
+    xx = x.contiguous()
+    dt = xx.dtype
+    w = (weight if weight.dtype == dt else weight.to(dt)).contiguous()
+    b = (bias if bias.dtype == dt else bias.to(dt)).contiguous()
+    y = out if out is not None else torch.empty_like(xx)
+    _lib.call("sp_layernorm", ptr(xx), ptr(w), ptr(b), ptr(y), xx.numel() // n, n, float(eps),
+              1 if unbiased else 0, dtype_code(dt), stream_ptr(dev))
+    return y
+
+
+class LayerNorm:
+    """sketchpad_core::layernorm::LayerNorm { weight, bias, eps }."""
+
+    def __init__(self, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5):
+        self.weight, self.bias, self.eps = weight, bias, eps
+
+    @classmethod
+    def new(cls, size: int, device="cuda", dtype=torch.bfloat16):
+        return cls(torch.ones(size, device=device, dtype=dtype),
+                   torch.zeros(size, device=device, dtype=dtype))
+
+    def forward(self, x):
+        return layer_norm(x, self.weight, self.bias, self.eps, True)
+
+    __call__ = forward
+
+
+__all__ = ["LayerNorm", "layer_norm"]

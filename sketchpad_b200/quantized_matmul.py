@@ -1,0 +1,133 @@
+"""Q8_0 (GGUF) linear layers with the dequantization fused into the GEMM mainloop.
+
+Host mirror of crates/sketchpad-cubecl/src/quantized_matmul.rs:
+  :33    GpuQuantType (Q8_0 is the format on this path; Q4_K/Q2_K/Q3_K are not built)
+  :376   dequantize_q8_0(packed, out_features, in_features)
+  :655   GpuQuantizedLinear { from_bytes :670, dequantize :705, forward_burn :726, forward :752 }
+Weights stay quantized in HBM (planar int8 + f16 block scales, a lossless repack of the
+34-byte GGUF blocks).  `dequantize()` in f32 is bit-exact with the CPU decode
+(crates/sketchpad-convert/src/gguf.rs:643-656); `forward` decodes to bf16 inside the GEMM.
+"""
+from __future__ import annotations
+
+import ctypes
+import enum
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._torch import dtype_code, ptr, require_cuda, stream_ptr
+
+
+class GpuQuantType(enum.Enum):
+    Q8_0 = "q8_0"
+
+
+def repack_q8_0_host(data: bytes | np.ndarray, out_features: int, in_features: int):
+    """GGUF Q8_0 bytes -> (q int8 [out, in], scale f16-bits uint16 [out, in/32]) on the host."""
+    buf = np.frombuffer(bytes(data), np.uint8) if not isinstance(data, np.ndarray) else \
+        np.ascontiguousarray(data, dtype=np.uint8)
+    q = np.empty((out_features, in_features), np.int8)
+    s = np.empty((out_features, in_features // 32), np.uint16)
+    _lib.call("sp_q8_0_repack_host", buf.ctypes.data_as(ctypes.c_void_p), buf.size, out_features,
+              in_features, q.ctypes.data_as(ctypes.c_void_p), s.ctypes.data_as(ctypes.c_void_p))
+    return q, s
+
+
+def dequantize_q8_0(q: torch.Tensor, scale: torch.Tensor, out_features: int, in_features: int,
+                    dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Planar Q8_0 -> [out_features, in_features] float (quantized_matmul.rs:376)."""
+    dev = require_cuda(q, scale)
+    out = torch.empty((out_features, in_features), dtype=dtype, device=dev)
+    _lib.call("sp_q8_0_dequant", ptr(q), ptr(scale), out_features, in_features, ptr(out),
+              dtype_code(dtype), stream_ptr(dev))
+    return out
+
+
+def repack_q8_0(gguf: torch.Tensor, out_features: int, in_features: int):
+    """Device repack of GGUF Q8_0 bytes already resident on the GPU (uint8 tensor)."""
+    dev = require_cuda(gguf)
+    q = torch.empty((out_features, in_features), dtype=torch.int8, device=dev)
+    s = torch.empty((out_features, in_features // 32), dtype=torch.int16, device=dev)
+    _lib.call("sp_q8_0_repack", ptr(gguf), gguf.numel(), out_features, in_features, ptr(q),
+              ptr(s), stream_ptr(dev))
+    return q, s
+
+
+class GpuQuantizedLinear:
+    """quantized_matmul.rs:655-767 for Q8_0: output = input @ weight.T (+ optional bias)."""
+
+    def __init__(self, q: torch.Tensor, scale: torch.Tensor, out_features: int, in_features: int,
+                 dtype: torch.dtype = torch.bfloat16, bias: Optional[torch.Tensor] = None):
+        self.q, self.scale = q, scale
+        self.quant_type = GpuQuantType.Q8_0
+        self.out_features, self.in_features = out_features, in_features
+        self.dtype = dtype
+        self.bias = bias
+
+    @classmethod
+    def from_bytes(cls, data, quant_type: GpuQuantType, out_features: int, in_features: int,
+                   device="cuda", dtype: torch.dtype = torch.bfloat16, bias=None):
+        """Upload raw GGUF bytes (little-endian Q8_0 blocks), repacked losslessly."""
+        if quant_type != GpuQuantType.Q8_0:
+            raise ValueError(f"{quant_type} is not supported (Q8_0 only)")
+        q, s = repack_q8_0_host(data, out_features, in_features)
+        return cls(torch.from_numpy(q).to(device), torch.from_numpy(s.view(np.int16)).to(device),
+                   out_features, in_features, dtype, bias)
+
+    def dequantize(self, dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        return dequantize_q8_0(self.q, self.scale, self.out_features, self.in_features,
+                               dtype or torch.float32)
+
+    def forward(self, input: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """[..., in_features] -> [..., out_features] via the fused dequant-GEMM (bf16)."""
+        dev = require_cuda(input, self.q)
+        lead = input.shape[:-1]
+        x = input.reshape(-1, self.in_features)
+        if x.dtype != torch.bfloat16:
+            x = x.to(torch.bfloat16)
+        x = x.contiguous()
+        M = x.shape[0]
+        y = out if out is not None else torch.empty((M, self.out_features), dtype=torch.bfloat16,
+                                                    device=dev)
+        b = self.bias
+        if b is not None and b.dtype != torch.bfloat16:
+            b = b.to(torch.bfloat16)
+        _lib.call("sp_q8_0_linear", ptr(x), ptr(self.q), ptr(self.scale), ptr(b), ptr(y), M,
+                  self.out_features, self.in_features, _lib.SP_BF16, stream_ptr(dev))
+        y = y.reshape(*lead, self.out_features)
+        return y if input.dtype == torch.bfloat16 else y.to(input.dtype)
+
+    forward_burn = forward
+    __call__ = forward
+
+
+def q8_0_quantize_reference(w: np.ndarray) -> bytes:
+    """GGUF Q8_0 encoder for building test/bench weights (ggml's scheme: per 32 values,
+    d = absmax/127 stored as f16, q = round(v/d)).  Used only to make synthetic inputs."""
+    w = np.asarray(w, np.float32).reshape(-1, 32)
+    amax = np.abs(w).max(axis=1)
+    d = (amax / 127.0).astype(np.float32)
+    d16 = d.astype(np.float16)
+    inv = np.where(d > 0, 1.0 / np.where(d > 0, d, 1), 0).astype(np.float32)
+    q = np.clip(np.rint(w * inv[:, None]), -128, 127).astype(np.int8)
+    out = np.empty((w.shape[0], 34), np.uint8)
+    out[:, :2] = d16.view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = q.view(np.uint8)
+    return out.tobytes()
+
+
+def make_q8_0_synthetic(out_features: int, in_features: int, seed: int = 0) -> bytes:
+    """BASELINE config 4's weights: int8 ~ U[-127,127], f16 scale ~ U(0.001, 0.02)."""
+    rng = np.random.default_rng(seed)
+    nb = out_features * in_features // 32
+    blocks = np.empty((nb, 34), np.uint8)
+    blocks[:, :2] = rng.uniform(0.001, 0.02, nb).astype(np.float16).view(np.uint8).reshape(-1, 2)
+    blocks[:, 2:] = rng.integers(-127, 128, (nb, 32), dtype=np.int8).view(np.uint8)
+    return blocks.tobytes()
+
+
+__all__ = ["GpuQuantType", "GpuQuantizedLinear", "dequantize_q8_0", "repack_q8_0",
+           "repack_q8_0_host", "q8_0_quantize_reference", "make_q8_0_synthetic"]

@@ -1,0 +1,76 @@
+"""The C-ABI library loads and exports every entry point include/sketchpad_b200.h declares,
+and its host-only paths (argument checks, host repack) work without a GPU."""
+import ctypes
+import os
+import re
+
+import numpy as np
+
+import oracle
+from sketchpad_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    src = open(os.path.join(ROOT, "include", "sketchpad_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(sp_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(L, n), f"{n} declared in the header but not exported"
+    assert set(names) == set(_lib.SIGNATURES), "ctypes binding and header disagree"
+
+
+def test_abi_version():
+    assert _lib.load().sp_abi_version() == 1
+
+
+def test_groupnorm_rejects_indivisible_channels_without_touching_the_gpu():
+    L = _lib.load()
+    st = _lib.i64_array((30 * 4, 4, 2, 1))
+    rc = L.sp_groupnorm_act(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16),
+                            ctypes.c_void_p(16), 1, 30, 2, 2, st, 32, 1e-5, 1, 0, None, 0, None)
+    assert rc == -2
+    assert b"divisible" in L.sp_last_error()
+
+
+def test_null_and_shape_errors_are_status_codes():
+    L = _lib.load()
+    s4 = _lib.i64_array((1, 1, 1, 1))
+    assert L.sp_flash_attn_fwd(None, None, None, None, 0, None, 1, 1, 1, 1, 64, 64, s4, s4, s4, s4,
+                               2, 2, 0, 0.0, None) == -1
+    p = ctypes.c_void_p(256)
+    assert L.sp_flash_attn_fwd(p, p, p, None, 0, p, 1, 1, 1, 1, 36, 36, s4, s4, s4, s4, 2, 2, 0,
+                               0.0, None) == -2  # head dim not a multiple of 8
+    assert L.sp_q8_0_linear(p, p, p, None, p, 4, 16, 48, 2, None) == -2  # K % 64
+    assert L.sp_fp8_linear(p, p, p, 3, None, p, 4, 16, 64, 2, None) == -2  # scale count
+    assert L.sp_layernorm(p, p, p, p, 4, 1, 1e-5, 1, 0, None) == -1
+
+
+def test_q8_0_host_repack_matches_oracle_decode():
+    rng = np.random.default_rng(0)
+    out_f, in_f = 8, 96
+    nb = out_f * in_f // 32
+    blocks = np.empty((nb, 34), np.uint8)
+    # include subnormal and negative f16 scales
+    scales = rng.uniform(-0.02, 0.02, nb).astype(np.float16)
+    scales[:3] = np.array([6e-8, -3e-6, 0.0], np.float16)
+    blocks[:, :2] = scales.view(np.uint8).reshape(-1, 2)
+    blocks[:, 2:] = rng.integers(-128, 128, (nb, 32), dtype=np.int8).view(np.uint8)
+    raw = blocks.tobytes()
+    q = np.empty((out_f, in_f), np.int8)
+    s = np.empty((out_f, in_f // 32), np.uint16)
+    buf = np.frombuffer(raw, np.uint8)
+    rc = _lib.load().sp_q8_0_repack_host(buf.ctypes.data_as(ctypes.c_void_p), buf.size, out_f, in_f,
+                                         q.ctypes.data_as(ctypes.c_void_p),
+                                         s.ctypes.data_as(ctypes.c_void_p))
+    assert rc == 0
+    dec = oracle.f16_bits_to_f32(s).repeat(32, axis=1) * q.astype(np.float32)
+    ref = oracle.q8_0_dequantize(buf, out_f * in_f).reshape(out_f, in_f)
+    assert np.array_equal(dec.view(np.uint32), ref.view(np.uint32))

@@ -1,0 +1,102 @@
+"""GroupNorm(+SiLU) CUDA kernel vs the CPU oracle (crates/sketchpad-core/src/groupnorm.rs:62-102).
+
+Metric: rel_err = max|gpu - oracle| / max|oracle|; bars: 1e-3 (fp32), 2e-2 (fp16/bf16).
+Inputs follow BASELINE config 2: x ~ N(0,1)*3+0.5, gamma ~ N(1,0.1), beta ~ N(0,0.1), seed 0.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from sketchpad_b200 import GroupNormSiLuLayer, GroupNormSiLuOptions, groupnorm, groupnorm_silu
+from helpers import TOL_F32, TOL_HALF, rel_err, to_np
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(2, 320, 64, 64), (2, 640, 32, 32), (2, 1280, 16, 16), (2, 512, 128, 128),
+          (8, 320, 64, 64), (8, 640, 32, 32), (8, 1280, 16, 16), (8, 512, 128, 128)]
+
+
+def make(shape, seed=0):
+    rng = np.random.default_rng(seed)
+    B, C, H, W = shape
+    x = (rng.standard_normal(shape, dtype=np.float32) * 3 + 0.5).astype(np.float32)
+    g = (rng.standard_normal(C, dtype=np.float32) * 0.1 + 1).astype(np.float32)
+    b = (rng.standard_normal(C, dtype=np.float32) * 0.1).astype(np.float32)
+    return x, g, b
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_groupnorm_silu_baseline_sweep(shape, dtype):
+    x, g, b = make(shape)
+    xt = torch.from_numpy(x).cuda().to(dtype)
+    # the oracle sees exactly the values the GPU sees
+    ref = oracle.groupnorm_act(to_np(xt), to_np(torch.from_numpy(g).to(dtype)),
+                               to_np(torch.from_numpy(b).to(dtype)), 32, 1e-5, silu=True)
+    y = groupnorm_silu(xt, torch.from_numpy(g).cuda().to(dtype), torch.from_numpy(b).cuda().to(dtype))
+    torch.cuda.synchronize()
+    tol = TOL_F32 if dtype == torch.float32 else TOL_HALF
+    assert rel_err(to_np(y), ref) < tol
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_groupnorm_without_silu(dtype):
+    x, g, b = make((2, 320, 64, 64), seed=1)
+    xt = torch.from_numpy(x).cuda().to(dtype)
+    ref = oracle.groupnorm_act(to_np(xt), to_np(torch.from_numpy(g).to(dtype)),
+                               to_np(torch.from_numpy(b).to(dtype)), 32, 1e-5, silu=False)
+    y = groupnorm(xt, torch.from_numpy(g).cuda(), torch.from_numpy(b).cuda())
+    tol = TOL_F32 if dtype == torch.float32 else TOL_HALF
+    assert rel_err(to_np(y), ref) < tol
+
+
+@pytest.mark.parametrize("shape,groups", [((1, 32, 8, 8), 8), ((3, 64, 7, 9), 32),
+                                          ((1, 4, 1, 1), 2), ((2, 96, 5, 5), 32),
+                                          ((1, 64, 300, 300), 32), ((1, 32, 96, 96), 1)])
+def test_groupnorm_ragged_and_general_paths(shape, groups):
+    # odd spatial sizes (no 16-byte vectors), tiny groups, and groups too large for one
+    # cluster (the two-pass workspace path)
+    x, _, _ = make(shape, seed=2)
+    C = shape[1]
+    rng = np.random.default_rng(3)
+    g = rng.uniform(0.5, 1.5, C).astype(np.float32)
+    b = rng.uniform(-0.5, 0.5, C).astype(np.float32)
+    ref = oracle.groupnorm_act(x, g, b, groups, 1e-5, silu=True)
+    y = groupnorm_silu(torch.from_numpy(x).cuda(), torch.from_numpy(g).cuda(),
+                       torch.from_numpy(b).cuda(), GroupNormSiLuOptions(groups, 1e-5))
+    assert rel_err(to_np(y), ref) < TOL_F32
+
+
+def test_groupnorm_strided_input():
+    # a channels-last view: non-contiguous NCHW strides go through the general path
+    x, g, b = make((2, 64, 16, 16), seed=4)
+    xt = torch.from_numpy(x).cuda().to(memory_format=torch.channels_last)
+    assert not xt.is_contiguous()
+    ref = oracle.groupnorm_act(x, g, b, 32, 1e-5, silu=True)
+    y = groupnorm_silu(xt, torch.from_numpy(g).cuda(), torch.from_numpy(b).cuda())
+    assert y.is_contiguous()
+    assert rel_err(to_np(y), ref) < TOL_F32
+
+
+def test_groupnorm_clamps_large_values():
+    x, g, b = make((1, 32, 4, 4), seed=5)
+    x[0, 0, 0, 0] = 1e6
+    x[0, 5, 1, 1] = -3e5
+    ref = oracle.groupnorm_act(x, g, b, 8, 1e-5, silu=False)
+    y = groupnorm(torch.from_numpy(x).cuda(), torch.from_numpy(g).cuda(),
+                  torch.from_numpy(b).cuda(), GroupNormSiLuOptions(8))
+    assert rel_err(to_np(y), ref) < TOL_F32
+
+
+def test_groupnorm_rejects_indivisible_channels():
+    x = torch.zeros(1, 30, 2, 2, device="cuda")
+    with pytest.raises(ValueError):
+        groupnorm_silu(x, torch.ones(30, device="cuda"), torch.zeros(30, device="cuda"))
+
+
+def test_groupnorm_layer_api():
+    x, g, b = make((2, 640, 32, 32), seed=6)
+    layer = GroupNormSiLuLayer.from_tensors(32, torch.from_numpy(g).cuda(), torch.from_numpy(b).cuda())
+    ref = oracle.groupnorm_act(x, g, b, 32, 1e-5, silu=True)
+    assert rel_err(to_np(layer.forward(torch.from_numpy(x).cuda())), ref) < TOL_F32

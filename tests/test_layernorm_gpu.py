@@ -1,0 +1,23 @@
+"""LayerNorm (unbiased variance, crates/sketchpad-core/src/layernorm.rs:63-73) vs the oracle.
+Metric rel_err = max|gpu - oracle| / max|oracle|: 1e-3 (fp32), 2e-2 (bf16)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from sketchpad_b200 import layer_norm
+from helpers import TOL_F32, TOL_HALF, rel_err, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("rows,n", [(8192, 320), (2048, 640), (512, 1280), (77, 768), (5, 3)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_layernorm(rows, n, dtype):
+    g = torch.Generator().manual_seed(rows + n)
+    x = (torch.randn(rows, n, generator=g) * 2 + 0.3).to(dtype)
+    w = (torch.randn(n, generator=g) * 0.1 + 1).to(dtype)
+    b = (torch.randn(n, generator=g) * 0.1).to(dtype)
+    y = layer_norm(x.cuda(), w.cuda(), b.cuda())
+    ref = oracle.layernorm(to_np(x), to_np(w), to_np(b))
+    assert rel_err(to_np(y), ref) < (TOL_F32 if dtype == torch.float32 else TOL_HALF)

@@ -1,0 +1,159 @@
+"""Q8_0 and FP8 weight paths vs the CPU oracle.
+
+Dequantized weights: bit-exact (f32).  Linears (bf16 activations, bf16 output): rel_err =
+max|gpu - oracle| / max|oracle| < 2e-2, the oracle running in fp32 on the same bf16 x.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from sketchpad_b200 import (Fp8Config, Fp8Linear, GpuQuantizedLinear, GpuQuantType,
+                            dequantize_q8_0, quantize_fp8, repack_q8_0)
+from sketchpad_b200.quantized_matmul import make_q8_0_synthetic, q8_0_quantize_reference
+from sketchpad_b200.quantization import Fp8Tensor, Fp8Format
+from helpers import TOL_HALF, rel_err, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def test_q8_0_golden_vectors_on_gpu():
+    import json, os
+    here = os.path.join(os.path.dirname(__file__), "golden")
+    for name in ("q8_0_decode_scale_half", "q8_0_decode_known_values"):
+        case = json.load(open(os.path.join(here, name + ".json")))
+        raw = bytes.fromhex(case["bytes_hex"])
+        lin = GpuQuantizedLinear.from_bytes(raw, GpuQuantType.Q8_0, 1, 32)
+        got = to_np(lin.dequantize()).ravel()
+        assert np.array_equal(got, np.array(case["expected"], np.float32))
+
+
+def test_q8_0_dequant_bit_exact_with_subnormal_scales():
+    out_f, in_f = 64, 256
+    raw = bytearray(make_q8_0_synthetic(out_f, in_f, seed=1))
+    blocks = np.frombuffer(raw, np.uint8).reshape(-1, 34).copy()
+    blocks[:4, :2] = np.array([6e-8, -3e-6, 0.0, 1e-5], np.float16).view(np.uint8).reshape(-1, 2)
+    raw = blocks.tobytes()
+    ref = oracle.q8_0_dequantize(np.frombuffer(raw, np.uint8), out_f * in_f).reshape(out_f, in_f)
+    lin = GpuQuantizedLinear.from_bytes(raw, GpuQuantType.Q8_0, out_f, in_f)
+    got = to_np(lin.dequantize(torch.float32))
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    # device repack of GGUF bytes gives the same planar layout
+    q, s = repack_q8_0(torch.frombuffer(bytearray(raw), dtype=torch.uint8).cuda(), out_f, in_f)
+    assert torch.equal(q, lin.q) and torch.equal(s, lin.scale)
+    got2 = to_np(dequantize_q8_0(q, s, out_f, in_f))
+    assert np.array_equal(got2.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (200, 48, 128), (4608, 3072, 3072),
+                                   (512, 9216, 3072), (77, 1280, 12288)])
+def test_q8_0_linear_vs_oracle(M, N, K):
+    raw = make_q8_0_synthetic(N, K, seed=M + N)
+    lin = GpuQuantizedLinear.from_bytes(raw, GpuQuantType.Q8_0, N, K)
+    g = torch.Generator(device="cpu").manual_seed(1)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    y = lin.forward(x.cuda())
+    torch.cuda.synchronize()
+    rows = slice(0, min(M, 256))  # the sequential-dot oracle is slow; check leading rows
+    ref = oracle.q8_0_matmul(np.frombuffer(raw, np.uint8), N, K, to_np(x[rows]))
+    assert rel_err(to_np(y[rows]), ref) < TOL_HALF
+    if M > 256:
+        ref_tail = oracle.q8_0_matmul(np.frombuffer(raw, np.uint8), N, K, to_np(x[-64:]))
+        assert rel_err(to_np(y[-64:]), ref_tail) < TOL_HALF
+
+
+def test_q8_0_linear_golden_2x32_padded():
+    # quantized.rs:516-552: out = [~3, ~7]; N is padded to 16 rows of zero weights
+    import json, os
+    case = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "q8_0_matmul_2x32.json")))
+    raw = bytes.fromhex(case["bytes_hex"])
+    zero_blocks = bytes(34 * 14 * 2)  # 14 more rows of 64 values (2 blocks each)
+    rows = []
+    blocks = np.frombuffer(raw, np.uint8).reshape(2, 34)
+    for r in range(2):  # widen each row to 64 values (K must be a multiple of 64)
+        rows.append(blocks[r].tobytes() + bytes(34))
+    full = b"".join(rows) + zero_blocks
+    lin = GpuQuantizedLinear.from_bytes(full, GpuQuantType.Q8_0, 16, 64)
+    x = torch.zeros(1, 64, dtype=torch.bfloat16)
+    x[0, :32] = torch.tensor(case["input"])
+    y = to_np(lin.forward(x.cuda()))[0]
+    assert abs(y[0] - 3.0) < case["tol"] and abs(y[1] - 7.0) < case["tol"]
+    assert np.all(y[2:] == 0)
+
+
+def test_q8_0_linear_with_bias_3d():
+    N, K = 256, 128
+    raw = q8_0_quantize_reference(np.random.default_rng(2).standard_normal((N, K)).astype(np.float32))
+    bias = torch.randn(N, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    lin = GpuQuantizedLinear.from_bytes(raw, GpuQuantType.Q8_0, N, K, bias=bias.cuda())
+    x = torch.randn(2, 3, K, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16)
+    y = lin.forward(x.cuda())
+    assert y.shape == (2, 3, N)
+    ref = oracle.q8_0_matmul(np.frombuffer(raw, np.uint8), N, K, to_np(x).reshape(6, K)) + to_np(bias)
+    assert rel_err(to_np(y).reshape(6, N), ref) < TOL_HALF
+
+
+def test_fp8_quantize_matches_reference_rounding():
+    g = torch.Generator(device="cpu").manual_seed(5)
+    w = torch.randn(64, 512, generator=g) * torch.rand(64, 1, generator=g) * 10
+    fp8 = quantize_fp8(w.cuda(), Fp8Config.e4m3().with_per_channel(True))
+    data_ref, scale_ref = oracle.fp8_quantize(w.numpy(), 0, True)
+    assert np.array_equal(to_np(fp8.scale), scale_ref)
+    deq = to_np(fp8.dequantize())
+    deq_ref = oracle.fp8_dequantize(data_ref, scale_ref)
+    # bit-exact wherever the reference's simulated value is on the e4m3 grid (|scaled| >= 2^-6)
+    scaled = np.abs(w.numpy() / scale_ref[:, None])
+    on_grid = scaled >= 2.0 ** -6
+    assert on_grid.mean() > 0.99
+    assert np.array_equal(deq[on_grid].view(np.uint32), deq_ref[on_grid].view(np.uint32))
+    # below 2^-6 the e4m3 subnormal grid differs from the reference by < 2^-10 * scale
+    off = ~on_grid
+    assert np.all(np.abs(deq[off] - deq_ref[off]) <= (2.0 ** -10) * np.broadcast_to(scale_ref[:, None], deq.shape)[off] * 1.0001)
+
+
+def test_fp8_per_tensor_and_explicit_scale():
+    w = torch.tensor([[1.0, 2.0, 3.0, 4.0], [0.5, 1.5, 2.5, 3.5]])
+    t = quantize_fp8(w.cuda(), Fp8Config.e4m3())
+    d_ref, s_ref = oracle.fp8_quantize(w.numpy(), 0, False)
+    assert np.array_equal(to_np(t.scale), s_ref)
+    assert np.array_equal(to_np(t.dequantize()), oracle.fp8_dequantize(d_ref, s_ref))
+    assert np.abs(to_np(t.dequantize()) - w.numpy()).max() < 0.5  # quantization.rs:815-831
+    t2 = quantize_fp8(w.cuda(), Fp8Config.e4m3().with_scale(0.01))
+    d2, s2 = oracle.fp8_quantize(w.numpy(), 0, False, scale=0.01)
+    assert np.array_equal(to_np(t2.dequantize()), oracle.fp8_dequantize(d2, s2))
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 160, 320), (2048, 5120, 5120),
+                                   (512, 13824, 5120), (256, 5120, 13824)])
+def test_fp8_linear_vs_oracle(M, N, K):
+    g = torch.Generator(device="cpu").manual_seed(M + K)
+    w = torch.randn(N, K, generator=g) * 0.02
+    bias = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+    lin = Fp8Linear.from_weight(w.cuda(), bias.cuda(), Fp8Config.e4m3().with_per_channel(True))
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    y = lin.forward(x.cuda())
+    torch.cuda.synchronize()
+    wdq = to_np(lin.weight.dequantize())  # bit-exact decode (tested above)
+    rows = slice(0, min(M, 256))
+    ref = oracle.linear_nt(to_np(x[rows]), wdq, to_np(bias))
+    assert rel_err(to_np(y[rows]), ref) < TOL_HALF
+
+
+def test_fp8_synthetic_bytes_roundtrip():
+    t = Fp8Tensor(torch.arange(256, dtype=torch.uint8).reshape(16, 16).cuda(),
+                  torch.ones(16).cuda(), Fp8Format.E4M3, (16, 16))
+    got = to_np(t.dequantize()).ravel()
+    # e4m3 decode from the OCP bit layout, computed independently here
+    exp = []
+    for b in range(256):
+        s = -1.0 if b & 0x80 else 1.0
+        e, m = (b >> 3) & 0xF, b & 7
+        if e == 0xF and m == 7:
+            exp.append(np.nan)
+        elif e == 0:
+            exp.append(s * m / 8 * 2.0 ** -6)
+        else:
+            exp.append(s * (1 + m / 8) * 2.0 ** (e - 7))
+    exp = np.array(exp, np.float32)
+    ok = ~np.isnan(exp)
+    assert np.array_equal(got[ok], exp[ok]) and np.all(np.isnan(got[~ok]))
