@@ -1,0 +1,261 @@
+"""Flux-shaped MMDiT denoise step with Q8_0 weights on the B200 kernels.
+
+Follows rhi-zone/sketchpad crates/sketchpad-dit/src/flux.rs:
+  :60-96     FluxConfig::flux_dev (hidden 3072, 24 heads x 128, 19 double + 38 single blocks,
+             text_dim 4096, time_dim 256, mlp_ratio 4); max_seq_len must cover 4608 tokens
+             for the single blocks (the reference's default 4096 cache would be sliced past)
+  :199-247   timestep_freqs / TimestepEmbedding::forward_scalar
+  :325-422   FluxAttention::forward (qkv -> RoPE on the stream's own q,k -> K/V = cat(self,
+             other stream through the SAME qkv, no RoPE) -> softmax(QK^T/sqrt(d))V -> proj)
+  :450-517   FluxDoubleBlock::forward (image stream first; the text stream attends to the
+             UPDATED image tokens)
+  :573-607   FluxSingleBlock::forward (one gate for both residual branches)
+  :620-636   FinalLayer, :686-741 Flux::forward
+  crates/sketchpad-core/src/rope.rs:60-170   1-D interleaved-pair RoPE, theta 10000
+  crates/sketchpad-core/src/glu.rs:91-96     SwiGLU: down(silu(gate(x)) * up(x)), biased
+  crates/sketchpad-core/src/dit.rs:299-345   PatchEmbed / unpatchify
+Every Linear is a Q8_0 GpuQuantizedLinear (fused dequant-GEMM); attention is the tcgen05
+flash kernel; LayerNorm is the unbiased kernel.  RoPE, modulation and SwiGLU gating are torch
+element-wise glue.  Weights: int8 ~ U[-127,127], f16 block scale ~ U(0.001, 0.02), biases
+~ N(0, 0.02) (the config's synthetic init; the values blow activations up over 57 blocks,
+so whole-model numbers are timing-only -- parity is checked per block).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from .attention import flash_attention
+from .layernorm import layer_norm
+from .quantized_matmul import GpuQuantizedLinear
+
+
+@dataclass(frozen=True)
+class FluxConfig:
+    in_channels: int = 16
+    patch_size: int = 2
+    hidden_size: int = 3072
+    num_heads: int = 24
+    num_double_blocks: int = 19
+    num_single_blocks: int = 38
+    text_dim: int = 4096
+    time_dim: int = 256
+    guidance_dim: int = 256
+    max_seq_len: int = 4608
+    mlp_ratio: float = 4.0
+
+    @property
+    def head_dim(self):
+        return self.hidden_size // self.num_heads
+
+    @property
+    def intermediate(self):
+        return int(self.hidden_size * self.mlp_ratio)
+
+
+def flux_timestep_freqs(dim: int) -> np.ndarray:
+    """flux.rs:199-207 (emb_scale = -ln(2) / (half - 1), as the reference writes it)."""
+    half = dim // 2
+    emb_scale = np.float32(-math.log(2.0)) / np.float32(half - 1)
+    return np.exp(emb_scale * np.arange(half, dtype=np.float32)).astype(np.float32)
+
+
+def rope_tables(head_dim: int, seq_len: int, base: float = 10000.0):
+    """rope.rs:60-94: cos/sin [seq, head_dim], each frequency repeated for its pair."""
+    half = head_dim // 2
+    inv = np.array([1.0 / (base ** ((2 * i) / head_dim)) for i in range(half)], np.float32)
+    ang = np.arange(seq_len, dtype=np.float32)[:, None] * inv[None, :]
+    cos = np.repeat(np.cos(ang), 2, axis=1).astype(np.float32)
+    sin = np.repeat(np.sin(ang), 2, axis=1).astype(np.float32)
+    return cos, sin
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """rope.rs:145-170: x*cos + rotate_half(x)*sin, rotate_half([x0,x1,..]) = [-x1,x0,..]."""
+    S = x.shape[2]
+    x2 = x.unflatten(-1, (-1, 2))
+    rot = torch.stack((-x2[..., 1], x2[..., 0]), dim=-1).flatten(-2)
+    return x * cos[:S] + rot * sin[:S]
+
+
+def _q8_linear(rng_seed: int, n: int, k: int, device, bias=True):
+    """A Q8_0 Linear [n out, k in] with the config's synthetic weights, drawn on the GPU."""
+    g = torch.Generator(device=device).manual_seed(rng_seed)
+    q = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int32).to(torch.int8)
+    s = (torch.rand((n, k // 32), generator=g, device=device) * 0.019 + 0.001).to(torch.float16)
+    b = (torch.randn(n, generator=g, device=device) * 0.02).to(torch.bfloat16) if bias else None
+    return GpuQuantizedLinear(q, s.view(torch.int16), n, k, torch.bfloat16, b)
+
+
+class _Attn:
+    def __init__(self, seed, cfg: FluxConfig, device):
+        h = cfg.hidden_size
+        self.qkv = _q8_linear(seed, 3 * h, h, device)
+        self.proj = _q8_linear(seed + 1, h, h, device)
+        # rows [h, 3h) of the qkv weight produce k and v: the cross stream needs only those
+        self.kv = GpuQuantizedLinear(self.qkv.q[h:], self.qkv.scale[h:], 2 * h, h, torch.bfloat16,
+                                     self.qkv.bias[h:])
+        self.H, self.D = cfg.num_heads, cfg.head_dim
+
+    def forward(self, x, cos, sin, cross=None):
+        b, s, _ = x.shape
+        qkv = self.qkv(x).view(b, s, 3, self.H, self.D)
+        q = apply_rope(qkv[:, :, 0].transpose(1, 2), cos, sin)
+        k = apply_rope(qkv[:, :, 1].transpose(1, 2), cos, sin)
+        v = qkv[:, :, 2].transpose(1, 2)
+        if cross is not None:
+            c = cross.shape[1]
+            kv = self.kv(cross).view(b, c, 2, self.H, self.D)
+            k = torch.cat([k, kv[:, :, 0].transpose(1, 2)], dim=2)
+            v = torch.cat([v, kv[:, :, 1].transpose(1, 2)], dim=2)
+        o = torch.empty((b, s, self.H, self.D), dtype=x.dtype, device=x.device)
+        flash_attention(q, k, v, out=o.transpose(1, 2))
+        return self.proj(o.view(b, s, self.H * self.D))
+
+
+class _SwiGlu:
+    def __init__(self, seed, cfg: FluxConfig, device):
+        h, i = cfg.hidden_size, cfg.intermediate
+        gate, up = _q8_linear(seed, i, h, device), _q8_linear(seed + 1, i, h, device)
+        # gate and up share x: one GEMM over the stacked rows
+        self.gate_up = GpuQuantizedLinear(torch.cat([gate.q, up.q]), torch.cat([gate.scale, up.scale]),
+                                          2 * i, h, torch.bfloat16, torch.cat([gate.bias, up.bias]))
+        self.down = _q8_linear(seed + 2, h, i, device)
+        self.i = i
+
+    def forward(self, x):
+        gu = self.gate_up(x)
+        return self.down(F.silu(gu[..., : self.i]) * gu[..., self.i:])
+
+
+def _ln(x):
+    # LayerNorm::new(hidden): gamma 1, beta 0, unbiased variance (layernorm.rs:63-73)
+    n = x.shape[-1]
+    one = torch.ones(n, dtype=x.dtype, device=x.device)
+    return layer_norm(x, one, torch.zeros_like(one), 1e-5, True)
+
+
+class FluxDoubleBlockB200:
+    def __init__(self, seed, cfg: FluxConfig, device):
+        h = cfg.hidden_size
+        self.img_attn, self.txt_attn = _Attn(seed, cfg, device), _Attn(seed + 10, cfg, device)
+        self.img_ffn, self.txt_ffn = _SwiGlu(seed + 20, cfg, device), _SwiGlu(seed + 30, cfg, device)
+        self.modulation = _q8_linear(seed + 40, 6 * h, h, device)
+        self.h = h
+
+    def forward(self, img, txt, cond, cos, sin):
+        b = img.shape[0]
+        m = self.modulation(cond).view(b, 1, 6, self.h)
+        shift, scale, gate = m[:, :, 0], m[:, :, 1], m[:, :, 2]
+        x = (1 + scale) * _ln(img) + shift
+        img = img + gate * self.img_attn.forward(x, cos, sin, txt)
+        img = img + gate * self.img_ffn.forward(_ln(img))
+        shift, scale, gate = m[:, :, 3], m[:, :, 4], m[:, :, 5]
+        x = (1 + scale) * _ln(txt) + shift
+        txt = txt + gate * self.txt_attn.forward(x, cos, sin, img)
+        txt = txt + gate * self.txt_ffn.forward(_ln(txt))
+        return img, txt
+
+
+class FluxSingleBlockB200:
+    def __init__(self, seed, cfg: FluxConfig, device):
+        h = cfg.hidden_size
+        self.attn = _Attn(seed, cfg, device)
+        self.ffn = _SwiGlu(seed + 20, cfg, device)
+        self.modulation = _q8_linear(seed + 40, 3 * h, h, device)
+        self.h = h
+
+    def forward(self, x, cond, cos, sin):
+        b = x.shape[0]
+        m = self.modulation(cond).view(b, 1, 3, self.h)
+        shift, scale, gate = m[:, :, 0], m[:, :, 1], m[:, :, 2]
+        xn = (1 + scale) * _ln(x) + shift
+        x = x + gate * self.attn.forward(xn, cos, sin)
+        return x + gate * self.ffn.forward(_ln(x))
+
+
+class FluxB200:
+    """Flux::forward (flux.rs:686-741) for one prompt per GPU."""
+
+    def __init__(self, cfg: FluxConfig = FluxConfig(), device="cuda", seed: int = 0,
+                 num_double: int | None = None, num_single: int | None = None):
+        self.cfg, self.device = cfg, torch.device(device)
+        h = cfg.hidden_size
+        pd = cfg.patch_size ** 2 * cfg.in_channels
+        # patch / text / time projections are tiny next to the blocks; K % 64 rules them
+        # onto bf16 torch linears (patch_dim 64 and time_dim 256 do satisfy it, text_dim too)
+        self.img_embed = _q8_linear(seed + 1, h, pd, device)
+        self.txt_embed = _q8_linear(seed + 2, h, cfg.text_dim, device)
+        self.t1, self.t2 = _q8_linear(seed + 3, h, cfg.time_dim, device), _q8_linear(seed + 4, h, h, device)
+        self.g1, self.g2 = _q8_linear(seed + 5, h, cfg.guidance_dim, device), _q8_linear(seed + 6, h, h, device)
+        nd = cfg.num_double_blocks if num_double is None else num_double
+        ns = cfg.num_single_blocks if num_single is None else num_single
+        self.double = [FluxDoubleBlockB200(seed + 100 + 50 * i, cfg, device) for i in range(nd)]
+        self.single = [FluxSingleBlockB200(seed + 5000 + 50 * i, cfg, device) for i in range(ns)]
+        self.final_mod = _q8_linear(seed + 7, 2 * h, h, device)
+        self.final_proj = _q8_linear(seed + 8, pd, h, device)
+        cos, sin = rope_tables(cfg.head_dim, cfg.max_seq_len)
+        self.cos = torch.from_numpy(cos).to(self.device, torch.bfloat16)
+        self.sin = torch.from_numpy(sin).to(self.device, torch.bfloat16)
+        self.tfreq = torch.from_numpy(flux_timestep_freqs(cfg.time_dim)).to(self.device)
+        self.gfreq = torch.from_numpy(flux_timestep_freqs(cfg.guidance_dim)).to(self.device)
+
+    def _temb(self, t: float, freqs, l1, l2):
+        a = freqs * t
+        e = torch.cat([torch.sin(a), torch.cos(a)])[None].to(torch.bfloat16)
+        return l2(F.silu(l1(e)))
+
+    def forward(self, latents: torch.Tensor, timestep: float, txt_embeds: torch.Tensor,
+                guidance: float | None = None) -> torch.Tensor:
+        cfg = self.cfg
+        B, C, Hh, Ww = latents.shape
+        ps = cfg.patch_size
+        ph, pw = Hh // ps, Ww // ps
+        # PatchEmbed (dit.rs:299-315): reshape, swap_dims(2,4), swap_dims(3,5), reshape
+        x = latents.to(torch.bfloat16).reshape(B, C, ph, ps, pw, ps).permute(0, 1, 4, 5, 2, 3)
+        img = self.img_embed(x.reshape(B, ph * pw, C * ps * ps))
+        txt = self.txt_embed(txt_embeds.to(torch.bfloat16))
+        cond = self._temb(timestep, self.tfreq, self.t1, self.t2)
+        if guidance is not None:
+            cond = cond + self._temb(guidance, self.gfreq, self.g1, self.g2)
+        for blk in self.double:
+            img, txt = blk.forward(img, txt, cond, self.cos, self.sin)
+        x = torch.cat([img, txt], dim=1)
+        for blk in self.single:
+            x = blk.forward(x, cond, self.cos, self.sin)
+        x = x[:, : ph * pw]
+        m = self.final_mod(cond).view(B, 1, 2 * cfg.hidden_size)
+        shift, scale = m[..., : cfg.hidden_size], m[..., cfg.hidden_size:]
+        out = self.final_proj((1 + scale) * _ln(x) + shift)
+        # unpatchify (dit.rs:327-345)
+        out = out.reshape(B, ph, pw, C, ps, ps).permute(0, 3, 4, 5, 1, 2)
+        return out.reshape(B, C, Hh, Ww)
+
+    __call__ = forward
+
+
+def flux_step_flops(cfg: FluxConfig = FluxConfig(), img_tokens=4096, txt_tokens=512,
+                    num_double=None, num_single=None) -> float:
+    """Algorithmic FLOPs of the blocks of one Flux step (2 per MAC; linears + attention)."""
+    h, i, H, D = cfg.hidden_size, cfg.intermediate, cfg.num_heads, cfg.head_dim
+    nd = cfg.num_double_blocks if num_double is None else num_double
+    ns = cfg.num_single_blocks if num_single is None else num_single
+    S = img_tokens + txt_tokens
+    lin = lambda m, n, k: 2.0 * m * n * k  # noqa: E731
+    dbl = 0.0
+    for s_self, s_other in ((img_tokens, txt_tokens), (txt_tokens, img_tokens)):
+        dbl += lin(s_self, 3 * h, h) + lin(s_other, 2 * h, h) + lin(s_self, h, h)
+        dbl += lin(s_self, 2 * i, h) + lin(s_self, h, i)
+        dbl += 4.0 * H * s_self * S * D
+    dbl += lin(1, 6 * h, h)
+    sgl = lin(S, 3 * h, h) + lin(S, h, h) + lin(S, 2 * i, h) + lin(S, h, i) + 4.0 * H * S * S * D
+    sgl += lin(1, 3 * h, h)
+    return nd * dbl + ns * sgl
+
+
+__all__ = ["FluxConfig", "FluxB200", "FluxDoubleBlockB200", "FluxSingleBlockB200",
+           "flux_step_flops", "rope_tables", "apply_rope", "flux_timestep_freqs"]

@@ -1,0 +1,411 @@
+"""SD 1.x-shaped UNet denoise step on top of the B200 kernels.
+
+Structure and semantics follow the reference's random-init UNet (rhi-zone/sketchpad):
+  crates/sketchpad-unet/src/unet_sd.rs:42-53      UNetConfig::sd1x (320 ch, mult 1/2/4/4,
+                                                   8 heads x 40 at EVERY level, ctx 768)
+  crates/sketchpad-unet/src/unet_sd.rs:108-272    UNet::new / UNet::forward
+  crates/sketchpad-unet/src/unet_sd.rs:341-483    DownBlock / MidBlock / UpBlock
+  crates/sketchpad-unet/src/blocks.rs:15-39       timestep embedding
+  crates/sketchpad-unet/src/blocks.rs:123-150     ResBlock::forward  (GN+SiLU -> conv, x2)
+  crates/sketchpad-unet/src/blocks.rs:213-231     SpatialTransformer (GN -> proj_in -> block)
+  crates/sketchpad-unet/src/blocks.rs:292-305     TransformerBlock (LN -> self, LN -> cross, LN -> GEGLU)
+  crates/sketchpad-unet/src/blocks.rs:370-410     CrossAttention
+  crates/sketchpad-unet/src/blocks.rs:446-458     FeedForward (GEGLU, erf gelu)
+The hot-path ops run on this package's sm_100a kernels (groupnorm_silu / groupnorm,
+flash_attention, the unbiased LayerNorm); convolutions and dense linears are cuDNN/cuBLAS
+calls through torch, the element-wise glue is torch.  Weights are the synthetic random init
+of BASELINE config 1 (every Linear/Conv weight and bias ~ N(0, 0.02), seed 0; norm affines
+at the reference's init gamma=1, beta=0), generated with numpy so the CPU oracle can rebuild
+the identical tensors.  burn Linear weights are stored [in, out] (x @ W + b).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict, List
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from .attention import flash_attention
+from .groupnorm_silu import GroupNormSiLuOptions, groupnorm, groupnorm_silu
+from .layernorm import layer_norm
+
+
+@dataclass(frozen=True)
+class UNetConfig:
+    in_channels: int = 4
+    out_channels: int = 4
+    model_channels: int = 320
+    channel_mult: tuple = (1, 2, 4, 4)
+    num_heads: int = 8
+    head_dim: int = 40
+    context_dim: int = 768
+    transformer_depth: int = 1
+
+    @staticmethod
+    def sd1x() -> "UNetConfig":
+        return UNetConfig()
+
+
+# ------------------------------------------------------------------------------------------
+# Architecture description (shared by the GPU step and the CPU oracle's restatement)
+# ------------------------------------------------------------------------------------------
+def res_spec(prefix, cin, cout, tdim):
+    s = [(prefix + ".norm1", ("norm", cin)), (prefix + ".conv1", ("conv", cin, cout, 3)),
+         (prefix + ".time_emb_proj", ("linear", tdim, cout, True)),
+         (prefix + ".norm2", ("norm", cout)), (prefix + ".conv2", ("conv", cout, cout, 3))]
+    if cin != cout:
+        s.append((prefix + ".skip_conv", ("conv", cin, cout, 1)))
+    return s
+
+
+def st_spec(prefix, ch, cfg: UNetConfig):
+    inner = cfg.num_heads * cfg.head_dim
+    s = [(prefix + ".norm", ("norm", ch)), (prefix + ".proj_in", ("conv", ch, inner, 1))]
+    for d in range(cfg.transformer_depth):
+        b = f"{prefix}.tb{d}"
+        s += [(b + ".norm1", ("ln", inner)),
+              (b + ".attn1.to_q", ("linear", inner, inner, False)),
+              (b + ".attn1.to_k", ("linear", inner, inner, False)),
+              (b + ".attn1.to_v", ("linear", inner, inner, False)),
+              (b + ".attn1.to_out", ("linear", inner, inner, True)),
+              (b + ".norm2", ("ln", inner)),
+              (b + ".attn2.to_q", ("linear", inner, inner, False)),
+              (b + ".attn2.to_k", ("linear", cfg.context_dim, inner, False)),
+              (b + ".attn2.to_v", ("linear", cfg.context_dim, inner, False)),
+              (b + ".attn2.to_out", ("linear", inner, inner, True)),
+              (b + ".norm3", ("ln", inner)),
+              (b + ".ff.net_0", ("linear", inner, inner * 4 * 2, True)),
+              (b + ".ff.net_2", ("linear", inner * 4, inner, True))]
+    s.append((prefix + ".proj_out", ("conv", inner, ch, 1)))
+    return s
+
+
+def unet_plan(cfg: UNetConfig):
+    """(param specs, block program) mirroring UNet::new (unet_sd.rs:108-232)."""
+    ch = cfg.model_channels
+    tdim = ch * 4
+    specs = [("time_embed_0", ("linear", ch, tdim, True)), ("time_embed_2", ("linear", tdim, tdim, True)),
+             ("conv_in", ("conv", cfg.in_channels, ch, 3))]
+    program: List[tuple] = []
+    chans = [ch]
+    ch_in = ch
+    nlev = len(cfg.channel_mult)
+    for level, mult in enumerate(cfg.channel_mult):
+        ch_out = ch * mult
+        last = level == nlev - 1
+        att = level < 3
+        p = f"down{level}"
+        specs += res_spec(p + ".res1", ch_in, ch_out, tdim)
+        if att:
+            specs += st_spec(p + ".attn1", ch_out, cfg)
+        specs += res_spec(p + ".res2", ch_out, ch_out, tdim)
+        if att:
+            specs += st_spec(p + ".attn2", ch_out, cfg)
+        if not last:
+            specs.append((p + ".downsample", ("conv", ch_out, ch_out, 3)))
+        program.append(("down", p, att, not last))
+        chans += [ch_out, ch_out] + ([ch_out] if not last else [])
+        ch_in = ch_out
+    specs += res_spec("mid.res1", ch_in, ch_in, tdim) + st_spec("mid.attn", ch_in, cfg) + \
+        res_spec("mid.res2", ch_in, ch_in, tdim)
+    program.append(("mid", "mid"))
+    ui = 0
+    for level, mult in enumerate(reversed(cfg.channel_mult)):
+        ch_out = ch * mult
+        last = level == nlev - 1
+        att = level > 0
+        for i in range(3):
+            skip = chans.pop()
+            bin_ = ch_in + skip
+            bout = ch * cfg.channel_mult[nlev - 2 - level] if (i == 2 and not last) else ch_out
+            up = i == 2 and not last
+            p = f"up{ui}"
+            specs += res_spec(p + ".res", bin_, bout, tdim)
+            if att:
+                specs += st_spec(p + ".attn", bout, cfg)
+            if up:
+                specs.append((p + ".upsample", ("conv", bout, bout, 3)))
+            program.append(("up", p, att, up))
+            ch_in = bout
+            ui += 1
+    specs += [("norm_out", ("norm", ch)), ("conv_out", ("conv", ch, cfg.out_channels, 3))]
+    program.append(("out",))
+    return specs, program
+
+
+def param_shapes(cfg: UNetConfig = UNetConfig()):
+    """[(name, shape, init)] with init 'normal' (weights, biases), 'ones' or 'zeros'."""
+    out = []
+    specs, _ = unet_plan(cfg)
+    for name, spec in specs:
+        kind = spec[0]
+        if kind == "linear":
+            _, fin, fout, bias = spec
+            out.append((name + ".weight", (fin, fout), "normal"))
+            if bias:
+                out.append((name + ".bias", (fout,), "normal"))
+        elif kind == "conv":
+            _, cin, cout, k = spec
+            out.append((name + ".weight", (cout, cin, k, k), "normal"))
+            out.append((name + ".bias", (cout,), "normal"))
+        else:  # GroupNorm / LayerNorm affine at the reference init
+            out.append((name + ".weight", (spec[1],), "ones"))
+            out.append((name + ".bias", (spec[1],), "zeros"))
+    return out
+
+
+def make_unet_params(cfg: UNetConfig = UNetConfig(), seed: int = 0, std: float = 0.02,
+                     device=None):
+    """Synthetic random init: Linear/Conv weights and biases ~ N(0, std); GroupNorm and
+    LayerNorm affines at the reference init (gamma 1, beta 0).  Linear weights are [in, out]
+    (burn layout), conv weights [out, in, k, k].
+
+    device=None: numpy float32 arrays from np.random.default_rng(seed) (what the CPU oracle
+    and the parity tests use).  device='cuda': the same distribution drawn directly on the
+    GPU with torch's CUDA generator (fast; for benchmarking)."""
+    shapes = param_shapes(cfg)
+    if device is None:
+        rng = np.random.default_rng(seed)
+        P: Dict[str, np.ndarray] = {}
+        for name, shape, init in shapes:
+            if init == "normal":
+                P[name] = rng.standard_normal(shape, dtype=np.float32) * np.float32(std)
+            else:
+                P[name] = (np.ones if init == "ones" else np.zeros)(shape, np.float32)
+        return P
+    g = torch.Generator(device=device).manual_seed(seed)
+    T = {}
+    for name, shape, init in shapes:
+        if init == "normal":
+            T[name] = torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std
+        else:
+            T[name] = (torch.ones if init == "ones" else torch.zeros)(shape, device=device)
+    return T
+
+
+def timestep_freqs(dim: int) -> np.ndarray:
+    """blocks.rs:15-24: exp(-(i / half) * ln(10000)), computed in f64, stored f32."""
+    half = dim // 2
+    return np.array([math.exp(-(i / half) * math.log(10000.0)) for i in range(half)], np.float32)
+
+
+def unet_flops(cfg: UNetConfig = UNetConfig(), batch: int = 2, hw: int = 64, ctx_len: int = 77) -> dict:
+    """Algorithmic FLOPs of one step (2 per MAC) split into conv, linear and attention."""
+    specs, program = unet_plan(cfg)
+    spec = dict(specs)
+    fl = {"conv": 0.0, "linear": 0.0, "attention": 0.0}
+    inner = cfg.num_heads * cfg.head_dim
+
+    def conv(name, res):
+        _, cin, cout, k = spec[name]
+        fl["conv"] += 2.0 * batch * res * res * cin * cout * k * k
+
+    def st(prefix, res):
+        conv(prefix + ".proj_in", res)
+        conv(prefix + ".proj_out", res)
+        s = res * res
+        for d in range(cfg.transformer_depth):
+            b = f"{prefix}.tb{d}"
+            for nm in ("attn1.to_q", "attn1.to_k", "attn1.to_v", "attn1.to_out", "attn2.to_q",
+                       "attn2.to_out", "ff.net_0", "ff.net_2"):
+                _, fin, fout, _ = spec[f"{b}.{nm}"]
+                fl["linear"] += 2.0 * batch * s * fin * fout
+            for nm in ("attn2.to_k", "attn2.to_v"):
+                _, fin, fout, _ = spec[f"{b}.{nm}"]
+                fl["linear"] += 2.0 * batch * ctx_len * fin * fout
+            fl["attention"] += 4.0 * batch * cfg.num_heads * s * s * cfg.head_dim
+            fl["attention"] += 4.0 * batch * cfg.num_heads * s * ctx_len * cfg.head_dim
+
+    def res(prefix, r):
+        conv(prefix + ".conv1", r)
+        conv(prefix + ".conv2", r)
+        if prefix + ".skip_conv" in spec:
+            conv(prefix + ".skip_conv", r)
+
+    r = hw
+    conv("conv_in", r)
+    for item in program:
+        if item[0] == "down":
+            _, p, att, down = item
+            res(p + ".res1", r)
+            if att:
+                st(p + ".attn1", r)
+            res(p + ".res2", r)
+            if att:
+                st(p + ".attn2", r)
+            if down:
+                r //= 2
+                fl["conv"] += 2.0 * batch * r * r * spec[p + ".downsample"][1] * spec[p + ".downsample"][2] * 9
+        elif item[0] == "mid":
+            res("mid.res1", r)
+            st("mid.attn", r)
+            res("mid.res2", r)
+        elif item[0] == "up":
+            _, p, att, up = item
+            res(p + ".res", r)
+            if att:
+                st(p + ".attn", r)
+            if up:
+                r *= 2
+                conv(p + ".upsample", r)
+        else:
+            conv("conv_out", r)
+    fl["total"] = sum(fl.values())
+    return fl
+
+
+class UNetB200:
+    """The denoise step on the GPU: bf16 activations, sm_100a kernels on the hot path."""
+
+    def __init__(self, params: Dict[str, np.ndarray], cfg: UNetConfig = UNetConfig(),
+                 device="cuda", dtype=torch.bfloat16):
+        self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
+        self.specs, self.program = unet_plan(cfg)
+        self.spec = dict(self.specs)
+        self.p = {k: (v if isinstance(v, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(v)))
+                  .to(self.device, dtype).contiguous() for k, v in params.items()}
+        # fused QKV weight for the self-attention projections (same math as three Linears)
+        for name, spec in self.specs:
+            if name.endswith(".attn1.to_q"):
+                b = name[: -len(".to_q")]
+                self.p[b + ".qkv"] = torch.cat([self.p[b + ".to_q.weight"], self.p[b + ".to_k.weight"],
+                                                self.p[b + ".to_v.weight"]], dim=1).contiguous()
+            if name.endswith(".attn2.to_k"):
+                b = name[: -len(".to_k")]
+                self.p[b + ".kv"] = torch.cat([self.p[b + ".to_k.weight"], self.p[b + ".to_v.weight"]],
+                                              dim=1).contiguous()
+        self.freqs = torch.from_numpy(timestep_freqs(cfg.model_channels)).to(self.device)
+        self.kernel_launches = 0
+        self.attn_events: list | None = None  # (start, end, flops) when timing attention
+
+    # -- ops ---------------------------------------------------------------------------------
+    def _lin(self, x, name, bias=True):
+        w = self.p[name + ".weight"]
+        y = torch.matmul(x, w)
+        if bias and (name + ".bias") in self.p:
+            y = y + self.p[name + ".bias"]
+        return y
+
+    def _conv(self, x, name, stride=1):
+        w = self.p[name + ".weight"]
+        k = w.shape[-1]
+        return F.conv2d(x, w, self.p[name + ".bias"], stride=stride, padding=k // 2)
+
+    def _gn(self, x, name, silu):
+        self.kernel_launches += 1
+        f = groupnorm_silu if silu else groupnorm
+        return f(x, self.p[name + ".weight"], self.p[name + ".bias"], GroupNormSiLuOptions(32, 1e-5))
+
+    def _ln(self, x, name):
+        self.kernel_launches += 1
+        return layer_norm(x, self.p[name + ".weight"], self.p[name + ".bias"], 1e-5, True)
+
+    def _attention(self, q, k, v, out):
+        self.kernel_launches += 1
+        if self.attn_events is not None:
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            B, H, Sq, D = q.shape
+            Skv = k.shape[2]
+            s.record()
+            flash_attention(q, k, v, out=out)
+            e.record()
+            self.attn_events.append((s, e, 4.0 * B * H * Sq * Skv * D))
+        else:
+            flash_attention(q, k, v, out=out)
+
+    # -- blocks ------------------------------------------------------------------------------
+    def _res(self, x, temb_silu, p):
+        residual = self._conv(x, p + ".skip_conv") if (p + ".skip_conv") in self.p else x
+        h = self._gn(x, p + ".norm1", True)
+        h = self._conv(h, p + ".conv1")
+        t = self._lin(temb_silu, p + ".time_emb_proj")
+        h = h + t[:, :, None, None]
+        h = self._gn(h, p + ".norm2", True)
+        h = self._conv(h, p + ".conv2")
+        return h + residual
+
+    def _xattn(self, x, p, ctx):
+        cfg = self.cfg
+        b, s, _ = x.shape
+        H, D = cfg.num_heads, cfg.head_dim
+        if ctx is None:
+            qkv = torch.matmul(x, self.p[p + ".qkv"]).view(b, s, 3, H, D)
+            q, k, v = qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2), qkv[:, :, 2].transpose(1, 2)
+        else:
+            q = torch.matmul(x, self.p[p + ".to_q.weight"]).view(b, s, H, D).transpose(1, 2)
+            c = ctx.shape[1]
+            kv = torch.matmul(ctx, self.p[p + ".kv"]).view(b, c, 2, H, D)
+            k, v = kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2)
+        o = torch.empty((b, s, H, D), dtype=x.dtype, device=x.device)
+        self._attention(q, k, v, o.transpose(1, 2))  # written straight into [b, s, h, d]
+        return self._lin(o.view(b, s, H * D), p + ".to_out")
+
+    def _st(self, x, ctx, p):
+        b, c, h, w = x.shape
+        residual = x
+        y = self._gn(x, p + ".norm", False)
+        y = self._conv(y, p + ".proj_in")
+        inner = y.shape[1]
+        y = y.reshape(b, inner, h * w).transpose(1, 2).contiguous()
+        for d in range(self.cfg.transformer_depth):
+            tb = f"{p}.tb{d}"
+            y = y + self._xattn(self._ln(y, tb + ".norm1"), tb + ".attn1", None)
+            y = y + self._xattn(self._ln(y, tb + ".norm2"), tb + ".attn2", ctx)
+            hdn = self._lin(self._ln(y, tb + ".norm3"), tb + ".ff.net_0")
+            half = hdn.shape[-1] // 2
+            y = y + self._lin(hdn[..., :half] * F.gelu(hdn[..., half:]), tb + ".ff.net_2")
+        y = y.transpose(1, 2).reshape(b, inner, h, w)
+        return self._conv(y, p + ".proj_out") + residual
+
+    def forward(self, x: torch.Tensor, timesteps: torch.Tensor, context: torch.Tensor) -> torch.Tensor:
+        """UNet::forward (unet_sd.rs:235-272): noisy latent [b,4,h,w] -> predicted noise."""
+        x = x.to(self.dtype)
+        context = context.to(self.dtype)
+        args = timesteps.float()[:, None] * self.freqs[None, :]
+        temb = torch.cat([torch.sin(args), torch.cos(args)], dim=1).to(self.dtype)
+        temb = self._lin(temb, "time_embed_0")
+        temb = self._lin(F.silu(temb), "time_embed_2")
+        temb_silu = F.silu(temb)  # every ResBlock applies silu to the embedding first
+        h = self._conv(x, "conv_in")
+        skips = [h]
+        for item in self.program:
+            if item[0] == "down":
+                _, p, att, down = item
+                h = self._res(h, temb_silu, p + ".res1")
+                if att:
+                    h = self._st(h, context, p + ".attn1")
+                skips.append(h)
+                h = self._res(h, temb_silu, p + ".res2")
+                if att:
+                    h = self._st(h, context, p + ".attn2")
+                skips.append(h)
+                if down:
+                    h = self._conv(h, p + ".downsample", stride=2)
+                    skips.append(h)
+            elif item[0] == "mid":
+                h = self._res(h, temb_silu, "mid.res1")
+                h = self._st(h, context, "mid.attn")
+                h = self._res(h, temb_silu, "mid.res2")
+            elif item[0] == "up":
+                _, p, att, up = item
+                h = torch.cat([h, skips.pop()], dim=1)
+                h = self._res(h, temb_silu, p + ".res")
+                if att:
+                    h = self._st(h, context, p + ".attn")
+                if up:
+                    h = F.interpolate(h, scale_factor=2, mode="nearest")
+                    h = self._conv(h, p + ".upsample")
+            else:
+                h = self._gn(h, "norm_out", True)
+                h = self._conv(h, "conv_out")
+        return h
+
+    __call__ = forward
+
+
+__all__ = ["UNetConfig", "UNetB200", "make_unet_params", "param_shapes", "unet_plan", "unet_flops",
+           "timestep_freqs"]
+_ = field
