@@ -213,7 +213,7 @@ def run_b200(args):
     peaks, peak_src = load_peaks()
 
     import sketchpad_b200
-    from sketchpad_b200.unet import UNetB200, make_unet_params, unet_flops
+    from sketchpad_b200.unet import UNetB200, UNetStepGraph, make_unet_params, unet_flops
 
     sketchpad_b200.load_library()
     net = UNetB200(make_unet_params(device=dev, seed=0), device=dev)
@@ -228,8 +228,28 @@ def run_b200(args):
             net(x, t, ctx)
         torch.cuda.synchronize()
 
+        # The whole step is captured once as a CUDA graph (the eager step issues ~1000
+        # launches); replays run the identical kernels on the same resident buffers.
+        graph = None
+        step = lambda: net(x, t, ctx)  # noqa: E731
+        launches_per_step = None
+        if not args.no_graph:
+            try:
+                graph = UNetStepGraph(net, warmup=2)
+                graph.x.copy_(x)
+                graph.t.copy_(t)
+                graph.ctx.copy_(ctx)
+                launches_per_step = graph.kernel_launches
+                step = graph.replay
+                for _ in range(args.warmup):
+                    step()
+                torch.cuda.synchronize()
+            except Exception as exc:  # capture unsupported: time the eager step instead
+                print(f"[bench] graph capture failed, timing eager steps: {exc}", file=sys.stderr)
+                graph = None
+                step = lambda: net(x, t, ctx)  # noqa: E731
+
         # ---------------- timed region: inputs resident in HBM ----------------
-        net.attn_events = []
         launches0 = net.kernel_launches
         if ws > 1:
             dist.barrier()
@@ -238,13 +258,25 @@ def run_b200(args):
         with ClockSampler(local) as clk:
             s.record()
             for _ in range(args.steps):
-                net(x, t, ctx)
+                step()
             e.record()
             torch.cuda.synchronize()
         if ws > 1:
             dist.barrier()
         ms = s.elapsed_time(e) / args.steps
-        launches = (net.kernel_launches - launches0) // args.steps
+        if launches_per_step is None:
+            launches_per_step = (net.kernel_launches - launches0) // args.steps
+
+        # ---------------- attention share: eager steps with events around each launch --------
+        net.attn_events = []
+        torch.cuda.synchronize()
+        s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s3.record()
+        for _ in range(args.steps):
+            net(x, t, ctx)
+        e3.record()
+        torch.cuda.synchronize()
+        eager_ms = s3.elapsed_time(e3) / args.steps
         attn = net.attn_events
         net.attn_events = None
         attn_ms = sum(a.elapsed_time(b) for a, b, _ in attn)
@@ -263,8 +295,11 @@ def run_b200(args):
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record()
         for _ in range(args.steps):
-            y = net(xh.to(dev, non_blocking=True), th.to(dev, non_blocking=True),
-                    ch.to(dev, non_blocking=True))
+            if graph is not None:
+                y = graph(xh, th, ch)  # host buffers in, captured step, host buffer out
+            else:
+                y = net(xh.to(dev, non_blocking=True), th.to(dev, non_blocking=True),
+                        ch.to(dev, non_blocking=True))
             yh.copy_(y, non_blocking=True)
         e2.record()
         torch.cuda.synchronize()
@@ -302,13 +337,16 @@ def run_b200(args):
                        "step_tflop": flops["total"] / 1e12},
             "e2e": {"value": ws * 1e3 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": launches * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
+            "cuda_graph": graph is not None, "eager_ms_per_step": eager_ms,
             "roofline": {"kernel": "sp flash attention (all 32 launches of the step)",
                          "bound": "tensor", "achieved": achieved,
                          "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                          "frac": achieved / peaks["bf16_tflops_sustained"],
                          "peak_source": f"{peak_src} bf16_tflops_sustained",
                          "launch_ms": attn_launch_ms, "share_of_step": attn_share,
+                         "timing": "CUDA events around each attention launch in the eager "
+                                   "pass that follows the timed graph replays",
                          "traffic": None},
             "achieved_step_tflops": flops["total"] / ms / 1e9,
             "kernels": kernels,
@@ -321,6 +359,99 @@ def run_b200(args):
     return 0
 
 
+# ------------------------------------------------------------------------------------------
+# Single-kernel cases (what the committed ncu summaries under profiles/ capture)
+# ------------------------------------------------------------------------------------------
+def _case_attention(torch, B, H, Sq, Skv, D):
+    from sketchpad_b200 import flash_attention
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, H, Sq, D, device="cuda", generator=g, dtype=torch.bfloat16)
+    k = torch.randn(B, H, Skv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+    v = torch.randn(B, H, Skv, D, device="cuda", generator=g, dtype=torch.bfloat16)
+    o = torch.empty(B, H, Sq, D, device="cuda", dtype=torch.bfloat16)
+    return (lambda: flash_attention(q, k, v, out=o)), 4.0 * B * H * Sq * Skv * D, "flop"
+
+
+def _case_groupnorm(torch, B, C, Hh, W, dt):
+    from sketchpad_b200 import groupnorm_bytes, groupnorm_silu
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = (torch.randn(B, C, Hh, W, device="cuda", generator=g) * 3 + 0.5).to(dt)
+    w = torch.ones(C, device="cuda", dtype=dt)
+    b = torch.zeros(C, device="cuda", dtype=dt)
+    y = torch.empty_like(x)
+    return (lambda: groupnorm_silu(x, w, b, out=y)), groupnorm_bytes(B, C, Hh, W, x.element_size()), "byte"
+
+
+def _case_q8(torch, M, N, K):
+    from sketchpad_b200.flux import _q8_linear
+    lin = _q8_linear(0, N, K, "cuda", bias=True)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    return (lambda: lin.forward(x, out=y)), 2.0 * M * N * K, "flop"
+
+
+def _case_fp8(torch, M, N, K):
+    from sketchpad_b200.wan import fp8_linear_synthetic
+    lin = fp8_linear_synthetic(0, N, K, "cuda", bias=True)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    return (lambda: lin.forward(x, out=y)), 2.0 * M * N * K, "flop"
+
+
+def _case_unet_step(torch):
+    from sketchpad_b200.unet import UNetB200, make_unet_params, unet_flops
+    net = UNetB200(make_unet_params(device="cuda", seed=0), device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(2, 4, 64, 64, device="cuda", generator=g)
+    ctx = torch.randn(2, 77, 768, device="cuda", generator=g)
+    t = torch.full((2,), 999.0, device="cuda")
+
+    def step():
+        with torch.inference_mode():
+            net(x, t, ctx)
+    return step, unet_flops()["total"], "flop"
+
+
+CASES = {
+    "unet_step_eager": _case_unet_step,
+    "attn_8x24x4608x128": lambda t: _case_attention(t, 8, 24, 4608, 4608, 128),
+    "attn_2x8x4096x40": lambda t: _case_attention(t, 2, 8, 4096, 4096, 40),
+    "attn_2x10x1024x64": lambda t: _case_attention(t, 2, 10, 1024, 1024, 64),
+    "attn_cross_2x8x4096x77x40": lambda t: _case_attention(t, 2, 8, 4096, 77, 40),
+    "gn_8x512x128x128_f32": lambda t: _case_groupnorm(t, 8, 512, 128, 128, t.float32),
+    "gn_8x512x128x128_f16": lambda t: _case_groupnorm(t, 8, 512, 128, 128, t.float16),
+    "gn_2x320x64x64_f32": lambda t: _case_groupnorm(t, 2, 320, 64, 64, t.float32),
+    "q8_0_4608x3072x3072": lambda t: _case_q8(t, 4608, 3072, 3072),
+    "q8_0_4608x12288x3072": lambda t: _case_q8(t, 4608, 12288, 3072),
+    "fp8_8192x13824x5120": lambda t: _case_fp8(t, 8192, 13824, 5120),
+}
+
+
+def run_case(args):
+    import torch
+    import sketchpad_b200
+    sketchpad_b200.load_library()
+    peaks, src = load_peaks()
+    fn, work, kind = CASES[args.case](torch)
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    if kind == "flop":
+        ach, peak, unit = work / ms / 1e9, peaks["bf16_tflops"], "TFLOP/s"
+    else:
+        ach, peak, unit = work / ms / 1e6, peaks["hbm_gbs"], "GB/s"
+    print(json.dumps({"case": args.case, "ms": ms, "achieved": ach, "unit": unit,
+                      "frac": ach / peak, "peak": peak, "peak_source": src, "work": work}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -328,9 +459,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time eager steps, no CUDA graph")
+    ap.add_argument("--case", default=None, choices=sorted(CASES),
+                    help="run one kernel workload only (for ncu captures); prints its timing")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.case:
+        return run_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

@@ -79,6 +79,20 @@ int num_sms() {
   return cache[dev];
 }
 
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  return dev;
+}
+
+bool first_time_on_device(unsigned long long* flag_bits) {
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return true;
+  const unsigned long long bit = 1ull << dev;
+  const unsigned long long old = __atomic_fetch_or(flag_bits, bit, __ATOMIC_ACQ_REL);
+  return (old & bit) == 0;
+}
+
 int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, const void* base,
                  const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                  CUtensorMapSwizzle swizzle) {

@@ -36,6 +36,13 @@ int require_sm100();
 // SM count of the current device (cached per device).
 int num_sms();
 
+// Current device index (cudaGetDevice; 0 on failure).
+int current_device();
+
+// True once per (flag, device): lets a launcher set a kernel attribute the first time it
+// runs on a device instead of on every call.
+bool first_time_on_device(unsigned long long* flag_bits);
+
 // cuTensorMapEncodeTiled obtained through cudaGetDriverEntryPoint (no libcuda link).
 int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, const void* base,
                  const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,

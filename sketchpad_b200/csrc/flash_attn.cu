@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     for (int j = 0; j < n_tiles; ++j) {
       const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
+      if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
         ok = false;
         break;
       }
@@ -295,13 +295,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&s_free[sb]);  // S buffer may be overwritten by QK_{j+2}
 
       // P is single-buffered and O is about to change: PV_{j-1} must have completed.
-      if (j >= 1 && !mbar_wait(o_done, (j - 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
+      if (j >= 1 && !mbar_wait_warp(o_done, (j - 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (rescale) {
-        const float alpha = ex2_approx((m_run == -INFINITY ? m_ref : m_run) - m_ref);
+      // tcgen05.ld/st are warp-collective: the whole warp rescales if any of its rows must,
+      // rows that need no rescale use alpha = 1.
+      if (__any_sync(0xffffffffu, rescale)) {
+        const float alpha = rescale ? ex2_approx(m_run - m_ref) : 1.0f;
         l_run *= alpha;
         for (int c = 0; c < p.dv_pad; c += 16) {
           uint32_t r[16];
@@ -330,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- epilogue: O / l -> global
     if (ok && n_tiles > 0 &&
-        mbar_wait(o_done, (n_tiles - 1) & 1, abort_flag, WD_EPILOGUE_WAIT)) {
+        mbar_wait_warp(o_done, (n_tiles - 1) & 1, abort_flag, WD_EPILOGUE_WAIT)) {
       tc_fence_after();
       const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
       const bool row_ok = qi < p.Sq;
@@ -397,9 +399,14 @@ int launch_fa(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& m
   using L = FaSmem<NBQ, NBV, STAGES>;
   auto kern = fa_fwd_kernel<NBQ, NBV, STAGES>;
   static_assert(L::kAlloc <= 232448, "flash_attn smem budget");
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-  if (e != cudaSuccess)
-    return set_error(SP_ERR_LAUNCH, "flash_attn: smem attribute failed: %s", cudaGetErrorString(e));
+  static unsigned long long attr_set = 0;
+  if (first_time_on_device(&attr_set)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) {
+      __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
+      return set_error(SP_ERR_LAUNCH, "flash_attn: smem attribute failed: %s", cudaGetErrorString(e));
+    }
+  }
   dim3 grid((unsigned)((p.Sq + kBM - 1) / kBM), (unsigned)p.H, (unsigned)B);
   kern<<<grid, kThreads, L::kAlloc, s>>>(mq, mk, mv, p);
   return check_launch("flash_attn");

@@ -352,11 +352,14 @@ GnPlan plan_gn(int64_t B, int64_t G, int64_t n, bool contiguous, bool vec_ok, in
 template <typename T, int VPT>
 int launch_cluster(const GnParams& p, int cs, int64_t BG, cudaStream_t stream) {
   auto kern = gn_cluster_kernel<T, VPT>;
-  if (cs > 8) {
+  static unsigned long long attr_set = 0;
+  if (cs > 8 && first_time_on_device(&attr_set)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess)
+    if (e != cudaSuccess) {
+      __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
       return set_error(SP_ERR_LAUNCH, "groupnorm: cluster size %d not allowed: %s", cs,
                        cudaGetErrorString(e));
+    }
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)cs, (unsigned)BG, 1);

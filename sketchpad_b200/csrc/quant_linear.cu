@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     }
 
     // ------------------------------------------------------------ epilogue
-    if (ok && mbar_wait(acc_full, 0, abort_flag, WD_EPILOGUE_WAIT)) {
+    if (__all_sync(0xffffffffu, ok) && mbar_wait_warp(acc_full, 0, abort_flag, WD_EPILOGUE_WAIT)) {
       tc_fence_after();
       const int quarter = warp & 3;
       const int row = quarter * 32 + lane;
@@ -286,9 +286,14 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
   }
   auto kern = qlinear_kernel<WF>;
   static_assert(QlSmem::kAlloc <= 232448, "quantized linear smem budget");
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, QlSmem::kAlloc);
-  if (e != cudaSuccess)
-    return set_error(SP_ERR_LAUNCH, "quantized linear: smem attribute failed: %s", cudaGetErrorString(e));
+  static unsigned long long attr_set = 0;
+  if (first_time_on_device(&attr_set)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, QlSmem::kAlloc);
+    if (e != cudaSuccess) {
+      __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
+      return set_error(SP_ERR_LAUNCH, "quantized linear: smem attribute failed: %s", cudaGetErrorString(e));
+    }
+  }
   dim3 grid((unsigned)((p.M + kQBM - 1) / kQBM), (unsigned)((p.N + kQBN - 1) / kQBN));
   kern<<<grid, kQThreads, QlSmem::kAlloc, s>>>(mx, mw, p);
   return check_launch("quantized linear");

@@ -91,6 +91,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Warp-uniform bounded wait: every lane of the (converged) warp gets the same answer, so
+// warp-collective tcgen05 instructions that follow are never reached by only part of a warp.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               int code) {
+  const bool ok = mbar_wait(bar, parity, abort, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ---------------------------------------------------------------------------------------
 // Proxy / tcgen05 fences
 // ---------------------------------------------------------------------------------------

@@ -406,6 +406,47 @@ class UNetB200:
     __call__ = forward
 
 
-__all__ = ["UNetConfig", "UNetB200", "make_unet_params", "param_shapes", "unet_plan", "unet_flops",
+class UNetStepGraph:
+    """One UNet denoise step captured as a CUDA graph over static device buffers.
+
+    The eager step issues about a thousand kernel launches; the captured graph replays the
+    same kernels (the package's sm_100a kernels and the cuDNN/cuBLAS calls) with one launch.
+    `__call__(x, t, context)` takes host or device tensors, copies them into the static
+    inputs, replays, and returns the static output (copy it before the next call)."""
+
+    def __init__(self, net: UNetB200, batch: int = 2, hw: int = 64, ctx_len: int = 77,
+                 warmup: int = 2):
+        dev = net.device
+        cfg = net.cfg
+        self.net = net
+        self.x = torch.zeros(batch, cfg.in_channels, hw, hw, device=dev)
+        self.t = torch.zeros(batch, device=dev)
+        self.ctx = torch.zeros(batch, ctx_len, cfg.context_dim, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                net(self.x, self.t, self.ctx)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        l0 = net.kernel_launches
+        with torch.cuda.graph(self.graph):
+            self.out = net(self.x, self.t, self.ctx)
+        self.kernel_launches = net.kernel_launches - l0  # package kernels per replay
+
+    def replay(self):
+        self.graph.replay()
+        return self.out
+
+    def __call__(self, x, t, context):
+        self.x.copy_(x, non_blocking=True)
+        self.t.copy_(t, non_blocking=True)
+        self.ctx.copy_(context, non_blocking=True)
+        self.graph.replay()
+        return self.out
+
+
+__all__ = ["UNetConfig", "UNetB200", "UNetStepGraph", "make_unet_params", "param_shapes", "unet_plan", "unet_flops",
            "timestep_freqs"]
 _ = field

@@ -1,0 +1,172 @@
+"""Wan-2.1-14B-shaped video DiT block with FP8 weights on the B200 kernels,
+optionally sequence-parallel (Ulysses) across the ranks of a process group.
+
+Follows rhi-zone/sketchpad crates/sketchpad-dit/src/wan.rs:
+  :188-221   wan_timestep_freqs / WanTimestepEmbed
+  :330-337   WanExpert (SwiGLU, no bias): down(silu(gate(x)) * up(x))
+  :351-402   WanAttention (to_qkv -> RoPE(q,k) -> softmax(QK^T/sqrt(d))V -> to_out)
+  :418-461   WanCrossAttention (to_q(x), to_kv(context))
+  :489-573   WanBlock::forward: 8x modulation; spatial attention over each frame's H*W tokens,
+             temporal attention over T frames per position, text cross-attention, MoE FFN
+  :576-601   forward_moe: softmax router, dense sum over experts (num_experts = 1 here, so
+             the router weight is exactly 1 and the FFN is one SwiGLU expert)
+Config 5: hidden 5120, 40 heads x 128, FFN 13824, 40 blocks, latent 16x21x90x160 with patch
+1x2x2 -> 21 frames x 45 x 80 = 75,600 tokens, text context 512 x 4096 (projected to hidden).
+
+Every Linear is an Fp8Linear (e4m3 bytes + per-output-channel f32 scale, decode fused into
+the GEMM mainloop).  Sequence parallel: each rank holds S/P tokens; around each attention
+`ulysses` regroups to all tokens x H/P heads with one all-to-all per tensor.  Spatial and
+temporal attention are then computed exactly as on one device; the cross-attention needs
+only the rank's own queries and the (replicated) 512-token context.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from .attention import flash_attention
+from .flux import apply_rope, rope_tables
+from .layernorm import layer_norm
+from .quantization import Fp8Format, Fp8Linear, Fp8Tensor
+from .ulysses import head_to_seq, seq_to_head
+
+
+@dataclass(frozen=True)
+class WanConfig:
+    in_channels: int = 16
+    patch_size: int = 2
+    temporal_patch_size: int = 1
+    hidden_size: int = 5120
+    num_heads: int = 40
+    num_blocks: int = 40
+    intermediate: int = 13824
+    text_dim: int = 4096
+    time_embed_dim: int = 256
+    max_spatial_len: int = 3600
+    max_temporal_len: int = 21
+
+    @property
+    def head_dim(self):
+        return self.hidden_size // self.num_heads
+
+
+def wan_timestep_freqs(dim: int) -> np.ndarray:
+    """wan.rs:188-196: exp(-ln(10000)/(half-1) * i)."""
+    half = dim // 2
+    s = np.float32(-math.log(10000.0)) / np.float32(half - 1)
+    return np.exp(s * np.arange(half, dtype=np.float32)).astype(np.float32)
+
+
+def fp8_linear_synthetic(seed: int, n: int, k: int, device, bias: bool) -> Fp8Linear:
+    """Random e4m3 weight bytes (finite codes) with per-output-channel scales sized so that
+    dequantized weights are ~N(0, 0.02)-like, plus an optional bf16 bias ~ N(0, 0.02)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    # draw values in the e4m3 range and encode them on the device: N(0,1) * 64 -> e4m3 bytes
+    w = torch.randn((n, k), generator=g, device=device) * 64.0
+    from .quantization import quantize_fp8, Fp8Config
+    t = quantize_fp8(w, Fp8Config.e4m3().with_scale(1.0))
+    scale = torch.full((n,), 0.02 / 64.0, device=device, dtype=torch.float32)
+    b = (torch.randn(n, generator=g, device=device) * 0.02).to(torch.bfloat16) if bias else None
+    return Fp8Linear(Fp8Tensor(t.data, scale, Fp8Format.E4M3, (n, k)), b)
+
+
+def _ln(x):
+    n = x.shape[-1]
+    one = torch.ones(n, dtype=x.dtype, device=x.device)
+    return layer_norm(x, one, torch.zeros_like(one), 1e-5, True)
+
+
+class WanBlockB200:
+    def __init__(self, seed: int, cfg: WanConfig, device, group: Optional[dist.ProcessGroup] = None):
+        h, i = cfg.hidden_size, cfg.intermediate
+        L = lambda s, n, k, b=True: fp8_linear_synthetic(seed + s, n, k, device, b)  # noqa: E731
+        self.s_qkv, self.s_out = L(1, 3 * h, h), L(2, h, h)
+        self.t_qkv, self.t_out = L(3, 3 * h, h), L(4, h, h)
+        self.c_q, self.c_kv, self.c_out = L(5, h, h), L(6, 2 * h, h), L(7, h, h)
+        gate, up = L(8, i, h, False), L(9, i, h, False)
+        self.gate_up = Fp8Linear(Fp8Tensor(torch.cat([gate.weight.data, up.weight.data]),
+                                           torch.cat([gate.weight.scale, up.weight.scale]),
+                                           Fp8Format.E4M3, (2 * i, h)), None)
+        self.down = L(10, h, i, False)
+        self.modulation = L(11, 8 * h, h)
+        self.cfg, self.group = cfg, group
+        self.P = dist.get_world_size(group) if group is not None else 1
+        sc, ss = rope_tables(cfg.head_dim, cfg.max_spatial_len)
+        tc, ts = rope_tables(cfg.head_dim, cfg.max_temporal_len)
+        f = lambda a: torch.from_numpy(a).to(device, torch.bfloat16)  # noqa: E731
+        self.s_cos, self.s_sin, self.t_cos, self.t_sin = f(sc), f(ss), f(tc), f(ts)
+
+    # attention over the full token sequence of this rank's head group (Ulysses) -----------
+    def _self_attn(self, xn, qkv_lin, out_lin, nt, nhw, temporal):
+        cfg, P = self.cfg, self.P
+        b, s_loc, _ = xn.shape
+        H, D = cfg.num_heads, cfg.head_dim
+        qkv = qkv_lin(xn).view(b, s_loc, 3, H, D)
+        if P > 1:
+            parts = [seq_to_head(qkv[:, :, j].contiguous(), self.group) for j in range(3)]
+            hh = H // P
+        else:
+            parts = [qkv[:, :, j] for j in range(3)]
+            hh = H
+        # parts: [b, S, hh, D] over all tokens (frame-major: t, then h*w)
+        if not temporal:
+            q, k, v = (p.reshape(b * nt, nhw, hh, D).transpose(1, 2) for p in parts)
+            cos, sin = self.s_cos, self.s_sin
+        else:
+            q, k, v = (p.reshape(b, nt, nhw, hh, D).permute(0, 2, 3, 1, 4).reshape(b * nhw, hh, nt, D)
+                       for p in parts)
+            cos, sin = self.t_cos, self.t_sin
+        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        o = flash_attention(q.contiguous(), k.contiguous(), v.contiguous())
+        if not temporal:
+            o = o.transpose(1, 2).reshape(b, nt * nhw, hh, D)
+        else:
+            o = o.reshape(b, nhw, hh, nt, D).permute(0, 3, 1, 2, 4).reshape(b, nt * nhw, hh, D)
+        if P > 1:
+            o = head_to_seq(o.contiguous(), self.group)
+        return out_lin(o.reshape(b, s_loc, H * D))
+
+    def forward(self, x, cond, context, nt: int, nh: int, nw: int):
+        """x: [b, S/P, hidden] (this rank's tokens), cond: [b, hidden], context: [b, 512, hidden]."""
+        cfg = self.cfg
+        b = x.shape[0]
+        m = self.modulation(cond).view(b, 8, 1, cfg.hidden_size)
+        nhw = nh * nw
+        xn = (1 + m[:, 1]) * _ln(x) + m[:, 0]
+        x = x + self._self_attn(xn, self.s_qkv, self.s_out, nt, nhw, temporal=False)
+        xn = (1 + m[:, 3]) * _ln(x) + m[:, 2]
+        x = x + self._self_attn(xn, self.t_qkv, self.t_out, nt, nhw, temporal=True)
+        xn = (1 + m[:, 5]) * _ln(x) + m[:, 4]
+        H, D = cfg.num_heads, cfg.head_dim
+        s_loc = x.shape[1]
+        q = self.c_q(xn).view(b, s_loc, H, D).transpose(1, 2)
+        kv = self.c_kv(context).view(b, context.shape[1], 2, H, D)
+        o = torch.empty((b, s_loc, H, D), dtype=x.dtype, device=x.device)
+        flash_attention(q, kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2),
+                        out=o.transpose(1, 2))
+        x = x + self.c_out(o.view(b, s_loc, H * D))
+        xn = (1 + m[:, 7]) * _ln(x) + m[:, 6]
+        gu = self.gate_up(xn)
+        i = cfg.intermediate
+        # one expert: softmax over a single router logit is exactly 1 (wan.rs:576-601)
+        return x + self.down(F.silu(gu[..., :i]) * gu[..., i:])
+
+
+def wan_block_flops(cfg: WanConfig = WanConfig(), nt=21, nhw=3600, ctx=512) -> dict:
+    """Algorithmic FLOPs of one WanBlock over the whole (unsharded) sequence."""
+    h, i, H, D = cfg.hidden_size, cfg.intermediate, cfg.num_heads, cfg.head_dim
+    S = nt * nhw
+    lin = 2.0 * S * (3 * h * h * 2 + h * h * 2 + h * h + h * h + 2 * i * h + h * i) + \
+        2.0 * ctx * 2 * h * h + 2.0 * 8 * h * h
+    att = 4.0 * H * D * (nt * nhw * nhw + nhw * nt * nt + S * ctx)
+    return {"linear": lin, "attention": att, "total": lin + att}
+
+
+__all__ = ["WanConfig", "WanBlockB200", "wan_block_flops", "wan_timestep_freqs",
+           "fp8_linear_synthetic"]
