@@ -39,6 +39,7 @@ struct FaParams {
   int dv_pad;           // Dv rounded up to 64 (whole MN-major swizzle atoms)
   int n_kv_tiles;       // tiles of kBN keys (before causal trimming)
   float scale_log2;     // softmax scale * log2(e)
+  float inv_scale;      // 1 / softmax scale (additive masks are applied to raw scores)
   int causal;
   const float* mask;
   int64_t mask_stride;
@@ -53,11 +54,11 @@ struct FaSmem {
   static constexpr int kQ = 0;
   static constexpr int kK = kQ + NBQ * kBox;
   static constexpr int kV = kK + STAGES * NBQ * kBox;
-  static constexpr int kP = kV + STAGES * NBV * kBox;
-  static constexpr int kBar = kP + 2 * kBox;
+  static constexpr int kP = kV + STAGES * NBV * kBox;  // two P buffers of 128 x 128 (2 boxes)
+  static constexpr int kBar = kP + 4 * kBox;
   // barriers: q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_free[2],
-  // p_full, o_done, drain
-  static constexpr int kNumBars = 1 + 4 * STAGES + 2 + 2 + 1 + 1 + 1;
+  // p_full[2], o_done[2], drain
+  static constexpr int kNumBars = 1 + 4 * STAGES + 2 + 2 + 2 + 2 + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;  // tmem base + abort flag
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-B alignment of the base
@@ -82,8 +83,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = v_empty + STAGES;
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
-  uint64_t* o_done = p_full + 1;
-  uint64_t* drain = o_done + 1;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
 
@@ -110,9 +111,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 128);
+      mbar_init(&p_full[s], 128);
+      mbar_init(&o_done[s], 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -135,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_expect_tx(q_full, NBQ * kBox);
       for (int blk = 0; blk < NBQ; ++blk)
         tma_load_4d(smem + L::kQ + blk * kBox, &tmq, q_full, blk * 64, q0, h, b);
-      int issued = 0;
+      int issued_k = 0, issued_v = 0;
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % STAGES;
         const uint32_t ph = (j / STAGES) & 1;
@@ -144,25 +145,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int blk = 0; blk < NBQ; ++blk)
           tma_load_4d(smem + L::kK + (st * NBQ + blk) * kBox, &tmk, &k_full[st], blk * 64,
                       j * kBN, h, b);
-        if (j >= STAGES && !mbar_wait(&v_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) {
-          issued = j + 1;  // K of tile j is in flight
-          break;
-        }
+        issued_k = j + 1;
+        if (j >= STAGES && !mbar_wait(&v_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) break;
         mbar_arrive_expect_tx(&v_full[st], NBV * kBox);
         for (int blk = 0; blk < NBV; ++blk)
           tma_load_4d(smem + L::kV + (st * NBV + blk) * kBox, &tmv, &v_full[st], blk * 64,
                       j * kBN, h, b);
-        issued = j + 1;
+        issued_v = j + 1;
       }
       if (*abort_flag) {
         // Let every copy still in flight land before the CTA can exit (bounded).
         mbar_wait(q_full, 0, nullptr, WD_TMA_WAIT);
-        for (int j = max(0, issued - STAGES); j < issued; ++j) {
-          const int st = j % STAGES;
-          const uint32_t ph = (j / STAGES) & 1;
-          mbar_wait(&k_full[st], ph, nullptr, WD_TMA_WAIT);
-          mbar_wait(&v_full[st], ph, nullptr, WD_TMA_WAIT);
-        }
+        for (int j = max(0, issued_k - STAGES); j < issued_k; ++j)
+          mbar_wait(&k_full[j % STAGES], (j / STAGES) & 1, nullptr, WD_TMA_WAIT);
+        for (int j = max(0, issued_v - STAGES); j < issued_v; ++j)
+          mbar_wait(&v_full[j % STAGES], (j / STAGES) & 1, nullptr, WD_TMA_WAIT);
       }
     }
   } else if (warp == 1) {
@@ -177,31 +174,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(q_full, 0, abort_flag, WD_MMA_WAIT);
       tc_fence_after();
 
+      // O += P_i V_i, P_i in shared buffer i % 2
       auto issue_pv = [&](int i) -> bool {
         const int st = i % STAGES;
-        const uint32_t ph = (i / STAGES) & 1;
-        if (!mbar_wait(&v_full[st], ph, abort_flag, WD_MMA_WAIT)) return false;
-        if (!mbar_wait(p_full, i & 1, abort_flag, WD_MMA_WAIT)) return false;
+        if (!mbar_wait(&v_full[st], (i / STAGES) & 1, abort_flag, WD_MMA_WAIT)) return false;
+        if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1, abort_flag, WD_MMA_WAIT)) return false;
         tc_fence_after();
         const uint32_t v_base = smem_u32(smem + L::kV + st * NBV * kBox);
+        const uint32_t pb = p_base + (i & 1) * 2 * kBox;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           // A = P (K-major, 2 boxes of 64 keys), B = V (MN-major: keys x Dv, Dv contiguous)
-          const uint64_t a = make_smem_desc(p_base + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024,
+          const uint64_t a = make_smem_desc(pb + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024,
                                             LAYOUT_SW128);
           const uint64_t bd = make_smem_desc(v_base + kk * 16 * 128, kBox, 1024, LAYOUT_SW128);
           umma_ss(tmem + kTmemO, a, bd, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&v_empty[st]);
-        umma_commit(o_done);
+        umma_commit(&o_done[i & 1]);
         return true;
       };
 
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int st = j % STAGES;
-        const uint32_t ph = (j / STAGES) & 1;
         const int sb = j & 1;
-        if (!mbar_wait(&k_full[st], ph, abort_flag, WD_MMA_WAIT)) break;
+        if (!mbar_wait(&k_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
         if (j >= 2 && !mbar_wait(&s_free[sb], ((j >> 1) - 1) & 1, abort_flag, WD_MMA_WAIT)) break;
         tc_fence_after();
         const uint32_t k_base = smem_u32(smem + L::kK + st * NBQ * kBox);
@@ -230,8 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;
     const int qi = q0 + row;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-    uint8_t* p_smem = smem + L::kP;
-    float m_run = -INFINITY, l_run = 0.f;
+    const float sl2 = p.scale_log2;
+    float m_run = -INFINITY, l_run = 0.f;  // running max in log2 units, running row sum
     bool ok = true;
 
     for (int j = 0; j < n_tiles; ++j) {
@@ -241,68 +238,76 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t s_addr = lane_addr + (sb ? kTmemS1 : kTmemS0);
-      const int kv0 = j * kBN;
-      // Masking is needed only on tiles that cross Skv, with causal masking, or with a mask.
-      const bool need_mask = p.mask != nullptr || (kv0 + kBN > p.Skv) || (p.causal && kv0 + kBN - 1 > q0);
-      auto score = [&](int c, float raw) -> float {
-        float x = raw * p.scale_log2;
-        if (need_mask) {
-          const int kv = kv0 + c;
-          const bool valid = kv < p.Skv && !(p.causal && kv > qi);
-          if (p.mask && valid && qi < p.Sq) x += p.mask[(int64_t)qi * p.mask_stride + kv] * kLog2e;
-          x = valid ? x : -INFINITY;
-        }
-        return x;
-      };
-      // pass A: row max (S stays in TMEM; it is read twice rather than held in registers)
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(s_addr + c * 32, r);
+      // S row: four 32-column loads in flight, one wait
+      float s[kBN];
+      {
+        const uint32_t s_addr = lane_addr + (sb ? kTmemS1 : kTmemS0);
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld32(s_addr + 0, r0);
+        tmem_ld32(s_addr + 32, r1);
+        tmem_ld32(s_addr + 64, r2);
+        tmem_ld32(s_addr + 96, r3);
         tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 32; ++t) mx = fmaxf(mx, score(c * 32 + t, __uint_as_float(r[t])));
-      }
-      float m_new = fmaxf(m_run, mx);
-      bool rescale = false;
-      float m_use = m_run;
-      if (j == 0 || m_run == -INFINITY) {
-        m_use = m_new;
-      } else if (m_new > m_run + kRescaleThreshold) {
-        rescale = true;
-        m_use = m_new;
-      }
-      const float m_ref = m_use == -INFINITY ? 0.f : m_use;  // fully masked so far: p = 0
-      // pass B: exponentials, row sum, 16-bit packing
-      float rsum = 0.f;
-      uint32_t pk[kBN / 2];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(s_addr + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int t = 0; t < 32; t += 2) {
-          const float e0 = ex2_approx(score(c * 32 + t, __uint_as_float(r[t])) - m_ref);
-          const float e1 = ex2_approx(score(c * 32 + t + 1, __uint_as_float(r[t + 1])) - m_ref);
-          rsum += e0 + e1;
-          pk[(c * 32 + t) >> 1] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+        for (int t = 0; t < 32; ++t) {
+          s[t] = __uint_as_float(r0[t]);
+          s[32 + t] = __uint_as_float(r1[t]);
+          s[64 + t] = __uint_as_float(r2[t]);
+          s[96 + t] = __uint_as_float(r3[t]);
         }
       }
       tc_fence_before();
       mbar_arrive(&s_free[sb]);  // S buffer may be overwritten by QK_{j+2}
 
-      // P is single-buffered and O is about to change: PV_{j-1} must have completed.
-      if (j >= 1 && !mbar_wait_warp(o_done, (j - 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
+      // Masks act on raw scores: x_log2 = (s + mask / scale) * scale * log2(e).
+      const int kv0 = j * kBN;
+      const bool need_mask = p.mask != nullptr || (kv0 + kBN > p.Skv) ||
+                             (p.causal && kv0 + kBN - 1 > q0);
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) {
+          const int kv = kv0 + c;
+          const bool valid = kv < p.Skv && !(p.causal && kv > qi);
+          float x = s[c];
+          if (p.mask && valid && qi < p.Sq) x += p.mask[(int64_t)qi * p.mask_stride + kv] * p.inv_scale;
+          s[c] = valid ? x : -INFINITY;
+        }
+      }
+      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+#pragma unroll
+      for (int c = 4; c < kBN; c += 4) {
+        mx0 = fmaxf(mx0, s[c]);
+        mx1 = fmaxf(mx1, s[c + 1]);
+        mx2 = fmaxf(mx2, s[c + 2]);
+        mx3 = fmaxf(mx3, s[c + 3]);
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl2;
+      const float m_new = fmaxf(m_run, m_tile);
+      bool rescale = false;
+      float m_use = m_run;
+      if (m_run == -INFINITY) {
+        m_use = m_new;  // nothing accumulated yet (O and l are zero)
+      } else if (m_new > m_run + kRescaleThreshold) {
+        rescale = true;
+        m_use = m_new;
+      }
+      const float m_ref = m_use == -INFINITY ? 0.f : m_use;  // fully masked so far: p = 0
+
+      // P buffer j % 2 was last read by PV_{j-2}
+      if (j >= 2 && !mbar_wait_warp(&o_done[sb], ((j - 2) >> 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
         ok = false;
         break;
       }
-      tc_fence_after();
       // tcgen05.ld/st are warp-collective: the whole warp rescales if any of its rows must,
-      // rows that need no rescale use alpha = 1.
+      // rows that need no rescale use alpha = 1.  O must hold PV_{j-1} first.
       if (__any_sync(0xffffffffu, rescale)) {
+        if (j >= 1 &&
+            !mbar_wait_warp(&o_done[sb ^ 1], ((j - 1) >> 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         const float alpha = rescale ? ex2_approx(m_run - m_ref) : 1.0f;
         l_run *= alpha;
         for (int c = 0; c < p.dv_pad; c += 16) {
@@ -315,24 +320,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_wait_st();
       }
-      l_run += rsum;
       m_run = m_use;
 
-      // P row -> shared memory, K-major SW128: box (c8 / 8), 16-byte chunk (c8 % 8) ^ (row % 8)
+      // exp2, row sum, 16-bit P into shared memory (UMMA K-major SW128: box c8/8,
+      // 16-byte chunk (c8 % 8) ^ (row % 8))
+      uint8_t* p_smem = smem + L::kP + sb * 2 * kBox;
+      float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
       for (int c8 = 0; c8 < kBN / 8; ++c8) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float e0 = ex2_approx(fmaf(s[c8 * 8 + 2 * t], sl2, -m_ref));
+          const float e1 = ex2_approx(fmaf(s[c8 * 8 + 2 * t + 1], sl2, -m_ref));
+          rs0 += e0;
+          rs1 += e1;
+          pk[t] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+        }
         const uint32_t off = (c8 >> 3) * kBox + row * 128 + (((c8 & 7) ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(p_smem + off) =
-            make_uint4(pk[c8 * 4 + 0], pk[c8 * 4 + 1], pk[c8 * 4 + 2], pk[c8 * 4 + 3]);
+        *reinterpret_cast<uint4*>(p_smem + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
+      l_run += rs0 + rs1;
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[sb]);
     }
 
     // ---- epilogue: O / l -> global
+    const int last = n_tiles - 1;
     if (ok && n_tiles > 0 &&
-        mbar_wait_warp(o_done, (n_tiles - 1) & 1, abort_flag, WD_EPILOGUE_WAIT)) {
+        mbar_wait_warp(&o_done[last & 1], (last >> 1) & 1, abort_flag, WD_EPILOGUE_WAIT)) {
       tc_fence_after();
       const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
       const bool row_ok = qi < p.Sq;
@@ -341,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[16];
         tmem_ld16(lane_addr + kTmemO + c, r);
         tmem_wait_ld();
-        if (!row_ok) continue;
+        if (!row_ok || c >= p.Dv) continue;
         float o[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) o[t] = __uint_as_float(r[t]) * inv_l;
@@ -464,7 +481,9 @@ extern "C" int sp_flash_attn_fwd(const void* q, const void* k, const void* v, co
   // product runs on whole atoms (Dv 40 -> N 64; the extra columns are TMA zero fill).
   p.dv_pad = (int)((Dv + 63) / 64 * 64);
   p.n_kv_tiles = (int)((Skv + kBN - 1) / kBN);
-  p.scale_log2 = (scale > 0.f ? scale : 1.0f / sqrtf((float)D)) * kLog2e;
+  const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
+  p.scale_log2 = sc * kLog2e;
+  p.inv_scale = 1.0f / sc;
   p.causal = causal ? 1 : 0;
   p.mask = mask;
   p.mask_stride = mask_row_stride;
@@ -476,8 +495,8 @@ extern "C" int sp_flash_attn_fwd(const void* q, const void* k, const void* v, co
   p.in_f16 = in_f16;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool qk2 = D > 64, v2 = Dv > 64;
-  if (!qk2 && !v2) return launch_fa<1, 1, 3>(mq, mk, mv, p, B, s);
-  if (qk2 && v2) return launch_fa<2, 2, 2>(mq, mk, mv, p, B, s);
+  if (!qk2 && !v2) return launch_fa<1, 1, 3>(mq, mk, mv, p, B, s);  // 176 KB smem
+  if (qk2 && v2) return launch_fa<2, 2, 2>(mq, mk, mv, p, B, s);     // 224 KB smem
   if (qk2) return launch_fa<2, 1, 2>(mq, mk, mv, p, B, s);
   return launch_fa<1, 2, 2>(mq, mk, mv, p, B, s);
 }

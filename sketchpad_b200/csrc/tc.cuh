@@ -25,14 +25,10 @@ enum WatchdogCode : int {
   WD_CLUSTER_WAIT = 6,
 };
 
-// Wall-clock budget for one wait (ns).  No correct schedule waits anywhere near this long.
-constexpr uint64_t kWaitBudgetNs = 2000000000ull;
-
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
+// Budget for one wait, in SM clock cycles (~2 s at the 1.965 GHz boost clock, longer at
+// lower clocks).  No correct schedule waits anywhere near this long.  clock64 is read with a
+// cheap CS2R, so the deadline check stays off the critical path of a satisfied wait.
+constexpr long long kWaitBudgetCycles = 4000000000ll;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -76,13 +72,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const long long t0 = clock64();
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
+    if ((++spins & 255u) == 0) {
       if (abort && *abort) return false;
-      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+      if (clock64() - t0 > kWaitBudgetCycles) {
         atomicCAS(&g_watchdog, 0, code);
         if (abort) *abort = 1;
         return false;

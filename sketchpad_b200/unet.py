@@ -318,7 +318,7 @@ class UNetB200:
 
     # -- blocks ------------------------------------------------------------------------------
     def _res(self, x, temb_silu, p):
-        residual = self._conv(x, p + ".skip_conv") if (p + ".skip_conv") in self.p else x
+        residual = self._conv(x, p + ".skip_conv") if (p + ".skip_conv.weight") in self.p else x
         h = self._gn(x, p + ".norm1", True)
         h = self._conv(h, p + ".conv1")
         t = self._lin(temb_silu, p + ".time_emb_proj")
