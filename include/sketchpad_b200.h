@@ -91,6 +91,23 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
                      float eps, int act, int dtype, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* GroupNorm (+ SiLU) that allocates nothing.  No counterpart in the reference: it exists
+ * for callers that cannot hand the library device memory -- hosts whose allocator must not
+ * be used while they run, or FFI hosts holding raw device pointers without access to a CUDA
+ * allocator.  Same semantics and arguments as sp_groupnorm_act minus the workspace; it
+ * always runs the two-pass kernels, keeping their per-chunk statistics in a fixed array
+ * inside the library (sp_groupnorm_act_noalloc_max_scratch_bytes() bytes, 256 KB, held on
+ * every device that loads the library until exit).  Shapes needing more are rejected with
+ * SP_ERR_WORKSPACE (the limit is batch x groups x ceil(C/groups*H*W / 16384) <= 21845).
+ * The first call on a device looks up the array's device address and must come before any
+ * stream capture on that device.  Calls sharing a device share the array, so calls that can
+ * overlap on the GPU race. */
+size_t sp_groupnorm_act_noalloc_max_scratch_bytes(void);
+int sp_groupnorm_act_noalloc(const void* x, const void* gamma, const void* beta, void* y,
+                             int64_t B, int64_t C, int64_t H, int64_t W,
+                             const int64_t x_strides[4], int64_t groups, float eps, int act,
+                             int dtype, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * Q8_0 (GGUF) weights.
  * A Q8_0 row of in_f values is in_f/32 blocks of 34 bytes: f16 LE scale + 32 int8.

@@ -503,3 +503,100 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// GroupNorm(+SiLU) for callers that cannot allocate device memory.
+//
+// sp_groupnorm_act needs caller-provided workspace whenever it takes the two-pass path.
+// Some callers have no way to provide it: a host whose allocator must not be touched while
+// it runs (a real-time or pre-reserved memory budget), or an FFI host that holds raw device
+// pointers for its tensors but no handle to any CUDA allocator.  This variant runs the same
+// two-pass kernels with their per-chunk statistics in a fixed array compiled into the
+// library, so it allocates nothing and needs no workspace argument.
+//
+// The array lives in every device that loads the library, until the process exits.  Its
+// device address is looked up (cudaGetSymbolAddress) the first time the entry point runs on
+// a device, with that device current; make that first call outside any stream capture.
+// All calls on a device share the array: calls that can overlap on the GPU (different
+// streams without ordering between them) race on it.  Every slot a call reads is written
+// earlier by the same call, so nothing needs clearing between calls.
+// ---------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace sp {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 256 * 1024;
+constexpr size_t kNoAllocScratchFloats = kNoAllocScratchBytes / sizeof(float);
+static __device__ __align__(256) float g_gn_noalloc_scratch[kNoAllocScratchFloats];
+
+std::mutex g_noalloc_mutex;
+float* g_noalloc_ptr[64] = {};
+
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return set_error(SP_ERR_DEVICE, "groupnorm (no-alloc): no usable current device");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_gn_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(SP_ERR_LAUNCH, "groupnorm (no-alloc): scratch address lookup failed: %s",
+                       cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return SP_OK;
+}
+
+}  // namespace
+}  // namespace sp
+
+extern "C" size_t sp_groupnorm_act_noalloc_max_scratch_bytes(void) {
+  return sp::kNoAllocScratchBytes;
+}
+
+extern "C" int sp_groupnorm_act_noalloc(const void* x, const void* gamma, const void* beta, void* y,
+                                        int64_t B, int64_t C, int64_t H, int64_t W,
+                                        const int64_t x_strides[4], int64_t groups, float eps,
+                                        int act, int dtype, void* stream) {
+  using namespace sp;
+  clear_error();
+  if (!x || !gamma || !beta || !y)
+    return set_error(SP_ERR_INVALID_ARG, "groupnorm (no-alloc): null tensor pointer");
+  if (B <= 0 || C <= 0 || H <= 0 || W <= 0 || groups <= 0)
+    return set_error(SP_ERR_INVALID_ARG, "groupnorm (no-alloc): non-positive dimension");
+  if (C % groups != 0)
+    return set_error(SP_ERR_SHAPE, "channels (%lld) must be divisible by num_groups (%lld)",
+                     (long long)C, (long long)groups);
+  if (act != SP_ACT_NONE && act != SP_ACT_SILU)
+    return set_error(SP_ERR_INVALID_ARG, "groupnorm (no-alloc): unknown activation %d", act);
+  if (!dtype_size(dtype)) return set_error(SP_ERR_DTYPE, "groupnorm (no-alloc): unknown dtype %d", dtype);
+  if (B * groups > 65535)
+    return set_error(SP_ERR_SHAPE, "groupnorm (no-alloc): batch*groups (%lld) exceeds 65535",
+                     (long long)(B * groups));
+  const size_t need = general_workspace_bytes(B, C, H, W, groups);
+  if (need > kNoAllocScratchBytes)
+    return set_error(SP_ERR_WORKSPACE,
+                     "groupnorm (no-alloc): this shape needs %zu bytes of statistics but the fixed "
+                     "scratch holds %zu; use sp_groupnorm_act with a workspace",
+                     need, kNoAllocScratchBytes);
+  if (int rc = require_sm100()) return rc;
+  float* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+
+  const int64_t HW = H * W, cg = C / groups, n = cg * HW;
+  int64_t st[4] = {C * HW, HW, W, 1};
+  if (!is_contiguous_nchw(B, C, H, W, x_strides))
+    for (int i = 0; i < 4; ++i) st[i] = x_strides[i];
+  const int64_t nchunks = (n + kGeneralChunk - 1) / kGeneralChunk;
+  GnGeneralParams p{x,     gamma, beta,  y,     B,     C,     H, W, groups, cg, n,
+                    st[0], st[1], st[2], st[3], kGeneralChunk, nchunks, scratch, eps, act};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SP_F32: return launch_general<float>(p, B * groups, s);
+    case SP_F16: return launch_general<__half>(p, B * groups, s);
+    default: return launch_general<__nv_bfloat16>(p, B * groups, s);
+  }
+}
