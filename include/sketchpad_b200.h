@@ -75,14 +75,16 @@ int sp_flash_attn_fwd(const void* q, const void* k, const void* v, const float* 
  *   (crates/sketchpad-cubecl/src/groupnorm_silu.rs:232, :323; GroupNormSiLuOptions :22-46)
  * with the semantics of the CPU path crates/sketchpad-core/src/groupnorm.rs:62-102
  * (clamp +-65000, f32 statistics, biased variance, clamp after the affine).
- *   x [B,C,H,W] with element strides x_strides (NULL = contiguous); y contiguous [B,C,H,W].
+ *   x [B,C,H,W] with element strides x_strides (NULL = contiguous NCHW).  y [B,C,H,W] is
+ *   written channels-last (strides C*H*W, 1, W*C, C) when x is channels-last -- the layout
+ *   sm_100 implicit-GEMM convolutions use -- and contiguous NCHW otherwise.
  *   gamma, beta [C]; x, y, gamma, beta all of `dtype` (SP_F32, SP_F16, SP_BF16).
  *   act: SP_ACT_SILU (groupnorm_silu) or SP_ACT_NONE (groupnorm).
  *   Returns SP_ERR_SHAPE when C % groups != 0 (the reference panics there).
- * workspace: strided inputs and groups larger than one thread-block cluster can hold on
- *   chip use a two-kernel path that needs device workspace; sp_groupnorm_act_workspace_size()
- *   returns its size, or 0 when x and y are 16-byte aligned and the single-pass path applies
- *   (workspace may then be NULL).
+ * workspace: channels-last inputs, other strided inputs and NCHW groups larger than one
+ *   thread-block cluster can hold on chip use two-kernel paths that need device workspace;
+ *   sp_groupnorm_act_workspace_size() returns its size, or 0 when x and y are 16-byte aligned
+ *   and the single-pass NCHW path applies (workspace may then be NULL).
  * ------------------------------------------------------------------------------------ */
 size_t sp_groupnorm_act_workspace_size(int64_t B, int64_t C, int64_t H, int64_t W,
                                        const int64_t x_strides[4], int64_t groups, int dtype);

@@ -438,6 +438,8 @@ size_t sp_groupnorm_act_workspace_size(int64_t B, int64_t C, int64_t H, int64_t 
                                        const int64_t x_strides[4], int64_t groups, int dtype) {
   const int es = sp::dtype_size(dtype);
   if (!es || B <= 0 || C <= 0 || H <= 0 || W <= 0 || groups <= 0 || C % groups) return 0;
+  if (sp::gn_nhwc_applicable(B, C, H, W, x_strides, es, groups))
+    return sp::gn_nhwc_workspace_bytes(B, C, H, W, es, groups);
   const bool contiguous = sp::is_contiguous_nchw(B, C, H, W, x_strides);
   const int vec = 16 / es;
   const sp::GnPlan pl = sp::plan_gn(B, groups, C / groups * H * W, contiguous,
@@ -469,6 +471,9 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
   const int64_t HW = H * W, cg = C / groups, n = cg * HW;
+  if (gn_nhwc_applicable(B, C, H, W, x_strides, es, groups))
+    return gn_nhwc_launch(x, gamma, beta, y, B, C, H, W, groups, eps, act, dtype, workspace,
+                          workspace_bytes, s);
   int64_t st[4] = {C * HW, HW, W, 1};
   const bool contiguous = is_contiguous_nchw(B, C, H, W, x_strides);
   if (!contiguous)

@@ -1,0 +1,328 @@
+// groupnorm_nhwc.cu -- GroupNorm(+SiLU) for channels-last (NHWC) activations.
+//
+// Same semantics as the NCHW kernels in groupnorm_act.cu (crates/sketchpad-core/src/
+// groupnorm.rs:62-102: clamp +-65000, f32 statistics, biased variance, clamp after the
+// affine, optional SiLU).  Channels-last is what cuDNN's implicit-GEMM convolutions on
+// sm_100 read and write, so a UNet kept channels-last runs no layout conversions.
+//
+// x is viewed as a row-major [B*H*W, C] matrix; group g owns channels [g*Cg, (g+1)*Cg) of
+// every row of its batch image.  Two kernels:
+//   stats  grid (chunks, B): each CTA reduces a chunk of rows to per-group (count, mean, M2)
+//          (two passes over the chunk, the second from L1/L2); the last CTA of a batch image
+//          (atomic ticket) merges all chunks with Chan's pairwise update into (mean, rstd).
+//   apply  grid (chunks, B): normalise + affine + activation, 16-byte loads and stores.
+// HBM sees one read and one write of x at UNet sizes (the second read is an L2 hit).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace sp {
+
+namespace {
+
+constexpr int kNhwcThreads = 256;
+
+__device__ __forceinline__ float nh_to_f32(float v) { return v; }
+__device__ __forceinline__ float nh_to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float nh_to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T>
+__device__ __forceinline__ T nh_from_f32(float v);
+template <>
+__device__ __forceinline__ float nh_from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half nh_from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 nh_from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+__device__ __forceinline__ float nh_clamp(float v) { return fminf(fmaxf(v, -65000.0f), 65000.0f); }
+
+__device__ __forceinline__ float nh_act(float v, int act) {
+  v = nh_clamp(v);
+  if (act == SP_ACT_SILU) {
+    float t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * v));
+    v = v * fmaf(0.5f, t, 0.5f);
+  }
+  return v;
+}
+
+struct NhwcParams {
+  const void* x;
+  const void* gamma;
+  const void* beta;
+  void* y;
+  int P;               // pixels per image (H*W)
+  int C, G, Cg;        // channels, groups, channels per group
+  int CV;              // 16-byte channel vectors per row
+  int TX, TY;          // block shape: TX channel-vector lanes x TY row lanes
+  int rows_per_chunk;  // rows of one batch image per CTA
+  int nchunks;         // chunks per batch image
+  float* part;         // [B, nchunks, G, 3] (count, mean, M2)
+  float* stats;        // [B, G, 2] (mean, rstd)
+  unsigned int* tickets;  // [B], zero before the stats kernel
+  float eps;
+  int act;
+};
+
+// Per-thread channel vectors: cv = tx + k*TX (k < NV).
+template <typename T, int NV>
+__global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_stats_kernel(NhwcParams p) {
+  constexpr int VE = 16 / sizeof(T);
+  extern __shared__ float csum[];  // [C] per-channel accumulators, then [G] group values
+  __shared__ float gval[1024];
+  __shared__ unsigned int is_last;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int tid = ty * p.TX + tx;
+  const int nthr = p.TX * p.TY;
+  const int b = blockIdx.y, chunk = blockIdx.x;
+  const int r0 = chunk * p.rows_per_chunk;
+  const int r1 = min(p.P, r0 + p.rows_per_chunk);
+  const T* xb = static_cast<const T*>(p.x) + (int64_t)b * p.P * p.C;
+
+  for (int i = tid; i < p.C; i += nthr) csum[i] = 0.f;
+  __syncthreads();
+  float acc[NV][VE];
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+#pragma unroll
+    for (int e = 0; e < VE; ++e) acc[k][e] = 0.f;
+  for (int r = r0 + ty; r < r1; r += p.TY) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int cv = tx + k * p.TX;
+      if (cv < p.CV) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(xb + (int64_t)r * p.C) + cv);
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int t = 0; t < VE; ++t) acc[k][t] += nh_clamp(nh_to_f32(e[t]));
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int cv = tx + k * p.TX;
+    if (cv < p.CV)
+#pragma unroll
+      for (int t = 0; t < VE; ++t) atomicAdd(&csum[cv * VE + t], acc[k][t]);
+  }
+  __syncthreads();
+  const float cnt = (float)(r1 - r0) * (float)p.Cg;
+  for (int g = tid; g < p.G; g += nthr) {
+    float s = 0.f;
+    for (int c = g * p.Cg; c < (g + 1) * p.Cg; ++c) s += csum[c];
+    gval[g] = s / cnt;  // chunk mean of group g
+  }
+  __syncthreads();
+  for (int i = tid; i < p.C; i += nthr) csum[i] = 0.f;
+  __syncthreads();
+  // second pass: centred sum of squares around the chunk mean (rows are L1/L2 resident)
+  float mine[NV][VE];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int cv = tx + k * p.TX;
+#pragma unroll
+    for (int t = 0; t < VE; ++t) {
+      acc[k][t] = 0.f;
+      mine[k][t] = cv < p.CV ? gval[(cv * VE + t) / p.Cg] : 0.f;
+    }
+  }
+  for (int r = r0 + ty; r < r1; r += p.TY) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int cv = tx + k * p.TX;
+      if (cv < p.CV) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(xb + (int64_t)r * p.C) + cv);
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int t = 0; t < VE; ++t) {
+          const float d = nh_clamp(nh_to_f32(e[t])) - mine[k][t];
+          acc[k][t] += d * d;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int cv = tx + k * p.TX;
+    if (cv < p.CV)
+#pragma unroll
+      for (int t = 0; t < VE; ++t) atomicAdd(&csum[cv * VE + t], acc[k][t]);
+  }
+  __syncthreads();
+  float* part = p.part + ((int64_t)b * p.nchunks + chunk) * p.G * 3;
+  for (int g = tid; g < p.G; g += nthr) {
+    float m2 = 0.f;
+    for (int c = g * p.Cg; c < (g + 1) * p.Cg; ++c) m2 += csum[c];
+    part[g * 3 + 0] = cnt;
+    part[g * 3 + 1] = gval[g];
+    part[g * 3 + 2] = m2;
+  }
+  // last CTA of this image merges every chunk (classic ticket pattern: no CTA waits)
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = (atomicAdd(&p.tickets[b], 1u) == (unsigned)p.nchunks - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  const float* pb = p.part + (int64_t)b * p.nchunks * p.G * 3;
+  for (int g = tid; g < p.G; g += nthr) {
+    double n = 0.0, mean = 0.0, m2 = 0.0;
+    for (int i = 0; i < p.nchunks; ++i) {
+      const float* q = pb + ((int64_t)i * p.G + g) * 3;
+      const double nb = __ldcg(q), mb = __ldcg(q + 1), m2b = __ldcg(q + 2);
+      const double nn = n + nb, d = mb - mean;
+      mean += d * nb / nn;
+      m2 += m2b + d * d * n * nb / nn;
+      n = nn;
+    }
+    p.stats[((int64_t)b * p.G + g) * 2 + 0] = (float)mean;
+    p.stats[((int64_t)b * p.G + g) * 2 + 1] = rsqrtf((float)(m2 / n) + p.eps);
+  }
+  if (tid == 0) p.tickets[b] = 0;  // ready for the next call on this workspace
+}
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_apply_kernel(NhwcParams p) {
+  constexpr int VE = 16 / sizeof(T);
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int b = blockIdx.y, chunk = blockIdx.x;
+  const int r0 = chunk * p.rows_per_chunk;
+  const int r1 = min(p.P, r0 + p.rows_per_chunk);
+  const T* xb = static_cast<const T*>(p.x) + (int64_t)b * p.P * p.C;
+  T* yb = static_cast<T*>(p.y) + (int64_t)b * p.P * p.C;
+  const T* gam = static_cast<const T*>(p.gamma);
+  const T* bet = static_cast<const T*>(p.beta);
+  const float* st = p.stats + (int64_t)b * p.G * 2;
+  // per-channel multiplier / offset: y = (x - mean) * (rstd * gamma) + beta
+  float mul[NV][VE], sub[NV][VE], add[NV][VE];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int cv = tx + k * p.TX;
+#pragma unroll
+    for (int t = 0; t < VE; ++t) {
+      const int c = min(cv * VE + t, p.C - 1);
+      const int g = c / p.Cg;
+      sub[k][t] = st[g * 2];
+      mul[k][t] = st[g * 2 + 1] * nh_to_f32(gam[c]);
+      add[k][t] = nh_to_f32(bet[c]);
+    }
+  }
+  for (int r = r0 + ty; r < r1; r += p.TY) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int cv = tx + k * p.TX;
+      if (cv < p.CV) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(xb + (int64_t)r * p.C) + cv);
+        const T* e = reinterpret_cast<const T*>(&u);
+        uint4 o;
+        T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int t = 0; t < VE; ++t)
+          oe[t] = nh_from_f32<T>(nh_act((nh_clamp(nh_to_f32(e[t])) - sub[k][t]) * mul[k][t] + add[k][t], p.act));
+        reinterpret_cast<uint4*>(yb + (int64_t)r * p.C)[cv] = o;
+      }
+    }
+  }
+}
+
+struct NhwcPlan {
+  int CV, NV, TX, TY, rows_per_chunk, nchunks;
+};
+
+NhwcPlan plan_nhwc(int64_t B, int64_t P, int64_t C, int es) {
+  NhwcPlan pl{};
+  const int VE = 16 / es;
+  pl.CV = (int)(C / VE);
+  pl.NV = (pl.CV + kNhwcThreads - 1) / kNhwcThreads;
+  pl.TX = (pl.CV + pl.NV - 1) / pl.NV;
+  pl.TY = std::max(1, kNhwcThreads / pl.TX);
+  const int64_t target_ctas = 4LL * num_sms();
+  const int64_t per_image = std::max<int64_t>(1, (target_ctas + B - 1) / B);
+  int64_t rows = (P + per_image - 1) / per_image;
+  rows = ((rows + pl.TY - 1) / pl.TY) * pl.TY;
+  rows = std::max<int64_t>(rows, pl.TY);
+  pl.rows_per_chunk = (int)rows;
+  pl.nchunks = (int)((P + rows - 1) / rows);
+  return pl;
+}
+
+}  // namespace
+
+bool gn_nhwc_applicable(int64_t B, int64_t C, int64_t H, int64_t W, const int64_t* st, int es,
+                        int64_t groups) {
+  if (!st) return false;
+  const int64_t want[4] = {H * W * C, 1, W * C, C};
+  const int64_t dims[4] = {B, C, H, W};
+  for (int i = 0; i < 4; ++i)
+    if (dims[i] > 1 && st[i] != want[i]) return false;
+  if (C == 1 && H * W > 1) return false;  // ambiguous with NCHW; leave it to the NCHW path
+  const int VE = 16 / es;
+  return C % VE == 0 && C / VE <= 2 * kNhwcThreads && groups <= 1024 && H * W < (1LL << 31);
+}
+
+size_t gn_nhwc_workspace_bytes(int64_t B, int64_t C, int64_t H, int64_t W, int es, int64_t groups) {
+  const NhwcPlan pl = plan_nhwc(B, H * W, C, es);
+  const size_t part = (size_t)B * pl.nchunks * groups * 3 * sizeof(float);
+  const size_t stats = (size_t)B * groups * 2 * sizeof(float);
+  return part + stats + (size_t)B * sizeof(unsigned int) + 64;
+}
+
+template <typename T>
+static int launch_nhwc_t(const NhwcParams& p, int NV, int64_t B, cudaStream_t s) {
+  dim3 block(p.TX, p.TY), grid(p.nchunks, (unsigned)B);
+  const size_t smem = (size_t)p.C * sizeof(float);
+  if (NV == 1) {
+    gn_nhwc_stats_kernel<T, 1><<<grid, block, smem, s>>>(p);
+    if (int rc = check_launch("groupnorm nhwc stats")) return rc;
+    gn_nhwc_apply_kernel<T, 1><<<grid, block, 0, s>>>(p);
+  } else {
+    gn_nhwc_stats_kernel<T, 2><<<grid, block, smem, s>>>(p);
+    if (int rc = check_launch("groupnorm nhwc stats")) return rc;
+    gn_nhwc_apply_kernel<T, 2><<<grid, block, 0, s>>>(p);
+  }
+  return check_launch("groupnorm nhwc apply");
+}
+
+int gn_nhwc_launch(const void* x, const void* gamma, const void* beta, void* y, int64_t B,
+                   int64_t C, int64_t H, int64_t W, int64_t groups, float eps, int act, int dtype,
+                   void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  const int es = dtype_size(dtype);
+  const size_t need = gn_nhwc_workspace_bytes(B, C, H, W, es, groups);
+  if (!workspace || workspace_bytes < need)
+    return set_error(SP_ERR_WORKSPACE, "groupnorm (channels-last): needs %zu bytes of workspace (got %zu)",
+                     need, workspace_bytes);
+  if (!aligned(workspace, 16) || !aligned(x, 16) || !aligned(y, 16))
+    return set_error(SP_ERR_ALIGN, "groupnorm (channels-last): x, y and workspace must be 16-byte aligned");
+  const NhwcPlan pl = plan_nhwc(B, H * W, C, es);
+  NhwcParams p{};
+  p.x = x;
+  p.gamma = gamma;
+  p.beta = beta;
+  p.y = y;
+  p.P = (int)(H * W);
+  p.C = (int)C;
+  p.G = (int)groups;
+  p.Cg = (int)(C / groups);
+  p.CV = pl.CV;
+  p.TX = pl.TX;
+  p.TY = pl.TY;
+  p.rows_per_chunk = pl.rows_per_chunk;
+  p.nchunks = pl.nchunks;
+  float* ws = static_cast<float*>(workspace);
+  p.part = ws;
+  p.stats = ws + (size_t)B * pl.nchunks * groups * 3;
+  p.tickets = reinterpret_cast<unsigned int*>(p.stats + (size_t)B * groups * 2);
+  p.eps = eps;
+  p.act = act;
+  if (cudaMemsetAsync(p.tickets, 0, (size_t)B * sizeof(unsigned int), s) != cudaSuccess)
+    return set_error(SP_ERR_LAUNCH, "groupnorm (channels-last): ticket reset failed");
+  switch (dtype) {
+    case SP_F32: return launch_nhwc_t<float>(p, pl.NV, B, s);
+    case SP_F16: return launch_nhwc_t<__half>(p, pl.NV, B, s);
+    default: return launch_nhwc_t<__nv_bfloat16>(p, pl.NV, B, s);
+  }
+}
+
+}  // namespace sp

@@ -44,8 +44,11 @@ def _run(input: torch.Tensor, weight, bias, options: GroupNormSiLuOptions, act: 
     w = weight if weight.dtype == dt else weight.to(dt)
     b = bias if bias.dtype == dt else bias.to(dt)
     w, b = w.contiguous(), b.contiguous()
+    channels_last = (not input.is_contiguous()) and input.is_contiguous(
+        memory_format=torch.channels_last)
     if out is None:
-        out = torch.empty((B, C, H, W), dtype=dt, device=dev)
+        fmt = torch.channels_last if channels_last else torch.contiguous_format
+        out = torch.empty((B, C, H, W), dtype=dt, device=dev, memory_format=fmt)
     code = dtype_code(dt)
     strides = _lib.i64_array(input.stride())
     ws_bytes = _lib.load().sp_groupnorm_act_workspace_size(B, C, H, W, strides, G, code)

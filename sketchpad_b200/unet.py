@@ -267,6 +267,15 @@ class UNetB200:
         self.spec = dict(self.specs)
         self.p = {k: (v if isinstance(v, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(v)))
                   .to(self.device, dtype).contiguous() for k, v in params.items()}
+        # Activations are kept channels-last (NHWC), the layout sm_100 implicit-GEMM
+        # convolutions use, so no convolution converts layouts.  Conv weights follow; the
+        # spatial transformers' 1x1 projections run as plain GEMMs on the NHWC buffer.
+        for name, spec in self.specs:
+            if spec[0] == "conv":
+                w = self.p[name + ".weight"]
+                if spec[3] == 1 and (".proj_in" in name or ".proj_out" in name):
+                    self.p[name + ".wmat"] = w.reshape(w.shape[0], w.shape[1]).t().contiguous()
+                self.p[name + ".weight"] = w.contiguous(memory_format=torch.channels_last)
         # fused QKV weight for the self-attention projections (same math as three Linears)
         for name, spec in self.specs:
             if name.endswith(".attn1.to_q"):
@@ -282,12 +291,14 @@ class UNetB200:
         self.attn_events: list | None = None  # (start, end, flops) when timing attention
 
     # -- ops ---------------------------------------------------------------------------------
-    def _lin(self, x, name, bias=True):
-        w = self.p[name + ".weight"]
-        y = torch.matmul(x, w)
-        if bias and (name + ".bias") in self.p:
-            y = y + self.p[name + ".bias"]
-        return y
+    def _lin(self, x, name, bias=True, wkey=".weight"):
+        w = self.p[name + wkey]
+        b = self.p.get(name + ".bias") if bias else None
+        if b is None:
+            return torch.matmul(x, w)
+        lead = x.shape[:-1]
+        y = torch.addmm(b, x.reshape(-1, x.shape[-1]), w)  # bias fused into the GEMM epilogue
+        return y.view(*lead, w.shape[1])
 
     def _conv(self, x, name, stride=1):
         w = self.p[name + ".weight"]
@@ -347,9 +358,9 @@ class UNetB200:
         b, c, h, w = x.shape
         residual = x
         y = self._gn(x, p + ".norm", False)
-        y = self._conv(y, p + ".proj_in")
-        inner = y.shape[1]
-        y = y.reshape(b, inner, h * w).transpose(1, 2).contiguous()
+        # NHWC memory is already [b, h*w, c]: proj_in (1x1 conv) is a GEMM over channels
+        y = self._lin(y.permute(0, 2, 3, 1).reshape(b, h * w, c), p + ".proj_in", wkey=".wmat")
+        inner = y.shape[-1]
         for d in range(self.cfg.transformer_depth):
             tb = f"{p}.tb{d}"
             y = y + self._xattn(self._ln(y, tb + ".norm1"), tb + ".attn1", None)
@@ -357,12 +368,12 @@ class UNetB200:
             hdn = self._lin(self._ln(y, tb + ".norm3"), tb + ".ff.net_0")
             half = hdn.shape[-1] // 2
             y = y + self._lin(hdn[..., :half] * F.gelu(hdn[..., half:]), tb + ".ff.net_2")
-        y = y.transpose(1, 2).reshape(b, inner, h, w)
-        return self._conv(y, p + ".proj_out") + residual
+        y = self._lin(y, p + ".proj_out", wkey=".wmat")  # [b, h*w, c] == NHWC memory
+        return y.view(b, h, w, c).permute(0, 3, 1, 2) + residual
 
     def forward(self, x: torch.Tensor, timesteps: torch.Tensor, context: torch.Tensor) -> torch.Tensor:
         """UNet::forward (unet_sd.rs:235-272): noisy latent [b,4,h,w] -> predicted noise."""
-        x = x.to(self.dtype)
+        x = x.to(self.dtype).contiguous(memory_format=torch.channels_last)
         context = context.to(self.dtype)
         args = timesteps.float()[:, None] * self.freqs[None, :]
         temb = torch.cat([torch.sin(args), torch.cos(args)], dim=1).to(self.dtype)
@@ -401,7 +412,7 @@ class UNetB200:
             else:
                 h = self._gn(h, "norm_out", True)
                 h = self._conv(h, "conv_out")
-        return h
+        return h.contiguous()
 
     __call__ = forward
 

@@ -79,6 +79,24 @@ def test_groupnorm_strided_input():
     assert rel_err(to_np(y), ref) < TOL_F32
 
 
+@pytest.mark.parametrize("shape", [(2, 320, 64, 64), (2, 640, 32, 32), (2, 1280, 8, 8),
+                                   (2, 2560, 8, 8), (2, 1920, 16, 16), (2, 960, 32, 32),
+                                   (1, 64, 300, 300), (3, 96, 7, 9)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_groupnorm_channels_last(shape, dtype):
+    # the UNet keeps activations channels-last; output keeps the input's layout
+    x, g, b = make(shape, seed=7)
+    xt = torch.from_numpy(x).cuda().to(dtype).to(memory_format=torch.channels_last)
+    ref = oracle.groupnorm_act(to_np(xt), to_np(torch.from_numpy(g).to(dtype)),
+                               to_np(torch.from_numpy(b).to(dtype)), 32, 1e-5, silu=True)
+    y = groupnorm_silu(xt, torch.from_numpy(g).cuda().to(dtype), torch.from_numpy(b).cuda().to(dtype))
+    assert y.is_contiguous(memory_format=torch.channels_last)
+    tol = TOL_F32 if dtype == torch.float32 else TOL_HALF
+    assert rel_err(to_np(y), ref) < tol
+    y2 = groupnorm_silu(xt, torch.from_numpy(g).cuda().to(dtype), torch.from_numpy(b).cuda().to(dtype))
+    assert torch.equal(y, y2)  # the ticket counters reset: a second call is identical
+
+
 def test_groupnorm_clamps_large_values():
     x, g, b = make((1, 32, 4, 4), seed=5)
     x[0, 0, 0, 0] = 1e6
