@@ -8,9 +8,10 @@
 // x is viewed as a row-major [B*H*W, C] matrix; group g owns channels [g*Cg, (g+1)*Cg) of
 // every row of its batch image.  Two kernels:
 //   stats  grid (chunks, B): each CTA reduces a chunk of rows to per-group (count, mean, M2)
-//          (two passes over the chunk, the second from L1/L2); the last CTA of a batch image
-//          (atomic ticket) merges all chunks with Chan's pairwise update into (mean, rstd).
-//   apply  grid (chunks, B): normalise + affine + activation, 16-byte loads and stores.
+//          (two passes over the chunk, the second from L1/L2).
+//   apply  grid (chunks, B): every CTA merges its image's chunk partials (lanes of a warp
+//          split the chunks, then a shuffle tree; Chan's pairwise update), then normalises +
+//          affine + activation with 16-byte loads and stores.
 // HBM sees one read and one write of x at UNet sizes (the second read is an L2 hit).
 #include <algorithm>
 
@@ -60,8 +61,6 @@ struct NhwcParams {
   int rows_per_chunk;  // rows of one batch image per CTA
   int nchunks;         // chunks per batch image
   float* part;         // [B, nchunks, G, 3] (count, mean, M2)
-  float* stats;        // [B, G, 2] (mean, rstd)
-  unsigned int* tickets;  // [B], zero before the stats kernel
   float eps;
   int act;
 };
@@ -72,7 +71,6 @@ __global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_stats_kernel(NhwcParams 
   constexpr int VE = 16 / sizeof(T);
   extern __shared__ float csum[];  // [C] per-channel accumulators, then [G] group values
   __shared__ float gval[1024];
-  __shared__ unsigned int is_last;
   const int tx = threadIdx.x, ty = threadIdx.y;
   const int tid = ty * p.TX + tx;
   const int nthr = p.TX * p.TY;
@@ -159,28 +157,6 @@ __global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_stats_kernel(NhwcParams 
     part[g * 3 + 1] = gval[g];
     part[g * 3 + 2] = m2;
   }
-  // last CTA of this image merges every chunk (classic ticket pattern: no CTA waits)
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) is_last = (atomicAdd(&p.tickets[b], 1u) == (unsigned)p.nchunks - 1) ? 1u : 0u;
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  const float* pb = p.part + (int64_t)b * p.nchunks * p.G * 3;
-  for (int g = tid; g < p.G; g += nthr) {
-    double n = 0.0, mean = 0.0, m2 = 0.0;
-    for (int i = 0; i < p.nchunks; ++i) {
-      const float* q = pb + ((int64_t)i * p.G + g) * 3;
-      const double nb = __ldcg(q), mb = __ldcg(q + 1), m2b = __ldcg(q + 2);
-      const double nn = n + nb, d = mb - mean;
-      mean += d * nb / nn;
-      m2 += m2b + d * d * n * nb / nn;
-      n = nn;
-    }
-    p.stats[((int64_t)b * p.G + g) * 2 + 0] = (float)mean;
-    p.stats[((int64_t)b * p.G + g) * 2 + 1] = rsqrtf((float)(m2 / n) + p.eps);
-  }
-  if (tid == 0) p.tickets[b] = 0;  // ready for the next call on this workspace
 }
 
 template <typename T, int NV>
@@ -194,7 +170,46 @@ __global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_apply_kernel(NhwcParams 
   T* yb = static_cast<T*>(p.y) + (int64_t)b * p.P * p.C;
   const T* gam = static_cast<const T*>(p.gamma);
   const T* bet = static_cast<const T*>(p.beta);
-  const float* st = p.stats + (int64_t)b * p.G * 2;
+  __shared__ float st[2048];  // (mean, rstd) per group
+  {
+    // merge the chunk partials of this image: whole warps only; a warp takes groups
+    // g = warp, warp + nwarps, ...; its lanes split the chunks, then a butterfly merges them
+    const int tid = ty * p.TX + tx;
+    const int nwarps = (p.TX * p.TY) / 32;
+    const int warp = tid >> 5, lane = tid & 31;
+    const float* pb = p.part + (int64_t)b * p.nchunks * p.G * 3;
+    if (warp < nwarps) {
+      for (int g = warp; g < p.G; g += nwarps) {
+        float n = 0.f, mean = 0.f, m2 = 0.f;
+        for (int i = lane; i < p.nchunks; i += 32) {
+          const float* q = pb + ((int64_t)i * p.G + g) * 3;
+          const float nb = q[0], mb = q[1], m2b = q[2];
+          const float nn = n + nb, d = mb - mean;
+          mean += d * (nb / nn);
+          m2 += m2b + d * d * (n * nb / nn);
+          n = nn;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float nb = __shfl_xor_sync(0xffffffffu, n, o);
+          const float mb = __shfl_xor_sync(0xffffffffu, mean, o);
+          const float m2b = __shfl_xor_sync(0xffffffffu, m2, o);
+          const float nn = n + nb;
+          if (nn > 0.f) {
+            const float d = mb - mean;
+            mean += d * (nb / nn);
+            m2 += m2b + d * d * (n * nb / nn);
+          }
+          n = nn;
+        }
+        if (lane == 0) {
+          st[2 * g] = mean;
+          st[2 * g + 1] = rsqrtf(m2 / n + p.eps);
+        }
+      }
+    }
+    __syncthreads();
+  }
   // per-channel multiplier / offset: y = (x - mean) * (rstd * gamma) + beta
   float mul[NV][VE], sub[NV][VE], add[NV][VE];
 #pragma unroll
@@ -238,7 +253,7 @@ NhwcPlan plan_nhwc(int64_t B, int64_t P, int64_t C, int es) {
   pl.NV = (pl.CV + kNhwcThreads - 1) / kNhwcThreads;
   pl.TX = (pl.CV + pl.NV - 1) / pl.NV;
   pl.TY = std::max(1, kNhwcThreads / pl.TX);
-  const int64_t target_ctas = 4LL * num_sms();
+  const int64_t target_ctas = 2LL * num_sms();
   const int64_t per_image = std::max<int64_t>(1, (target_ctas + B - 1) / B);
   int64_t rows = (P + per_image - 1) / per_image;
   rows = ((rows + pl.TY - 1) / pl.TY) * pl.TY;
@@ -259,14 +274,13 @@ bool gn_nhwc_applicable(int64_t B, int64_t C, int64_t H, int64_t W, const int64_
     if (dims[i] > 1 && st[i] != want[i]) return false;
   if (C == 1 && H * W > 1) return false;  // ambiguous with NCHW; leave it to the NCHW path
   const int VE = 16 / es;
+  // blocks always hold >= 32 threads (TX <= 256 and TY = 256 / TX), which the merge needs
   return C % VE == 0 && C / VE <= 2 * kNhwcThreads && groups <= 1024 && H * W < (1LL << 31);
 }
 
 size_t gn_nhwc_workspace_bytes(int64_t B, int64_t C, int64_t H, int64_t W, int es, int64_t groups) {
   const NhwcPlan pl = plan_nhwc(B, H * W, C, es);
-  const size_t part = (size_t)B * pl.nchunks * groups * 3 * sizeof(float);
-  const size_t stats = (size_t)B * groups * 2 * sizeof(float);
-  return part + stats + (size_t)B * sizeof(unsigned int) + 64;
+  return (size_t)B * pl.nchunks * groups * 3 * sizeof(float);
 }
 
 template <typename T>
@@ -310,14 +324,9 @@ int gn_nhwc_launch(const void* x, const void* gamma, const void* beta, void* y, 
   p.TY = pl.TY;
   p.rows_per_chunk = pl.rows_per_chunk;
   p.nchunks = pl.nchunks;
-  float* ws = static_cast<float*>(workspace);
-  p.part = ws;
-  p.stats = ws + (size_t)B * pl.nchunks * groups * 3;
-  p.tickets = reinterpret_cast<unsigned int*>(p.stats + (size_t)B * groups * 2);
+  p.part = static_cast<float*>(workspace);
   p.eps = eps;
   p.act = act;
-  if (cudaMemsetAsync(p.tickets, 0, (size_t)B * sizeof(unsigned int), s) != cudaSuccess)
-    return set_error(SP_ERR_LAUNCH, "groupnorm (channels-last): ticket reset failed");
   switch (dtype) {
     case SP_F32: return launch_nhwc_t<float>(p, pl.NV, B, s);
     case SP_F16: return launch_nhwc_t<__half>(p, pl.NV, B, s);

@@ -69,11 +69,11 @@ def test_groupnorm_ragged_and_general_paths(shape, groups):
 
 
 def test_groupnorm_strided_input():
-    # a channels-last view: non-contiguous NCHW strides go through the general path
-    x, g, b = make((2, 64, 16, 16), seed=4)
-    xt = torch.from_numpy(x).cuda().to(memory_format=torch.channels_last)
-    assert not xt.is_contiguous()
-    ref = oracle.groupnorm_act(x, g, b, 32, 1e-5, silu=True)
+    # an H/W-transposed view is neither NCHW- nor NHWC-contiguous: the general strided path
+    x, g, b = make((2, 64, 16, 24), seed=4)
+    xt = torch.from_numpy(x).cuda().transpose(2, 3)
+    assert not xt.is_contiguous() and not xt.is_contiguous(memory_format=torch.channels_last)
+    ref = oracle.groupnorm_act(np.ascontiguousarray(x.transpose(0, 1, 3, 2)), g, b, 32, 1e-5, silu=True)
     y = groupnorm_silu(xt, torch.from_numpy(g).cuda(), torch.from_numpy(b).cuda())
     assert y.is_contiguous()
     assert rel_err(to_np(y), ref) < TOL_F32
