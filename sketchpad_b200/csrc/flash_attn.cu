@@ -5,30 +5,36 @@
 // operation of sketchpad_cubecl::flash_attention (crates/sketchpad-cubecl/src/attention.rs:97-178)
 // and of the CPU attention it must match (crates/sketchpad-unet/src/blocks.rs:370-410).
 //
-// One CTA = one 128-query tile of one (batch, head).  Warp roles (192 threads):
-//   warp 0      TMA producer: Q once, then K/V tiles of 128 keys through a STAGES-deep ring.
-//   warp 1      TMEM owner + MMA issuer (one elected lane):
-//                 S[j%2] = Q K_j^T         (M=128, N=128, K=D padded to 16)
-//                 O     += P_{j-1} V_{j-1} (M=128, N=Dv padded to 64, K=128)
-//   warps 2..5  softmax + epilogue, one query row per thread (= one TMEM lane):
-//                 tcgen05.ld S row -> mask -> exp2 -> P (16-bit) into shared memory in the
-//                 UMMA K-major 128B-swizzled layout; O is rescaled in TMEM only when the row
-//                 max grows by more than 2^8 (exact: P and l always use the same reference).
-// TMEM: S0 = cols [0,128), S1 = [128,256), O = [256, 256+DvPad).
-// Tiles in shared memory are 128 rows x 64 elements (128 B) boxes with the 128B swizzle, the
-// canonical K-major layout for Q, K and P and the MN-major layout for V.
+// One CTA = two 128-query tiles (T0, T1) of one (batch, head); 320 threads:
+//   warp 0      TMA producer: both Q tiles once, then K/V tiles of 128 keys (STAGES ring).
+//   warp 1      TMEM owner + MMA issuer (one elected lane), per key tile j:
+//                 S_t = Q_t K_j^T   (M=128, N=128, K=D padded to 16; f32 in TMEM)
+//                 O_t += P_t V_j    (M=128, N=Dv padded to 64, K=128; P_t read from TMEM)
+//               issued as S_0(0) S_1(0) | PV_0(j) S_0(j+1) PV_1(j) S_1(j+1) | ... so the tensor
+//               core works on one tile while the other tile's softmax runs.
+//   warps 2..5  softmax + epilogue of T0, warps 6..9 of T1: one query row per thread (=
+//               TMEM lane): tcgen05.ld S, mask, exp2, write P (16-bit, 2 per column) back to
+//               TMEM with tcgen05.st; O is rescaled in TMEM only when the row max grows by
+//               more than 2^8 (P and the row sum always share one reference maximum).
+// TMEM per tile t (base 256*t): Dv <= 64: S [0,128) P [128,192) O [192,256);
+//                              Dv  > 64: S and P share [0,128) (P in [0,64)), O [128,256).
+// A commit makes its mbarrier wait for every earlier tcgen05 op of the issuing thread, so
+// when S_t(j) is ready, PV_t(j-1) has completed: P_t may be rewritten and O_t rescaled
+// without further waits.  When P aliases S, S_t(j+1) is issued after PV_t(j) by the same
+// thread and the tensor core executes a thread's MMAs in issue order.
+// Q, K, V tiles in shared memory are 128 rows x 64 elements (128 B) boxes with the 128B
+// swizzle: the canonical K-major layout for Q and K, MN-major for V.
 #include "common.cuh"
 #include "tc.cuh"
 
 namespace sp {
 namespace {
 
-constexpr int kBM = 128;            // queries per CTA
+constexpr int kBM = 128;            // queries per tile (two tiles per CTA)
 constexpr int kBN = 128;            // keys per KV tile
 constexpr int kBox = 16384;         // bytes of one 128 x 64 16-bit box
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS0 = 0, kTmemS1 = 128, kTmemO = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when max grows > 2^8
 
@@ -51,14 +57,13 @@ struct FaParams {
 
 template <int NBQ, int NBV, int STAGES>
 struct FaSmem {
-  static constexpr int kQ = 0;
-  static constexpr int kK = kQ + NBQ * kBox;
+  static constexpr int kQ = 0;                                // two tiles x NBQ boxes
+  static constexpr int kK = kQ + 2 * NBQ * kBox;
   static constexpr int kV = kK + STAGES * NBQ * kBox;
-  static constexpr int kP = kV + STAGES * NBV * kBox;  // two P buffers of 128 x 128 (2 boxes)
-  static constexpr int kBar = kP + 4 * kBox;
-  // barriers: q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_free[2],
-  // p_full[2], o_done[2], drain
-  static constexpr int kNumBars = 1 + 4 * STAGES + 2 + 2 + 2 + 2 + 1;
+  static constexpr int kBar = kV + STAGES * NBV * kBox;
+  // barriers: q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2],
+  // o_done[2], drain
+  static constexpr int kNumBars = 1 + 4 * STAGES + 2 + 2 + 2 + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;  // tmem base + abort flag
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-B alignment of the base
@@ -66,11 +71,20 @@ struct FaSmem {
 
 __device__ __forceinline__ uint32_t float_bits(float f) { return __float_as_uint(f); }
 
+// TMEM column offsets inside one tile's 256 columns
+template <int NBV>
+struct FaTmem {
+  static constexpr uint32_t kS = 0;
+  static constexpr uint32_t kP = NBV == 1 ? 128 : 0;   // Dv > 64: P overwrites S
+  static constexpr uint32_t kO = NBV == 1 ? 192 : 128;
+};
+
 template <int NBQ, int NBV, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __maxnreg__(200)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const FaParams p) {
   using L = FaSmem<NBQ, NBV, STAGES>;
+  using TM = FaTmem<NBV>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -81,8 +95,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_full = k_empty + STAGES;
   uint64_t* v_empty = v_full + STAGES;
   uint64_t* s_full = v_empty + STAGES;
-  uint64_t* s_free = s_full + 2;
-  uint64_t* p_full = s_free + 2;
+  uint64_t* p_full = s_full + 2;
   uint64_t* o_done = p_full + 2;
   uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
@@ -91,12 +104,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int q0 = qt * kBM;
+  const int q0 = qt * 2 * kBM;
 
-  // KV tiles this query tile needs (causal: keys <= last query of the tile).
+  // KV tiles this pair of query tiles needs (causal: keys <= last query of tile 1).
   int n_tiles = p.n_kv_tiles;
   if (p.causal) {
-    const int last_q = min((int)p.Sq - 1, q0 + kBM - 1);
+    const int last_q = min((int)p.Sq - 1, q0 + 2 * kBM - 1);
     n_tiles = min(n_tiles, last_q / kBN + 1);
   }
 
@@ -108,11 +121,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 128);
-      mbar_init(&p_full[s], 128);
-      mbar_init(&o_done[s], 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&o_done[t], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -133,9 +145,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmq);
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
-      mbar_arrive_expect_tx(q_full, NBQ * kBox);
-      for (int blk = 0; blk < NBQ; ++blk)
-        tma_load_4d(smem + L::kQ + blk * kBox, &tmq, q_full, blk * 64, q0, h, b);
+      mbar_arrive_expect_tx(q_full, 2 * NBQ * kBox);
+      for (int t = 0; t < 2; ++t)
+        for (int blk = 0; blk < NBQ; ++blk)
+          tma_load_4d(smem + L::kQ + (t * NBQ + blk) * kBox, &tmq, q_full, blk * 64, q0 + t * kBM,
+                      h, b);
       int issued_k = 0, issued_v = 0;
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % STAGES;
@@ -169,71 +183,79 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc_qk = make_idesc_f16(kBM, kBN, ab, 0, 0);
       const uint32_t idesc_pv = make_idesc_f16(kBM, (uint32_t)p.dv_pad, ab, 0, 1);
       const uint32_t q_base = smem_u32(smem + L::kQ);
-      const uint32_t p_base = smem_u32(smem + L::kP);
       const int qk_steps = p.dqk_pad / 16;
-      bool ok = mbar_wait(q_full, 0, abort_flag, WD_MMA_WAIT);
-      tc_fence_after();
 
-      // O += P_i V_i, P_i in shared buffer i % 2
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i % STAGES;
-        if (!mbar_wait(&v_full[st], (i / STAGES) & 1, abort_flag, WD_MMA_WAIT)) return false;
-        if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1, abort_flag, WD_MMA_WAIT)) return false;
-        tc_fence_after();
-        const uint32_t v_base = smem_u32(smem + L::kV + st * NBV * kBox);
-        const uint32_t pb = p_base + (i & 1) * 2 * kBox;
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          // A = P (K-major, 2 boxes of 64 keys), B = V (MN-major: keys x Dv, Dv contiguous)
-          const uint64_t a = make_smem_desc(pb + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024,
-                                            LAYOUT_SW128);
-          const uint64_t bd = make_smem_desc(v_base + kk * 16 * 128, kBox, 1024, LAYOUT_SW128);
-          umma_ss(tmem + kTmemO, a, bd, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&v_empty[st]);
-        umma_commit(&o_done[i & 1]);
-        return true;
-      };
-
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int st = j % STAGES;
-        const int sb = j & 1;
-        if (!mbar_wait(&k_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
-        if (j >= 2 && !mbar_wait(&s_free[sb], ((j >> 1) - 1) & 1, abort_flag, WD_MMA_WAIT)) break;
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(smem + L::kK + st * NBQ * kBox);
-        const uint32_t s_col = sb ? kTmemS1 : kTmemS0;
+      // S_t = Q_t K_j^T
+      auto issue_qk = [&](int t, int j) {
+        const uint32_t k_base = smem_u32(smem + L::kK + (j % STAGES) * NBQ * kBox);
+        const uint32_t qb = q_base + t * NBQ * kBox;
         for (int kk = 0; kk < qk_steps; ++kk) {
           const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-          const uint64_t a = make_smem_desc(q_base + off, 16, 1024, LAYOUT_SW128);
+          const uint64_t a = make_smem_desc(qb + off, 16, 1024, LAYOUT_SW128);
           const uint64_t bd = make_smem_desc(k_base + off, 16, 1024, LAYOUT_SW128);
-          umma_ss(tmem + s_col, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          umma_ss(tmem + t * 256 + TM::kS, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[sb]);
-        umma_commit(&k_empty[st]);
-        if (j >= 1 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
+        umma_commit(&s_full[t]);
+      };
+      // O_t += P_t V_j, P_t from TMEM (8 columns per 16 keys)
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t v_base = smem_u32(smem + L::kV + (j % STAGES) * NBV * kBox);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bd = make_smem_desc(v_base + kk * 16 * 128, kBox, 1024, LAYOUT_SW128);
+          umma_ts(tmem + t * 256 + TM::kO, tmem + t * 256 + TM::kP + kk * 8, bd, idesc_pv,
+                  (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&o_done[t]);
+      };
+
+      bool ok = mbar_wait(q_full, 0, abort_flag, WD_MMA_WAIT) &&
+                (n_tiles == 0 || mbar_wait(&k_full[0], 0, abort_flag, WD_MMA_WAIT));
+      tc_fence_after();
+      if (ok && n_tiles > 0) {
+        issue_qk(0, 0);
+        issue_qk(1, 0);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int st = j % STAGES;
+        const bool more = j + 1 < n_tiles;
+        const int st1 = (j + 1) % STAGES;
+        if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
+        if (!mbar_wait(&p_full[0], j & 1, abort_flag, WD_MMA_WAIT)) break;
+        tc_fence_after();
+        issue_pv(0, j);
+        if (more) {
+          if (!mbar_wait(&k_full[st1], ((j + 1) / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
+          tc_fence_after();
+          issue_qk(0, j + 1);
+        }
+        if (!mbar_wait(&p_full[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
+        tc_fence_after();
+        issue_pv(1, j);
+        umma_commit(&v_empty[st]);
+        if (more) {
+          issue_qk(1, j + 1);
+          umma_commit(&k_empty[st1]);
         }
       }
-      if (ok && !*abort_flag && n_tiles > 0) issue_pv(n_tiles - 1);
       // Drain: every MMA issued above has completed once this commit arrives.
       umma_commit(drain);
       mbar_wait(drain, 0, nullptr, WD_MMA_WAIT);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int t = (warp - 2) >> 2;  // query tile of this warpgroup
+    const int quarter = warp & 3;   // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
-    const int qi = q0 + row;
-    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int qi = q0 + t * kBM + row;
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + t * 256;
     const float sl2 = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;  // running max in log2 units, running row sum
     bool ok = true;
 
     for (int j = 0; j < n_tiles; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait_warp(&s_full[sb], (j >> 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
+      if (!mbar_wait_warp(&s_full[t], j & 1, abort_flag, WD_SOFTMAX_WAIT)) {
         ok = false;
         break;
       }
@@ -241,28 +263,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       // S row: four 32-column loads in flight, one wait
       float s[kBN];
       {
-        const uint32_t s_addr = lane_addr + (sb ? kTmemS1 : kTmemS0);
         uint32_t r0[32], r1[32], r2[32], r3[32];
-        tmem_ld32(s_addr + 0, r0);
-        tmem_ld32(s_addr + 32, r1);
-        tmem_ld32(s_addr + 64, r2);
-        tmem_ld32(s_addr + 96, r3);
+        tmem_ld32(lane_addr + TM::kS + 0, r0);
+        tmem_ld32(lane_addr + TM::kS + 32, r1);
+        tmem_ld32(lane_addr + TM::kS + 64, r2);
+        tmem_ld32(lane_addr + TM::kS + 96, r3);
         tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          s[t] = __uint_as_float(r0[t]);
-          s[32 + t] = __uint_as_float(r1[t]);
-          s[64 + t] = __uint_as_float(r2[t]);
-          s[96 + t] = __uint_as_float(r3[t]);
+        for (int c = 0; c < 32; ++c) {
+          s[c] = __uint_as_float(r0[c]);
+          s[32 + c] = __uint_as_float(r1[c]);
+          s[64 + c] = __uint_as_float(r2[c]);
+          s[96 + c] = __uint_as_float(r3[c]);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&s_free[sb]);  // S buffer may be overwritten by QK_{j+2}
 
       // Masks act on raw scores: x_log2 = (s + mask / scale) * scale * log2(e).
       const int kv0 = j * kBN;
       const bool need_mask = p.mask != nullptr || (kv0 + kBN > p.Skv) ||
-                             (p.causal && kv0 + kBN - 1 > q0);
+                             (p.causal && kv0 + kBN - 1 > q0 + t * kBM);
       if (need_mask) {
 #pragma unroll
         for (int c = 0; c < kBN; ++c) {
@@ -294,91 +313,76 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float m_ref = m_use == -INFINITY ? 0.f : m_use;  // fully masked so far: p = 0
 
-      // P buffer j % 2 was last read by PV_{j-2}
-      if (j >= 2 && !mbar_wait_warp(&o_done[sb], ((j - 2) >> 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
-        ok = false;
-        break;
-      }
-      // tcgen05.ld/st are warp-collective: the whole warp rescales if any of its rows must,
-      // rows that need no rescale use alpha = 1.  O must hold PV_{j-1} first.
+      // O_t holds PV_t(j-1) already (its commit preceded S_t(j)'s).  tcgen05.ld/st are
+      // warp-collective: the whole warp rescales if any of its rows must (alpha = 1 else).
       if (__any_sync(0xffffffffu, rescale)) {
-        if (j >= 1 &&
-            !mbar_wait_warp(&o_done[sb ^ 1], ((j - 1) >> 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
         const float alpha = rescale ? ex2_approx(m_run - m_ref) : 1.0f;
         l_run *= alpha;
         for (int c = 0; c < p.dv_pad; c += 16) {
           uint32_t r[16];
-          tmem_ld16(lane_addr + kTmemO + c, r);
+          tmem_ld16(lane_addr + TM::kO + c, r);
           tmem_wait_ld();
 #pragma unroll
-          for (int t = 0; t < 16; ++t) r[t] = float_bits(__uint_as_float(r[t]) * alpha);
-          tmem_st16(lane_addr + kTmemO + c, r);
+          for (int u = 0; u < 16; ++u) r[u] = float_bits(__uint_as_float(r[u]) * alpha);
+          tmem_st16(lane_addr + TM::kO + c, r);
         }
-        tmem_wait_st();
       }
       m_run = m_use;
 
-      // exp2, row sum, 16-bit P into shared memory (UMMA K-major SW128: box c8/8,
-      // 16-byte chunk (c8 % 8) ^ (row % 8))
-      uint8_t* p_smem = smem + L::kP + sb * 2 * kBox;
+      // exp2, row sum, 16-bit P back into TMEM (column c holds keys 2c, 2c+1)
       float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
-      for (int c8 = 0; c8 < kBN / 8; ++c8) {
-        uint32_t pk[4];
+      for (int c16 = 0; c16 < kBN / 32; ++c16) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float e0 = ex2_approx(fmaf(s[c8 * 8 + 2 * t], sl2, -m_ref));
-          const float e1 = ex2_approx(fmaf(s[c8 * 8 + 2 * t + 1], sl2, -m_ref));
+        for (int u = 0; u < 16; ++u) {
+          const float e0 = ex2_approx(fmaf(s[c16 * 32 + 2 * u], sl2, -m_ref));
+          const float e1 = ex2_approx(fmaf(s[c16 * 32 + 2 * u + 1], sl2, -m_ref));
           rs0 += e0;
           rs1 += e1;
-          pk[t] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+          pk[u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
         }
-        const uint32_t off = (c8 >> 3) * kBox + row * 128 + (((c8 & 7) ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(p_smem + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        tmem_st16(lane_addr + TM::kP + c16 * 16, pk);
       }
       l_run += rs0 + rs1;
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[sb]);
+      mbar_arrive(&p_full[t]);
     }
 
     // ---- epilogue: O / l -> global
     const int last = n_tiles - 1;
     if (ok && n_tiles > 0 &&
-        mbar_wait_warp(&o_done[last & 1], (last >> 1) & 1, abort_flag, WD_EPILOGUE_WAIT)) {
+        mbar_wait_warp(&o_done[t], last & 1, abort_flag, WD_EPILOGUE_WAIT)) {
       tc_fence_after();
       const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
       const bool row_ok = qi < p.Sq;
       const int64_t obase = (int64_t)b * p.os0 + (int64_t)h * p.os1 + (int64_t)qi * p.os2;
       for (int c = 0; c < p.dv_pad; c += 16) {
         uint32_t r[16];
-        tmem_ld16(lane_addr + kTmemO + c, r);
+        tmem_ld16(lane_addr + TM::kO + c, r);
         tmem_wait_ld();
         if (!row_ok || c >= p.Dv) continue;
         float o[16];
 #pragma unroll
-        for (int t = 0; t < 16; ++t) o[t] = __uint_as_float(r[t]) * inv_l;
+        for (int u = 0; u < 16; ++u) o[u] = __uint_as_float(r[u]) * inv_l;
         const int ncol = min(16, p.Dv - c);  // multiple of 8
         if (p.out_dtype == SP_F32) {
           float* dst = static_cast<float*>(p.out) + obase + c;
-          for (int t = 0; t < ncol; t += 4)
-            *reinterpret_cast<float4*>(dst + t) = make_float4(o[t], o[t + 1], o[t + 2], o[t + 3]);
+          for (int u = 0; u < ncol; u += 4)
+            *reinterpret_cast<float4*>(dst + u) = make_float4(o[u], o[u + 1], o[u + 2], o[u + 3]);
         } else {
           uint16_t* dst = static_cast<uint16_t*>(p.out) + obase + c;
-          for (int t = 0; t < ncol; t += 8) {
-            uint4 u;
+          for (int u = 0; u < ncol; u += 8) {
+            uint4 w;
             if (p.out_dtype == SP_BF16) {
-              u = make_uint4(pack_bf16x2(o[t], o[t + 1]), pack_bf16x2(o[t + 2], o[t + 3]),
-                             pack_bf16x2(o[t + 4], o[t + 5]), pack_bf16x2(o[t + 6], o[t + 7]));
+              w = make_uint4(pack_bf16x2(o[u], o[u + 1]), pack_bf16x2(o[u + 2], o[u + 3]),
+                             pack_bf16x2(o[u + 4], o[u + 5]), pack_bf16x2(o[u + 6], o[u + 7]));
             } else {
-              u = make_uint4(pack_f16x2(o[t], o[t + 1]), pack_f16x2(o[t + 2], o[t + 3]),
-                             pack_f16x2(o[t + 4], o[t + 5]), pack_f16x2(o[t + 6], o[t + 7]));
+              w = make_uint4(pack_f16x2(o[u], o[u + 1]), pack_f16x2(o[u + 2], o[u + 3]),
+                             pack_f16x2(o[u + 4], o[u + 5]), pack_f16x2(o[u + 6], o[u + 7]));
             }
-            *reinterpret_cast<uint4*>(dst + t) = u;
+            *reinterpret_cast<uint4*>(dst + u) = w;
           }
         }
       }
@@ -424,7 +428,7 @@ int launch_fa(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& m
       return set_error(SP_ERR_LAUNCH, "flash_attn: smem attribute failed: %s", cudaGetErrorString(e));
     }
   }
-  dim3 grid((unsigned)((p.Sq + kBM - 1) / kBM), (unsigned)p.H, (unsigned)B);
+  dim3 grid((unsigned)((p.Sq + 2 * kBM - 1) / (2 * kBM)), (unsigned)p.H, (unsigned)B);
   kern<<<grid, kThreads, L::kAlloc, s>>>(mq, mk, mv, p);
   return check_launch("flash_attn");
 }
@@ -495,8 +499,8 @@ extern "C" int sp_flash_attn_fwd(const void* q, const void* k, const void* v, co
   p.in_f16 = in_f16;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool qk2 = D > 64, v2 = Dv > 64;
-  if (!qk2 && !v2) return launch_fa<1, 1, 3>(mq, mk, mv, p, B, s);  // 176 KB smem
-  if (qk2 && v2) return launch_fa<2, 2, 2>(mq, mk, mv, p, B, s);     // 224 KB smem
-  if (qk2) return launch_fa<2, 1, 2>(mq, mk, mv, p, B, s);
-  return launch_fa<1, 2, 2>(mq, mk, mv, p, B, s);
+  if (!qk2 && !v2) return launch_fa<1, 1, 4>(mq, mk, mv, p, B, s);  // 160 KB smem
+  if (qk2 && v2) return launch_fa<2, 2, 2>(mq, mk, mv, p, B, s);     // 192 KB smem
+  if (qk2) return launch_fa<2, 1, 3>(mq, mk, mv, p, B, s);           // 208 KB smem
+  return launch_fa<1, 2, 3>(mq, mk, mv, p, B, s);                    // 176 KB smem
 }

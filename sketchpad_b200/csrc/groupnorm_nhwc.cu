@@ -65,11 +65,25 @@ struct NhwcParams {
   int act;
 };
 
+// Deterministic block reduction of per-thread channel accumulators: every thread stores
+// its values into red[ty][c], then each channel is summed over ty in a fixed order.
+template <int NV, int VE>
+__device__ __forceinline__ void stage_channels(float* red, const float (&acc)[NV][VE], int tx,
+                                               int ty, int TX, int CV, int C) {
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int cv = tx + k * TX;
+    if (cv < CV)
+#pragma unroll
+      for (int t = 0; t < VE; ++t) red[ty * C + cv * VE + t] = acc[k][t];
+  }
+}
+
 // Per-thread channel vectors: cv = tx + k*TX (k < NV).
 template <typename T, int NV>
 __global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_stats_kernel(NhwcParams p) {
   constexpr int VE = 16 / sizeof(T);
-  extern __shared__ float csum[];  // [C] per-channel accumulators, then [G] group values
+  extern __shared__ float red[];  // [TY][C] staging for the fixed-order reductions
   __shared__ float gval[1024];
   const int tx = threadIdx.x, ty = threadIdx.y;
   const int tid = ty * p.TX + tx;
@@ -79,8 +93,6 @@ __global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_stats_kernel(NhwcParams 
   const int r1 = min(p.P, r0 + p.rows_per_chunk);
   const T* xb = static_cast<const T*>(p.x) + (int64_t)b * p.P * p.C;
 
-  for (int i = tid; i < p.C; i += nthr) csum[i] = 0.f;
-  __syncthreads();
   float acc[NV][VE];
 #pragma unroll
   for (int k = 0; k < NV; ++k)
@@ -98,22 +110,16 @@ __global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_stats_kernel(NhwcParams 
       }
     }
   }
-#pragma unroll
-  for (int k = 0; k < NV; ++k) {
-    const int cv = tx + k * p.TX;
-    if (cv < p.CV)
-#pragma unroll
-      for (int t = 0; t < VE; ++t) atomicAdd(&csum[cv * VE + t], acc[k][t]);
-  }
+  stage_channels<NV, VE>(red, acc, tx, ty, p.TX, p.CV, p.C);
   __syncthreads();
-  const float cnt = (float)(r1 - r0) * (float)p.Cg;
+  const int rows = r1 - r0;
+  const float cnt = (float)rows * (float)p.Cg;
   for (int g = tid; g < p.G; g += nthr) {
     float s = 0.f;
-    for (int c = g * p.Cg; c < (g + 1) * p.Cg; ++c) s += csum[c];
+    for (int c = g * p.Cg; c < (g + 1) * p.Cg; ++c)
+      for (int y = 0; y < p.TY; ++y) s += red[y * p.C + c];
     gval[g] = s / cnt;  // chunk mean of group g
   }
-  __syncthreads();
-  for (int i = tid; i < p.C; i += nthr) csum[i] = 0.f;
   __syncthreads();
   // second pass: centred sum of squares around the chunk mean (rows are L1/L2 resident)
   float mine[NV][VE];
@@ -141,18 +147,14 @@ __global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_stats_kernel(NhwcParams 
       }
     }
   }
-#pragma unroll
-  for (int k = 0; k < NV; ++k) {
-    const int cv = tx + k * p.TX;
-    if (cv < p.CV)
-#pragma unroll
-      for (int t = 0; t < VE; ++t) atomicAdd(&csum[cv * VE + t], acc[k][t]);
-  }
+  __syncthreads();  // red is rewritten below
+  stage_channels<NV, VE>(red, acc, tx, ty, p.TX, p.CV, p.C);
   __syncthreads();
   float* part = p.part + ((int64_t)b * p.nchunks + chunk) * p.G * 3;
   for (int g = tid; g < p.G; g += nthr) {
     float m2 = 0.f;
-    for (int c = g * p.Cg; c < (g + 1) * p.Cg; ++c) m2 += csum[c];
+    for (int c = g * p.Cg; c < (g + 1) * p.Cg; ++c)
+      for (int y = 0; y < p.TY; ++y) m2 += red[y * p.C + c];
     part[g * 3 + 0] = cnt;
     part[g * 3 + 1] = gval[g];
     part[g * 3 + 2] = m2;
@@ -162,7 +164,11 @@ __global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_stats_kernel(NhwcParams 
 template <typename T, int NV>
 __global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_apply_kernel(NhwcParams p) {
   constexpr int VE = 16 / sizeof(T);
+  extern __shared__ float pst[];  // this image's chunk partials [nchunks][G][3]
+  __shared__ float st[2048];      // (mean, rstd) per group
   const int tx = threadIdx.x, ty = threadIdx.y;
+  const int tid = ty * p.TX + tx;
+  const int nthr = p.TX * p.TY;
   const int b = blockIdx.y, chunk = blockIdx.x;
   const int r0 = chunk * p.rows_per_chunk;
   const int r1 = min(p.P, r0 + p.rows_per_chunk);
@@ -170,43 +176,29 @@ __global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_apply_kernel(NhwcParams 
   T* yb = static_cast<T*>(p.y) + (int64_t)b * p.P * p.C;
   const T* gam = static_cast<const T*>(p.gamma);
   const T* bet = static_cast<const T*>(p.beta);
-  __shared__ float st[2048];  // (mean, rstd) per group
   {
-    // merge the chunk partials of this image: whole warps only; a warp takes groups
-    // g = warp, warp + nwarps, ...; its lanes split the chunks, then a butterfly merges them
-    const int tid = ty * p.TX + tx;
-    const int nwarps = (p.TX * p.TY) / 32;
-    const int warp = tid >> 5, lane = tid & 31;
-    const float* pb = p.part + (int64_t)b * p.nchunks * p.G * 3;
-    if (warp < nwarps) {
-      for (int g = warp; g < p.G; g += nwarps) {
-        float n = 0.f, mean = 0.f, m2 = 0.f;
-        for (int i = lane; i < p.nchunks; i += 32) {
-          const float* q = pb + ((int64_t)i * p.G + g) * 3;
-          const float nb = q[0], mb = q[1], m2b = q[2];
-          const float nn = n + nb, d = mb - mean;
-          mean += d * (nb / nn);
-          m2 += m2b + d * d * (n * nb / nn);
-          n = nn;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float nb = __shfl_xor_sync(0xffffffffu, n, o);
-          const float mb = __shfl_xor_sync(0xffffffffu, mean, o);
-          const float m2b = __shfl_xor_sync(0xffffffffu, m2, o);
-          const float nn = n + nb;
-          if (nn > 0.f) {
-            const float d = mb - mean;
-            mean += d * (nb / nn);
-            m2 += m2b + d * d * (n * nb / nn);
-          }
-          n = nn;
-        }
-        if (lane == 0) {
-          st[2 * g] = mean;
-          st[2 * g + 1] = rsqrtf(m2 / n + p.eps);
-        }
+    // coalesced copy of the partials, then per group (fixed order, no divisions in the loop):
+    // mean = sum(n_i mean_i) / N;  M2 = sum(M2_i + n_i (mean_i - mean)^2)   (Chan et al.)
+    const int nfl = p.nchunks * p.G * 3;
+    const float* pb = p.part + (int64_t)b * nfl;
+    for (int i = tid; i < nfl; i += nthr) pst[i] = pb[i];
+    __syncthreads();
+    for (int g = tid; g < p.G; g += nthr) {
+      float n = 0.f, s = 0.f;
+      for (int i = 0; i < p.nchunks; ++i) {
+        const float* q = pst + (i * p.G + g) * 3;
+        n += q[0];
+        s += q[0] * q[1];
       }
+      const float mean = s / n;
+      float m2 = 0.f;
+      for (int i = 0; i < p.nchunks; ++i) {
+        const float* q = pst + (i * p.G + g) * 3;
+        const float d = q[1] - mean;
+        m2 += q[2] + q[0] * d * d;
+      }
+      st[2 * g] = mean;
+      st[2 * g + 1] = rsqrtf(m2 / n + p.eps);
     }
     __syncthreads();
   }
@@ -246,7 +238,7 @@ struct NhwcPlan {
   int CV, NV, TX, TY, rows_per_chunk, nchunks;
 };
 
-NhwcPlan plan_nhwc(int64_t B, int64_t P, int64_t C, int es) {
+NhwcPlan plan_nhwc(int64_t B, int64_t P, int64_t C, int es, int64_t groups) {
   NhwcPlan pl{};
   const int VE = 16 / es;
   pl.CV = (int)(C / VE);
@@ -254,7 +246,9 @@ NhwcPlan plan_nhwc(int64_t B, int64_t P, int64_t C, int es) {
   pl.TX = (pl.CV + pl.NV - 1) / pl.NV;
   pl.TY = std::max(1, kNhwcThreads / pl.TX);
   const int64_t target_ctas = 2LL * num_sms();
-  const int64_t per_image = std::max<int64_t>(1, (target_ctas + B - 1) / B);
+  int64_t per_image = std::max<int64_t>(1, (target_ctas + B - 1) / B);
+  // the apply kernel stages [chunks][groups][3] floats in shared memory: keep it <= 40 KB
+  per_image = std::min<int64_t>(per_image, std::max<int64_t>(1, 40960 / (groups * 12)));
   int64_t rows = (P + per_image - 1) / per_image;
   rows = ((rows + pl.TY - 1) / pl.TY) * pl.TY;
   rows = std::max<int64_t>(rows, pl.TY);
@@ -279,22 +273,23 @@ bool gn_nhwc_applicable(int64_t B, int64_t C, int64_t H, int64_t W, const int64_
 }
 
 size_t gn_nhwc_workspace_bytes(int64_t B, int64_t C, int64_t H, int64_t W, int es, int64_t groups) {
-  const NhwcPlan pl = plan_nhwc(B, H * W, C, es);
+  const NhwcPlan pl = plan_nhwc(B, H * W, C, es, groups);
   return (size_t)B * pl.nchunks * groups * 3 * sizeof(float);
 }
 
 template <typename T>
 static int launch_nhwc_t(const NhwcParams& p, int NV, int64_t B, cudaStream_t s) {
   dim3 block(p.TX, p.TY), grid(p.nchunks, (unsigned)B);
-  const size_t smem = (size_t)p.C * sizeof(float);
+  const size_t smem_stats = (size_t)p.TY * p.C * sizeof(float);
+  const size_t smem_apply = (size_t)p.nchunks * p.G * 3 * sizeof(float);
   if (NV == 1) {
-    gn_nhwc_stats_kernel<T, 1><<<grid, block, smem, s>>>(p);
+    gn_nhwc_stats_kernel<T, 1><<<grid, block, smem_stats, s>>>(p);
     if (int rc = check_launch("groupnorm nhwc stats")) return rc;
-    gn_nhwc_apply_kernel<T, 1><<<grid, block, 0, s>>>(p);
+    gn_nhwc_apply_kernel<T, 1><<<grid, block, smem_apply, s>>>(p);
   } else {
-    gn_nhwc_stats_kernel<T, 2><<<grid, block, smem, s>>>(p);
+    gn_nhwc_stats_kernel<T, 2><<<grid, block, smem_stats, s>>>(p);
     if (int rc = check_launch("groupnorm nhwc stats")) return rc;
-    gn_nhwc_apply_kernel<T, 2><<<grid, block, 0, s>>>(p);
+    gn_nhwc_apply_kernel<T, 2><<<grid, block, smem_apply, s>>>(p);
   }
   return check_launch("groupnorm nhwc apply");
 }
@@ -309,7 +304,7 @@ int gn_nhwc_launch(const void* x, const void* gamma, const void* beta, void* y, 
                      need, workspace_bytes);
   if (!aligned(workspace, 16) || !aligned(x, 16) || !aligned(y, 16))
     return set_error(SP_ERR_ALIGN, "groupnorm (channels-last): x, y and workspace must be 16-byte aligned");
-  const NhwcPlan pl = plan_nhwc(B, H * W, C, es);
+  const NhwcPlan pl = plan_nhwc(B, H * W, C, es, groups);
   NhwcParams p{};
   p.x = x;
   p.gamma = gamma;
