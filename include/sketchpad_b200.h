@@ -76,8 +76,8 @@ int sp_flash_attn_fwd(const void* q, const void* k, const void* v, const float* 
  * with the semantics of the CPU path crates/sketchpad-core/src/groupnorm.rs:62-102
  * (clamp +-65000, f32 statistics, biased variance, clamp after the affine).
  *   x [B,C,H,W] with element strides x_strides (NULL = contiguous NCHW).  y [B,C,H,W] is
- *   written channels-last (strides C*H*W, 1, W*C, C) when x is channels-last -- the layout
- *   sm_100 implicit-GEMM convolutions use -- and contiguous NCHW otherwise.
+ *   written channels-last (strides C*H*W, 1, W*C, C) when x is dense channels-last -- the
+ *   layout sm_100 implicit-GEMM convolutions use -- and contiguous NCHW otherwise.
  *   gamma, beta [C]; x, y, gamma, beta all of `dtype` (SP_F32, SP_F16, SP_BF16).
  *   act: SP_ACT_SILU (groupnorm_silu) or SP_ACT_NONE (groupnorm).
  *   Returns SP_ERR_SHAPE when C % groups != 0 (the reference panics there).

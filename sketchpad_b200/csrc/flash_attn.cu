@@ -80,7 +80,7 @@ struct FaTmem {
 };
 
 template <int NBQ, int NBV, int STAGES>
-__global__ void __maxnreg__(200)
+__global__ void __maxnreg__(192)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const FaParams p) {
   using L = FaSmem<NBQ, NBV, STAGES>;
@@ -423,9 +423,15 @@ int launch_fa(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& m
   static unsigned long long attr_set = 0;
   if (first_time_on_device(&attr_set)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-    if (e != cudaSuccess) {
+    cudaFuncAttributes fa{};
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess || fa.maxThreadsPerBlock < kThreads) {
       __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
-      return set_error(SP_ERR_LAUNCH, "flash_attn: smem attribute failed: %s", cudaGetErrorString(e));
+      return set_error(SP_ERR_LAUNCH,
+                       "flash_attn: kernel cannot launch %d threads (%s; regs/thread %d, max threads "
+                       "%d, dynamic smem %d of %d)",
+                       kThreads, cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, L::kAlloc,
+                       fa.maxDynamicSharedSizeBytes);
     }
   }
   dim3 grid((unsigned)((p.Sq + 2 * kBM - 1) / (2 * kBM)), (unsigned)p.H, (unsigned)B);

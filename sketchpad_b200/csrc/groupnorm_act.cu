@@ -232,6 +232,7 @@ struct GnGeneralParams {
   void* y;
   int64_t B, C, H, W, G, cg, n;
   int64_t sb, sc, sh, sw;  // element strides of x
+  int64_t yb, yc, yh, yw;  // element strides of y (NCHW-contiguous, or x's NHWC layout)
   int64_t chunk;           // elements per chunk
   int64_t nchunks;         // chunks per group
   float* part;             // [B*G, nchunks, 3] : count, mean, M2
@@ -298,11 +299,15 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GnGeneralParams p)
   const T* x = static_cast<const T*>(p.x);
   const T* gam = static_cast<const T*>(p.gamma);
   const T* bet = static_cast<const T*>(p.beta);
-  T* y = static_cast<T*>(p.y) + bg * p.n;  // output is contiguous
+  T* y = static_cast<T*>(p.y);
   for (int64_t e = e0 + threadIdx.x; e < e1; e += kGnThreads) {
-    const int64_t c = g * p.cg + e / (p.H * p.W);
+    const int64_t cl = e / (p.H * p.W);
+    const int64_t hw = e - cl * p.H * p.W;
+    const int64_t hh = hw / p.W, ww = hw - hh * p.W;
+    const int64_t c = g * p.cg + cl;
     const float v = (clamp65k(to_f32(x[gn_offset(p, b, g, e)])) - mean) * rstd;
-    y[e] = from_f32<T>(apply_act(v * to_f32(gam[c]) + to_f32(bet[c]), p.act));
+    y[b * p.yb + c * p.yc + hh * p.yh + ww * p.yw] =
+        from_f32<T>(apply_act(v * to_f32(gam[c]) + to_f32(bet[c]), p.act));
   }
 }
 
@@ -423,6 +428,23 @@ size_t general_workspace_bytes(int64_t B, int64_t C, int64_t H, int64_t W, int64
   const int64_t nchunks = (n + kGeneralChunk - 1) / kGeneralChunk;
   return (size_t)(B * groups * nchunks * 3 * sizeof(float));
 }
+// y follows x when x is dense channels-last (NHWC), else it is contiguous NCHW.
+void output_strides(int64_t B, int64_t C, int64_t H, int64_t W, const int64_t* xs, int64_t* ys) {
+  bool nhwc = xs != nullptr;
+  if (nhwc) {
+    const int64_t want[4] = {H * W * C, 1, W * C, C};
+    const int64_t dims[4] = {B, C, H, W};
+    for (int i = 0; i < 4; ++i)
+      if (dims[i] > 1 && xs[i] != want[i]) nhwc = false;
+    if (C == 1) nhwc = false;
+  }
+  if (nhwc) {
+    ys[0] = H * W * C; ys[1] = 1; ys[2] = W * C; ys[3] = C;
+  } else {
+    ys[0] = C * H * W; ys[1] = H * W; ys[2] = W; ys[3] = 1;
+  }
+}
+
 bool is_contiguous_nchw(int64_t B, int64_t C, int64_t H, int64_t W, const int64_t* st) {
   if (!st) return true;
   const int64_t want[4] = {C * H * W, H * W, W, 1};
@@ -497,9 +519,11 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
                      "of workspace (got %zu)",
                      need, workspace_bytes);
   if (!aligned(workspace, 4)) return set_error(SP_ERR_ALIGN, "groupnorm: workspace misaligned");
-  GnGeneralParams p{x,  gamma, beta,  y,     B,     C,     H, W, groups, cg, n,
-                    st[0], st[1], st[2], st[3], kGeneralChunk, pl.nchunks,
-                    static_cast<float*>(workspace), eps, act};
+  int64_t ys[4];
+  output_strides(B, C, H, W, x_strides, ys);
+  GnGeneralParams p{x,     gamma, beta,  y,     B,     C,     H,     W,     groups, cg, n,
+                    st[0], st[1], st[2], st[3], ys[0], ys[1], ys[2], ys[3], kGeneralChunk,
+                    pl.nchunks, static_cast<float*>(workspace), eps, act};
   switch (dtype) {
     case SP_F32: return launch_general<float>(p, B * groups, s);
     case SP_F16: return launch_general<__half>(p, B * groups, s);
@@ -596,8 +620,11 @@ extern "C" int sp_groupnorm_act_noalloc(const void* x, const void* gamma, const 
   if (!is_contiguous_nchw(B, C, H, W, x_strides))
     for (int i = 0; i < 4; ++i) st[i] = x_strides[i];
   const int64_t nchunks = (n + kGeneralChunk - 1) / kGeneralChunk;
-  GnGeneralParams p{x,     gamma, beta,  y,     B,     C,     H, W, groups, cg, n,
-                    st[0], st[1], st[2], st[3], kGeneralChunk, nchunks, scratch, eps, act};
+  int64_t ys[4];
+  output_strides(B, C, H, W, x_strides, ys);
+  GnGeneralParams p{x,     gamma, beta,  y,     B,     C,     H,     W,     groups, cg, n,
+                    st[0], st[1], st[2], st[3], ys[0], ys[1], ys[2], ys[3], kGeneralChunk,
+                    nchunks, scratch, eps, act};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case SP_F32: return launch_general<float>(p, B * groups, s);

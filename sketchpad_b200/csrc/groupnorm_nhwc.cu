@@ -243,6 +243,7 @@ NhwcPlan plan_nhwc(int64_t B, int64_t P, int64_t C, int es, int64_t groups) {
   const int VE = 16 / es;
   pl.CV = (int)(C / VE);
   pl.NV = (pl.CV + kNhwcThreads - 1) / kNhwcThreads;
+  if (pl.NV == 3) pl.NV = 4;
   pl.TX = (pl.CV + pl.NV - 1) / pl.NV;
   pl.TY = std::max(1, kNhwcThreads / pl.TX);
   const int64_t target_ctas = 2LL * num_sms();
@@ -269,7 +270,7 @@ bool gn_nhwc_applicable(int64_t B, int64_t C, int64_t H, int64_t W, const int64_
   if (C == 1 && H * W > 1) return false;  // ambiguous with NCHW; leave it to the NCHW path
   const int VE = 16 / es;
   // blocks always hold >= 32 threads (TX <= 256 and TY = 256 / TX), which the merge needs
-  return C % VE == 0 && C / VE <= 2 * kNhwcThreads && groups <= 1024 && H * W < (1LL << 31);
+  return C % VE == 0 && C / VE <= 4 * kNhwcThreads && groups <= 1024 && H * W < (1LL << 31);
 }
 
 size_t gn_nhwc_workspace_bytes(int64_t B, int64_t C, int64_t H, int64_t W, int es, int64_t groups) {
@@ -286,10 +287,14 @@ static int launch_nhwc_t(const NhwcParams& p, int NV, int64_t B, cudaStream_t s)
     gn_nhwc_stats_kernel<T, 1><<<grid, block, smem_stats, s>>>(p);
     if (int rc = check_launch("groupnorm nhwc stats")) return rc;
     gn_nhwc_apply_kernel<T, 1><<<grid, block, smem_apply, s>>>(p);
-  } else {
+  } else if (NV == 2) {
     gn_nhwc_stats_kernel<T, 2><<<grid, block, smem_stats, s>>>(p);
     if (int rc = check_launch("groupnorm nhwc stats")) return rc;
     gn_nhwc_apply_kernel<T, 2><<<grid, block, smem_apply, s>>>(p);
+  } else {
+    gn_nhwc_stats_kernel<T, 4><<<grid, block, smem_stats, s>>>(p);
+    if (int rc = check_launch("groupnorm nhwc stats")) return rc;
+    gn_nhwc_apply_kernel<T, 4><<<grid, block, smem_apply, s>>>(p);
   }
   return check_launch("groupnorm nhwc apply");
 }
