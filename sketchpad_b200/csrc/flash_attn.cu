@@ -5,15 +5,16 @@
 // operation of sketchpad_cubecl::flash_attention (crates/sketchpad-cubecl/src/attention.rs:97-178)
 // and of the CPU attention it must match (crates/sketchpad-unet/src/blocks.rs:370-410).
 //
-// One CTA = two 128-query tiles (T0, T1) of one (batch, head); 320 threads:
-//   warp 0      TMA producer: both Q tiles once, then K/V tiles of 128 keys (STAGES ring).
-//   warp 1      TMEM owner + MMA issuer (one elected lane), per key tile j:
+// One CTA = two 128-query tiles (T0, T1) of one (batch, head); 384 threads = 3 warpgroups:
+//   warps 0..3  softmax + epilogue of T0, warps 4..7 of T1
+//   warp 8      TMA producer: both Q tiles once, then K/V tiles of 128 keys (STAGES ring).
+//   warp 9      TMEM owner + MMA issuer (one elected lane), per key tile j:
 //                 S_t = Q_t K_j^T   (M=128, N=128, K=D padded to 16; f32 in TMEM)
 //                 O_t += P_t V_j    (M=128, N=Dv padded to 64, K=128; P_t read from TMEM)
 //               issued as S_0(0) S_1(0) | PV_0(j) S_0(j+1) PV_1(j) S_1(j+1) | ... so the tensor
 //               core works on one tile while the other tile's softmax runs.
-//   warps 2..5  softmax + epilogue of T0, warps 6..9 of T1: one query row per thread (=
-//               TMEM lane): tcgen05.ld S, mask, exp2, write P (16-bit, 2 per column) back to
+//   softmax:    one query row per thread (= TMEM lane): tcgen05.ld S, mask, exp2, write P
+//               (16-bit, 2 per column) back to
 //               TMEM with tcgen05.st; O is rescaled in TMEM only when the row max grows by
 //               more than 2^8 (P and the row sum always share one reference maximum).
 // TMEM per tile t (base 256*t): Dv <= 64: S [0,128) P [128,192) O [192,256);
@@ -33,7 +34,9 @@ namespace {
 constexpr int kBM = 128;            // queries per tile (two tiles per CTA)
 constexpr int kBN = 128;            // keys per KV tile
 constexpr int kBox = 16384;         // bytes of one 128 x 64 16-bit box
-constexpr int kThreads = 320;
+// Three whole warpgroups: registers are reserved per warpgroup, so 320 threads would cost
+// as much as 384; warps 10 and 11 have no role.  168 registers per thread.
+constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when max grows > 2^8
@@ -80,7 +83,7 @@ struct FaTmem {
 };
 
 template <int NBQ, int NBV, int STAGES>
-__global__ void __maxnreg__(192)
+__global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const FaParams p) {
   using L = FaSmem<NBQ, NBV, STAGES>;
@@ -130,7 +133,7 @@ __global__ void __maxnreg__(192)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -139,7 +142,7 @@ __global__ void __maxnreg__(192)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == 8) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmq);
@@ -176,7 +179,7 @@ __global__ void __maxnreg__(192)
           mbar_wait(&v_full[j % STAGES], (j / STAGES) & 1, nullptr, WD_TMA_WAIT);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t ab = p.in_f16 ? 0u : 1u;
@@ -243,10 +246,10 @@ __global__ void __maxnreg__(192)
       umma_commit(drain);
       mbar_wait(drain, 0, nullptr, WD_MMA_WAIT);
     }
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------------ softmax + epilogue
-    const int t = (warp - 2) >> 2;  // query tile of this warpgroup
-    const int quarter = warp & 3;   // TMEM lane quarter this warp may access
+    const int t = warp >> 2;       // query tile of this warpgroup
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
     const int qi = q0 + t * kBM + row;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + t * 256;
@@ -391,7 +394,7 @@ __global__ void __maxnreg__(192)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
