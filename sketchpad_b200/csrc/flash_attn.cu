@@ -74,6 +74,22 @@ struct FaSmem {
 
 __device__ __forceinline__ uint32_t float_bits(float f) { return __float_as_uint(f); }
 
+// 2^x on the FMA pipe (for x <= 8; x < -125 flushes to ~2^-125): x = n + f with n = rint(x)
+// from the 1.5*2^23 rounding trick, 2^f on [-1/2, 1/2] by a degree-3 polynomial fitted for
+// this kernel (relative error <= 7.5e-5, far below the 16-bit rounding of P), and n added
+// to the exponent field.  Used for part of each row so the MUFU unit is not the only
+// source of exponentials.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.0f);
+  const float j = __fadd_rn(x, 12582912.0f);
+  const float f = __fsub_rn(x, __fsub_rn(j, 12582912.0f));
+  const float p = fmaf(fmaf(fmaf(0.055171624f, f, 0.24261113f), f, 0.69326098f), f, 0.99992806f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+}
+
+// Pairs of columns (out of every 16) whose exponentials use exp2_fma on unmasked tiles.
+constexpr uint32_t kPolyPairs = 0x4924;  // pairs 2, 5, 8, 11, 14: 31 % of the row
+
 // TMEM column offsets inside one tile's 256 columns
 template <int NBV>
 struct FaTmem {
@@ -263,47 +279,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      // S row: four 32-column loads in flight, one wait
-      float s[kBN];
-      {
-        uint32_t r0[32], r1[32], r2[32], r3[32];
-        tmem_ld32(lane_addr + TM::kS + 0, r0);
-        tmem_ld32(lane_addr + TM::kS + 32, r1);
-        tmem_ld32(lane_addr + TM::kS + 64, r2);
-        tmem_ld32(lane_addr + TM::kS + 96, r3);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          s[c] = __uint_as_float(r0[c]);
-          s[32 + c] = __uint_as_float(r1[c]);
-          s[64 + c] = __uint_as_float(r2[c]);
-          s[96 + c] = __uint_as_float(r3[c]);
-        }
-      }
-
       // Masks act on raw scores: x_log2 = (s + mask / scale) * scale * log2(e).
       const int kv0 = j * kBN;
       const bool need_mask = p.mask != nullptr || (kv0 + kBN > p.Skv) ||
                              (p.causal && kv0 + kBN - 1 > q0 + t * kBM);
-      if (need_mask) {
+      auto masked = [&](int c, float raw) -> float {
+        const int kv = kv0 + c;
+        const bool valid = kv < p.Skv && !(p.causal && kv > qi);
+        float x = raw;
+        if (p.mask && valid && qi < p.Sq) x += p.mask[(int64_t)qi * p.mask_stride + kv] * p.inv_scale;
+        return valid ? x : -INFINITY;
+      };
+      // pass A: row max over the 128 scores, two halves of two loads each
+      float mx;
+      {
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          const int kv = kv0 + c;
-          const bool valid = kv < p.Skv && !(p.causal && kv > qi);
-          float x = s[c];
-          if (p.mask && valid && qi < p.Sq) x += p.mask[(int64_t)qi * p.mask_stride + kv] * p.inv_scale;
-          s[c] = valid ? x : -INFINITY;
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t r[2][32];
+          tmem_ld32(lane_addr + TM::kS + hh * 64, r[0]);
+          tmem_ld32(lane_addr + TM::kS + hh * 64 + 32, r[1]);
+          tmem_wait_ld();
+          if (need_mask) {
+#pragma unroll
+            for (int q = 0; q < 2; ++q)
+#pragma unroll
+              for (int c = 0; c < 32; ++c)
+                m4[c & 3] = fmaxf(m4[c & 3], masked(hh * 64 + q * 32 + c, __uint_as_float(r[q][c])));
+          } else {
+#pragma unroll
+            for (int q = 0; q < 2; ++q)
+#pragma unroll
+              for (int c = 0; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(r[q][c]));
+          }
         }
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
-#pragma unroll
-      for (int c = 4; c < kBN; c += 4) {
-        mx0 = fmaxf(mx0, s[c]);
-        mx1 = fmaxf(mx1, s[c + 1]);
-        mx2 = fmaxf(mx2, s[c + 2]);
-        mx3 = fmaxf(mx3, s[c + 3]);
-      }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
       const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl2;
       const float m_new = fmaxf(m_run, m_tile);
       bool rescale = false;
@@ -332,20 +343,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       m_run = m_use;
 
-      // exp2, row sum, 16-bit P back into TMEM (column c holds keys 2c, 2c+1)
+      // pass B: exp2, row sum, 16-bit P back into TMEM (column c holds keys 2c, 2c+1); S is
+      // re-read in two 64-column halves so only half a row is live in registers
       float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
-      for (int c16 = 0; c16 < kBN / 32; ++c16) {
-        uint32_t pk[16];
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t r[2][32];
+        tmem_ld32(lane_addr + TM::kS + hh * 64, r[0]);
+        tmem_ld32(lane_addr + TM::kS + hh * 64 + 32, r[1]);
+        tmem_wait_ld();
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          const float e0 = ex2_approx(fmaf(s[c16 * 32 + 2 * u], sl2, -m_ref));
-          const float e1 = ex2_approx(fmaf(s[c16 * 32 + 2 * u + 1], sl2, -m_ref));
-          rs0 += e0;
-          rs1 += e1;
-          pk[u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+        for (int q = 0; q < 2; ++q) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int c = hh * 64 + q * 32 + 2 * u;
+            float x0 = __uint_as_float(r[q][2 * u]), x1 = __uint_as_float(r[q][2 * u + 1]);
+            float e0, e1;
+            if (need_mask) {
+              x0 = masked(c, x0);
+              x1 = masked(c + 1, x1);
+              e0 = ex2_approx(fmaf(x0, sl2, -m_ref));
+              e1 = ex2_approx(fmaf(x1, sl2, -m_ref));
+            } else if ((kPolyPairs >> u) & 1u) {
+              e0 = exp2_fma(fmaf(x0, sl2, -m_ref));
+              e1 = exp2_fma(fmaf(x1, sl2, -m_ref));
+            } else {
+              e0 = ex2_approx(fmaf(x0, sl2, -m_ref));
+              e1 = ex2_approx(fmaf(x1, sl2, -m_ref));
+            }
+            rs0 += e0;
+            rs1 += e1;
+            pk[u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+          }
+          tmem_st16(lane_addr + TM::kP + hh * 32 + q * 16, pk);
         }
-        tmem_st16(lane_addr + TM::kP + c16 * 16, pk);
       }
       l_run += rs0 + rs1;
       tmem_wait_st();

@@ -289,6 +289,7 @@ class UNetB200:
         self.freqs = torch.from_numpy(timestep_freqs(cfg.model_channels)).to(self.device)
         self.kernel_launches = 0
         self.attn_events: list | None = None  # (start, end, flops) when timing attention
+        self.attn_events_external = False     # record as graph nodes during a capture
 
     # -- ops ---------------------------------------------------------------------------------
     def _lin(self, x, name, bias=True, wkey=".weight"):
@@ -317,7 +318,9 @@ class UNetB200:
     def _attention(self, q, k, v, out):
         self.kernel_launches += 1
         if self.attn_events is not None:
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ext = self.attn_events_external
+            s = torch.cuda.Event(enable_timing=True, external=ext)
+            e = torch.cuda.Event(enable_timing=True, external=ext)
             B, H, Sq, D = q.shape
             Skv = k.shape[2]
             s.record()
@@ -426,7 +429,7 @@ class UNetStepGraph:
     inputs, replays, and returns the static output (copy it before the next call)."""
 
     def __init__(self, net: UNetB200, batch: int = 2, hw: int = 64, ctx_len: int = 77,
-                 warmup: int = 2):
+                 warmup: int = 2, time_attention: bool = False):
         dev = net.device
         cfg = net.cfg
         self.net = net
@@ -442,9 +445,24 @@ class UNetStepGraph:
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
         l0 = net.kernel_launches
-        with torch.cuda.graph(self.graph):
-            self.out = net(self.x, self.t, self.ctx)
+        # time_attention: event-record nodes around every attention launch of the step
+        # (read them after each replay with attention_ms()); off for the timed graph
+        self.attn_events = None
+        if time_attention:
+            net.attn_events, net.attn_events_external = [], True
+        try:
+            with torch.cuda.graph(self.graph):
+                self.out = net(self.x, self.t, self.ctx)
+        finally:
+            if time_attention:
+                self.attn_events = net.attn_events
+                net.attn_events, net.attn_events_external = None, False
         self.kernel_launches = net.kernel_launches - l0  # package kernels per replay
+
+    def attention_ms(self):
+        """(milliseconds, flops) of the attention launches in the last replay."""
+        return (sum(a.elapsed_time(b) for a, b, _ in self.attn_events),
+                sum(f for _, _, f in self.attn_events))
 
     def replay(self):
         self.graph.replay()
