@@ -58,6 +58,13 @@ struct FaParams {
   int in_f16;  // 1 if inputs are f16 (P is then f16 too), 0 for bf16
 };
 
+__device__ __forceinline__ float mask_score(const FaParams& p, int kv, int qi, float raw) {
+  const bool valid = kv < p.Skv && !(p.causal && kv > qi);
+  float x = raw;
+  if (p.mask && valid && qi < p.Sq) x += p.mask[(int64_t)qi * p.mask_stride + kv] * p.inv_scale;
+  return valid ? x : -INFINITY;
+}
+
 template <int NBQ, int NBV, int STAGES>
 struct FaSmem {
   static constexpr int kQ = 0;                                // two tiles x NBQ boxes
@@ -87,8 +94,13 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
 }
 
+// Raw score of key kv for query qi after masking: tail keys and causal positions -> -inf,
+// the additive mask applied in raw units (x_log2 = (s + mask / scale) * scale * log2 e).
+struct FaParams;
+__device__ __forceinline__ float mask_score(const FaParams& p, int kv, int qi, float raw);
+
 // Pairs of columns (out of every 16) whose exponentials use exp2_fma on unmasked tiles.
-constexpr uint32_t kPolyPairs = 0x4924;  // pairs 2, 5, 8, 11, 14: 31 % of the row
+constexpr uint32_t kPolyPairs = 0;  // none: measured slower than MUFU-only on B200 (issue-bound)
 
 // TMEM column offsets inside one tile's 256 columns
 template <int NBV>
@@ -283,36 +295,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int kv0 = j * kBN;
       const bool need_mask = p.mask != nullptr || (kv0 + kBN > p.Skv) ||
                              (p.causal && kv0 + kBN - 1 > q0 + t * kBM);
-      auto masked = [&](int c, float raw) -> float {
-        const int kv = kv0 + c;
-        const bool valid = kv < p.Skv && !(p.causal && kv > qi);
-        float x = raw;
-        if (p.mask && valid && qi < p.Sq) x += p.mask[(int64_t)qi * p.mask_stride + kv] * p.inv_scale;
-        return valid ? x : -INFINITY;
-      };
-      // pass A: row max over the 128 scores, two halves of two loads each
+      // the whole S row: four 32-column loads in flight, one wait; masked tiles (tail keys,
+      // causal, additive mask) are rewritten in place on a separate, rarely taken path
+      uint32_t r[4][32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tmem_ld32(lane_addr + TM::kS + q * 32, r[q]);
+      tmem_wait_ld();
+      if (need_mask) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            r[q][c] = float_bits(mask_score(p, kv0 + q * 32 + c, qi, __uint_as_float(r[q][c])));
+      }
       float mx;
       {
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t r[2][32];
-          tmem_ld32(lane_addr + TM::kS + hh * 64, r[0]);
-          tmem_ld32(lane_addr + TM::kS + hh * 64 + 32, r[1]);
-          tmem_wait_ld();
-          if (need_mask) {
+        for (int q = 0; q < 4; ++q)
 #pragma unroll
-            for (int q = 0; q < 2; ++q)
-#pragma unroll
-              for (int c = 0; c < 32; ++c)
-                m4[c & 3] = fmaxf(m4[c & 3], masked(hh * 64 + q * 32 + c, __uint_as_float(r[q][c])));
-          } else {
-#pragma unroll
-            for (int q = 0; q < 2; ++q)
-#pragma unroll
-              for (int c = 0; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(r[q][c]));
-          }
-        }
+          for (int c = 0; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(r[q][c]));
         mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
       const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl2;
@@ -343,40 +345,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       m_run = m_use;
 
-      // pass B: exp2, row sum, 16-bit P back into TMEM (column c holds keys 2c, 2c+1); S is
-      // re-read in two 64-column halves so only half a row is live in registers
+      // exp2, row sum, 16-bit P back into TMEM (column c holds keys 2c, 2c+1).  Unmasked
+      // tiles send 31 % of the exponentials to the FMA pipe; masked tiles use MUFU only, so
+      // -inf scores give exactly 0.
       float rs0 = 0.f, rs1 = 0.f;
+      if (!need_mask) {
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t r[2][32];
-        tmem_ld32(lane_addr + TM::kS + hh * 64, r[0]);
-        tmem_ld32(lane_addr + TM::kS + hh * 64 + 32, r[1]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
+        for (int q = 0; q < 4; ++q) {
           uint32_t pk[16];
 #pragma unroll
           for (int u = 0; u < 16; ++u) {
-            const int c = hh * 64 + q * 32 + 2 * u;
-            float x0 = __uint_as_float(r[q][2 * u]), x1 = __uint_as_float(r[q][2 * u + 1]);
+            const float x0 = fmaf(__uint_as_float(r[q][2 * u]), sl2, -m_ref);
+            const float x1 = fmaf(__uint_as_float(r[q][2 * u + 1]), sl2, -m_ref);
             float e0, e1;
-            if (need_mask) {
-              x0 = masked(c, x0);
-              x1 = masked(c + 1, x1);
-              e0 = ex2_approx(fmaf(x0, sl2, -m_ref));
-              e1 = ex2_approx(fmaf(x1, sl2, -m_ref));
-            } else if ((kPolyPairs >> u) & 1u) {
-              e0 = exp2_fma(fmaf(x0, sl2, -m_ref));
-              e1 = exp2_fma(fmaf(x1, sl2, -m_ref));
+            if ((kPolyPairs >> u) & 1u) {  // resolved at compile time
+              e0 = exp2_fma(x0);
+              e1 = exp2_fma(x1);
             } else {
-              e0 = ex2_approx(fmaf(x0, sl2, -m_ref));
-              e1 = ex2_approx(fmaf(x1, sl2, -m_ref));
+              e0 = ex2_approx(x0);
+              e1 = ex2_approx(x1);
             }
             rs0 += e0;
             rs1 += e1;
             pk[u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
           }
-          tmem_st16(lane_addr + TM::kP + hh * 32 + q * 16, pk);
+          tmem_st16(lane_addr + TM::kP + q * 16, pk);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const float e0 = ex2_approx(fmaf(__uint_as_float(r[q][2 * u]), sl2, -m_ref));
+            const float e1 = ex2_approx(fmaf(__uint_as_float(r[q][2 * u + 1]), sl2, -m_ref));
+            rs0 += e0;
+            rs1 += e1;
+            pk[u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+          }
+          tmem_st16(lane_addr + TM::kP + q * 16, pk);
         }
       }
       l_run += rs0 + rs1;
