@@ -72,8 +72,8 @@ struct FaSmem {
   static constexpr int kV = kK + STAGES * NBQ * kBox;
   static constexpr int kBar = kV + STAGES * NBV * kBox;
   // barriers: q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2],
-  // o_done[2], drain
-  static constexpr int kNumBars = 1 + 4 * STAGES + 2 + 2 + 2 + 1;
+  // o_done[2], s_free[2], drain
+  static constexpr int kNumBars = 1 + 4 * STAGES + 2 + 2 + 2 + 2 + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;  // tmem base + abort flag
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-B alignment of the base
@@ -128,7 +128,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = v_empty + STAGES;
   uint64_t* p_full = s_full + 2;
   uint64_t* o_done = p_full + 2;
-  uint64_t* drain = o_done + 2;
+  uint64_t* s_free = o_done + 2;
+  uint64_t* drain = s_free + 2;
+  // Dv <= 64: P has its own TMEM columns, so S_t(j+1) is issued as soon as the softmax has
+  // loaded S_t(j) (s_free) instead of after PV_t(j): the MMA round trip leaves the softmax's
+  // critical path, and the softmax waits for PV_t(j-1) (o_done) only before writing P.
+  constexpr bool kEarlyQK = NBV == 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
 
@@ -156,6 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 128);
       mbar_init(&o_done[t], 1);
+      mbar_init(&s_free[t], 128);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -252,6 +258,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = j % STAGES;
         const bool more = j + 1 < n_tiles;
         const int st1 = (j + 1) % STAGES;
+        if constexpr (kEarlyQK) {
+          if (more) {
+            if (!mbar_wait(&k_full[st1], ((j + 1) / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
+            if (!mbar_wait(&s_free[0], j & 1, abort_flag, WD_MMA_WAIT)) break;
+            tc_fence_after();
+            issue_qk(0, j + 1);
+            if (!mbar_wait(&s_free[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
+            tc_fence_after();
+            issue_qk(1, j + 1);
+            umma_commit(&k_empty[st1]);
+          }
+          if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
+          if (!mbar_wait(&p_full[0], j & 1, abort_flag, WD_MMA_WAIT)) break;
+          tc_fence_after();
+          issue_pv(0, j);
+          if (!mbar_wait(&p_full[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
+          tc_fence_after();
+          issue_pv(1, j);
+          umma_commit(&v_empty[st]);
+          continue;
+        }
         if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
         if (!mbar_wait(&p_full[0], j & 1, abort_flag, WD_MMA_WAIT)) break;
         tc_fence_after();
@@ -301,6 +328,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int q = 0; q < 4; ++q) tmem_ld32(lane_addr + TM::kS + q * 32, r[q]);
       tmem_wait_ld();
+      if constexpr (kEarlyQK) {
+        tc_fence_before();
+        mbar_arrive(&s_free[t]);  // S_t may now be overwritten by S_t(j+1)
+      }
       if (need_mask) {
 #pragma unroll
         for (int q = 0; q < 4; ++q)
@@ -329,30 +360,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float m_ref = m_use == -INFINITY ? 0.f : m_use;  // fully masked so far: p = 0
 
-      // O_t holds PV_t(j-1) already (its commit preceded S_t(j)'s).  tcgen05.ld/st are
-      // warp-collective: the whole warp rescales if any of its rows must (alpha = 1 else).
-      if (__any_sync(0xffffffffu, rescale)) {
-        const float alpha = rescale ? ex2_approx(m_run - m_ref) : 1.0f;
-        l_run *= alpha;
-        for (int c = 0; c < p.dv_pad; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(lane_addr + TM::kO + c, r);
-          tmem_wait_ld();
+      // tcgen05.ld/st are warp-collective: the whole warp rescales O if any of its rows
+      // must (alpha = 1 for the others).  O must already hold PV_t(j-1).
+      auto rescale_o = [&]() {
+        if (__any_sync(0xffffffffu, rescale)) {
+          const float alpha = rescale ? ex2_approx(m_run - m_ref) : 1.0f;
+          l_run *= alpha;
+          for (int c = 0; c < p.dv_pad; c += 16) {
+            uint32_t ro[16];
+            tmem_ld16(lane_addr + TM::kO + c, ro);
+            tmem_wait_ld();
 #pragma unroll
-          for (int u = 0; u < 16; ++u) r[u] = float_bits(__uint_as_float(r[u]) * alpha);
-          tmem_st16(lane_addr + TM::kO + c, r);
+            for (int u = 0; u < 16; ++u) ro[u] = float_bits(__uint_as_float(ro[u]) * alpha);
+            tmem_st16(lane_addr + TM::kO + c, ro);
+          }
         }
-      }
-      m_run = m_use;
+      };
+      // Aliased layout: S_t(j)'s commit followed PV_t(j-1), so O is final here.
+      if constexpr (!kEarlyQK) rescale_o();
 
-      // exp2, row sum, 16-bit P back into TMEM (column c holds keys 2c, 2c+1).  Unmasked
-      // tiles send 31 % of the exponentials to the FMA pipe; masked tiles use MUFU only, so
-      // -inf scores give exactly 0.
+      // exp2, row sum, 16-bit P (column c holds keys 2c, 2c+1).  Unmasked tiles may send
+      // some exponentials to the FMA pipe (kPolyPairs); masked tiles use MUFU only, so -inf
+      // scores give exactly 0.
       float rs0 = 0.f, rs1 = 0.f;
+      uint32_t pk[4][16];
       if (!need_mask) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          uint32_t pk[16];
 #pragma unroll
           for (int u = 0; u < 16; ++u) {
             const float x0 = fmaf(__uint_as_float(r[q][2 * u]), sl2, -m_ref);
@@ -367,25 +401,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             rs0 += e0;
             rs1 += e1;
-            pk[u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+            pk[q][u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
           }
-          tmem_st16(lane_addr + TM::kP + q * 16, pk);
+          if constexpr (!kEarlyQK) tmem_st16(lane_addr + TM::kP + q * 16, pk[q]);
         }
       } else {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          uint32_t pk[16];
 #pragma unroll
           for (int u = 0; u < 16; ++u) {
             const float e0 = ex2_approx(fmaf(__uint_as_float(r[q][2 * u]), sl2, -m_ref));
             const float e1 = ex2_approx(fmaf(__uint_as_float(r[q][2 * u + 1]), sl2, -m_ref));
             rs0 += e0;
             rs1 += e1;
-            pk[u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+            pk[q][u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
           }
-          tmem_st16(lane_addr + TM::kP + q * 16, pk);
+          if constexpr (!kEarlyQK) tmem_st16(lane_addr + TM::kP + q * 16, pk[q]);
         }
       }
+      if constexpr (kEarlyQK) {
+        // PV_t(j-1) must be done before P_t is rewritten and O rescaled
+        if (j >= 1 && !mbar_wait_warp(&o_done[t], (j - 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        rescale_o();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_st16(lane_addr + TM::kP + q * 16, pk[q]);
+      }
+      m_run = m_use;
       l_run += rs0 + rs1;
       tmem_wait_st();
       tc_fence_before();
