@@ -113,8 +113,9 @@ int sp_groupnorm_act_noalloc(const void* x, const void* gamma, const void* beta,
 /* ------------------------------------------------------------------------------------
  * Q8_0 (GGUF) weights.
  * A Q8_0 row of in_f values is in_f/32 blocks of 34 bytes: f16 LE scale + 32 int8.
- * The GPU layout is planar: q [out_f, in_f] int8 and scale [out_f, in_f/32] f16 bits;
- * the repack is lossless, so decode stays bit-exact.
+ * The GPU layout is planar: q [out_f, in_f] int8 and scale [in_f/32, out_f] f16 bits
+ * (k-block-major: scale[kb][n] belongs to q[n][32*kb .. 32*kb+31]); the repack is
+ * lossless, so decode stays bit-exact.
  * ------------------------------------------------------------------------------------ */
 /* Host repack of GGUF bytes (replaces the upload in GpuQuantizedLinear::from_bytes,
  * crates/sketchpad-cubecl/src/quantized_matmul.rs:670-702). */
@@ -130,7 +131,8 @@ int sp_q8_0_dequant(const void* q, const void* scale, int64_t out_f, int64_t in_
                     int out_dtype, void* stream);
 /* y[M,N] = x[M,K] . dequant(W)[N,K]^T (+ bias[N]); the dequantization happens inside the
  * GEMM mainloop (replaces GpuQuantizedLinear::forward, quantized_matmul.rs:752-766).
- * x, y, bias: SP_BF16.  K % 64 == 0, N % 16 == 0.  bias may be NULL. */
+ * x, y, bias: SP_BF16.  K % 64 == 0, N % 16 == 0.  bias may be NULL.  x, q, scale and y
+ * must be 16-byte aligned. */
 int sp_q8_0_linear(const void* x, const void* q, const void* scale, const void* bias, void* y,
                    int64_t M, int64_t N, int64_t K, int dtype, void* stream);
 

@@ -11,13 +11,16 @@
 namespace sp {
 namespace {
 
-// One thread per 34-byte GGUF block -> 32 int8 quants (8 x u32) + one f16 scale.
-__global__ void q8_0_repack_kernel(const uint8_t* __restrict__ gguf, int64_t nblocks,
-                                   int8_t* __restrict__ q, uint16_t* __restrict__ scale) {
+// One thread per 34-byte GGUF block -> 32 int8 quants (8 x u32) + one f16 scale.  Block i
+// is (row n = i / kb, k-block i % kb); its scale goes to scale[i % kb][n] (k-block-major, so
+// the GEMM loads a k-tile's scales for 256 consecutive rows as one 512-byte TMA row).
+__global__ void q8_0_repack_kernel(const uint8_t* __restrict__ gguf, int64_t nblocks, int64_t kb,
+                                   int64_t rows, int8_t* __restrict__ q,
+                                   uint16_t* __restrict__ scale) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nblocks) return;
   const uint8_t* blk = gguf + i * 34;
-  scale[i] = (uint16_t)(blk[0] | (blk[1] << 8));
+  scale[(i % kb) * rows + i / kb] = (uint16_t)(blk[0] | (blk[1] << 8));
   uint32_t w[8];
 #pragma unroll
   for (int t = 0; t < 8; ++t)
@@ -42,11 +45,12 @@ __device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float v) {
 // One thread per 4 consecutive quants: out = f32(f16 scale) * int8, exact in f32.
 template <typename T>
 __global__ void q8_0_dequant_kernel(const int8_t* __restrict__ q, const uint16_t* __restrict__ scale,
-                                    int64_t n4, T* __restrict__ out) {
+                                    int64_t n4, int64_t rows, int64_t cols, T* __restrict__ out) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n4) return;
   const char4 v = reinterpret_cast<const char4*>(q)[i];
-  const float s = __half2float(__ushort_as_half(scale[(i * 4) >> 5]));
+  const int64_t n = (i * 4) / cols, k = (i * 4) % cols;
+  const float s = __half2float(__ushort_as_half(scale[(k >> 5) * rows + n]));
   T* o = out + i * 4;
   o[0] = cvt_out<T>(s * (float)v.x);
   o[1] = cvt_out<T>(s * (float)v.y);
@@ -123,9 +127,10 @@ int sp_q8_0_repack_host(const uint8_t* gguf_host, size_t nbytes, int64_t out_f, 
   const int64_t nblocks = out_f * (in_f / 32);
   if (nbytes < (size_t)nblocks * 34)
     return set_error(SP_ERR_SHAPE, "q8_0 repack: %zu bytes < %lld blocks x 34", nbytes, (long long)nblocks);
+  const int64_t kb = in_f / 32;
   for (int64_t i = 0; i < nblocks; ++i) {
     const uint8_t* blk = gguf_host + i * 34;
-    scale_host[i] = (uint16_t)(blk[0] | (blk[1] << 8));
+    scale_host[(i % kb) * out_f + i / kb] = (uint16_t)(blk[0] | (blk[1] << 8));
     std::memcpy(q_host + i * 32, blk + 2, 32);
   }
   return SP_OK;
@@ -145,7 +150,8 @@ int sp_q8_0_repack(const void* gguf, size_t nbytes, int64_t out_f, int64_t in_f,
   if (!aligned(q, 16) || !aligned(scale, 2)) return set_error(SP_ERR_ALIGN, "q8_0 repack: output misaligned");
   if (int rc = require_sm100()) return rc;
   q8_0_repack_kernel<<<grid_for(nblocks, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(gguf), nblocks, static_cast<int8_t*>(q), static_cast<uint16_t*>(scale));
+      static_cast<const uint8_t*>(gguf), nblocks, in_f / 32, out_f, static_cast<int8_t*>(q),
+      static_cast<uint16_t*>(scale));
   return check_launch("q8_0 repack");
 }
 
@@ -164,9 +170,9 @@ int sp_q8_0_dequant(const void* q, const void* scale, int64_t out_f, int64_t in_
   const int8_t* qq = static_cast<const int8_t*>(q);
   const uint16_t* ss = static_cast<const uint16_t*>(scale);
   switch (out_dtype) {
-    case SP_F32: q8_0_dequant_kernel<float><<<grid_for(n4, 256), 256, 0, s>>>(qq, ss, n4, static_cast<float*>(out)); break;
-    case SP_F16: q8_0_dequant_kernel<__half><<<grid_for(n4, 256), 256, 0, s>>>(qq, ss, n4, static_cast<__half*>(out)); break;
-    case SP_BF16: q8_0_dequant_kernel<__nv_bfloat16><<<grid_for(n4, 256), 256, 0, s>>>(qq, ss, n4, static_cast<__nv_bfloat16*>(out)); break;
+    case SP_F32: q8_0_dequant_kernel<float><<<grid_for(n4, 256), 256, 0, s>>>(qq, ss, n4, out_f, in_f, static_cast<float*>(out)); break;
+    case SP_F16: q8_0_dequant_kernel<__half><<<grid_for(n4, 256), 256, 0, s>>>(qq, ss, n4, out_f, in_f, static_cast<__half*>(out)); break;
+    case SP_BF16: q8_0_dequant_kernel<__nv_bfloat16><<<grid_for(n4, 256), 256, 0, s>>>(qq, ss, n4, out_f, in_f, static_cast<__nv_bfloat16*>(out)); break;
     default: return set_error(SP_ERR_DTYPE, "q8_0 dequant: unknown dtype %d", out_dtype);
   }
   return check_launch("q8_0 dequant");

@@ -5,12 +5,18 @@
 // which materialises the whole dequantized matrix and then runs a separate matmul, and
 // Fp8Linear::forward (crates/sketchpad-core/src/quantization.rs:601-609).
 //
-// CTA tile: 128 rows of x (UMMA M) x 256 weight rows (UMMA N), K in steps of 64.
-//   warp 0      TMA: x tile (bf16, 128B swizzle) + raw 8-bit weight tile, RAW_STAGES deep.
-//   warp 1      TMEM owner + MMA issuer: acc[128 x 256 f32] += x_tile . wtile^T.
-//   warps 2..5  decoders: raw 8-bit tile -> bf16 tile in the UMMA K-major 128B-swizzled
-//               layout (Q8_0: f16 block scale * int8; FP8: exact e4m3 -> bf16), CVT_STAGES
-//               deep; then the epilogue (TMEM -> per-channel scale, bias -> bf16 -> HBM).
+// CTA tile: 256 rows of x (two UMMA M=128 halves) x 256 weight rows (UMMA N), K in steps of
+// 64.  Every decoded weight tile feeds both halves, so one decode serves 2*256 FLOPs per weight.
+//   warp 0       TMA: x tile (bf16, 128B swizzle), raw 8-bit weight tile and (Q8_0) the
+//                k-tile's block scales, RAW_STAGES deep.
+//   warp 1       TMEM owner (512 columns: two 128 x 256 f32 accumulators) + MMA issuer.
+//   warps 2, 3   idle (the block is sized in whole warpgroups).
+//   warps 4..11  decoders: raw 8-bit tile -> bf16 tile in the UMMA K-major 128B-swizzled
+//                layout (Q8_0: f16 block scale * int8; FP8: exact e4m3 -> bf16), CVT_STAGES
+//                deep; then the epilogue (warps 4-7 half 0, 8-11 half 1: TMEM -> per-channel
+//                scale, bias -> bf16 -> HBM).
+#include <cstring>
+
 #include "common.cuh"
 #include "quant_codec.cuh"
 #include "tc.cuh"
@@ -18,11 +24,12 @@
 namespace sp {
 namespace {
 
-constexpr int kQBM = 128, kQBN = 256, kQBK = 64;
-constexpr int kQThreads = 192;
-constexpr int kRawStages = 4, kCvtStages = 2;
-constexpr int kXBytes = kQBM * kQBK * 2;    // 16 KB
+constexpr int kQBM = 256, kQHalf = 128, kQBN = 256, kQBK = 64;
+constexpr int kQThreads = 384, kQDecoders = 256, kQFirstDecoderWarp = 4;
+constexpr int kRawStages = 3, kCvtStages = 2;
+constexpr int kXBytes = kQBM * kQBK * 2;    // 32 KB
 constexpr int kWRawBytes = kQBN * kQBK;     // 16 KB
+constexpr int kScBytes = 2 * kQBN * 2;      // 1 KB: two k-blocks x 256 rows of f16
 constexpr int kWCvtBytes = kQBN * kQBK * 2; // 32 KB
 
 enum WFormat : int { W_Q8_0 = 0, W_FP8 = 1 };
@@ -30,7 +37,8 @@ enum WFormat : int { W_Q8_0 = 0, W_FP8 = 1 };
 struct QlSmem {
   static constexpr int kX = 0;
   static constexpr int kWRaw = kX + kRawStages * kXBytes;
-  static constexpr int kWCvt = kWRaw + kRawStages * kWRawBytes;
+  static constexpr int kSc = kWRaw + kRawStages * kWRawBytes;
+  static constexpr int kWCvt = kSc + kRawStages * kScBytes;
   static constexpr int kBar = kWCvt + kCvtStages * kWCvtBytes;
   static constexpr int kNumBars = 2 * kRawStages + 2 * kCvtStages + 1 + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
@@ -39,7 +47,7 @@ struct QlSmem {
 
 struct QlParams {
   int64_t M, N, K;
-  const uint16_t* q8_scale;  // Q8_0: [N, K/32] f16 bits
+  const uint16_t* q8_scale;  // Q8_0: [K/32, N] f16 bits (loaded by TMA)
   const float* fp8_scale;    // FP8: [N] or [1]
   int64_t nscale;
   const __nv_bfloat16* bias;  // [N] or null
@@ -80,7 +88,7 @@ __device__ __forceinline__ void e4m3x4_to_bf16(uint32_t w, uint32_t& lo, uint32_
 template <int WF>
 __global__ void __launch_bounds__(kQThreads, 1)
     qlinear_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
-                   const QlParams p) {
+                   const __grid_constant__ CUtensorMap tms, const QlParams p) {
   using L = QlSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -103,10 +111,10 @@ __global__ void __launch_bounds__(kQThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRawStages; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], 1 + 128);  // MMA commit (x consumed) + 128 decoders (raw W)
+      mbar_init(&raw_empty[s], 1 + kQDecoders);  // MMA commit (x consumed) + decoders (raw W)
     }
     for (int s = 0; s < kCvtStages; ++s) {
-      mbar_init(&cvt_full[s], 128);
+      mbar_init(&cvt_full[s], kQDecoders);
       mbar_init(&cvt_empty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -115,7 +123,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -127,14 +135,18 @@ __global__ void __launch_bounds__(kQThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmx);
       tma_prefetch_desc(&tmw);
+      if constexpr (WF == W_Q8_0) tma_prefetch_desc(&tms);
+      constexpr uint32_t kTx = kXBytes + kWRawBytes + (WF == W_Q8_0 ? kScBytes : 0);
       int issued = 0;
       for (int kt = 0; kt < ktiles; ++kt) {
         const int st = kt % kRawStages;
         const uint32_t ph = (kt / kRawStages) & 1;
         if (kt >= kRawStages && !mbar_wait(&raw_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) break;
-        mbar_arrive_expect_tx(&raw_full[st], kXBytes + kWRawBytes);
+        mbar_arrive_expect_tx(&raw_full[st], kTx);
         tma_load_2d(smem + L::kX + st * kXBytes, &tmx, &raw_full[st], kt * kQBK, m0);
         tma_load_2d(smem + L::kWRaw + st * kWRawBytes, &tmw, &raw_full[st], kt * kQBK, n0);
+        if constexpr (WF == W_Q8_0)
+          tma_load_2d(smem + L::kSc + st * kScBytes, &tms, &raw_full[st], n0, kt * (kQBK / 32));
         issued = kt + 1;
       }
       if (*abort_flag)
@@ -143,7 +155,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = make_idesc_f16(kQBM, kQBN, 1u, 0, 0);
+      const uint32_t idesc = make_idesc_f16(kQHalf, kQBN, 1u, 0, 0);
       bool ok = true;
       for (int kt = 0; kt < ktiles; ++kt) {
         const int rs = kt % kRawStages, cs = kt % kCvtStages;
@@ -157,9 +169,12 @@ __global__ void __launch_bounds__(kQThreads, 1)
         const uint32_t wb = smem_u32(smem + L::kWCvt + cs * kWCvtBytes);
 #pragma unroll
         for (int kk = 0; kk < kQBK / 16; ++kk) {
-          const uint64_t a = make_smem_desc(xa + kk * 32, 16, 1024, LAYOUT_SW128);
           const uint64_t b = make_smem_desc(wb + kk * 32, 16, 1024, LAYOUT_SW128);
-          umma_ss(tmem, a, b, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+          // rows 0..127 and 128..255 of the x tile (16 KB apart, whole swizzle atoms)
+          umma_ss(tmem, make_smem_desc(xa + kk * 32, 16, 1024, LAYOUT_SW128), b, idesc, acc);
+          umma_ss(tmem + kQBN, make_smem_desc(xa + kQHalf * 128 + kk * 32, 16, 1024, LAYOUT_SW128),
+                  b, idesc, acc);
         }
         umma_commit(&raw_empty[rs]);
         umma_commit(&cvt_empty[cs]);
@@ -168,9 +183,9 @@ __global__ void __launch_bounds__(kQThreads, 1)
       umma_commit(drain);
       mbar_wait(drain, 0, nullptr, WD_MMA_WAIT);
     }
-  } else {
+  } else if (warp >= kQFirstDecoderWarp) {
     // ------------------------------------------------------------ decoders
-    const int t = threadIdx.x - 64;  // 0..127
+    const int t = threadIdx.x - kQFirstDecoderWarp * 32;  // 0..255
     bool ok = true;
     for (int kt = 0; kt < ktiles; ++kt) {
       const int rs = kt % kRawStages, cs = kt % kCvtStages;
@@ -184,19 +199,17 @@ __global__ void __launch_bounds__(kQThreads, 1)
         break;
       }
       const uint8_t* raw = smem + L::kWRaw + rs * kWRawBytes;
+      const __half* sc = reinterpret_cast<const __half*>(smem + L::kSc + rs * kScBytes);
       uint8_t* cvt = smem + L::kWCvt + cs * kWCvtBytes;
 #pragma unroll 2
-      for (int it = 0; it < (kQBN * 4) / 128; ++it) {
-        const int task = t + it * 128;
+      for (int it = 0; it < (kQBN * 4) / kQDecoders; ++it) {
+        const int task = t + it * kQDecoders;
         const int row = task >> 2, ch = task & 3;  // 16 weights: k = 16*ch .. 16*ch+15
         const uint4 w = *reinterpret_cast<const uint4*>(raw + row * 64 + ch * 16);
         uint32_t o[8];
         if constexpr (WF == W_Q8_0) {
-          const int64_t n = n0 + row;
-          float s = 0.f;
-          if (n < p.N)
-            s = __half2float(__ushort_as_half(
-                p.q8_scale[n * (p.K / 32) + (int64_t)kt * 2 + (ch >> 1)]));
+          // rows past N read TMA zero fill: scale 0, weights 0
+          const float s = __half2float(sc[(ch >> 1) * kQBN + row]);
           q8x4_to_bf16(w.x, s, o[0], o[1]);
           q8x4_to_bf16(w.y, s, o[2], o[3]);
           q8x4_to_bf16(w.z, s, o[4], o[5]);
@@ -222,10 +235,11 @@ __global__ void __launch_bounds__(kQThreads, 1)
     // ------------------------------------------------------------ epilogue
     if (__all_sync(0xffffffffu, ok) && mbar_wait_warp(acc_full, 0, abort_flag, WD_EPILOGUE_WAIT)) {
       tc_fence_after();
-      const int quarter = warp & 3;
-      const int row = quarter * 32 + lane;
+      const int half = (warp - kQFirstDecoderWarp) >> 2;
+      const int quarter = warp & 3;  // the TMEM lane quarter this warp may access
+      const int row = half * kQHalf + quarter * 32 + lane;
       const int64_t m = m0 + row;
-      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+      const uint32_t taddr = tmem + half * kQBN + ((uint32_t)(quarter * 32) << 16);
       for (int c = 0; c < kQBN; c += 32) {
         uint32_t r[32];
         tmem_ld32(taddr + c, r);
@@ -259,15 +273,18 @@ __global__ void __launch_bounds__(kQThreads, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
 template <int WF>
 int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_t s) {
-  if (!aligned(x, 16) || !aligned(w8, 16) || !aligned(p.y, 16))
-    return set_error(SP_ERR_ALIGN, "quantized linear: x, weights and y must be 16-byte aligned");
-  CUtensorMap mx, mw;
+  if (!aligned(x, 16) || !aligned(w8, 16) || !aligned(p.y, 16) ||
+      (WF == W_Q8_0 && !aligned(p.q8_scale, 16)))
+    return set_error(SP_ERR_ALIGN,
+                     "quantized linear: x, weights, scales and y must be 16-byte aligned");
+  CUtensorMap mx, mw, ms;
+  std::memset(&ms, 0, sizeof(ms));
   {
     const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
     const uint64_t strides[1] = {(uint64_t)p.K * 2};
@@ -284,6 +301,15 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
                               CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
   }
+  if (WF == W_Q8_0) {
+    // scales [K/32, N] f16: one box = the 2 k-blocks of a k-tile x 256 rows
+    const uint64_t dims[2] = {(uint64_t)p.N, (uint64_t)(p.K / 32)};
+    const uint64_t strides[1] = {(uint64_t)p.N * 2};
+    const uint32_t box[2] = {kQBN, kQBK / 32};
+    if (int rc = encode_tiled(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.q8_scale, dims, strides,
+                              box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+  }
   auto kern = qlinear_kernel<WF>;
   static_assert(QlSmem::kAlloc <= 232448, "quantized linear smem budget");
   static unsigned long long attr_set = 0;
@@ -295,7 +321,7 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
     }
   }
   dim3 grid((unsigned)((p.M + kQBM - 1) / kQBM), (unsigned)((p.N + kQBN - 1) / kQBN));
-  kern<<<grid, kQThreads, QlSmem::kAlloc, s>>>(mx, mw, p);
+  kern<<<grid, kQThreads, QlSmem::kAlloc, s>>>(mx, mw, ms, p);
   return check_launch("quantized linear");
 }
 

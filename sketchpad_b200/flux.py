@@ -86,7 +86,7 @@ def _q8_linear(rng_seed: int, n: int, k: int, device, bias=True):
     """A Q8_0 Linear [n out, k in] with the config's synthetic weights, drawn on the GPU."""
     g = torch.Generator(device=device).manual_seed(rng_seed)
     q = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int32).to(torch.int8)
-    s = (torch.rand((n, k // 32), generator=g, device=device) * 0.019 + 0.001).to(torch.float16)
+    s = (torch.rand((k // 32, n), generator=g, device=device) * 0.019 + 0.001).to(torch.float16)
     b = (torch.randn(n, generator=g, device=device) * 0.02).to(torch.bfloat16) if bias else None
     return GpuQuantizedLinear(q, s.view(torch.int16), n, k, torch.bfloat16, b)
 
@@ -97,7 +97,8 @@ class _Attn:
         self.qkv = _q8_linear(seed, 3 * h, h, device)
         self.proj = _q8_linear(seed + 1, h, h, device)
         # rows [h, 3h) of the qkv weight produce k and v: the cross stream needs only those
-        self.kv = GpuQuantizedLinear(self.qkv.q[h:], self.qkv.scale[h:], 2 * h, h, torch.bfloat16,
+        self.kv = GpuQuantizedLinear(self.qkv.q[h:], self.qkv.scale[:, h:].contiguous(), 2 * h, h,
+                                     torch.bfloat16,
                                      self.qkv.bias[h:])
         self.H, self.D = cfg.num_heads, cfg.head_dim
 
@@ -122,7 +123,8 @@ class _SwiGlu:
         h, i = cfg.hidden_size, cfg.intermediate
         gate, up = _q8_linear(seed, i, h, device), _q8_linear(seed + 1, i, h, device)
         # gate and up share x: one GEMM over the stacked rows
-        self.gate_up = GpuQuantizedLinear(torch.cat([gate.q, up.q]), torch.cat([gate.scale, up.scale]),
+        self.gate_up = GpuQuantizedLinear(torch.cat([gate.q, up.q]),
+                                          torch.cat([gate.scale, up.scale], dim=1),
                                           2 * i, h, torch.bfloat16, torch.cat([gate.bias, up.bias]))
         self.down = _q8_linear(seed + 2, h, i, device)
         self.i = i

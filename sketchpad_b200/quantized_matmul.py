@@ -26,11 +26,13 @@ class GpuQuantType(enum.Enum):
 
 
 def repack_q8_0_host(data: bytes | np.ndarray, out_features: int, in_features: int):
-    """GGUF Q8_0 bytes -> (q int8 [out, in], scale f16-bits uint16 [out, in/32]) on the host."""
+    """GGUF Q8_0 bytes -> (q int8 [out, in], scale f16-bits uint16 [in/32, out]) on the host.
+
+    The scales are k-block-major: scale[kb, n] belongs to quants q[n, 32*kb : 32*kb + 32]."""
     buf = np.frombuffer(bytes(data), np.uint8) if not isinstance(data, np.ndarray) else \
         np.ascontiguousarray(data, dtype=np.uint8)
     q = np.empty((out_features, in_features), np.int8)
-    s = np.empty((out_features, in_features // 32), np.uint16)
+    s = np.empty((in_features // 32, out_features), np.uint16)
     _lib.call("sp_q8_0_repack_host", buf.ctypes.data_as(ctypes.c_void_p), buf.size, out_features,
               in_features, q.ctypes.data_as(ctypes.c_void_p), s.ctypes.data_as(ctypes.c_void_p))
     return q, s
@@ -50,7 +52,7 @@ def repack_q8_0(gguf: torch.Tensor, out_features: int, in_features: int):
     """Device repack of GGUF Q8_0 bytes already resident on the GPU (uint8 tensor)."""
     dev = require_cuda(gguf)
     q = torch.empty((out_features, in_features), dtype=torch.int8, device=dev)
-    s = torch.empty((out_features, in_features // 32), dtype=torch.int16, device=dev)
+    s = torch.empty((in_features // 32, out_features), dtype=torch.int16, device=dev)
     _lib.call("sp_q8_0_repack", ptr(gguf), gguf.numel(), out_features, in_features, ptr(q),
               ptr(s), stream_ptr(dev))
     return q, s

@@ -65,12 +65,12 @@ def test_q8_0_host_repack_matches_oracle_decode():
     blocks[:, 2:] = rng.integers(-128, 128, (nb, 32), dtype=np.int8).view(np.uint8)
     raw = blocks.tobytes()
     q = np.empty((out_f, in_f), np.int8)
-    s = np.empty((out_f, in_f // 32), np.uint16)
+    s = np.empty((in_f // 32, out_f), np.uint16)
     buf = np.frombuffer(raw, np.uint8)
     rc = _lib.load().sp_q8_0_repack_host(buf.ctypes.data_as(ctypes.c_void_p), buf.size, out_f, in_f,
                                          q.ctypes.data_as(ctypes.c_void_p),
                                          s.ctypes.data_as(ctypes.c_void_p))
     assert rc == 0
-    dec = oracle.f16_bits_to_f32(s).repeat(32, axis=1) * q.astype(np.float32)
+    dec = oracle.f16_bits_to_f32(s.T).repeat(32, axis=1) * q.astype(np.float32)
     ref = oracle.q8_0_dequantize(buf, out_f * in_f).reshape(out_f, in_f)
     assert np.array_equal(dec.view(np.uint32), ref.view(np.uint32))
