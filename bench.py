@@ -438,8 +438,49 @@ def _case_unet_step(torch):
     return step, unet_flops()["total"], "flop"
 
 
+def _case_flux_block(torch, single: bool):
+    from sketchpad_b200.flux import (FluxConfig, FluxDoubleBlockB200, FluxSingleBlockB200,
+                                     flux_step_flops, rope_tables)
+    cfg = FluxConfig()
+    g = torch.Generator(device="cuda").manual_seed(1)
+    rnd = lambda *s: torch.randn(*s, device="cuda", generator=g).to(torch.bfloat16)  # noqa: E731
+    cos, sin = (torch.from_numpy(t).to("cuda", torch.bfloat16) for t in rope_tables(128, 4608))
+    cond = rnd(1, cfg.hidden_size)
+    if single:
+        blk, x = FluxSingleBlockB200(7, cfg, "cuda"), rnd(1, 4608, cfg.hidden_size)
+        return (lambda: blk.forward(x, cond, cos, sin)), flux_step_flops(cfg, num_double=0, num_single=1), "flop"
+    blk = FluxDoubleBlockB200(7, cfg, "cuda")
+    img, txt = rnd(1, 4096, cfg.hidden_size), rnd(1, 512, cfg.hidden_size)
+    return (lambda: blk.forward(img, txt, cond, cos, sin)), flux_step_flops(cfg, num_double=1, num_single=0), "flop"
+
+
+def _case_flux_step(torch):
+    from sketchpad_b200.flux import FluxB200, FluxConfig, flux_step_flops
+    cfg = FluxConfig()
+    net = FluxB200(cfg, "cuda", seed=0)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    lat = torch.randn(1, 16, 128, 128, device="cuda", generator=g)
+    txt = torch.randn(1, 512, cfg.text_dim, device="cuda", generator=g).to(torch.bfloat16)
+    return (lambda: net.forward(lat, 1.0, txt)), flux_step_flops(cfg), "flop"
+
+
+def _case_wan_block(torch):
+    from sketchpad_b200.wan import WanBlockB200, WanConfig, wan_block_flops
+    cfg = WanConfig()
+    blk = WanBlockB200(0, cfg, "cuda")
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(1, 21 * 45 * 80, cfg.hidden_size, device="cuda", generator=g).to(torch.bfloat16)
+    ctx = torch.randn(1, 512, cfg.hidden_size, device="cuda", generator=g).to(torch.bfloat16)
+    cond = torch.randn(1, cfg.hidden_size, device="cuda", generator=g).to(torch.bfloat16)
+    return (lambda: blk.forward(x, cond, ctx, 21, 45, 80)), wan_block_flops(cfg)["total"], "flop"
+
+
 CASES = {
     "unet_step_eager": _case_unet_step,
+    "flux_double_4096x512": lambda t: _case_flux_block(t, False),
+    "flux_single_4608": lambda t: _case_flux_block(t, True),
+    "flux_step": _case_flux_step,
+    "wan_block_21x45x80": _case_wan_block,
     "attn_8x24x4608x128": lambda t: _case_attention(t, 8, 24, 4608, 4608, 128),
     "attn_2x8x4096x40": lambda t: _case_attention(t, 2, 8, 4096, 4096, 40),
     "attn_2x10x1024x64": lambda t: _case_attention(t, 2, 10, 1024, 1024, 64),

@@ -170,6 +170,20 @@ def fp8_quantize(w, fmt: int = 0, per_channel: bool = True, scale=None):
     return data, sc
 
 
+def e4m3_bytes_to_f32(codes) -> np.ndarray:
+    """Value of each e4m3 byte (crates/sketchpad-core/src/quantization.rs:311-368: 4 exponent
+    bits with bias 7, 3 mantissa bits, smallest normal 2^-6, subnormal step 2^-9, max 448).
+    Gives the f32 values the reference's simulated Fp8Tensor holds for the same grid points."""
+    c = np.ascontiguousarray(codes, dtype=np.uint8).astype(np.int32)
+    sign = np.where(c & 0x80, -1.0, 1.0).astype(np.float32)
+    e = (c >> 3) & 0xF
+    m = (c & 0x7).astype(np.float32)
+    normal = np.ldexp(1.0 + m / 8.0, e - 7).astype(np.float32)
+    sub = (m * np.float32(2.0 ** -9)).astype(np.float32)
+    v = np.where(e == 0, sub, normal).astype(np.float32) * sign
+    return np.where((e == 0xF) & (c & 0x7 == 0x7), np.float32(np.nan), v).astype(np.float32)
+
+
 def fp8_dequantize(data, scale):
     data, pd = _f(data)
     scale, ps = _f(scale)

@@ -47,6 +47,8 @@ class FluxConfig:
     guidance_dim: int = 256
     max_seq_len: int = 4608
     mlp_ratio: float = 4.0
+    # synthetic Q8_0 block scales ~ U(lo, hi) (config 4: 0.001 .. 0.02)
+    weight_scale: tuple = (0.001, 0.02)
 
     @property
     def head_dim(self):
@@ -82,11 +84,13 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return x * cos[:S] + rot * sin[:S]
 
 
-def _q8_linear(rng_seed: int, n: int, k: int, device, bias=True):
-    """A Q8_0 Linear [n out, k in] with the config's synthetic weights, drawn on the GPU."""
+def _q8_linear(rng_seed: int, n: int, k: int, device, bias=True, scale_range=(0.001, 0.02)):
+    """A Q8_0 Linear [n out, k in] with the config's synthetic weights, drawn on the device:
+    int8 ~ U[-127, 127], f16 block scale ~ U(scale_range), bias ~ N(0, 0.02)."""
     g = torch.Generator(device=device).manual_seed(rng_seed)
     q = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int32).to(torch.int8)
-    s = (torch.rand((k // 32, n), generator=g, device=device) * 0.019 + 0.001).to(torch.float16)
+    lo, hi = scale_range
+    s = (torch.rand((k // 32, n), generator=g, device=device) * (hi - lo) + lo).to(torch.float16)
     b = (torch.randn(n, generator=g, device=device) * 0.02).to(torch.bfloat16) if bias else None
     return GpuQuantizedLinear(q, s.view(torch.int16), n, k, torch.bfloat16, b)
 
@@ -94,8 +98,8 @@ def _q8_linear(rng_seed: int, n: int, k: int, device, bias=True):
 class _Attn:
     def __init__(self, seed, cfg: FluxConfig, device):
         h = cfg.hidden_size
-        self.qkv = _q8_linear(seed, 3 * h, h, device)
-        self.proj = _q8_linear(seed + 1, h, h, device)
+        self.qkv = _q8_linear(seed, 3 * h, h, device, scale_range=cfg.weight_scale)
+        self.proj = _q8_linear(seed + 1, h, h, device, scale_range=cfg.weight_scale)
         # rows [h, 3h) of the qkv weight produce k and v: the cross stream needs only those
         self.kv = GpuQuantizedLinear(self.qkv.q[h:], self.qkv.scale[:, h:].contiguous(), 2 * h, h,
                                      torch.bfloat16,
@@ -121,12 +125,13 @@ class _Attn:
 class _SwiGlu:
     def __init__(self, seed, cfg: FluxConfig, device):
         h, i = cfg.hidden_size, cfg.intermediate
-        gate, up = _q8_linear(seed, i, h, device), _q8_linear(seed + 1, i, h, device)
+        gate = _q8_linear(seed, i, h, device, scale_range=cfg.weight_scale)
+        up = _q8_linear(seed + 1, i, h, device, scale_range=cfg.weight_scale)
         # gate and up share x: one GEMM over the stacked rows
         self.gate_up = GpuQuantizedLinear(torch.cat([gate.q, up.q]),
                                           torch.cat([gate.scale, up.scale], dim=1),
                                           2 * i, h, torch.bfloat16, torch.cat([gate.bias, up.bias]))
-        self.down = _q8_linear(seed + 2, h, i, device)
+        self.down = _q8_linear(seed + 2, h, i, device, scale_range=cfg.weight_scale)
         self.i = i
 
     def forward(self, x):
@@ -146,7 +151,7 @@ class FluxDoubleBlockB200:
         h = cfg.hidden_size
         self.img_attn, self.txt_attn = _Attn(seed, cfg, device), _Attn(seed + 10, cfg, device)
         self.img_ffn, self.txt_ffn = _SwiGlu(seed + 20, cfg, device), _SwiGlu(seed + 30, cfg, device)
-        self.modulation = _q8_linear(seed + 40, 6 * h, h, device)
+        self.modulation = _q8_linear(seed + 40, 6 * h, h, device, scale_range=cfg.weight_scale)
         self.h = h
 
     def forward(self, img, txt, cond, cos, sin):
@@ -168,7 +173,7 @@ class FluxSingleBlockB200:
         h = cfg.hidden_size
         self.attn = _Attn(seed, cfg, device)
         self.ffn = _SwiGlu(seed + 20, cfg, device)
-        self.modulation = _q8_linear(seed + 40, 3 * h, h, device)
+        self.modulation = _q8_linear(seed + 40, 3 * h, h, device, scale_range=cfg.weight_scale)
         self.h = h
 
     def forward(self, x, cond, cos, sin):
@@ -188,18 +193,21 @@ class FluxB200:
         self.cfg, self.device = cfg, torch.device(device)
         h = cfg.hidden_size
         pd = cfg.patch_size ** 2 * cfg.in_channels
-        # patch / text / time projections are tiny next to the blocks; K % 64 rules them
-        # onto bf16 torch linears (patch_dim 64 and time_dim 256 do satisfy it, text_dim too)
-        self.img_embed = _q8_linear(seed + 1, h, pd, device)
-        self.txt_embed = _q8_linear(seed + 2, h, cfg.text_dim, device)
-        self.t1, self.t2 = _q8_linear(seed + 3, h, cfg.time_dim, device), _q8_linear(seed + 4, h, h, device)
-        self.g1, self.g2 = _q8_linear(seed + 5, h, cfg.guidance_dim, device), _q8_linear(seed + 6, h, h, device)
+        # patch / text / time projections are Q8_0 linears too (patch_dim 64, time_dim 256
+        # and text_dim 4096 all satisfy K % 64 == 0)
+        ws = cfg.weight_scale
+        self.img_embed = _q8_linear(seed + 1, h, pd, device, scale_range=ws)
+        self.txt_embed = _q8_linear(seed + 2, h, cfg.text_dim, device, scale_range=ws)
+        self.t1 = _q8_linear(seed + 3, h, cfg.time_dim, device, scale_range=ws)
+        self.t2 = _q8_linear(seed + 4, h, h, device, scale_range=ws)
+        self.g1 = _q8_linear(seed + 5, h, cfg.guidance_dim, device, scale_range=ws)
+        self.g2 = _q8_linear(seed + 6, h, h, device, scale_range=ws)
         nd = cfg.num_double_blocks if num_double is None else num_double
         ns = cfg.num_single_blocks if num_single is None else num_single
         self.double = [FluxDoubleBlockB200(seed + 100 + 50 * i, cfg, device) for i in range(nd)]
         self.single = [FluxSingleBlockB200(seed + 5000 + 50 * i, cfg, device) for i in range(ns)]
-        self.final_mod = _q8_linear(seed + 7, 2 * h, h, device)
-        self.final_proj = _q8_linear(seed + 8, pd, h, device)
+        self.final_mod = _q8_linear(seed + 7, 2 * h, h, device, scale_range=ws)
+        self.final_proj = _q8_linear(seed + 8, pd, h, device, scale_range=ws)
         cos, sin = rope_tables(cfg.head_dim, cfg.max_seq_len)
         self.cos = torch.from_numpy(cos).to(self.device, torch.bfloat16)
         self.sin = torch.from_numpy(sin).to(self.device, torch.bfloat16)

@@ -83,7 +83,8 @@ def _ln(x):
 
 
 class WanBlockB200:
-    def __init__(self, seed: int, cfg: WanConfig, device, group: Optional[dist.ProcessGroup] = None):
+    def __init__(self, seed: int, cfg: WanConfig, device, group: Optional[dist.ProcessGroup] = None,
+                 rope_dtype: torch.dtype = torch.bfloat16):
         h, i = cfg.hidden_size, cfg.intermediate
         L = lambda s, n, k, b=True: fp8_linear_synthetic(seed + s, n, k, device, b)  # noqa: E731
         self.s_qkv, self.s_out = L(1, 3 * h, h), L(2, h, h)
@@ -99,7 +100,7 @@ class WanBlockB200:
         self.P = dist.get_world_size(group) if group is not None else 1
         sc, ss = rope_tables(cfg.head_dim, cfg.max_spatial_len)
         tc, ts = rope_tables(cfg.head_dim, cfg.max_temporal_len)
-        f = lambda a: torch.from_numpy(a).to(device, torch.bfloat16)  # noqa: E731
+        f = lambda a: torch.from_numpy(a).to(device, rope_dtype)  # noqa: E731
         self.s_cos, self.s_sin, self.t_cos, self.t_sin = f(sc), f(ss), f(tc), f(ts)
 
     # attention over the full token sequence of this rank's head group (Ulysses) -----------

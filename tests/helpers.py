@@ -21,3 +21,34 @@ def rel_err(got, ref) -> float:
 
 def to_np(t):
     return t.detach().float().cpu().numpy()
+
+
+def q8_linear_f32(lin):
+    """(W [N, K] f32, bias [N] f32 or None) of a GpuQuantizedLinear, decoded by the oracle
+    from GGUF Q8_0 blocks rebuilt out of the planar q / k-block-major scales."""
+    import oracle
+    q = lin.q.detach().cpu().numpy().astype(np.int8)
+    s = lin.scale.detach().cpu().numpy().view(np.uint16)  # [K/32, N]
+    N, K = q.shape
+    blocks = np.empty((N, K // 32, 34), np.uint8)
+    blocks[..., :2] = np.ascontiguousarray(s.T).view(np.uint8).reshape(N, K // 32, 2)
+    blocks[..., 2:] = q.view(np.uint8).reshape(N, K // 32, 32)
+    w = oracle.q8_0_dequantize(blocks.reshape(-1), N * K).reshape(N, K)
+    b = None if lin.bias is None else to_np(lin.bias)
+    return w, b
+
+
+def fp8_linear_f32(lin):
+    """(W [N, K] f32, bias or None) of an Fp8Linear: e4m3 bytes decoded by the oracle, times
+    the per-channel (or per-tensor) scale as Fp8Tensor::dequantize does."""
+    import oracle
+    vals = oracle.e4m3_bytes_to_f32(lin.weight.data.detach().cpu().numpy())
+    w = oracle.fp8_dequantize(vals, to_np(lin.weight.scale))
+    b = None if lin.bias is None else to_np(lin.bias)
+    return w, b
+
+
+def split_rows(wb, i):
+    """Split a stacked (W, b) pair at output row i (gate/up share one GEMM in the harness)."""
+    w, b = wb
+    return (w[:i], None if b is None else b[:i]), (w[i:], None if b is None else b[i:])
