@@ -14,6 +14,8 @@
 // General path (strided x, or a group larger than a 16-CTA cluster holds): two kernels.
 // Pass 1 writes per-chunk (count, mean, M2) partials to a caller workspace; pass 2 merges
 // its group's partials (Chan et al.'s pairwise update) and normalises (x is read twice).
+#include <algorithm>
+
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -223,6 +225,413 @@ __global__ void __launch_bounds__(kGnThreads, 2) gn_cluster_kernel(GnParams p) {
 }
 
 // ---------------------------------------------------------------------------------------
+// Streaming path for large contiguous groups (hundreds of KB and up).  Holding such a group
+// in registers takes a 16-CTA cluster per group, few of which fit on the GPU at once, and
+// each serialises load -> reduce -> store.  Here a persistent cluster of CS CTAs owns a
+// sequence of (batch, group)s; each CTA owns one contiguous slice of every group.
+//   warp 8 (producers): bulk-copies the slice into shared memory twice per group: lane 0
+//     through ring A from HBM (L2 evict-last), lane 1 through ring B from L2 (evict-first);
+//     each runs ahead across groups as far as its ring allows.
+//   warps 0-7 (consumers): pass 1 forms per-thread (count, mean, M2) of clamp(x) from sums
+//     shifted by the thread's first value, and max |x|; the partials merge (Chan et al.)
+//     over the warps, then every CTA pushes its partial into every cluster peer's shared
+//     memory and arrives on the peer's mbarrier; each CTA merges the CS partials in rank
+//     order (so all agree on mean and rstd) and tabulates gamma_c * rstd, beta_c for the
+//     group's channels.  Pass 2 normalises, applies the affine map and SiLU (packed f32x2
+//     arithmetic, and no clamps when max |x| and the affine bound show none can bite), and
+//     stores.
+// HBM sees one read and one write of x.
+// ---------------------------------------------------------------------------------------
+constexpr int kGrConsumers = 256;
+constexpr int kGrThreads = kGrConsumers + 32;
+constexpr int kGrChunk = 32768;  // bytes per ring stage
+// Two rings: A carries pass-1 chunks (from HBM), B pass-2 chunks (from L2), so the HBM
+// stream of the next group's pass 1 never waits behind the current group's pass 2.
+constexpr int kGrStagesA = 2;
+constexpr int kGrStagesB = 1;
+constexpr int kGrStages = kGrStagesA + kGrStagesB;  // 96 KB: two CTAs per SM
+constexpr int kGrMaxCluster = 16;
+constexpr int kGrMaxCg = 1024;   // channels per group the shared affine table holds
+
+struct Welford {
+  float n, mean, m2;
+};
+
+__device__ __forceinline__ Welford welford_merge(Welford a, Welford b) {
+  const float n = a.n + b.n;
+  if (n == 0.f) return a;
+  const float d = b.mean - a.mean;
+  const float fb = b.n / n;
+  return {n, fmaf(d, fb, a.mean), a.m2 + b.m2 + d * d * a.n * fb};
+}
+
+// packed f32x2 arithmetic (sm_100): two lanes per instruction
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t l2_policy(bool keep) {
+  uint64_t pol;
+  if (keep)
+    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  else
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// contiguous global -> shared copy completing on an mbarrier (bytes % 16 == 0, both 16-B
+// aligned)
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t map_rank(const void* p, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void arrive_cluster(uint32_t bar_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_addr)
+               : "memory");
+}
+
+// bounded wait with cluster-scope acquire (the arrivals come from peer CTAs)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort) {
+  const long long t0 = clock64();
+  uint32_t spins = 0;
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((++spins & 255u) == 0) {
+      if (*abort) return false;
+      if (clock64() - t0 > kWaitBudgetCycles) {
+        atomicCAS(&g_watchdog, 0, WD_CLUSTER_WAIT);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kGrConsumers) : "memory");
+}
+
+// grid = (n_clusters * CS), cluster = (CS, 1, 1), kGrThreads threads, dynamic smem =
+// kGrStages * kGrChunk (+ alignment).  x, y contiguous NCHW, HW % VE == 0, 16-B aligned.
+// p.chunk_vecs = vectors per CTA slice.
+template <typename T>
+__global__ void __launch_bounds__(kGrThreads, 2) gn_ring_kernel(GnParams p, int64_t BG) {
+  constexpr int VE = VecTraits<T>::kElems;
+  constexpr int kCWarps = kGrConsumers / 32;
+  extern __shared__ uint8_t gr_smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gr_smem_raw) + 127) &
+                                             ~uintptr_t(127));
+  __shared__ uint64_t full[kGrStages], empty[kGrStages], stats_bar[2];  // A stages first
+  // partials (n, mean, M2, max|x|) pushed by every rank, per parity
+  __shared__ float slot[2][kGrMaxCluster][4];
+  __shared__ Welford wpart[kCWarps];
+  __shared__ float wamax[kCWarps];
+  __shared__ float2 aff[kGrMaxCg];  // this group's (gamma_c * rstd, beta_c)
+  __shared__ float gb_max[2];       // max |gamma|, max |beta| over all channels
+  __shared__ int abort_flag_s;
+  volatile int* abort_flag = &abort_flag_s;
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int cs = (int)cluster.num_blocks();
+  const int64_t cid = blockIdx.x / cs, ncl = gridDim.x / cs;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGrStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kCWarps);
+    }
+    mbar_init(&stats_bar[0], cs);
+    mbar_init(&stats_bar[1], cs);
+    abort_flag_s = 0;
+    fence_mbar_init();
+  }
+  // peers arrive on these barriers: they must be initialised cluster-wide first
+  cluster.sync();
+
+  // n < 2^31 on this path: slice indices fit 32 bits
+  const int nvec = (int)(p.n / VE);
+  const int v0 = min(nvec, rank * (int)p.chunk_vecs);
+  const int v1 = min(nvec, v0 + (int)p.chunk_vecs);
+  const uint32_t slice_bytes = (uint32_t)(v1 - v0) * 16u;
+  const uint32_t nchunks = (slice_bytes + kGrChunk - 1) / kGrChunk;
+
+  if (warp == kCWarps) {
+    // ------------------------------------------------------------------ producers
+    // lane 0 feeds ring A (pass 1, HBM, L2 evict-last); lane 1 feeds ring B (pass 2, the
+    // same bytes again from L2, evict-first).  Each runs ahead as far as its ring allows.
+    if (lane < 2) {
+      const int pass = lane;
+      const uint32_t nst = pass == 0 ? kGrStagesA : kGrStagesB;
+      const uint32_t base = pass == 0 ? 0 : kGrStagesA;
+      const uint64_t pol = l2_policy(pass == 0);
+      uint32_t k = 0;
+      bool ok = true;
+      for (int64_t bg = cid; ok && bg < BG; bg += ncl) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(static_cast<const T*>(p.x) + bg * p.n) +
+                             (size_t)v0 * 16;
+        for (uint32_t c = 0; c < nchunks; ++c, ++k) {
+          const uint32_t st = base + k % nst, ph = (k / nst) & 1;
+          if (k >= nst && !mbar_wait(&empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bytes = min((uint32_t)kGrChunk, slice_bytes - c * kGrChunk);
+          mbar_arrive_expect_tx(&full[st], bytes);
+          bulk_load(ring + st * kGrChunk, src + (size_t)c * kGrChunk, bytes, &full[st], pol);
+        }
+      }
+      if (!ok) {
+        // let the copies in flight land before the CTA can exit (bounded)
+        for (uint32_t j = k > nst ? k - nst : 0; j < k; ++j)
+          mbar_wait(&full[base + j % nst], (j / nst) & 1, nullptr, WD_TMA_WAIT);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ consumers
+    // A failed (expired) wait sets the shared abort flag before it returns.  Warps never
+    // leave the group loop on their own: they skip work once `ok` is false and leave
+    // together right after a named barrier, where every consumer sees the flag.
+    const T* gam = static_cast<const T*>(p.gamma);
+    const T* bet = static_cast<const T*>(p.beta);
+    // max |gamma|, max |beta| over all channels: bounds the affine output of a group
+    {
+      float gm = 0.f, bm = 0.f;
+      for (int64_t c = threadIdx.x; c < p.C; c += kGrConsumers) {
+        gm = fmaxf(gm, fabsf(to_f32(gam[c])));
+        bm = fmaxf(bm, fabsf(to_f32(bet[c])));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+      }
+      if (lane == 0) wpart[warp] = Welford{gm, bm, 0.f};
+      consumer_sync();
+      if (threadIdx.x == 0) {
+        for (int i = 1; i < kCWarps; ++i) {
+          gm = fmaxf(gm, wpart[i].n);
+          bm = fmaxf(bm, wpart[i].mean);
+        }
+        gb_max[0] = fmaxf(gm, wpart[0].n);
+        gb_max[1] = fmaxf(bm, wpart[0].mean);
+      }
+      consumer_sync();
+    }
+    const float gmax = gb_max[0], bmax = gb_max[1];
+    const uint32_t vpc = (uint32_t)(p.HW / VE);  // vectors per channel
+    const float inv_vpc = 1.0f / (float)vpc;
+    uint32_t ka = 0, kb = 0;  // chunks taken from ring A / ring B
+    int it = 0;
+    bool ok = true;  // warp-uniform
+    for (int64_t bg = cid; bg < BG; bg += ncl, ++it) {
+      const int64_t g = bg % p.G;
+      uint4* yv = reinterpret_cast<uint4*>(static_cast<T*>(p.y) + bg * p.n) + v0;
+
+      // ---- pass 1: statistics of clamp(x) and max |x|
+      const uint64_t zero2 = f2(0.f, 0.f);
+      uint64_t sh2 = zero2, s1 = zero2, s2 = zero2;
+      float amax = 0.f, cnt = 0.f;
+      bool first = true;
+      for (uint32_t c = 0; ok && c < nchunks; ++c, ++ka) {
+        const uint32_t st = ka % kGrStagesA, ph = (ka / kGrStagesA) & 1;
+        if (!mbar_wait_warp(&full[st], ph, abort_flag, WD_CONVERT_WAIT)) {
+          ok = false;
+          break;
+        }
+        const uint32_t cv = min((uint32_t)kGrChunk, slice_bytes - c * kGrChunk) / 16u;
+        const uint4* sv = reinterpret_cast<const uint4*>(ring + st * kGrChunk);
+        for (uint32_t i = threadIdx.x; i < cv; i += kGrConsumers) {
+          float f[VE];
+          unpack<T>(sv[i], f);
+#pragma unroll
+          for (int e = 0; e < VE; ++e) {
+            amax = fmaxf(amax, fabsf(f[e]));
+            f[e] = clamp65k(f[e]);
+          }
+          if (first) {
+            sh2 = f2(f[0], f[0]);
+            first = false;
+          }
+#pragma unroll
+          for (int e = 0; e < VE; e += 2) {
+            const uint64_t d = f2_sub(f2(f[e], f[e + 1]), sh2);
+            s1 = f2_add(s1, d);
+            s2 = f2_fma(d, d, s2);
+          }
+          cnt += (float)VE;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+      }
+      Welford w{cnt, 0.f, 0.f};
+      if (cnt > 0.f) {
+        float a, b, shift, dummy;
+        f2_split(s1, a, b);
+        const float t1 = a + b;
+        f2_split(s2, a, b);
+        const float t2 = a + b;
+        f2_split(sh2, shift, dummy);
+        const float m = t1 / cnt;
+        w.mean = shift + m;
+        w.m2 = fmaxf(t2 - t1 * m, 0.f);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        Welford b{__shfl_xor_sync(0xffffffffu, w.n, o), __shfl_xor_sync(0xffffffffu, w.mean, o),
+                  __shfl_xor_sync(0xffffffffu, w.m2, o)};
+        w = welford_merge(w, b);
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      }
+      if (lane == 0) {
+        wpart[warp] = w;
+        wamax[warp] = amax;
+      }
+      consumer_sync();
+      if (*abort_flag) break;  // uniform across the consumer warps
+      const int par = it & 1;
+      if (threadIdx.x == 0) {
+        Welford t = wpart[0];
+        float am = wamax[0];
+        for (int i = 1; i < kCWarps; ++i) {
+          t = welford_merge(t, wpart[i]);
+          am = fmaxf(am, wamax[i]);
+        }
+        // push the partial into every rank's slot[par][rank], then arrive there
+        for (int r = 0; r < cs; ++r) {
+          const uint32_t a = map_rank(&slot[par][rank][0], r);
+          st_cluster_f32(a, t.n);
+          st_cluster_f32(a + 4, t.mean);
+          st_cluster_f32(a + 8, t.m2);
+          st_cluster_f32(a + 12, am);
+          arrive_cluster(map_rank(&stats_bar[par], r));
+        }
+      }
+      __syncwarp();
+      ok = __all_sync(0xffffffffu, mbar_wait_cluster(&stats_bar[par], (it >> 1) & 1, abort_flag));
+      float mean = 0.f, rstd = 0.f, gamax = 0.f;
+      if (ok) {
+        Welford t{slot[par][0][0], slot[par][0][1], slot[par][0][2]};
+        gamax = slot[par][0][3];
+        for (int r = 1; r < cs; ++r) {
+          t = welford_merge(t, Welford{slot[par][r][0], slot[par][r][1], slot[par][r][2]});
+          gamax = fmaxf(gamax, slot[par][r][3]);
+        }
+        mean = t.mean;
+        rstd = rsqrtf(t.m2 / t.n + p.eps);
+        for (int c = threadIdx.x; c < (int)p.cg; c += kGrConsumers)
+          aff[c] = make_float2(to_f32(gam[g * p.cg + c]) * rstd, to_f32(bet[g * p.cg + c]));
+      }
+      consumer_sync();
+      if (!ok) continue;  // leaves at the next named barrier (or at the end)
+      // no clamp can bite when |x| <= 65000 and |(x - mean) * w + b| <= 65000 for all x, c
+      const bool no_clamp =
+          gamax <= kClamp && (gamax + fabsf(mean)) * gmax * rstd + bmax <= kClamp;
+      const uint64_t mean2 = f2(mean, mean);
+      const uint64_t half2 = f2(0.5f, 0.5f);
+
+      // ---- pass 2: normalise, affine, activation, store
+      for (uint32_t c = 0; c < nchunks; ++c, ++kb) {
+        const uint32_t st = kGrStagesA + kb % kGrStagesB, ph = (kb / kGrStagesB) & 1;
+        if (!mbar_wait_warp(&full[st], ph, abort_flag, WD_CONVERT_WAIT)) {
+          ok = false;
+          break;
+        }
+        const uint32_t c0 = c * (kGrChunk / 16);  // first vector of this chunk in the slice
+        const uint32_t cv = min((uint32_t)kGrChunk, slice_bytes - c * kGrChunk) / 16u;
+        const uint4* sv = reinterpret_cast<const uint4*>(ring + st * kGrChunk);
+        for (uint32_t i = threadIdx.x; i < cv; i += kGrConsumers) {
+          float f[VE];
+          unpack<T>(sv[i], f);
+          // channel of this vector: vi / vpc via a float estimate and one correction step
+          const uint32_t vi = (uint32_t)v0 + c0 + i;
+          uint32_t q = __float2uint_rz((float)vi * inv_vpc);
+          const int32_t rem = (int32_t)(vi - q * vpc);
+          q = rem < 0 ? q - 1 : (rem >= (int32_t)vpc ? q + 1 : q);
+          const float2 ab = aff[q];
+          const uint64_t w2 = f2(ab.x, ab.x), b2 = f2(ab.y, ab.y);
+          if (no_clamp) {
+#pragma unroll
+            for (int e = 0; e < VE; e += 2) {
+              uint64_t v = f2_fma(f2_sub(f2(f[e], f[e + 1]), mean2), w2, b2);
+              if (p.act == SP_ACT_SILU) {
+                float t0, t1;
+                f2_split(f2_mul(v, half2), t0, t1);
+                const uint64_t sg = f2_fma(f2(tanh_approx(t0), tanh_approx(t1)), half2, half2);
+                v = f2_mul(v, sg);
+              }
+              f2_split(v, f[e], f[e + 1]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < VE; ++e)
+              f[e] = apply_act((clamp65k(f[e]) - mean) * ab.x + ab.y, p.act);
+          }
+          yv[c0 + i] = pack<T>(f);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+      }
+    }
+  }
+  // no CTA may leave while a peer could still push into its shared memory (the barrier is
+  // warp-aligned: reconverge the producer warp and any consumer lanes first)
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------------
 // General path: strided input, or groups beyond one cluster's capacity.
 // ---------------------------------------------------------------------------------------
 struct GnGeneralParams {
@@ -315,18 +724,35 @@ constexpr int64_t kGeneralChunk = 16384;
 
 struct GnPlan {
   bool cluster_path;
+  bool stream_path;  // persistent streaming clusters (large groups)
   int cs;      // cluster size
   int vpt;     // vectors per thread
   int64_t chunk_vecs;
   int64_t nchunks;  // general path
 };
 
-GnPlan plan_gn(int64_t B, int64_t G, int64_t n, bool contiguous, bool vec_ok, int vec_elems) {
+// Groups of at least this many bytes take the streaming path.
+constexpr int64_t kStreamMinGroupBytes = 256 * 1024;
+
+GnPlan plan_gn(int64_t B, int64_t G, int64_t cg, int64_t n, bool contiguous, bool vec_ok,
+               int vec_elems) {
   GnPlan pl{};
   const int64_t nvec = n / vec_elems;
   // 16 vectors (64 f32) per thread for f32, 8 vectors (64 halves) for 16-bit types: both
   // stay within the 128 registers that two resident CTAs per SM allow.
   const int max_vpt = vec_elems == 4 ? 16 : 8;
+  const int64_t group_bytes = n * (16 / vec_elems);
+  if (contiguous && vec_ok && n < (1LL << 31) && group_bytes >= kStreamMinGroupBytes &&
+      cg <= kGrMaxCg) {
+    // two CTAs per SM; the smallest cluster (>= 2) that still gives every CTA slot a
+    // slice (measured on B200: larger slices per CTA beat keeping fewer groups in flight)
+    int cs = 2;
+    while (cs < kMaxCluster && B * G * cs < (2LL * num_sms() * 7) / 8) cs *= 2;
+    pl.stream_path = true;
+    pl.cs = cs;
+    pl.chunk_vecs = (nvec + cs - 1) / cs;
+    return pl;
+  }
   if (contiguous && vec_ok && n < (1LL << 31)) {
     static const int kVpts[] = {1, 2, 4, 8, 16};
     int best_cs = 0, best_vpt = 0;
@@ -406,6 +832,57 @@ int launch_cluster_vpt(const GnParams& p, int cs, int vpt, int64_t BG, cudaStrea
   }
 }
 
+constexpr int kGrSmem = kGrStages * kGrChunk + 128;
+
+template <typename T>
+int launch_stream(const GnParams& p, int cs, int64_t BG, cudaStream_t stream) {
+  auto kern = gn_ring_kernel<T>;
+  static unsigned long long attr_set = 0;
+  if (first_time_on_device(&attr_set)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGrSmem);
+    if (e != cudaSuccess) {
+      __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
+      return set_error(SP_ERR_LAUNCH, "groupnorm: kernel attribute failed: %s",
+                       cudaGetErrorString(e));
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kGrThreads, 1, 1);
+  cfg.dynamicSmemBytes = kGrSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // as many clusters as can be resident at once (each loops over groups), found once per
+  // device and cluster size
+  static int resident[64][5] = {};
+  const int dev = current_device();
+  int lg = 0;
+  while ((1 << lg) < cs) ++lg;
+  int ncl = (dev >= 0 && dev < 64) ? __atomic_load_n(&resident[dev][lg], __ATOMIC_ACQUIRE) : 0;
+  if (ncl <= 0) {
+    cfg.gridDim = dim3((unsigned)(cs * (2 * num_sms() / cs)), 1, 1);
+    if (cudaOccupancyMaxActiveClusters(&ncl, kern, &cfg) != cudaSuccess || ncl <= 0) {
+      cudaGetLastError();
+      ncl = 2 * num_sms() / cs;
+    }
+    if (dev >= 0 && dev < 64) __atomic_store_n(&resident[dev][lg], ncl, __ATOMIC_RELEASE);
+  }
+  const int64_t nclusters = std::min<int64_t>(ncl, BG);
+  cfg.gridDim = dim3((unsigned)(nclusters * cs), 1, 1);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, BG);
+  if (e != cudaSuccess)
+    return set_error(SP_ERR_LAUNCH, "groupnorm stream launch (cs=%d) failed: %s", cs,
+                     cudaGetErrorString(e));
+  return SP_OK;
+}
+
 template <typename T>
 int launch_general(const GnGeneralParams& p, int64_t BG, cudaStream_t s) {
   dim3 grid((unsigned)p.nchunks, (unsigned)BG, 1);
@@ -464,9 +941,9 @@ size_t sp_groupnorm_act_workspace_size(int64_t B, int64_t C, int64_t H, int64_t 
     return sp::gn_nhwc_workspace_bytes(B, C, H, W, es, groups);
   const bool contiguous = sp::is_contiguous_nchw(B, C, H, W, x_strides);
   const int vec = 16 / es;
-  const sp::GnPlan pl = sp::plan_gn(B, groups, C / groups * H * W, contiguous,
+  const sp::GnPlan pl = sp::plan_gn(B, groups, C / groups, C / groups * H * W, contiguous,
                                     contiguous && (H * W) % vec == 0, vec);
-  return pl.cluster_path ? 0 : sp::general_workspace_bytes(B, C, H, W, groups);
+  return (pl.cluster_path || pl.stream_path) ? 0 : sp::general_workspace_bytes(B, C, H, W, groups);
 }
 
 int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y, int64_t B,
@@ -502,8 +979,16 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
     for (int i = 0; i < 4; ++i) st[i] = x_strides[i];
   const int vec_elems = 16 / es;
   const bool vec_ok = contiguous && (HW % vec_elems == 0) && aligned(x, 16) && aligned(y, 16);
-  const GnPlan pl = plan_gn(B, groups, n, contiguous, vec_ok, vec_elems);
+  const GnPlan pl = plan_gn(B, groups, cg, n, contiguous, vec_ok, vec_elems);
 
+  if (pl.stream_path) {
+    GnParams p{x, gamma, beta, y, C, HW, groups, cg, n, pl.chunk_vecs, eps, act};
+    switch (dtype) {
+      case SP_F32: return launch_stream<float>(p, pl.cs, B * groups, s);
+      case SP_F16: return launch_stream<__half>(p, pl.cs, B * groups, s);
+      default: return launch_stream<__nv_bfloat16>(p, pl.cs, B * groups, s);
+    }
+  }
   if (pl.cluster_path) {
     GnParams p{x, gamma, beta, y, C, HW, groups, cg, n, pl.chunk_vecs, eps, act};
     switch (dtype) {

@@ -68,6 +68,24 @@ def test_groupnorm_ragged_and_general_paths(shape, groups):
     assert rel_err(to_np(y), ref) < TOL_F32
 
 
+@pytest.mark.parametrize("shape,groups,offset", [((1, 48, 100, 100), 3, 1000.0),
+                                                 ((3, 64, 64, 64), 2, -300.0)])
+def test_groupnorm_streaming_path_offset_mean(shape, groups, offset):
+    # groups of 640 KB / 2 MB f32 take the persistent streaming path (per-thread sums shifted
+    # by the thread's first value, merged across the cluster); a mean far from zero checks
+    # that the variance does not cancel
+    x, _, _ = make(shape, seed=4)
+    x = (x / 3.0 + offset).astype(np.float32)
+    C = shape[1]
+    rng = np.random.default_rng(5)
+    g = rng.uniform(0.5, 1.5, C).astype(np.float32)
+    b = rng.uniform(-0.5, 0.5, C).astype(np.float32)
+    ref = oracle.groupnorm_act(x, g, b, groups, 1e-5, silu=True)
+    y = groupnorm_silu(torch.from_numpy(x).cuda(), torch.from_numpy(g).cuda(),
+                       torch.from_numpy(b).cuda(), GroupNormSiLuOptions(groups, 1e-5))
+    assert rel_err(to_np(y), ref) < TOL_F32
+
+
 def test_groupnorm_strided_input():
     # an H/W-transposed view is neither NCHW- nor NHWC-contiguous: the general strided path
     x, g, b = make((2, 64, 16, 24), seed=4)
