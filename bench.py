@@ -127,6 +127,11 @@ def cpu_unet_step_time(max_seconds: float = 60.0, min_steps: int = 1, max_steps:
     return sum(times) / len(times), len(times), oracle.get_threads()
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one (2,8,4096,40) attention launch, from the
+# ncu capture summarised in profiles/flash_attn_fwd_2x8x4096x40_bf16.md
+ATTN_D40_TRAFFIC_BYTES = 15_822_592
+
+
 def run_reference(args):
     ws, rank, _ = dist_env()
     if rank != 0:
@@ -373,7 +378,11 @@ def run_b200(args):
                          "peak_source": f"{peak_src} bf16_tflops_sustained",
                          "launch_ms": attn_launch_ms, "share_of_step": attn_share,
                          "timing": attn_timing,
-                         "traffic": None},
+                         # ncu dram read+write of one (2,8,4096,40) self-attention launch
+                         # (the step's dominant attention shape): Q+K+V read once, O left
+                         # in L2 -- equal to the algorithmic input bytes (15.7 MB)
+                         "traffic": ATTN_D40_TRAFFIC_BYTES,
+                         "traffic_case": "(2,8,4096,40) launch, profiles/flash_attn_fwd_2x8x4096x40_bf16.md"},
             "achieved_step_tflops": flops["total"] / ms / 1e9,
             "kernels": kernels,
             "cpu_baseline": cpu,

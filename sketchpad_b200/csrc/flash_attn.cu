@@ -11,18 +11,21 @@
 //   warp 9      TMEM owner + MMA issuer (one elected lane), per key tile j:
 //                 S_t = Q_t K_j^T   (M=128, N=128, K=D padded to 16; f32 in TMEM)
 //                 O_t += P_t V_j    (M=128, N=Dv padded to 64, K=128; P_t read from TMEM)
-//               issued as S_0(0) S_1(0) | PV_0(j) S_0(j+1) PV_1(j) S_1(j+1) | ... so the tensor
-//               core works on one tile while the other tile's softmax runs.
+//               so the tensor core works on one tile while the other tile's softmax runs.
+//               Dv > 64 (P aliases S): S_0(0) S_1(0) | PV_0(j) S_0(j+1) PV_1(j) S_1(j+1) | ...
+//               Dv <= 64 (P has its own columns): S_t(j+1) is issued as soon as the softmax
+//               has loaded S_t(j) into registers (s_free barrier), then PV_0(j), PV_1(j).
 //   softmax:    one query row per thread (= TMEM lane): tcgen05.ld S, mask, exp2, write P
 //               (16-bit, 2 per column) back to
 //               TMEM with tcgen05.st; O is rescaled in TMEM only when the row max grows by
 //               more than 2^8 (P and the row sum always share one reference maximum).
 // TMEM per tile t (base 256*t): Dv <= 64: S [0,128) P [128,192) O [192,256);
 //                              Dv  > 64: S and P share [0,128) (P in [0,64)), O [128,256).
-// A commit makes its mbarrier wait for every earlier tcgen05 op of the issuing thread, so
-// when S_t(j) is ready, PV_t(j-1) has completed: P_t may be rewritten and O_t rescaled
-// without further waits.  When P aliases S, S_t(j+1) is issued after PV_t(j) by the same
-// thread and the tensor core executes a thread's MMAs in issue order.
+// A commit makes its mbarrier wait for every earlier tcgen05 op of the issuing thread.  When
+// P aliases S, S_t(j) is issued after PV_t(j-1), so once S_t(j) is ready P_t may be rewritten
+// and O_t rescaled without further waits (and the tensor core executes a thread's MMAs in
+// issue order).  With the early-S schedule the softmax instead waits for PV_t(j-1)
+// (o_done) after computing its exponentials, just before it rescales O_t and writes P_t.
 // Q, K, V tiles in shared memory are 128 rows x 64 elements (128 B) boxes with the 128B
 // swizzle: the canonical K-major layout for Q and K, MN-major for V.
 #include "common.cuh"
