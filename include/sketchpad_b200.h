@@ -93,6 +93,18 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
                      float eps, int act, int dtype, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* GroupNorm (+ SiLU) of x + x_add[b, c]: the ResBlock's time-embedding add (h + temb[:, :,
+ * None, None]) followed by its second GroupNorm(+SiLU), as ResBlockCubeCL::forward does in two
+ * steps (crates/sketchpad-unet/src/cubecl.rs:115-124; CPU: ResBlock::forward,
+ * crates/sketchpad-unet/src/blocks.rs:123-150), in one pass over x.  x_add is [B, C] in the
+ * same dtype (contiguous); the sum is formed in f32 and never stored.  x must be dense
+ * channels-last (NHWC) -- the layout the UNet keeps -- otherwise SP_ERR_SHAPE.  Workspace:
+ * sp_groupnorm_act_workspace_size() for the same arguments. */
+int sp_groupnorm_add_act(const void* x, const void* x_add, const void* gamma, const void* beta,
+                         void* y, int64_t B, int64_t C, int64_t H, int64_t W,
+                         const int64_t x_strides[4], int64_t groups, float eps, int act,
+                         int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 /* GroupNorm (+ SiLU) that allocates nothing.  No counterpart in the reference: it exists
  * for callers that cannot hand the library device memory -- hosts whose allocator must not
  * be used while they run, or FFI hosts holding raw device pointers without access to a CUDA

@@ -40,6 +40,8 @@ SIGNATURES = {
     "sp_groupnorm_act_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64p, _i64, _int]),
     "sp_groupnorm_act": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p, _i64, _f,
                                 _int, _int, _vp, _sz, _vp]),
+    "sp_groupnorm_add_act": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p,
+                                    _i64, _f, _int, _int, _vp, _sz, _vp]),
     "sp_groupnorm_act_noalloc_max_scratch_bytes": (_sz, []),
     "sp_groupnorm_act_noalloc": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p, _i64,
                                         _f, _int, _int, _vp]),

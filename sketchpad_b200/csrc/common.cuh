@@ -52,8 +52,8 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, const 
 bool gn_nhwc_applicable(int64_t B, int64_t C, int64_t H, int64_t W, const int64_t* x_strides, int es,
                         int64_t groups);
 size_t gn_nhwc_workspace_bytes(int64_t B, int64_t C, int64_t H, int64_t W, int es, int64_t groups);
-int gn_nhwc_launch(const void* x, const void* gamma, const void* beta, void* y, int64_t B,
-                   int64_t C, int64_t H, int64_t W, int64_t groups, float eps, int act, int dtype,
-                   void* workspace, size_t workspace_bytes, cudaStream_t s);
+int gn_nhwc_launch(const void* x, const void* x_add, const void* gamma, const void* beta, void* y,
+                   int64_t B, int64_t C, int64_t H, int64_t W, int64_t groups, float eps, int act,
+                   int dtype, void* workspace, size_t workspace_bytes, cudaStream_t s);
 
 }  // namespace sp

@@ -971,8 +971,8 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
 
   const int64_t HW = H * W, cg = C / groups, n = cg * HW;
   if (gn_nhwc_applicable(B, C, H, W, x_strides, es, groups))
-    return gn_nhwc_launch(x, gamma, beta, y, B, C, H, W, groups, eps, act, dtype, workspace,
-                          workspace_bytes, s);
+    return gn_nhwc_launch(x, nullptr, gamma, beta, y, B, C, H, W, groups, eps, act, dtype,
+                          workspace, workspace_bytes, s);
   int64_t st[4] = {C * HW, HW, W, 1};
   const bool contiguous = is_contiguous_nchw(B, C, H, W, x_strides);
   if (!contiguous)
@@ -1014,6 +1014,35 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
     case SP_F16: return launch_general<__half>(p, B * groups, s);
     default: return launch_general<__nv_bfloat16>(p, B * groups, s);
   }
+}
+
+int sp_groupnorm_add_act(const void* x, const void* x_add, const void* gamma, const void* beta,
+                         void* y, int64_t B, int64_t C, int64_t H, int64_t W,
+                         const int64_t x_strides[4], int64_t groups, float eps, int act,
+                         int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace sp;
+  clear_error();
+  if (!x || !x_add || !gamma || !beta || !y)
+    return set_error(SP_ERR_INVALID_ARG, "groupnorm_add: null tensor pointer");
+  if (B <= 0 || C <= 0 || H <= 0 || W <= 0 || groups <= 0)
+    return set_error(SP_ERR_INVALID_ARG, "groupnorm_add: non-positive dimension");
+  if (C % groups != 0)
+    return set_error(SP_ERR_SHAPE, "channels (%lld) must be divisible by num_groups (%lld)",
+                     (long long)C, (long long)groups);
+  if (act != SP_ACT_NONE && act != SP_ACT_SILU)
+    return set_error(SP_ERR_INVALID_ARG, "groupnorm_add: unknown activation %d", act);
+  const int es = dtype_size(dtype);
+  if (!es) return set_error(SP_ERR_DTYPE, "groupnorm_add: unknown dtype %d", dtype);
+  if (B * groups > 65535)
+    return set_error(SP_ERR_SHAPE, "groupnorm_add: batch*groups (%lld) exceeds 65535",
+                     (long long)(B * groups));
+  if (!gn_nhwc_applicable(B, C, H, W, x_strides, es, groups))
+    return set_error(SP_ERR_SHAPE,
+                     "groupnorm_add: x must be dense channels-last (NHWC) with C a multiple of "
+                     "the 16-byte vector and at most 1024 groups");
+  if (int rc = require_sm100()) return rc;
+  return gn_nhwc_launch(x, x_add, gamma, beta, y, B, C, H, W, groups, eps, act, dtype, workspace,
+                        workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

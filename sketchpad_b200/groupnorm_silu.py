@@ -30,7 +30,7 @@ class GroupNormSiLuOptions:
 
 
 def _run(input: torch.Tensor, weight, bias, options: GroupNormSiLuOptions, act: int,
-         out=None) -> torch.Tensor:
+         out=None, add=None) -> torch.Tensor:
     if input.dim() != 4:
         raise ValueError("input must be [batch, channels, height, width]")
     dev = require_cuda(input, weight, bias, out)
@@ -60,16 +60,27 @@ def _run(input: torch.Tensor, weight, bias, options: GroupNormSiLuOptions, act: 
     ws = None
     if ws_bytes:
         ws = torch.empty((ws_bytes + 3) // 4, dtype=torch.float32, device=dev)
+    nws = 0 if ws is None else ws.numel() * 4
+    if add is not None:
+        if tuple(add.shape) != (B, C):
+            raise ValueError("add must be [batch, channels]")
+        a = (add if add.dtype == dt else add.to(dt)).contiguous()
+        _lib.call("sp_groupnorm_add_act", ptr(input), ptr(a), ptr(w), ptr(b), ptr(out), B, C, H,
+                  W, strides, G, float(options.eps), act, code, ptr(ws), nws, stream_ptr(dev))
+        return out
     _lib.call("sp_groupnorm_act", ptr(input), ptr(w), ptr(b), ptr(out), B, C, H, W, strides, G,
-              float(options.eps), act, code, ptr(ws), 0 if ws is None else ws.numel() * 4,
-              stream_ptr(dev))
+              float(options.eps), act, code, ptr(ws), nws, stream_ptr(dev))
     return out
 
 
 def groupnorm_silu(input, weight, bias, options: GroupNormSiLuOptions = GroupNormSiLuOptions(),
-                   out=None):
-    """silu(groupnorm(x)) in one pass over HBM (groupnorm_silu.rs:232)."""
-    return _run(input, weight, bias, options, _lib.SP_ACT_SILU, out)
+                   out=None, add=None):
+    """silu(groupnorm(x)) in one pass over HBM (groupnorm_silu.rs:232).
+
+    add: optional [batch, channels] tensor; normalises x + add[:, :, None, None] without
+    storing the sum (ResBlock's time-embedding add, crates/sketchpad-unet/src/cubecl.rs:115-124).
+    Channels-last x only."""
+    return _run(input, weight, bias, options, _lib.SP_ACT_SILU, out, add)
 
 
 def groupnorm(input, weight, bias, options: GroupNormSiLuOptions = GroupNormSiLuOptions(),

@@ -306,10 +306,13 @@ class UNetB200:
         k = w.shape[-1]
         return F.conv2d(x, w, self.p[name + ".bias"], stride=stride, padding=k // 2)
 
-    def _gn(self, x, name, silu):
+    def _gn(self, x, name, silu, add=None):
         self.kernel_launches += 1
+        w, b = self.p[name + ".weight"], self.p[name + ".bias"]
+        if add is not None:  # GroupNorm(+SiLU) of x + add[:, :, None, None], one pass
+            return groupnorm_silu(x, w, b, GroupNormSiLuOptions(32, 1e-5), add=add)
         f = groupnorm_silu if silu else groupnorm
-        return f(x, self.p[name + ".weight"], self.p[name + ".bias"], GroupNormSiLuOptions(32, 1e-5))
+        return f(x, w, b, GroupNormSiLuOptions(32, 1e-5))
 
     def _ln(self, x, name):
         self.kernel_launches += 1
@@ -336,8 +339,7 @@ class UNetB200:
         h = self._gn(x, p + ".norm1", True)
         h = self._conv(h, p + ".conv1")
         t = self._lin(temb_silu, p + ".time_emb_proj")
-        h = h + t[:, :, None, None]
-        h = self._gn(h, p + ".norm2", True)
+        h = self._gn(h, p + ".norm2", True, add=t)  # norm2(h + t[:, :, None, None])
         h = self._conv(h, p + ".conv2")
         return h + residual
 

@@ -115,6 +115,33 @@ def test_groupnorm_channels_last(shape, dtype):
     assert torch.equal(y, y2)  # the ticket counters reset: a second call is identical
 
 
+@pytest.mark.parametrize("shape", [(2, 320, 64, 64), (2, 1280, 16, 16), (2, 2560, 8, 8)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_groupnorm_add_channels_last(shape, dtype):
+    # ResBlock's norm2(h + temb[:, :, None, None]) in one pass: the oracle normalises the
+    # explicit sum (formed in f32 from the same rounded inputs)
+    x, g, b = make(shape, seed=11)
+    B, C = shape[:2]
+    t = np.random.default_rng(12).standard_normal((B, C)).astype(np.float32)
+    xt = torch.from_numpy(x).cuda().to(dtype).to(memory_format=torch.channels_last)
+    tt = torch.from_numpy(t).cuda().to(dtype)
+    xs = to_np(xt) + to_np(tt)[:, :, None, None]
+    ref = oracle.groupnorm_act(xs, to_np(torch.from_numpy(g).to(dtype)),
+                               to_np(torch.from_numpy(b).to(dtype)), 32, 1e-5, silu=True)
+    y = groupnorm_silu(xt, torch.from_numpy(g).cuda().to(dtype), torch.from_numpy(b).cuda().to(dtype),
+                       add=tt)
+    assert y.is_contiguous(memory_format=torch.channels_last)
+    tol = TOL_F32 if dtype == torch.float32 else TOL_HALF
+    assert rel_err(to_np(y), ref) < tol
+
+
+def test_groupnorm_add_rejects_nchw():
+    x = torch.zeros(1, 32, 4, 4, device="cuda")
+    with pytest.raises(Exception, match="channels-last"):
+        groupnorm_silu(x, torch.ones(32, device="cuda"), torch.zeros(32, device="cuda"),
+                       add=torch.zeros(1, 32, device="cuda"))
+
+
 def test_groupnorm_clamps_large_values():
     x, g, b = make((1, 32, 4, 4), seed=5)
     x[0, 0, 0, 0] = 1e6

@@ -12,7 +12,9 @@ import sketchpad_b200.unet as U
 from oracle.unet import OracleUNet
 
 
-def _gn(x, w, b, silu):
+def _gn(x, w, b, silu, add=None):
+    if add is not None:
+        x = x + add[:, :, None, None]
     y = F.group_norm(x.float(), 32, w.float(), b.float(), 1e-5)
     y = F.silu(y) if silu else y
     if x.is_contiguous(memory_format=torch.channels_last) and not x.is_contiguous():
@@ -26,7 +28,8 @@ def _ln(x, w, b, eps, unbiased, out=None):
 
 
 def test_unet_harness_wiring_matches_oracle(monkeypatch):
-    monkeypatch.setattr(U, "groupnorm_silu", lambda x, w, b, opt, out=None: _gn(x, w, b, True))
+    monkeypatch.setattr(U, "groupnorm_silu",
+                        lambda x, w, b, opt, out=None, add=None: _gn(x, w, b, True, add))
     monkeypatch.setattr(U, "groupnorm", lambda x, w, b, opt, out=None: _gn(x, w, b, False))
     monkeypatch.setattr(U, "layer_norm", _ln)
     monkeypatch.setattr(U, "flash_attention", lambda q, k, v, out=None: out.copy_(
