@@ -122,6 +122,18 @@ int sp_groupnorm_act_noalloc(const void* x, const void* gamma, const void* beta,
                              const int64_t x_strides[4], int64_t groups, float eps, int act,
                              int dtype, void* stream);
 
+/* Gated-linear-unit gate of a feed-forward, one pass over the stacked [rows, 2F] hidden:
+ *   SP_GLU_GEGLU:  y = x[:, :F] * gelu(x[:, F:])  (erf GELU; UNet FeedForward::forward,
+ *                  crates/sketchpad-unet/src/blocks.rs:446-458)
+ *   SP_GLU_SWIGLU: y = silu(x[:, :F]) * x[:, F:]  (SwiGluFfn::forward,
+ *                  crates/sketchpad-core/src/glu.rs:91-96; WanExpert::forward,
+ *                  crates/sketchpad-dit/src/wan.rs:330-337)
+ * Row strides in elements (x >= 2F, y >= F); F and both strides multiples of the 16-byte
+ * vector; x, y 16-byte aligned; f32 arithmetic for every dtype. */
+typedef enum sp_glu_kind { SP_GLU_GEGLU = 0, SP_GLU_SWIGLU = 1 } sp_glu_kind;
+int sp_glu_gate(const void* x, void* y, int64_t rows, int64_t F, int64_t x_row_stride,
+                int64_t y_row_stride, int kind, int dtype, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * Q8_0 (GGUF) weights.
  * A Q8_0 row of in_f values is in_f/32 blocks of 34 bytes: f16 LE scale + 32 int8.

@@ -30,6 +30,7 @@ import torch
 import torch.nn.functional as F
 
 from .attention import flash_attention
+from .glu import swiglu
 from .layernorm import layer_norm
 from .quantized_matmul import GpuQuantizedLinear
 
@@ -135,8 +136,7 @@ class _SwiGlu:
         self.i = i
 
     def forward(self, x):
-        gu = self.gate_up(x)
-        return self.down(F.silu(gu[..., : self.i]) * gu[..., self.i:])
+        return self.down(swiglu(self.gate_up(x)))  # silu(gate) * up, one pass
 
 
 def _ln(x):

@@ -30,6 +30,7 @@ import torch.nn.functional as F
 
 from .attention import flash_attention
 from .groupnorm_silu import GroupNormSiLuOptions, groupnorm, groupnorm_silu
+from .glu import geglu
 from .layernorm import layer_norm
 
 
@@ -371,8 +372,8 @@ class UNetB200:
             y = y + self._xattn(self._ln(y, tb + ".norm1"), tb + ".attn1", None)
             y = y + self._xattn(self._ln(y, tb + ".norm2"), tb + ".attn2", ctx)
             hdn = self._lin(self._ln(y, tb + ".norm3"), tb + ".ff.net_0")
-            half = hdn.shape[-1] // 2
-            y = y + self._lin(hdn[..., :half] * F.gelu(hdn[..., half:]), tb + ".ff.net_2")
+            self.kernel_launches += 1
+            y = y + self._lin(geglu(hdn), tb + ".ff.net_2")  # value * gelu(gate), one pass
         y = self._lin(y, p + ".proj_out", wkey=".wmat")  # [b, h*w, c] == NHWC memory
         return y.view(b, h, w, c).permute(0, 3, 1, 2) + residual
 

@@ -32,6 +32,7 @@ import torch.nn.functional as F
 
 from .attention import flash_attention
 from .flux import apply_rope, rope_tables
+from .glu import swiglu
 from .layernorm import layer_norm
 from .quantization import Fp8Format, Fp8Linear, Fp8Tensor
 from .ulysses import head_to_seq, seq_to_head
@@ -153,10 +154,8 @@ class WanBlockB200:
                         out=o.transpose(1, 2))
         x = x + self.c_out(o.view(b, s_loc, H * D))
         xn = (1 + m[:, 7]) * _ln(x) + m[:, 6]
-        gu = self.gate_up(xn)
-        i = cfg.intermediate
         # one expert: softmax over a single router logit is exactly 1 (wan.rs:576-601)
-        return x + self.down(F.silu(gu[..., :i]) * gu[..., i:])
+        return x + self.down(swiglu(self.gate_up(xn)))  # silu(gate) * up, one pass
 
 
 def wan_block_flops(cfg: WanConfig = WanConfig(), nt=21, nhw=3600, ctx=512) -> dict:

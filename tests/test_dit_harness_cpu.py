@@ -52,6 +52,11 @@ def _sdpa(q, k, v, out=None):
     return out.copy_(o) if out is not None else o
 
 
+def _swiglu(h):
+    f = h.shape[-1] // 2
+    return F.silu(h[..., :f]) * h[..., f:]
+
+
 def _patch(monkeypatch):
     monkeypatch.setattr(QM.GpuQuantizedLinear, "forward", _q8_forward)
     monkeypatch.setattr(QM.GpuQuantizedLinear, "__call__", _q8_forward)
@@ -62,6 +67,8 @@ def _patch(monkeypatch):
     monkeypatch.setattr(WN, "layer_norm", _ln)
     monkeypatch.setattr(FX, "flash_attention", _sdpa)
     monkeypatch.setattr(WN, "flash_attention", _sdpa)
+    monkeypatch.setattr(FX, "swiglu", _swiglu)
+    monkeypatch.setattr(WN, "swiglu", _swiglu)
 
 
 def test_flux_blocks_wiring_match_oracle(monkeypatch):
