@@ -491,13 +491,14 @@ struct NhwcClusterParams {
   int P, C, G, Cg;
   int gpc, SC, SV;  // groups per cluster, channels and 16-byte vectors per row slice
   int TY, RP;       // row lanes per CTA, rows per CTA
+  int R;            // rows per thread (staged in shared memory)
   float eps;
   int act;
 };
 
 constexpr int kClMaxGpc = 16;
 constexpr int kClMaxCluster = 8;  // CTAs per cluster (8: portable; 16 measured slower)
-constexpr int kClMaxRows = 32;     // rows per thread held in registers
+constexpr int kClMaxRows = 32;     // rows per thread staged in shared memory
 
 // Per-group sums of the staged [TY][SC] values (fixed order): Q threads per channel sum
 // strided row subsets into col[Q][SC], one thread per channel adds its Q partials, then one
@@ -526,10 +527,13 @@ __device__ __forceinline__ void cl_group_sums(const float* red, float* col, floa
   __syncthreads();
 }
 
+// Register variant for few rows per thread (R <= 8): each thread loads its R rows of one
+// channel vector into registers at once and every pass reads the registers.
 template <typename T, int R>
-__global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_cluster_kernel(NhwcClusterParams p) {
+__global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_cluster_reg_kernel(NhwcClusterParams p) {
   constexpr int VE = 16 / sizeof(T);
-  extern __shared__ float red[];             // [TY][SC] staging, then col [9][SC]
+  extern __shared__ float red_reg[];  // [TY][SC] staging, then col [9][SC]
+  float* red = red_reg;
   float* col = red + p.TY * p.SC;
   __shared__ float gsum[kClMaxGpc];
   __shared__ float part[kClMaxGpc][3];       // this CTA's (n, mean, M2) per group
@@ -674,10 +678,177 @@ __global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_cluster_kernel(NhwcClust
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// Shared-memory variant (R > 8): the CTA's slice is staged by cp.async (all rows in flight at
+// once) and the passes loop over it; the fully unrolled register variant was bound by
+// instruction-cache misses at 16+ rows per thread.
+__device__ __forceinline__ uint32_t smem_u32_nh(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32_nh(dst)), "l"(src)
+               : "memory");
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNhwcThreads) gn_nhwc_cluster_kernel(NhwcClusterParams p) {
+  constexpr int VE = 16 / sizeof(T);
+  extern __shared__ uint4 dsm[];  // [R][nthr] x vectors | red [TY][SC] | col [9][SC] (floats)
+  __shared__ float part[kClMaxGpc][3];  // this CTA's (n, mean, M2) per group
+  __shared__ float gst[kClMaxGpc][2];   // merged (mean, rstd) per group
+  __shared__ float gsum[kClMaxGpc];
+  cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int cs = (int)cluster.num_blocks();
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int TX = p.SV;
+  const int tid = ty * TX + tx;
+  const int nthr = TX * p.TY;
+  const int R = p.R;
+  uint4* xs = dsm;
+  float* red = reinterpret_cast<float*>(dsm + (size_t)R * nthr);
+  float* col = red + p.TY * p.SC;
+  const int b = blockIdx.z, slice = blockIdx.y;
+  const int c0 = slice * p.SC;  // first channel of the slice
+  const int r0 = rank * p.RP;
+  const int r1 = min(p.P, r0 + p.RP);
+  const T* xb = static_cast<const T*>(p.x) + (int64_t)b * p.P * p.C + c0;
+  T* yb = static_cast<T*>(p.y) + (int64_t)b * p.P * p.C + c0;
+  // rows of this thread: r0 + ty + k * TY, k < R (those < r1)
+  const int kmax = r1 > r0 + ty ? min(R, (r1 - r0 - ty + p.TY - 1) / p.TY) : 0;
+
+  for (int k = 0; k < kmax; ++k) {
+    const int r = r0 + ty + k * p.TY;
+    cp_async16(xs + k * nthr + tid, reinterpret_cast<const uint4*>(xb + (int64_t)r * p.C) + tx);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  float addv[VE], gmv[VE], btv[VE];  // issued while the copies fly, used later
+  {
+    const T* gam = static_cast<const T*>(p.gamma) + c0 + tx * VE;
+    const T* bet = static_cast<const T*>(p.beta) + c0 + tx * VE;
+#pragma unroll
+    for (int t = 0; t < VE; ++t) {
+      addv[t] = p.x_add ? nh_to_f32(static_cast<const T*>(p.x_add)[(int64_t)b * p.C + c0 + tx * VE + t])
+                        : 0.f;
+      gmv[t] = nh_to_f32(gam[t]);
+      btv[t] = nh_to_f32(bet[t]);
+    }
+  }
+  const int rows = max(0, r1 - r0);
+  const float cnt = (float)rows * (float)p.Cg;
+  asm volatile("cp.async.wait_all;" ::: "memory");  // each thread reads only its own vectors
+
+  // pass 1: per-channel sums of this thread's rows -> per-group sums
+  float acc[VE];
+#pragma unroll
+  for (int t = 0; t < VE; ++t) acc[t] = 0.f;
+#pragma unroll 2
+  for (int k = 0; k < kmax; ++k) {
+    float f[VE];
+    nh_unpack<T>(xs[k * nthr + tid], f);
+#pragma unroll
+    for (int t = 0; t < VE; ++t) acc[t] += nh_clamp(f[t] + addv[t]);
+  }
+#pragma unroll
+  for (int t = 0; t < VE; ++t) red[ty * p.SC + tx * VE + t] = acc[t];
+  __syncthreads();
+  cl_group_sums(red, col, gsum, p, tid, nthr);
+  if (tid < p.gpc) part[tid][1] = cnt > 0.f ? gsum[tid] / cnt : 0.f;
+  __syncthreads();
+  // pass 2: M2 about this CTA's group means
+  float gmean[VE];
+#pragma unroll
+  for (int t = 0; t < VE; ++t) {
+    gmean[t] = part[(tx * VE + t) / p.Cg][1];
+    acc[t] = 0.f;
+  }
+#pragma unroll 2
+  for (int k = 0; k < kmax; ++k) {
+    float f[VE];
+    nh_unpack<T>(xs[k * nthr + tid], f);
+#pragma unroll
+    for (int t = 0; t < VE; ++t) {
+      const float d = nh_clamp(f[t] + addv[t]) - gmean[t];
+      acc[t] = fmaf(d, d, acc[t]);
+    }
+  }
+  __syncthreads();  // red is rewritten
+#pragma unroll
+  for (int t = 0; t < VE; ++t) red[ty * p.SC + tx * VE + t] = acc[t];
+  __syncthreads();
+  cl_group_sums(red, col, gsum, p, tid, nthr);
+  if (tid < p.gpc) {
+    part[tid][0] = cnt;
+    part[tid][2] = gsum[tid];
+  }
+  // exchange: every CTA reads every peer's partials (rank order) after the cluster barrier
+  cluster.sync();
+  if (tid < p.gpc) {
+    float pn[kClMaxCluster], pm[kClMaxCluster], pq2[kClMaxCluster];
+#pragma unroll
+    for (int q = 0; q < kClMaxCluster; ++q) {
+      if (q < cs) {
+        const float* pq = cluster.map_shared_rank(&part[tid][0], q);
+        pn[q] = pq[0];
+        pm[q] = pq[1];
+        pq2[q] = pq[2];
+      }
+    }
+    float n = 0.f, mean = 0.f, m2 = 0.f;
+#pragma unroll
+    for (int q = 0; q < kClMaxCluster; ++q) {
+      if (q < cs) {
+        const float nn = n + pn[q];
+        if (nn > 0.f) {
+          const float d = pm[q] - mean, f = pn[q] / nn;
+          mean = fmaf(d, f, mean);
+          m2 = m2 + pq2[q] + d * d * n * f;
+        }
+        n = nn;
+      }
+    }
+    gst[tid][0] = mean;
+    gst[tid][1] = rsqrtf(m2 / n + p.eps);
+  }
+  // peers may still read this CTA's `part`: arrive now, wait before leaving
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  __syncthreads();
+  float mul[VE], sub[VE];
+#pragma unroll
+  for (int t = 0; t < VE; ++t) {
+    const int g = (tx * VE + t) / p.Cg;
+    sub[t] = gst[g][0];
+    mul[t] = gst[g][1] * gmv[t];
+  }
+#pragma unroll 2
+  for (int k = 0; k < kmax; ++k) {
+    const int r = r0 + ty + k * p.TY;
+    float f[VE];
+    nh_unpack<T>(xs[k * nthr + tid], f);
+    uint4 o;
+    T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int t = 0; t < VE; ++t)
+      oe[t] = nh_from_f32<T>(nh_act((nh_clamp(f[t] + addv[t]) - sub[t]) * mul[t] + btv[t], p.act));
+    reinterpret_cast<uint4*>(yb + (int64_t)r * p.C)[tx] = o;
+  }
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 struct ClusterPlan {
   bool ok;
   int gpc, SC, SV, TY, CS, RP, R;
+  size_t smem;
 };
+
+constexpr int kClRegRows = 8;  // up to this many rows per thread: the register variant
+
+// dynamic shared memory: [TY][SC] staging floats and [9][SC] column sums, after the staged
+// slice [R][threads] of 16-byte vectors in the shared-memory variant
+size_t cluster_smem_bytes(const ClusterPlan& pl) {
+  const size_t sums = (size_t)(pl.TY + 9) * pl.SC * sizeof(float);
+  return pl.R <= kClRegRows ? sums : (size_t)pl.R * pl.SV * pl.TY * 16 + sums;
+}
 
 ClusterPlan plan_cluster(int64_t B, int64_t P, int64_t C, int es, int64_t G) {
   ClusterPlan pl{};
@@ -700,7 +871,7 @@ ClusterPlan plan_cluster(int64_t B, int64_t P, int64_t C, int es, int64_t G) {
     const int64_t rp = (P + cs - 1) / cs;
     return (int)((rp + TY - 1) / TY);
   };
-  const int max_rows = es == 4 ? kClMaxRows / 2 : kClMaxRows;
+  const int max_rows = kClMaxRows;
   int cs = 1;
   while (cs < kClMaxCluster && rows_per_thread(cs) > max_rows) cs *= 2;
   if (rows_per_thread(cs) > max_rows) return pl;
@@ -714,9 +885,9 @@ ClusterPlan plan_cluster(int64_t B, int64_t P, int64_t C, int es, int64_t G) {
   pl.TY = TY;
   pl.CS = cs;
   pl.RP = (int)((P + cs - 1) / cs);
-  const int r = rows_per_thread(cs);
-  pl.R = r <= 1 ? 1 : r <= 2 ? 2 : r <= 4 ? 4 : r <= 8 ? 8 : r <= 16 ? 16 : 32;
-  pl.ok = slices <= 65535 && (size_t)(TY + 9) * SC * sizeof(float) <= 48 * 1024;
+  pl.R = rows_per_thread(cs);
+  pl.smem = cluster_smem_bytes(pl);
+  pl.ok = slices <= 65535 && pl.smem <= 200 * 1024;
   return pl;
 }
 
@@ -788,23 +959,31 @@ size_t gn_nhwc_workspace_bytes(int64_t B, int64_t C, int64_t H, int64_t W, int e
   return std::max(two, one);
 }
 
-template <typename T, int R>
+template <typename T>
 static int launch_cluster_nhwc(const NhwcClusterParams& p, const ClusterPlan& pl, int64_t B,
                                cudaStream_t s) {
-  auto kern = gn_nhwc_cluster_kernel<T, R>;
-  static unsigned long long attr_set = 0;
-  if (pl.CS > 8 && first_time_on_device(&attr_set)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) {
-      __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
-      return set_error(SP_ERR_LAUNCH, "groupnorm (channels-last): cluster attribute failed: %s",
-                       cudaGetErrorString(e));
+  void (*kern)(NhwcClusterParams) =
+      pl.R > kClRegRows ? gn_nhwc_cluster_kernel<T>
+      : pl.R > 4        ? gn_nhwc_cluster_reg_kernel<T, 8>
+      : pl.R > 2        ? gn_nhwc_cluster_reg_kernel<T, 4>
+      : pl.R > 1        ? gn_nhwc_cluster_reg_kernel<T, 2>
+                        : gn_nhwc_cluster_reg_kernel<T, 1>;
+  if (pl.R > kClRegRows) {
+    static unsigned long long attr_set = 0;
+    if (first_time_on_device(&attr_set)) {
+      cudaError_t e = cudaFuncSetAttribute(gn_nhwc_cluster_kernel<T>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (e != cudaSuccess) {
+        __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
+        return set_error(SP_ERR_LAUNCH, "groupnorm (channels-last): smem attribute failed: %s",
+                         cudaGetErrorString(e));
+      }
     }
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)pl.CS, (unsigned)(p.G / pl.gpc), (unsigned)B);
   cfg.blockDim = dim3((unsigned)pl.SV, (unsigned)pl.TY, 1);
-  cfg.dynamicSmemBytes = (size_t)(pl.TY + 9) * pl.SC * sizeof(float);
+  cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -818,24 +997,6 @@ static int launch_cluster_nhwc(const NhwcClusterParams& p, const ClusterPlan& pl
     return set_error(SP_ERR_LAUNCH, "groupnorm (channels-last) cluster launch failed: %s",
                      cudaGetErrorString(e));
   return SP_OK;
-}
-
-template <typename T>
-static int launch_cluster_nhwc_r(const NhwcClusterParams& p, const ClusterPlan& pl, int64_t B,
-                                 cudaStream_t s) {
-  switch (pl.R) {
-    case 1: return launch_cluster_nhwc<T, 1>(p, pl, B, s);
-    case 2: return launch_cluster_nhwc<T, 2>(p, pl, B, s);
-    case 4: return launch_cluster_nhwc<T, 4>(p, pl, B, s);
-    case 8: return launch_cluster_nhwc<T, 8>(p, pl, B, s);
-    case 16: return launch_cluster_nhwc<T, 16>(p, pl, B, s);
-    default:
-      // 32 rows of f32 vectors do not fit in registers; the planner never asks for them
-      if constexpr (sizeof(T) == 4)
-        return set_error(SP_ERR_SHAPE, "groupnorm (channels-last): internal plan error");
-      else
-        return launch_cluster_nhwc<T, 32>(p, pl, B, s);
-  }
 }
 
 // The single-launch kernel when every CTA of its grid can be resident at once (checked with
@@ -923,12 +1084,13 @@ int gn_nhwc_launch(const void* x, const void* x_add, const void* gamma, const vo
   p.act = act;
   const ClusterPlan cpl = plan_cluster(B, H * W, C, es, groups);
   if (cpl.ok) {
-    NhwcClusterParams cp{x, x_add, gamma, beta, y, (int)(H * W), (int)C, (int)groups,
-                         (int)(C / groups), cpl.gpc, cpl.SC, cpl.SV, cpl.TY, cpl.RP, eps, act};
+    NhwcClusterParams cp{x,   x_add,          gamma,      beta, y, (int)(H * W), (int)C, (int)groups,
+                         (int)(C / groups), cpl.gpc, cpl.SC, cpl.SV, cpl.TY, cpl.RP, cpl.R, eps,
+                         act};
     switch (dtype) {
-      case SP_F32: return launch_cluster_nhwc_r<float>(cp, cpl, B, s);
-      case SP_F16: return launch_cluster_nhwc_r<__half>(cp, cpl, B, s);
-      default: return launch_cluster_nhwc_r<__nv_bfloat16>(cp, cpl, B, s);
+      case SP_F32: return launch_cluster_nhwc<float>(cp, cpl, B, s);
+      case SP_F16: return launch_cluster_nhwc<__half>(cp, cpl, B, s);
+      default: return launch_cluster_nhwc<__nv_bfloat16>(cp, cpl, B, s);
     }
   }
   const FusedPlan f = plan_fused(H * W, C, es, groups);
