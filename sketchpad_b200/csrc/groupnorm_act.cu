@@ -125,6 +125,7 @@ __device__ __forceinline__ float block_sum(float v, float* scratch /* >= 32 floa
 }
 
 struct GnParams {
+  int resident;  // streaming path: the slice stays in shared memory between the passes
   const void* x;
   const void* gamma;
   const void* beta;
@@ -405,12 +406,35 @@ __global__ void __launch_bounds__(kGrThreads, 2) gn_ring_kernel(GnParams p, int6
   const int v1 = min(nvec, v0 + (int)p.chunk_vecs);
   const uint32_t slice_bytes = (uint32_t)(v1 - v0) * 16u;
   const uint32_t nchunks = (slice_bytes + kGrChunk - 1) / kGrChunk;
+  // the whole slice fits the stages: load it once per group, both passes read it
+  const bool resident = p.resident != 0;
 
   if (warp == kCWarps) {
     // ------------------------------------------------------------------ producers
     // lane 0 feeds ring A (pass 1, HBM, L2 evict-last); lane 1 feeds ring B (pass 2, the
     // same bytes again from L2, evict-first).  Each runs ahead as far as its ring allows.
-    if (lane < 2) {
+    if (resident && lane == 0) {
+      // resident: chunk c of every group lives in stage c and is read by both passes; the
+      // stage is refilled once the consumers have finished pass 2 of the previous group
+      const uint64_t pol = l2_policy(false);
+      int it = 0;
+      bool ok = true;
+      for (int64_t bg = cid; ok && bg < BG; bg += ncl, ++it) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(static_cast<const T*>(p.x) + bg * p.n) +
+                             (size_t)v0 * 16;
+        for (uint32_t c = 0; c < nchunks; ++c) {
+          if (it > 0 && !mbar_wait(&empty[c], (it - 1) & 1, abort_flag, WD_TMA_WAIT)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bytes = min((uint32_t)kGrChunk, slice_bytes - c * kGrChunk);
+          mbar_arrive_expect_tx(&full[c], bytes);
+          bulk_load(ring + c * kGrChunk, src + (size_t)c * kGrChunk, bytes, &full[c], pol);
+        }
+      }
+      if (!ok)  // let the copies in flight land before the CTA can exit (bounded)
+        for (uint32_t c = 0; c < nchunks; ++c) mbar_wait(&full[c], (it & 1), nullptr, WD_TMA_WAIT);
+    } else if (!resident && lane < 2) {
       const int pass = lane;
       const uint32_t nst = pass == 0 ? kGrStagesA : kGrStagesB;
       const uint32_t base = pass == 0 ? 0 : kGrStagesA;
@@ -484,7 +508,8 @@ __global__ void __launch_bounds__(kGrThreads, 2) gn_ring_kernel(GnParams p, int6
       float amax = 0.f, cnt = 0.f;
       bool first = true;
       for (uint32_t c = 0; ok && c < nchunks; ++c, ++ka) {
-        const uint32_t st = ka % kGrStagesA, ph = (ka / kGrStagesA) & 1;
+        const uint32_t st = resident ? c : ka % kGrStagesA;
+        const uint32_t ph = resident ? (uint32_t)(it & 1) : (ka / kGrStagesA) & 1;
         if (!mbar_wait_warp(&full[st], ph, abort_flag, WD_CONVERT_WAIT)) {
           ok = false;
           break;
@@ -512,7 +537,7 @@ __global__ void __launch_bounds__(kGrThreads, 2) gn_ring_kernel(GnParams p, int6
           cnt += (float)VE;
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
+        if (lane == 0 && !resident) mbar_arrive(&empty[st]);
       }
       Welford w{cnt, 0.f, 0.f};
       if (cnt > 0.f) {
@@ -582,8 +607,10 @@ __global__ void __launch_bounds__(kGrThreads, 2) gn_ring_kernel(GnParams p, int6
 
       // ---- pass 2: normalise, affine, activation, store
       for (uint32_t c = 0; c < nchunks; ++c, ++kb) {
-        const uint32_t st = kGrStagesA + kb % kGrStagesB, ph = (kb / kGrStagesB) & 1;
-        if (!mbar_wait_warp(&full[st], ph, abort_flag, WD_CONVERT_WAIT)) {
+        const uint32_t st = resident ? c : kGrStagesA + kb % kGrStagesB;
+        const uint32_t ph = (kb / kGrStagesB) & 1;
+        // resident: the chunk is still in its stage from pass 1
+        if (!resident && !mbar_wait_warp(&full[st], ph, abort_flag, WD_CONVERT_WAIT)) {
           ok = false;
           break;
         }
@@ -725,6 +752,7 @@ constexpr int64_t kGeneralChunk = 16384;
 struct GnPlan {
   bool cluster_path;
   bool stream_path;  // persistent streaming clusters (large groups)
+  bool resident;     // streaming path with the whole slice held in shared memory
   int cs;      // cluster size
   int vpt;     // vectors per thread
   int64_t chunk_vecs;
@@ -744,10 +772,13 @@ GnPlan plan_gn(int64_t B, int64_t G, int64_t cg, int64_t n, bool contiguous, boo
   const int64_t group_bytes = n * (16 / vec_elems);
   if (contiguous && vec_ok && n < (1LL << 31) && group_bytes >= kStreamMinGroupBytes &&
       cg <= kGrMaxCg) {
-    // two CTAs per SM; the smallest cluster (>= 2) that still gives every CTA slot a
-    // slice (measured on B200: larger slices per CTA beat keeping fewer groups in flight)
+    // two CTAs per SM; the smallest cluster (>= 2) that still gives every CTA slot a slice
+    // (measured on B200: larger slices per CTA beat keeping fewer groups in flight, and
+    // clusters grown just to shrink slices into shared memory ran slower)
     int cs = 2;
-    while (cs < kMaxCluster && B * G * cs < (2LL * num_sms() * 7) / 8) cs *= 2;
+    while (cs < 8 && B * G * cs < (2LL * num_sms() * 7) / 8) cs *= 2;  // 16: measured slower
+    // when the slice fits the stages: one HBM read, both passes from shared memory
+    pl.resident = (nvec + cs - 1) / cs * 16 <= (int64_t)kGrStages * kGrChunk;
     pl.stream_path = true;
     pl.cs = cs;
     pl.chunk_vecs = (nvec + cs - 1) / cs;
@@ -982,7 +1013,8 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
   const GnPlan pl = plan_gn(B, groups, cg, n, contiguous, vec_ok, vec_elems);
 
   if (pl.stream_path) {
-    GnParams p{x, gamma, beta, y, C, HW, groups, cg, n, pl.chunk_vecs, eps, act};
+    GnParams p{pl.resident ? 1 : 0, x, gamma, beta, y, C, HW, groups, cg, n, pl.chunk_vecs, eps,
+               act};
     switch (dtype) {
       case SP_F32: return launch_stream<float>(p, pl.cs, B * groups, s);
       case SP_F16: return launch_stream<__half>(p, pl.cs, B * groups, s);
@@ -990,7 +1022,7 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
     }
   }
   if (pl.cluster_path) {
-    GnParams p{x, gamma, beta, y, C, HW, groups, cg, n, pl.chunk_vecs, eps, act};
+    GnParams p{0, x, gamma, beta, y, C, HW, groups, cg, n, pl.chunk_vecs, eps, act};
     switch (dtype) {
       case SP_F32: return launch_cluster_vpt<float>(p, pl.cs, pl.vpt, B * groups, s);
       case SP_F16: return launch_cluster_vpt<__half>(p, pl.cs, pl.vpt, B * groups, s);
