@@ -135,6 +135,29 @@ def test_groupnorm_add_channels_last(shape, dtype):
     assert rel_err(to_np(y), ref) < tol
 
 
+@pytest.mark.parametrize("shape,groups,dtype", [
+    ((1, 4096, 6, 6), 1, torch.bfloat16),   # cooperative single-launch kernel
+    ((1, 2048, 6, 6), 1, torch.float32),    # cooperative single-launch kernel
+    ((2, 8192, 4, 4), 2, torch.bfloat16),   # stats + apply kernel pair
+    ((1, 4096, 6, 6), 1, torch.float32)])   # stats + apply kernel pair
+def test_groupnorm_channels_last_fallback_paths(shape, groups, dtype):
+    # groups wider than one cluster's channel slice take the fallback channels-last paths
+    x, g, b = make(shape, seed=13)
+    xt = torch.from_numpy(x).cuda().to(dtype).to(memory_format=torch.channels_last)
+    gt, bt = torch.from_numpy(g).to(dtype), torch.from_numpy(b).to(dtype)
+    ref = oracle.groupnorm_act(to_np(xt), to_np(gt), to_np(bt), groups, 1e-5, silu=True)
+    t = torch.from_numpy(np.random.default_rng(14).standard_normal(shape[:2]).astype(np.float32))
+    y = groupnorm_silu(xt, gt.cuda(), bt.cuda(), GroupNormSiLuOptions(groups, 1e-5))
+    tol = TOL_F32 if dtype == torch.float32 else TOL_HALF
+    assert rel_err(to_np(y), ref) < tol
+    # and the folded time-embedding add on the same paths
+    tt = t.to(dtype)
+    ref2 = oracle.groupnorm_act(to_np(xt) + to_np(tt)[:, :, None, None], to_np(gt), to_np(bt),
+                                groups, 1e-5, silu=True)
+    y2 = groupnorm_silu(xt, gt.cuda(), bt.cuda(), GroupNormSiLuOptions(groups, 1e-5), add=tt.cuda())
+    assert rel_err(to_np(y2), ref2) < tol
+
+
 def test_groupnorm_add_rejects_nchw():
     x = torch.zeros(1, 32, 4, 4, device="cuda")
     with pytest.raises(Exception, match="channels-last"):
