@@ -134,6 +134,14 @@ typedef enum sp_glu_kind { SP_GLU_GEGLU = 0, SP_GLU_SWIGLU = 1 } sp_glu_kind;
 int sp_glu_gate(const void* x, void* y, int64_t rows, int64_t F, int64_t x_row_stride,
                 int64_t y_row_stride, int kind, int dtype, void* stream);
 
+/* out[p, c] = y[p, c] + bias[c] (+ r[p, c]) over channels-last [rows, C] activations: a
+ * convolution's bias together with the ResBlock residual add (ResBlock::forward,
+ * crates/sketchpad-unet/src/blocks.rs:123-150, conv2(h) + skip(x)), one pass.  r may be NULL
+ * (bias only) and may alias out.  C a multiple of the 16-byte vector; all pointers 16-byte
+ * aligned; f32 arithmetic. */
+int sp_add_bias_residual(const void* y, const void* r, const void* bias, void* out, int64_t rows,
+                         int64_t C, int dtype, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * Q8_0 (GGUF) weights.
  * A Q8_0 row of in_f values is in_f/32 blocks of 34 bytes: f16 LE scale + 32 int8.

@@ -46,6 +46,7 @@ SIGNATURES = {
     "sp_groupnorm_act_noalloc": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p, _i64,
                                         _f, _int, _int, _vp]),
     "sp_glu_gate": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp]),
+    "sp_add_bias_residual": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _int, _vp]),
     "sp_q8_0_repack_host": (_int, [_vp, _sz, _i64, _i64, _vp, _vp]),
     "sp_q8_0_repack": (_int, [_vp, _sz, _i64, _i64, _vp, _vp, _vp]),
     "sp_q8_0_dequant": (_int, [_vp, _vp, _i64, _i64, _vp, _int, _vp]),

@@ -31,6 +31,7 @@ import torch.nn.functional as F
 from .attention import flash_attention
 from .groupnorm_silu import GroupNormSiLuOptions, groupnorm, groupnorm_silu
 from .glu import geglu
+from .residual import add_bias_residual
 from .layernorm import layer_norm
 
 
@@ -287,25 +288,38 @@ class UNetB200:
                 b = name[: -len(".to_k")]
                 self.p[b + ".kv"] = torch.cat([self.p[b + ".to_k.weight"], self.p[b + ".to_v.weight"]],
                                               dim=1).contiguous()
+        # ResBlock biases folded forward (same sums, fewer passes): conv1's bias joins the
+        # time-embedding projection's bias (both are per-channel adds before norm2), and
+        # conv2's bias joins the skip convolution's (both are added with the residual)
+        for name, spec in self.specs:
+            if name.endswith(".conv1"):
+                r = name[: -len(".conv1")]
+                self.p[r + ".time_emb_proj.tbias"] = (self.p[r + ".time_emb_proj.bias"] +
+                                                      self.p[name + ".bias"])
+                ob = self.p[r + ".conv2.bias"]
+                if (r + ".skip_conv.bias") in self.p:
+                    ob = ob + self.p[r + ".skip_conv.bias"]
+                self.p[r + ".obias"] = ob.contiguous()
         self.freqs = torch.from_numpy(timestep_freqs(cfg.model_channels)).to(self.device)
         self.kernel_launches = 0
         self.attn_events: list | None = None  # (start, end, flops) when timing attention
         self.attn_events_external = False     # record as graph nodes during a capture
 
     # -- ops ---------------------------------------------------------------------------------
-    def _lin(self, x, name, bias=True, wkey=".weight"):
+    def _lin(self, x, name, bias=True, wkey=".weight", bkey=".bias"):
         w = self.p[name + wkey]
-        b = self.p.get(name + ".bias") if bias else None
+        b = self.p.get(name + bkey) if bias else None
         if b is None:
             return torch.matmul(x, w)
         lead = x.shape[:-1]
         y = torch.addmm(b, x.reshape(-1, x.shape[-1]), w)  # bias fused into the GEMM epilogue
         return y.view(*lead, w.shape[1])
 
-    def _conv(self, x, name, stride=1):
+    def _conv(self, x, name, stride=1, bias=True):
         w = self.p[name + ".weight"]
         k = w.shape[-1]
-        return F.conv2d(x, w, self.p[name + ".bias"], stride=stride, padding=k // 2)
+        return F.conv2d(x, w, self.p[name + ".bias"] if bias else None, stride=stride,
+                        padding=k // 2)
 
     def _gn(self, x, name, silu, add=None):
         self.kernel_launches += 1
@@ -336,13 +350,17 @@ class UNetB200:
 
     # -- blocks ------------------------------------------------------------------------------
     def _res(self, x, temb_silu, p):
-        residual = self._conv(x, p + ".skip_conv") if (p + ".skip_conv.weight") in self.p else x
+        # blocks.rs:123-150 with the biases moved: conv1's bias rides with the time embedding
+        # into norm2's add, conv2's and the skip convolution's are added with the residual
+        skip = (p + ".skip_conv.weight") in self.p
+        residual = self._conv(x, p + ".skip_conv", bias=False) if skip else x
         h = self._gn(x, p + ".norm1", True)
-        h = self._conv(h, p + ".conv1")
-        t = self._lin(temb_silu, p + ".time_emb_proj")
-        h = self._gn(h, p + ".norm2", True, add=t)  # norm2(h + t[:, :, None, None])
-        h = self._conv(h, p + ".conv2")
-        return h + residual
+        h = self._conv(h, p + ".conv1", bias=False)
+        t = self._lin(temb_silu, p + ".time_emb_proj", bkey=".tbias")
+        h = self._gn(h, p + ".norm2", True, add=t)  # norm2(conv1(h) + b1 + temb)
+        h = self._conv(h, p + ".conv2", bias=False)
+        self.kernel_launches += 1
+        return add_bias_residual(h, self.p[p + ".obias"], residual)
 
     def _xattn(self, x, p, ctx):
         cfg = self.cfg

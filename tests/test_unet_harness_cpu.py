@@ -33,6 +33,8 @@ def test_unet_harness_wiring_matches_oracle(monkeypatch):
     monkeypatch.setattr(U, "groupnorm", lambda x, w, b, opt, out=None: _gn(x, w, b, False))
     monkeypatch.setattr(U, "layer_norm", _ln)
     monkeypatch.setattr(U, "geglu", lambda h: h[..., : h.shape[-1] // 2] * F.gelu(h[..., h.shape[-1] // 2:]))
+    monkeypatch.setattr(U, "add_bias_residual",
+                        lambda y, b, r=None: y + b[None, :, None, None] + (0 if r is None else r))
     monkeypatch.setattr(U, "flash_attention", lambda q, k, v, out=None: out.copy_(
         F.scaled_dot_product_attention(q.float(), k.float(), v.float())))
     P = U.make_unet_params(seed=0)
