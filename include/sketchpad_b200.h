@@ -201,6 +201,14 @@ int sp_fp8_linear(const void* x, const void* w_e4m3, const float* scale, int64_t
  * ------------------------------------------------------------------------------------ */
 int sp_layernorm(const void* x, const void* gamma, const void* beta, void* y, int64_t rows,
                  int64_t n, float eps, int unbiased, int dtype, void* stream);
+/* LayerNorm of x + x_add[column] (x_add: n values, the same dtype; the sum is rounded to the
+ * dtype as a separate element-wise add would round it, then normalised).  Lets a caller carry
+ * a residual stream whose per-channel bias is added only where it is read -- the UNet
+ * transformer accumulates its projection biases that way (BasicTransformerBlock residuals,
+ * crates/sketchpad-unet/src/blocks.rs:292-305). */
+int sp_layernorm_add(const void* x, const void* x_add, const void* gamma, const void* beta,
+                     void* y, int64_t rows, int64_t n, float eps, int unbiased, int dtype,
+                     void* stream);
 
 #ifdef __cplusplus
 }

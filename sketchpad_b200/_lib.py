@@ -55,6 +55,7 @@ SIGNATURES = {
     "sp_fp8_dequant": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _int, _vp]),
     "sp_fp8_linear": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "sp_layernorm": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _f, _int, _int, _vp]),
+    "sp_layernorm_add": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _int, _int, _vp]),
 }
 
 

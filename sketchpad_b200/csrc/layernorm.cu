@@ -33,6 +33,7 @@ constexpr int kLnWarps = 8;
 // VPL = 16-byte vectors per lane; row length n = nvec * (16 / sizeof(T)), nvec <= 32 * VPL.
 template <typename T, int VPL>
 __global__ void __launch_bounds__(kLnWarps * 32) ln_reg_kernel(const T* __restrict__ x,
+                                                               const T* __restrict__ xadd,
                                                                const T* __restrict__ w,
                                                                const T* __restrict__ bias,
                                                                T* __restrict__ y, int64_t rows,
@@ -50,6 +51,13 @@ __global__ void __launch_bounds__(kLnWarps * 32) ln_reg_kernel(const T* __restri
     const int vi = lane + 32 * j;
     if (vi < nvec) {
       buf[j] = __ldg(xv + vi);
+      if (xadd) {  // x + xadd[column], rounded back to T like a separate add would
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(xadd) + vi);
+        T* e = reinterpret_cast<T*>(&buf[j]);
+        const T* ea = reinterpret_cast<const T*>(&a);
+#pragma unroll
+        for (int t = 0; t < VE; ++t) e[t] = ln_from_f32<T>(ln_to_f32(e[t]) + ln_to_f32(ea[t]));
+      }
       const T* e = reinterpret_cast<const T*>(&buf[j]);
 #pragma unroll
       for (int t = 0; t < VE; ++t) s += ln_to_f32(e[t]);
@@ -93,6 +101,7 @@ __global__ void __launch_bounds__(kLnWarps * 32) ln_reg_kernel(const T* __restri
 // Any n: two reads of the row, one warp per row.
 template <typename T>
 __global__ void __launch_bounds__(kLnWarps * 32) ln_generic_kernel(const T* __restrict__ x,
+                                                                   const T* __restrict__ xadd,
                                                                    const T* __restrict__ w,
                                                                    const T* __restrict__ bias,
                                                                    T* __restrict__ y,
@@ -102,49 +111,53 @@ __global__ void __launch_bounds__(kLnWarps * 32) ln_generic_kernel(const T* __re
   const int64_t row = (int64_t)blockIdx.x * kLnWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
   const T* xr = x + row * n;
+  auto xi = [&](int i) {
+    return xadd ? ln_to_f32(ln_from_f32<T>(ln_to_f32(xr[i]) + ln_to_f32(xadd[i])))
+                : ln_to_f32(xr[i]);
+  };
   float s = 0.f;
-  for (int i = lane; i < n; i += 32) s += ln_to_f32(xr[i]);
+  for (int i = lane; i < n; i += 32) s += xi(i);
   const float mean = ln_warp_sum(s) / (float)n;
   float ss = 0.f;
   for (int i = lane; i < n; i += 32) {
-    const float d = ln_to_f32(xr[i]) - mean;
+    const float d = xi(i) - mean;
     ss += d * d;
   }
   const float rstd = rsqrtf(ln_warp_sum(ss) / (float)(unbiased ? n - 1 : n) + eps);
   for (int i = lane; i < n; i += 32)
-    y[row * n + i] =
-        ln_from_f32<T>((ln_to_f32(xr[i]) - mean) * rstd * ln_to_f32(w[i]) + ln_to_f32(bias[i]));
+    y[row * n + i] = ln_from_f32<T>((xi(i) - mean) * rstd * ln_to_f32(w[i]) + ln_to_f32(bias[i]));
 }
 
 template <typename T>
-int launch_ln(const void* x, const void* w, const void* b, void* y, int64_t rows, int n, float eps,
-              int unbiased, cudaStream_t s) {
+int launch_ln(const void* x, const void* xadd, const void* w, const void* b, void* y, int64_t rows,
+              int n, float eps, int unbiased, cudaStream_t s) {
   constexpr int VE = 16 / sizeof(T);
   const dim3 grid((unsigned)((rows + kLnWarps - 1) / kLnWarps));
   const T* xt = static_cast<const T*>(x);
+  const T* at = static_cast<const T*>(xadd);
   const T* wt = static_cast<const T*>(w);
   const T* bt = static_cast<const T*>(b);
   T* yt = static_cast<T*>(y);
-  const bool vec = n % VE == 0 && aligned(x, 16) && aligned(y, 16);
+  const bool vec = n % VE == 0 && aligned(x, 16) && aligned(y, 16) && aligned(xadd, 16);
   const int nvec = n / VE;
   if (vec && nvec <= 32 * 2)
-    ln_reg_kernel<T, 2><<<grid, kLnWarps * 32, 0, s>>>(xt, wt, bt, yt, rows, n, eps, unbiased);
+    ln_reg_kernel<T, 2><<<grid, kLnWarps * 32, 0, s>>>(xt, at, wt, bt, yt, rows, n, eps, unbiased);
   else if (vec && nvec <= 32 * 4)
-    ln_reg_kernel<T, 4><<<grid, kLnWarps * 32, 0, s>>>(xt, wt, bt, yt, rows, n, eps, unbiased);
+    ln_reg_kernel<T, 4><<<grid, kLnWarps * 32, 0, s>>>(xt, at, wt, bt, yt, rows, n, eps, unbiased);
   else if (vec && nvec <= 32 * 8)
-    ln_reg_kernel<T, 8><<<grid, kLnWarps * 32, 0, s>>>(xt, wt, bt, yt, rows, n, eps, unbiased);
+    ln_reg_kernel<T, 8><<<grid, kLnWarps * 32, 0, s>>>(xt, at, wt, bt, yt, rows, n, eps, unbiased);
   else
-    ln_generic_kernel<T><<<grid, kLnWarps * 32, 0, s>>>(xt, wt, bt, yt, rows, n, eps, unbiased);
+    ln_generic_kernel<T><<<grid, kLnWarps * 32, 0, s>>>(xt, at, wt, bt, yt, rows, n, eps, unbiased);
   return check_launch("layernorm");
 }
 
 }  // namespace
 }  // namespace sp
 
-extern "C" int sp_layernorm(const void* x, const void* gamma, const void* beta, void* y,
-                            int64_t rows, int64_t n, float eps, int unbiased, int dtype,
-                            void* stream) {
-  using namespace sp;
+namespace sp {
+namespace {
+int layernorm_entry(const void* x, const void* xadd, const void* gamma, const void* beta, void* y,
+                    int64_t rows, int64_t n, float eps, int unbiased, int dtype, void* stream) {
   clear_error();
   if (!x || !gamma || !beta || !y) return set_error(SP_ERR_INVALID_ARG, "layernorm: null pointer");
   if (rows <= 0 || n <= 1 || n > (1LL << 30))
@@ -154,9 +167,25 @@ extern "C" int sp_layernorm(const void* x, const void* gamma, const void* beta, 
   if (int rc = require_sm100()) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case SP_F32: return launch_ln<float>(x, gamma, beta, y, rows, (int)n, eps, unbiased, s);
-    case SP_F16: return launch_ln<__half>(x, gamma, beta, y, rows, (int)n, eps, unbiased, s);
-    case SP_BF16: return launch_ln<__nv_bfloat16>(x, gamma, beta, y, rows, (int)n, eps, unbiased, s);
+    case SP_F32: return launch_ln<float>(x, xadd, gamma, beta, y, rows, (int)n, eps, unbiased, s);
+    case SP_F16: return launch_ln<__half>(x, xadd, gamma, beta, y, rows, (int)n, eps, unbiased, s);
+    case SP_BF16:
+      return launch_ln<__nv_bfloat16>(x, xadd, gamma, beta, y, rows, (int)n, eps, unbiased, s);
     default: return set_error(SP_ERR_DTYPE, "layernorm: unknown dtype %d", dtype);
   }
+}
+}  // namespace
+}  // namespace sp
+
+extern "C" int sp_layernorm(const void* x, const void* gamma, const void* beta, void* y,
+                            int64_t rows, int64_t n, float eps, int unbiased, int dtype,
+                            void* stream) {
+  return sp::layernorm_entry(x, nullptr, gamma, beta, y, rows, n, eps, unbiased, dtype, stream);
+}
+
+extern "C" int sp_layernorm_add(const void* x, const void* x_add, const void* gamma,
+                                const void* beta, void* y, int64_t rows, int64_t n, float eps,
+                                int unbiased, int dtype, void* stream) {
+  if (!x_add) return sp::set_error(SP_ERR_INVALID_ARG, "layernorm_add: x_add is NULL");
+  return sp::layernorm_entry(x, x_add, gamma, beta, y, rows, n, eps, unbiased, dtype, stream);
 }

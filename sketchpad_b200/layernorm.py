@@ -12,14 +12,20 @@ from ._torch import dtype_code, ptr, require_cuda, stream_ptr
 
 
 def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5,
-               unbiased: bool = True, out=None) -> torch.Tensor:
-    dev = require_cuda(x, weight, bias, out)
+               unbiased: bool = True, out=None, add=None) -> torch.Tensor:
+    """LayerNorm over the last dim; with `add` ([n]), of x + add (rounded like an add)."""
+    dev = require_cuda(x, weight, bias, out, add)
     n = x.shape[-1]
     xx = x.contiguous()
     dt = xx.dtype
     w = (weight if weight.dtype == dt else weight.to(dt)).contiguous()
     b = (bias if bias.dtype == dt else bias.to(dt)).contiguous()
     y = out if out is not None else torch.empty_like(xx)
+    if add is not None:
+        a = (add if add.dtype == dt else add.to(dt)).contiguous()
+        _lib.call("sp_layernorm_add", ptr(xx), ptr(a), ptr(w), ptr(b), ptr(y), xx.numel() // n,
+                  n, float(eps), 1 if unbiased else 0, dtype_code(dt), stream_ptr(dev))
+        return y
     _lib.call("sp_layernorm", ptr(xx), ptr(w), ptr(b), ptr(y), xx.numel() // n, n, float(eps),
               1 if unbiased else 0, dtype_code(dt), stream_ptr(dev))
     return y

@@ -300,6 +300,24 @@ class UNetB200:
                 if (r + ".skip_conv.bias") in self.p:
                     ob = ob + self.p[r + ".skip_conv.bias"]
                 self.p[r + ".obias"] = ob.contiguous()
+        # Spatial transformers: the residual stream y is kept without the projection biases
+        # (each residual add is the projection GEMM accumulating into y); the sum of the
+        # biases added so far is a constant per point of the block, applied where y is read:
+        # in the LayerNorms (x + bias vector) and, through proj_out's weight, in proj_out's bias.
+        for name, spec in self.specs:
+            if name.endswith(".proj_in"):
+                st = name[: -len(".proj_in")]
+                acc = torch.zeros(self.p[st + ".tb0.attn1.to_out.bias"].shape[0],
+                                  dtype=torch.float32, device=self.device)
+                for d in range(cfg.transformer_depth):
+                    tb = f"{st}.tb{d}"
+                    for ln, proj in ((".norm1", ".attn1.to_out"), (".norm2", ".attn2.to_out"),
+                                     (".norm3", ".ff.net_2")):
+                        self.p[tb + ln + ".resbias"] = acc.to(dtype)
+                        acc = acc + self.p[tb + proj + ".bias"].float()
+                wm = self.p[st + ".proj_out.wmat"].float()
+                self.p[st + ".proj_out.obias"] = (self.p[st + ".proj_out.bias"].float() +
+                                                  acc @ wm).to(dtype)
         self.freqs = torch.from_numpy(timestep_freqs(cfg.model_channels)).to(self.device)
         self.kernel_launches = 0
         self.attn_events: list | None = None  # (start, end, flops) when timing attention
@@ -331,7 +349,8 @@ class UNetB200:
 
     def _ln(self, x, name):
         self.kernel_launches += 1
-        return layer_norm(x, self.p[name + ".weight"], self.p[name + ".bias"], 1e-5, True)
+        add = self.p.get(name + ".resbias")  # the residual stream's pending biases
+        return layer_norm(x, self.p[name + ".weight"], self.p[name + ".bias"], 1e-5, True, add=add)
 
     def _attention(self, q, k, v, out):
         self.kernel_launches += 1
@@ -362,7 +381,8 @@ class UNetB200:
         self.kernel_launches += 1
         return add_bias_residual(h, self.p[p + ".obias"], residual)
 
-    def _xattn(self, x, p, ctx):
+    def _xattn(self, x, p, ctx, resid):
+        """Attention of x; its output projection (bias-free) accumulates into resid."""
         cfg = self.cfg
         b, s, _ = x.shape
         H, D = cfg.num_heads, cfg.head_dim
@@ -376,24 +396,32 @@ class UNetB200:
             k, v = kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2)
         o = torch.empty((b, s, H, D), dtype=x.dtype, device=x.device)
         self._attention(q, k, v, o.transpose(1, 2))  # written straight into [b, s, h, d]
-        return self._lin(o.view(b, s, H * D), p + ".to_out")
+        self._accumulate(resid, o.view(b * s, H * D), p + ".to_out")
+
+    def _accumulate(self, resid, x2d, name):
+        """resid += x2d @ W (no bias; cuBLAS accumulates into resid in place)."""
+        r2d = resid.view(-1, resid.shape[-1])
+        torch.addmm(r2d, x2d, self.p[name + ".weight"], out=r2d)
 
     def _st(self, x, ctx, p):
+        # blocks.rs:213-231 / :292-305: y is the residual stream without its biases; the
+        # accumulated bias vector is added by each LayerNorm and folded into proj_out's bias
         b, c, h, w = x.shape
         residual = x
         y = self._gn(x, p + ".norm", False)
         # NHWC memory is already [b, h*w, c]: proj_in (1x1 conv) is a GEMM over channels
         y = self._lin(y.permute(0, 2, 3, 1).reshape(b, h * w, c), p + ".proj_in", wkey=".wmat")
-        inner = y.shape[-1]
         for d in range(self.cfg.transformer_depth):
             tb = f"{p}.tb{d}"
-            y = y + self._xattn(self._ln(y, tb + ".norm1"), tb + ".attn1", None)
-            y = y + self._xattn(self._ln(y, tb + ".norm2"), tb + ".attn2", ctx)
+            self._xattn(self._ln(y, tb + ".norm1"), tb + ".attn1", None, y)
+            self._xattn(self._ln(y, tb + ".norm2"), tb + ".attn2", ctx, y)
             hdn = self._lin(self._ln(y, tb + ".norm3"), tb + ".ff.net_0")
             self.kernel_launches += 1
-            y = y + self._lin(geglu(hdn), tb + ".ff.net_2")  # value * gelu(gate), one pass
-        y = self._lin(y, p + ".proj_out", wkey=".wmat")  # [b, h*w, c] == NHWC memory
-        return y.view(b, h, w, c).permute(0, 3, 1, 2) + residual
+            self._accumulate(y, geglu(hdn).view(b * h * w, -1), tb + ".ff.net_2")
+        yo = torch.matmul(y, self.p[p + ".proj_out.wmat"])  # [b, h*w, c] == NHWC memory
+        self.kernel_launches += 1
+        return add_bias_residual(yo.view(b, h, w, c).permute(0, 3, 1, 2),
+                                 self.p[p + ".proj_out.obias"], residual)
 
     def forward(self, x: torch.Tensor, timesteps: torch.Tensor, context: torch.Tensor) -> torch.Tensor:
         """UNet::forward (unet_sd.rs:235-272): noisy latent [b,4,h,w] -> predicted noise."""

@@ -21,3 +21,18 @@ def test_layernorm(rows, n, dtype):
     y = layer_norm(x.cuda(), w.cuda(), b.cuda())
     ref = oracle.layernorm(to_np(x), to_np(w), to_np(b))
     assert rel_err(to_np(y), ref) < (TOL_F32 if dtype == torch.float32 else TOL_HALF)
+
+
+@pytest.mark.parametrize("rows,n", [(8192, 320), (77, 768), (5, 3)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_layernorm_add(rows, n, dtype):
+    # LayerNorm of x + a[column]: the sum rounded to the dtype first, as a separate add would
+    g = torch.Generator().manual_seed(rows * 3 + n)
+    x = (torch.randn(rows, n, generator=g) * 2 + 0.3).to(dtype)
+    a = (torch.randn(n, generator=g) * 0.5).to(dtype)
+    w = (torch.randn(n, generator=g) * 0.1 + 1).to(dtype)
+    b = (torch.randn(n, generator=g) * 0.1).to(dtype)
+    y = layer_norm(x.cuda(), w.cuda(), b.cuda(), add=a.cuda())
+    xs = to_np((x + a[None, :]).to(dtype))
+    ref = oracle.layernorm(xs, to_np(w), to_np(b))
+    assert rel_err(to_np(y), ref) < (TOL_F32 if dtype == torch.float32 else TOL_HALF)

@@ -22,8 +22,8 @@ def _gn(x, w, b, silu, add=None):
     return y
 
 
-def _ln(x, w, b, eps, unbiased, out=None):
-    xf = x.float()
+def _ln(x, w, b, eps, unbiased, out=None, add=None):
+    xf = x.float() if add is None else x.float() + add.float()
     return (xf - xf.mean(-1, keepdim=True)) / torch.sqrt(xf.var(-1, keepdim=True, unbiased=unbiased) + eps) * w + b
 
 
