@@ -266,6 +266,10 @@ class UNetB200:
                  device="cuda", dtype=torch.bfloat16):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         self.specs, self.program = unet_plan(cfg)
+        if self.device.type == "cuda":
+            # let cuDNN time its convolution algorithms for these fixed shapes once (the
+            # choice is made in the warm-up steps, before any graph capture)
+            torch.backends.cudnn.benchmark = True
         self.spec = dict(self.specs)
         self.p = {k: (v if isinstance(v, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(v)))
                   .to(self.device, dtype).contiguous() for k, v in params.items()}
