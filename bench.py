@@ -417,6 +417,18 @@ def _case_groupnorm(torch, B, C, Hh, W, dt):
     return (lambda: groupnorm_silu(x, w, b, out=y)), groupnorm_bytes(B, C, Hh, W, x.element_size()), "byte"
 
 
+def _case_groupnorm_nhwc(torch, B, C, Hh, W, dt):
+    """Channels-last GroupNorm+SiLU as the UNet step calls it (bf16, NHWC)."""
+    from sketchpad_b200 import groupnorm_bytes, groupnorm_silu
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = (torch.randn(B, C, Hh, W, device="cuda", generator=g) * 3 + 0.5).to(dt)
+    x = x.contiguous(memory_format=torch.channels_last)
+    w = torch.ones(C, device="cuda", dtype=dt)
+    b = torch.zeros(C, device="cuda", dtype=dt)
+    y = torch.empty_like(x)
+    return (lambda: groupnorm_silu(x, w, b, out=y)), groupnorm_bytes(B, C, Hh, W, x.element_size()), "byte"
+
+
 def _case_q8(torch, M, N, K):
     from sketchpad_b200.flux import _q8_linear
     lin = _q8_linear(0, N, K, "cuda", bias=True)
@@ -497,6 +509,8 @@ CASES = {
     "gn_8x512x128x128_f32": lambda t: _case_groupnorm(t, 8, 512, 128, 128, t.float32),
     "gn_8x512x128x128_f16": lambda t: _case_groupnorm(t, 8, 512, 128, 128, t.float16),
     "gn_2x320x64x64_f32": lambda t: _case_groupnorm(t, 2, 320, 64, 64, t.float32),
+    "gn_nhwc_2x320x64x64_bf16": lambda t: _case_groupnorm_nhwc(t, 2, 320, 64, 64, t.bfloat16),
+    "gn_nhwc_2x1280x16x16_bf16": lambda t: _case_groupnorm_nhwc(t, 2, 1280, 16, 16, t.bfloat16),
     "q8_0_4608x3072x3072": lambda t: _case_q8(t, 4608, 3072, 3072),
     "q8_0_4608x12288x3072": lambda t: _case_q8(t, 4608, 12288, 3072),
     "fp8_8192x13824x5120": lambda t: _case_fp8(t, 8192, 13824, 5120),
