@@ -167,6 +167,14 @@ int sp_q8_0_dequant(const void* q, const void* scale, int64_t out_f, int64_t in_
  * must be 16-byte aligned. */
 int sp_q8_0_linear(const void* x, const void* q, const void* scale, const void* bias, void* y,
                    int64_t M, int64_t N, int64_t K, int dtype, void* stream);
+/* sp_q8_0_linear with a gated-residual epilogue: y = residual + gate[n] * (x.W^T + bias[n]).
+ * The DiT blocks' `x + gate * attn(...)` / `x + gate * ffn(...)` (crates/sketchpad-dit/src/
+ * flux.rs:450-517, :573-607) and Wan's ungated residuals (wan.rs:489-573, gate NULL) without
+ * the two element-wise passes.  gate [N] or NULL, residual [M, N] or NULL (may equal y);
+ * bf16; residual 16-byte aligned. */
+int sp_q8_0_linear_gated(const void* x, const void* q, const void* scale, const void* bias,
+                         const void* gate, const void* residual, void* y, int64_t M, int64_t N,
+                         int64_t K, int dtype, void* stream);
 
 /* ------------------------------------------------------------------------------------
  * FP8 (e4m3) weights with f32 scales (per output channel, or one per tensor).
@@ -193,6 +201,32 @@ int sp_fp8_dequant(const void* w_e4m3, const float* scale, int64_t nscale, int64
 int sp_fp8_linear(const void* x, const void* w_e4m3, const float* scale, int64_t nscale,
                   const void* bias, void* y, int64_t M, int64_t N, int64_t K, int dtype,
                   void* stream);
+/* sp_fp8_linear with the gated-residual epilogue of sp_q8_0_linear_gated. */
+int sp_fp8_linear_gated(const void* x, const void* w_e4m3, const float* scale, int64_t nscale,
+                        const void* bias, const void* gate, const void* residual, void* y,
+                        int64_t M, int64_t N, int64_t K, int dtype, void* stream);
+/* The attention projection GEMM of the DiT blocks with its rotary embedding done in the
+ * epilogue, written into a strided output:
+ *   y[m, n] (row stride ldy >= N, ldy % 8 == 0) = rope(x . W^T + bias)[m, n]
+ * where columns [0, rope_cols) form head_dim-wide heads (8 | head_dim, head_dim | rope_cols)
+ * whose (even, odd) column pairs (x0, x1) become (x0 c - x1 s, x1 c + x0 s), the RoPE of
+ * crates/sketchpad-dit/src/rope.rs:145-170 applied to q and k after FluxAttention's qkv
+ * projection (crates/sketchpad-dit/src/flux.rs:330-352) and WanAttention's to_qkv
+ * (crates/sketchpad-dit/src/wan.rs:371-390).  (c, s) = rope_cos_sin[pos * head_dim/2 + pair]
+ * as f32 pairs, pos = ((m + pos_offset) / pos_div) % pos_mod, pos_mod <= rope_positions
+ * (the table's rows).  rope_cos_sin may be NULL (no rotation: a plain strided-output GEMM,
+ * used to write the cross stream's k/v next to the self stream's in one buffer). */
+int sp_q8_0_linear_rope(const void* x, const void* q, const void* scale, const void* bias, void* y,
+                        int64_t ldy, int64_t M, int64_t N, int64_t K, const float* rope_cos_sin,
+                        int64_t rope_positions, int64_t rope_cols, int64_t head_dim,
+                        int64_t pos_offset, int64_t pos_div, int64_t pos_mod, int dtype,
+                        void* stream);
+/* sp_fp8_linear with the strided-output RoPE epilogue of sp_q8_0_linear_rope. */
+int sp_fp8_linear_rope(const void* x, const void* w_e4m3, const float* scale, int64_t nscale,
+                       const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                       const float* rope_cos_sin, int64_t rope_positions, int64_t rope_cols,
+                       int64_t head_dim, int64_t pos_offset, int64_t pos_div, int64_t pos_mod,
+                       int dtype, void* stream);
 
 /* ------------------------------------------------------------------------------------
  * LayerNorm over the last dimension (crates/sketchpad-core/src/layernorm.rs:63-73), which
@@ -209,6 +243,17 @@ int sp_layernorm(const void* x, const void* gamma, const void* beta, void* y, in
 int sp_layernorm_add(const void* x, const void* x_add, const void* gamma, const void* beta,
                      void* y, int64_t rows, int64_t n, float eps, int unbiased, int dtype,
                      void* stream);
+/* The DiT blocks' modulated norm: y = LN(x) * (1 + scale[g]) + shift[g] with LN = LayerNorm::new
+ * (gamma 1, beta 0), g = row / rows_per_group, and group g's scale / shift vectors starting
+ * g * mod_stride elements after `scale` / `shift` (so both may point into the modulation
+ * GEMM's output [batch, k, n]).  Replaces the norm + `(ones_like(scale) + scale) * x + shift`
+ * of FluxDoubleBlock / FluxSingleBlock (crates/sketchpad-dit/src/flux.rs:479-481, 504-506,
+ * 597-599) and WanBlock (crates/sketchpad-dit/src/wan.rs:541-542, 549-550, 564-565,
+ * 569-570).  A null scale reads as 0 and a null shift as 0 (plain LayerNorm::new); computed
+ * in f32 and rounded once. */
+int sp_layernorm_modulate(const void* x, const void* scale, const void* shift, void* y,
+                          int64_t rows, int64_t n, int64_t rows_per_group, int64_t mod_stride,
+                          float eps, int unbiased, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -10,7 +10,7 @@ from .attention import (AttentionSetupError, FlashAttentionOptions, attention_fl
                         causal_mask, flash_attention, flash_attention_masked, qkv_attention)
 from .groupnorm_silu import (GroupNormSiLuLayer, GroupNormSiLuOptions, groupnorm,  # noqa: F401
                              groupnorm_bytes, groupnorm_silu)
-from .layernorm import LayerNorm, layer_norm  # noqa: F401
+from .layernorm import LayerNorm, layer_norm, layer_norm_modulate  # noqa: F401
 from .quantization import (Fp8Config, Fp8Format, Fp8Linear, Fp8Tensor, quantize_fp8)  # noqa: F401
 from .quantized_matmul import (GpuQuantizedLinear, GpuQuantType, dequantize_q8_0,  # noqa: F401
                                repack_q8_0, repack_q8_0_host)

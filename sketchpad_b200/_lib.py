@@ -51,11 +51,20 @@ SIGNATURES = {
     "sp_q8_0_repack": (_int, [_vp, _sz, _i64, _i64, _vp, _vp, _vp]),
     "sp_q8_0_dequant": (_int, [_vp, _vp, _i64, _i64, _vp, _int, _vp]),
     "sp_q8_0_linear": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "sp_q8_0_linear_gated": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "sp_fp8_quantize": (_int, [_vp, _i64, _i64, _int, _vp, _vp, _vp]),
     "sp_fp8_dequant": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _int, _vp]),
     "sp_fp8_linear": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "sp_fp8_linear_gated": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int,
+                                   _vp]),
+    "sp_q8_0_linear_rope": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64,
+                                   _i64, _i64, _i64, _i64, _i64, _int, _vp]),
+    "sp_fp8_linear_rope": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp,
+                                  _i64, _i64, _i64, _i64, _i64, _i64, _int, _vp]),
     "sp_layernorm": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _f, _int, _int, _vp]),
     "sp_layernorm_add": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _int, _int, _vp]),
+    "sp_layernorm_modulate": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f, _int, _int,
+                                     _vp]),
 }
 
 

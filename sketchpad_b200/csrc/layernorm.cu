@@ -30,31 +30,78 @@ __device__ __forceinline__ float ln_warp_sum(float v) {
 
 constexpr int kLnWarps = 8;
 
+// One launch's operands.  gamma/beta are either the affine vectors of LayerNorm::forward
+// (w, b: [n]) or, with `modulate`, the DiT blocks' per-group `scale` / `shift` vectors:
+// y = LN(x) * (1 + scale[g]) + shift[g], g = row / rows_per_group, vectors mod_stride apart
+// (flux.rs:479-481, wan.rs:541-542 after a LayerNorm::new, i.e. gamma 1 and beta 0).  A null
+// gamma reads as 1 and a null beta as 0 (so modulate with neither is the plain LN::new).
+template <typename T>
+struct LnArgs {
+  const T* x;
+  const T* xadd;  // [n] added to every row before the statistics, or null
+  const T* w;
+  const T* b;
+  T* y;
+  int64_t rows;
+  int64_t rows_per_group;
+  int64_t mod_stride;
+  int n;
+  float eps;
+  int unbiased;
+  int modulate;
+};
+
+// gamma / beta of one row's columns c .. c+VE-1 (16-byte vectors; w and b 16-byte aligned)
+template <typename T>
+__device__ __forceinline__ void ln_affine(const LnArgs<T>& a, const T* wr, const T* br, int vi,
+                                          float* g, float* bb) {
+  constexpr int VE = 16 / sizeof(T);
+  if (wr) {
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr) + vi);
+    const T* e = reinterpret_cast<const T*>(&wv);
+    const float base = a.modulate ? 1.f : 0.f;
+#pragma unroll
+    for (int t = 0; t < VE; ++t) g[t] = base + ln_to_f32(e[t]);
+  } else {
+#pragma unroll
+    for (int t = 0; t < VE; ++t) g[t] = 1.f;
+  }
+  if (br) {
+    const uint4 bv = __ldg(reinterpret_cast<const uint4*>(br) + vi);
+    const T* e = reinterpret_cast<const T*>(&bv);
+#pragma unroll
+    for (int t = 0; t < VE; ++t) bb[t] = ln_to_f32(e[t]);
+  } else {
+#pragma unroll
+    for (int t = 0; t < VE; ++t) bb[t] = 0.f;
+  }
+}
+
 // VPL = 16-byte vectors per lane; row length n = nvec * (16 / sizeof(T)), nvec <= 32 * VPL.
 template <typename T, int VPL>
-__global__ void __launch_bounds__(kLnWarps * 32) ln_reg_kernel(const T* __restrict__ x,
-                                                               const T* __restrict__ xadd,
-                                                               const T* __restrict__ w,
-                                                               const T* __restrict__ bias,
-                                                               T* __restrict__ y, int64_t rows,
-                                                               int n, float eps, int unbiased) {
+__global__ void __launch_bounds__(kLnWarps * 32) ln_reg_kernel(const LnArgs<T> a) {
   constexpr int VE = 16 / sizeof(T);
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kLnWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;
+  if (row >= a.rows) return;
+  const int n = a.n;
   const int nvec = n / VE;
-  const uint4* xv = reinterpret_cast<const uint4*>(x + row * n);
+  const uint4* xv = reinterpret_cast<const uint4*>(a.x + row * n);
   uint4 buf[VPL];
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int vi = lane + 32 * j;
+    if (vi < nvec) buf[j] = __ldg(xv + vi);
+  }
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int vi = lane + 32 * j;
     if (vi < nvec) {
-      buf[j] = __ldg(xv + vi);
-      if (xadd) {  // x + xadd[column], rounded back to T like a separate add would
-        const uint4 a = __ldg(reinterpret_cast<const uint4*>(xadd) + vi);
+      if (a.xadd) {  // x + xadd[column], rounded back to T like a separate add would
+        const uint4 av = __ldg(reinterpret_cast<const uint4*>(a.xadd) + vi);
         T* e = reinterpret_cast<T*>(&buf[j]);
-        const T* ea = reinterpret_cast<const T*>(&a);
+        const T* ea = reinterpret_cast<const T*>(&av);
 #pragma unroll
         for (int t = 0; t < VE; ++t) e[t] = ln_from_f32<T>(ln_to_f32(e[t]) + ln_to_f32(ea[t]));
       }
@@ -77,43 +124,39 @@ __global__ void __launch_bounds__(kLnWarps * 32) ln_reg_kernel(const T* __restri
       }
     }
   }
-  const float var = ln_warp_sum(ss) / (float)(unbiased ? n - 1 : n);
-  const float rstd = rsqrtf(var + eps);
-  uint4* yv = reinterpret_cast<uint4*>(y + row * n);
+  const float var = ln_warp_sum(ss) / (float)(a.unbiased ? n - 1 : n);
+  const float rstd = rsqrtf(var + a.eps);
+  const int64_t goff = a.modulate ? (row / a.rows_per_group) * a.mod_stride : 0;
+  const T* wr = a.w ? a.w + goff : nullptr;
+  const T* br = a.b ? a.b + goff : nullptr;
+  uint4* yv = reinterpret_cast<uint4*>(a.y + row * n);
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int vi = lane + 32 * j;
     if (vi < nvec) {
+      float g[VE], bb[VE];
+      ln_affine(a, wr, br, vi, g, bb);
       const T* e = reinterpret_cast<const T*>(&buf[j]);
       uint4 o;
       T* oe = reinterpret_cast<T*>(&o);
 #pragma unroll
-      for (int t = 0; t < VE; ++t) {
-        const int c = vi * VE + t;
-        oe[t] = ln_from_f32<T>((ln_to_f32(e[t]) - mean) * rstd * ln_to_f32(w[c]) +
-                               ln_to_f32(bias[c]));
-      }
+      for (int t = 0; t < VE; ++t) oe[t] = ln_from_f32<T>((ln_to_f32(e[t]) - mean) * rstd * g[t] + bb[t]);
       yv[vi] = o;
     }
   }
 }
 
-// Any n: two reads of the row, one warp per row.
+// Any n (and unaligned rows): two reads of the row, one warp per row.
 template <typename T>
-__global__ void __launch_bounds__(kLnWarps * 32) ln_generic_kernel(const T* __restrict__ x,
-                                                                   const T* __restrict__ xadd,
-                                                                   const T* __restrict__ w,
-                                                                   const T* __restrict__ bias,
-                                                                   T* __restrict__ y,
-                                                                   int64_t rows, int n, float eps,
-                                                                   int unbiased) {
+__global__ void __launch_bounds__(kLnWarps * 32) ln_generic_kernel(const LnArgs<T> a) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kLnWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const T* xr = x + row * n;
+  if (row >= a.rows) return;
+  const int n = a.n;
+  const T* xr = a.x + row * n;
   auto xi = [&](int i) {
-    return xadd ? ln_to_f32(ln_from_f32<T>(ln_to_f32(xr[i]) + ln_to_f32(xadd[i])))
-                : ln_to_f32(xr[i]);
+    return a.xadd ? ln_to_f32(ln_from_f32<T>(ln_to_f32(xr[i]) + ln_to_f32(a.xadd[i])))
+                  : ln_to_f32(xr[i]);
   };
   float s = 0.f;
   for (int i = lane; i < n; i += 32) s += xi(i);
@@ -123,31 +166,33 @@ __global__ void __launch_bounds__(kLnWarps * 32) ln_generic_kernel(const T* __re
     const float d = xi(i) - mean;
     ss += d * d;
   }
-  const float rstd = rsqrtf(ln_warp_sum(ss) / (float)(unbiased ? n - 1 : n) + eps);
-  for (int i = lane; i < n; i += 32)
-    y[row * n + i] = ln_from_f32<T>((xi(i) - mean) * rstd * ln_to_f32(w[i]) + ln_to_f32(bias[i]));
+  const float rstd = rsqrtf(ln_warp_sum(ss) / (float)(a.unbiased ? n - 1 : n) + a.eps);
+  const int64_t goff = a.modulate ? (row / a.rows_per_group) * a.mod_stride : 0;
+  const float base = a.modulate ? 1.f : 0.f;
+  for (int i = lane; i < n; i += 32) {
+    const float g = a.w ? base + ln_to_f32(a.w[goff + i]) : 1.f;
+    const float bb = a.b ? ln_to_f32(a.b[goff + i]) : 0.f;
+    a.y[row * n + i] = ln_from_f32<T>((xi(i) - mean) * rstd * g + bb);
+  }
 }
 
 template <typename T>
-int launch_ln(const void* x, const void* xadd, const void* w, const void* b, void* y, int64_t rows,
-              int n, float eps, int unbiased, cudaStream_t s) {
+int launch_ln(const LnArgs<T>& a, cudaStream_t s) {
   constexpr int VE = 16 / sizeof(T);
-  const dim3 grid((unsigned)((rows + kLnWarps - 1) / kLnWarps));
-  const T* xt = static_cast<const T*>(x);
-  const T* at = static_cast<const T*>(xadd);
-  const T* wt = static_cast<const T*>(w);
-  const T* bt = static_cast<const T*>(b);
-  T* yt = static_cast<T*>(y);
-  const bool vec = n % VE == 0 && aligned(x, 16) && aligned(y, 16) && aligned(xadd, 16);
-  const int nvec = n / VE;
-  if (vec && nvec <= 32 * 2)
-    ln_reg_kernel<T, 2><<<grid, kLnWarps * 32, 0, s>>>(xt, at, wt, bt, yt, rows, n, eps, unbiased);
-  else if (vec && nvec <= 32 * 4)
-    ln_reg_kernel<T, 4><<<grid, kLnWarps * 32, 0, s>>>(xt, at, wt, bt, yt, rows, n, eps, unbiased);
-  else if (vec && nvec <= 32 * 8)
-    ln_reg_kernel<T, 8><<<grid, kLnWarps * 32, 0, s>>>(xt, at, wt, bt, yt, rows, n, eps, unbiased);
-  else
-    ln_generic_kernel<T><<<grid, kLnWarps * 32, 0, s>>>(xt, at, wt, bt, yt, rows, n, eps, unbiased);
+  const dim3 grid((unsigned)((a.rows + kLnWarps - 1) / kLnWarps));
+  const dim3 block(kLnWarps * 32);
+  const bool vec = a.n % VE == 0 && aligned(a.x, 16) && aligned(a.y, 16) &&
+                   aligned(a.xadd, 16) && aligned(a.w, 16) && aligned(a.b, 16) &&
+                   (a.mod_stride * (int64_t)sizeof(T)) % 16 == 0;
+  const int nvec = a.n / VE;
+  // the row stays in registers up to 32 x 20 vectors (5120 bf16: Flux 3072, Wan 5120)
+  if (vec && nvec <= 32 * 2) ln_reg_kernel<T, 2><<<grid, block, 0, s>>>(a);
+  else if (vec && nvec <= 32 * 4) ln_reg_kernel<T, 4><<<grid, block, 0, s>>>(a);
+  else if (vec && nvec <= 32 * 8) ln_reg_kernel<T, 8><<<grid, block, 0, s>>>(a);
+  else if (vec && nvec <= 32 * 12) ln_reg_kernel<T, 12><<<grid, block, 0, s>>>(a);
+  else if (vec && nvec <= 32 * 16) ln_reg_kernel<T, 16><<<grid, block, 0, s>>>(a);
+  else if (vec && nvec <= 32 * 20) ln_reg_kernel<T, 20><<<grid, block, 0, s>>>(a);
+  else ln_generic_kernel<T><<<grid, block, 0, s>>>(a);
   return check_launch("layernorm");
 }
 
@@ -156,23 +201,34 @@ int launch_ln(const void* x, const void* xadd, const void* w, const void* b, voi
 
 namespace sp {
 namespace {
+template <typename T>
+LnArgs<T> ln_args(const void* x, const void* xadd, const void* w, const void* b, void* y,
+                  int64_t rows, int64_t n, int64_t rows_per_group, int64_t mod_stride, float eps,
+                  int unbiased, int modulate) {
+  return LnArgs<T>{static_cast<const T*>(x), static_cast<const T*>(xadd),
+                   static_cast<const T*>(w), static_cast<const T*>(b), static_cast<T*>(y), rows,
+                   rows_per_group, mod_stride, (int)n, eps, unbiased, modulate};
+}
+
 int layernorm_entry(const void* x, const void* xadd, const void* gamma, const void* beta, void* y,
-                    int64_t rows, int64_t n, float eps, int unbiased, int dtype, void* stream) {
-  clear_error();
-  if (!x || !gamma || !beta || !y) return set_error(SP_ERR_INVALID_ARG, "layernorm: null pointer");
+                    int64_t rows, int64_t n, int64_t rows_per_group, int64_t mod_stride,
+                    float eps, int unbiased, int modulate, int dtype, void* stream) {
+  if (!x || !y) return set_error(SP_ERR_INVALID_ARG, "layernorm: null pointer");
   if (rows <= 0 || n <= 1 || n > (1LL << 30))
     return set_error(SP_ERR_INVALID_ARG, "layernorm: bad shape rows=%lld n=%lld",
                      (long long)rows, (long long)n);
   if (rows > (int64_t)kLnWarps * 2147483647LL) return set_error(SP_ERR_SHAPE, "layernorm: too many rows");
   if (int rc = require_sm100()) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define SP_LN_ARGS(T) \
+  ln_args<T>(x, xadd, gamma, beta, y, rows, n, rows_per_group, mod_stride, eps, unbiased, modulate)
   switch (dtype) {
-    case SP_F32: return launch_ln<float>(x, xadd, gamma, beta, y, rows, (int)n, eps, unbiased, s);
-    case SP_F16: return launch_ln<__half>(x, xadd, gamma, beta, y, rows, (int)n, eps, unbiased, s);
-    case SP_BF16:
-      return launch_ln<__nv_bfloat16>(x, xadd, gamma, beta, y, rows, (int)n, eps, unbiased, s);
+    case SP_F32: return launch_ln<float>(SP_LN_ARGS(float), s);
+    case SP_F16: return launch_ln<__half>(SP_LN_ARGS(__half), s);
+    case SP_BF16: return launch_ln<__nv_bfloat16>(SP_LN_ARGS(__nv_bfloat16), s);
     default: return set_error(SP_ERR_DTYPE, "layernorm: unknown dtype %d", dtype);
   }
+#undef SP_LN_ARGS
 }
 }  // namespace
 }  // namespace sp
@@ -180,12 +236,29 @@ int layernorm_entry(const void* x, const void* xadd, const void* gamma, const vo
 extern "C" int sp_layernorm(const void* x, const void* gamma, const void* beta, void* y,
                             int64_t rows, int64_t n, float eps, int unbiased, int dtype,
                             void* stream) {
-  return sp::layernorm_entry(x, nullptr, gamma, beta, y, rows, n, eps, unbiased, dtype, stream);
+  sp::clear_error();
+  if (!gamma || !beta) return sp::set_error(SP_ERR_INVALID_ARG, "layernorm: null pointer");
+  return sp::layernorm_entry(x, nullptr, gamma, beta, y, rows, n, 1, 0, eps, unbiased, 0, dtype,
+                             stream);
 }
 
 extern "C" int sp_layernorm_add(const void* x, const void* x_add, const void* gamma,
                                 const void* beta, void* y, int64_t rows, int64_t n, float eps,
                                 int unbiased, int dtype, void* stream) {
+  sp::clear_error();
   if (!x_add) return sp::set_error(SP_ERR_INVALID_ARG, "layernorm_add: x_add is NULL");
-  return sp::layernorm_entry(x, x_add, gamma, beta, y, rows, n, eps, unbiased, dtype, stream);
+  if (!gamma || !beta) return sp::set_error(SP_ERR_INVALID_ARG, "layernorm: null pointer");
+  return sp::layernorm_entry(x, x_add, gamma, beta, y, rows, n, 1, 0, eps, unbiased, 0, dtype,
+                             stream);
+}
+
+extern "C" int sp_layernorm_modulate(const void* x, const void* scale, const void* shift,
+                                     void* y, int64_t rows, int64_t n, int64_t rows_per_group,
+                                     int64_t mod_stride, float eps, int unbiased, int dtype,
+                                     void* stream) {
+  sp::clear_error();
+  if (rows_per_group <= 0 || mod_stride < 0)
+    return sp::set_error(SP_ERR_INVALID_ARG, "layernorm_modulate: bad rows_per_group / stride");
+  return sp::layernorm_entry(x, nullptr, scale, shift, y, rows, n, rows_per_group, mod_stride,
+                             eps, unbiased, 1, dtype, stream);
 }

@@ -51,7 +51,17 @@ struct QlParams {
   const float* fp8_scale;    // FP8: [N] or [1]
   int64_t nscale;
   const __nv_bfloat16* bias;  // [N] or null
-  __nv_bfloat16* y;           // [M, N]
+  __nv_bfloat16* y;           // [M, ldy]: columns [0, N) written
+  // epilogue y = residual + gate[n] * rope(x.W^T + bias): the DiT blocks' gated residual
+  const __nv_bfloat16* gate;      // [N] or null (gate 1)
+  const __nv_bfloat16* residual;  // [M, ldy] or null; may alias y
+  int64_t ldy;                    // row stride of y and residual (elements, >= N)
+  // rotary embedding of the attention projections (rope.rs:145-170) on columns
+  // [0, rope_cols): head_dim-wide heads whose (even, odd) column pairs rotate by the angle of
+  // position ((m + rope_off) / rope_div) % rope_mod; rope = {cos, sin} per (position, pair)
+  const float2* rope;             // [positions, head_dim / 2] or null
+  int64_t rope_off, rope_div, rope_mod;
+  int rope_cols, rope_half;
 };
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -240,6 +250,8 @@ __global__ void __launch_bounds__(kQThreads, 1)
       const int row = half * kQHalf + quarter * 32 + lane;
       const int64_t m = m0 + row;
       const uint32_t taddr = tmem + half * kQBN + ((uint32_t)(quarter * 32) << 16);
+      const float2* rope_row =
+          p.rope ? p.rope + ((m + p.rope_off) / p.rope_div % p.rope_mod) * p.rope_half : nullptr;
       for (int c = 0; c < kQBN; c += 32) {
         uint32_t r[32];
         tmem_ld32(taddr + c, r);
@@ -247,10 +259,14 @@ __global__ void __launch_bounds__(kQThreads, 1)
         if (m >= p.M) continue;
         const int64_t nb = n0 + c;
         if (nb >= p.N) continue;
-        __nv_bfloat16* dst = p.y + m * p.N + nb;
+        __nv_bfloat16* dst = p.y + m * p.ldy + nb;
+        const __nv_bfloat16* res = p.residual ? p.residual + m * p.ldy + nb : nullptr;
 #pragma unroll
         for (int g = 0; g < 32; g += 8) {
           if (nb + g >= p.N) break;  // N % 16 == 0, so groups of 8 are whole
+          uint4 rv = make_uint4(0, 0, 0, 0);
+          if (res) rv = *reinterpret_cast<const uint4*>(res + g);
+          const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rv);
           float v[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
@@ -259,6 +275,23 @@ __global__ void __launch_bounds__(kQThreads, 1)
             if constexpr (WF == W_FP8) a *= p.fp8_scale[p.nscale == 1 ? 0 : n];
             if (p.bias) a += __bfloat162float(p.bias[n]);
             v[e] = a;
+          }
+          if (rope_row && nb + g < p.rope_cols) {
+            // x*cos + rotate_half(x)*sin, rotate_half([x0, x1]) = [-x1, x0]; 8 | head_dim, so
+            // the group's 4 pairs sit in one head
+            const float2* cs = rope_row + (int)((nb + g) % (2 * p.rope_half)) / 2;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 t = cs[e];
+              const float x0 = v[2 * e], x1 = v[2 * e + 1];
+              v[2 * e] = x0 * t.x - x1 * t.y;
+              v[2 * e + 1] = x1 * t.x + x0 * t.y;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (p.gate) v[e] *= __bfloat162float(p.gate[nb + g + e]);
+            if (res) v[e] += __bfloat162float(re[e]);
           }
           *reinterpret_cast<uint4*>(dst + g) =
               make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
@@ -338,32 +371,126 @@ int check_ql_shape(int64_t M, int64_t N, int64_t K, int dtype) {
 }  // namespace
 }  // namespace sp
 
+namespace sp {
+namespace {
+// Shared argument checks and launch for every quantized-linear entry point.
+struct QlEpilogue {
+  const void* gate = nullptr;
+  const void* residual = nullptr;
+  int64_t ldy = 0;  // 0: N
+  const float* rope = nullptr;
+  int64_t rope_positions = 0, rope_cols = 0, head_dim = 0, pos_off = 0, pos_div = 1, pos_mod = 1;
+};
+
+template <int WF>
+int ql_entry(const char* what, const void* x, const void* w, const void* q8_scale,
+             const float* fp8_scale, int64_t nscale, const void* bias, void* y, int64_t M,
+             int64_t N, int64_t K, int dtype, const QlEpilogue& e, void* stream) {
+  clear_error();
+  if (!x || !w || (!q8_scale && !fp8_scale) || !y)
+    return set_error(SP_ERR_INVALID_ARG, "%s: null pointer", what);
+  if (WF == W_FP8 && nscale != 1 && nscale != N)
+    return set_error(SP_ERR_SHAPE, "%s: scale count %lld must be 1 or N", what, (long long)nscale);
+  if (int rc = check_ql_shape(M, N, K, dtype)) return rc;
+  const int64_t ldy = e.ldy ? e.ldy : N;
+  if (ldy < N || ldy % 8)
+    return set_error(SP_ERR_SHAPE, "%s: row stride %lld must be >= N and a multiple of 8", what,
+                     (long long)ldy);
+  if (e.residual && !aligned(e.residual, 16))
+    return set_error(SP_ERR_ALIGN, "%s: residual must be 16-byte aligned", what);
+  if (e.rope) {
+    if (e.head_dim <= 0 || e.head_dim % 8 || e.rope_cols <= 0 || e.rope_cols % e.head_dim ||
+        e.rope_cols > N)
+      return set_error(SP_ERR_SHAPE, "%s: rope needs 8 | head_dim, head_dim | rope_cols <= N",
+                       what);
+    if (e.pos_div < 1 || e.pos_mod < 1 || e.pos_off < 0 || e.pos_mod > e.rope_positions)
+      return set_error(SP_ERR_INVALID_ARG,
+                       "%s: rope positions need div, mod >= 1, offset >= 0, mod <= table rows",
+                       what);
+    if (!aligned(e.rope, 8)) return set_error(SP_ERR_ALIGN, "%s: rope table must be 8-byte aligned", what);
+  }
+  if (int rc = require_sm100()) return rc;
+  QlParams p{M, N, K, static_cast<const uint16_t*>(q8_scale), fp8_scale, nscale,
+             static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
+             static_cast<const __nv_bfloat16*>(e.gate), static_cast<const __nv_bfloat16*>(e.residual),
+             ldy, reinterpret_cast<const float2*>(e.rope), e.pos_off, e.pos_div, e.pos_mod,
+             (int)e.rope_cols, (int)(e.head_dim / 2)};
+  return launch_qlinear<WF>(x, w, p, static_cast<cudaStream_t>(stream));
+}
+
+QlEpilogue gated(const void* gate, const void* residual) {
+  QlEpilogue e;
+  e.gate = gate;
+  e.residual = residual;
+  return e;
+}
+
+QlEpilogue roped(int64_t ldy, const float* rope, int64_t positions, int64_t cols, int64_t hd,
+                 int64_t off, int64_t div, int64_t mod) {
+  QlEpilogue e;
+  e.ldy = ldy;
+  e.rope = rope;
+  e.rope_positions = positions;
+  e.rope_cols = cols;
+  e.head_dim = hd;
+  e.pos_off = off;
+  e.pos_div = div;
+  e.pos_mod = mod;
+  return e;
+}
+}  // namespace
+}  // namespace sp
+
 extern "C" {
 
 int sp_q8_0_linear(const void* x, const void* q, const void* scale, const void* bias, void* y, int64_t M,
                    int64_t N, int64_t K, int dtype, void* stream) {
-  using namespace sp;
-  clear_error();
-  if (!x || !q || !scale || !y) return set_error(SP_ERR_INVALID_ARG, "q8_0 linear: null pointer");
-  if (int rc = check_ql_shape(M, N, K, dtype)) return rc;
-  if (int rc = require_sm100()) return rc;
-  QlParams p{M, N, K, static_cast<const uint16_t*>(scale), nullptr, 0,
-             static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y)};
-  return launch_qlinear<W_Q8_0>(x, q, p, static_cast<cudaStream_t>(stream));
+  return sp::ql_entry<sp::W_Q8_0>("q8_0 linear", x, q, scale, nullptr, 0, bias, y, M, N, K, dtype,
+                                  sp::QlEpilogue{}, stream);
+}
+
+int sp_q8_0_linear_gated(const void* x, const void* q, const void* scale, const void* bias,
+                         const void* gate, const void* residual, void* y, int64_t M, int64_t N,
+                         int64_t K, int dtype, void* stream) {
+  return sp::ql_entry<sp::W_Q8_0>("q8_0 linear", x, q, scale, nullptr, 0, bias, y, M, N, K, dtype,
+                                  sp::gated(gate, residual), stream);
+}
+
+int sp_q8_0_linear_rope(const void* x, const void* q, const void* scale, const void* bias, void* y,
+                        int64_t ldy, int64_t M, int64_t N, int64_t K, const float* rope_cos_sin,
+                        int64_t rope_positions, int64_t rope_cols, int64_t head_dim,
+                        int64_t pos_offset, int64_t pos_div, int64_t pos_mod, int dtype,
+                        void* stream) {
+  return sp::ql_entry<sp::W_Q8_0>(
+      "q8_0 linear", x, q, scale, nullptr, 0, bias, y, M, N, K, dtype,
+      sp::roped(ldy, rope_cos_sin, rope_positions, rope_cols, head_dim, pos_offset, pos_div,
+                pos_mod),
+      stream);
 }
 
 int sp_fp8_linear(const void* x, const void* w_e4m3, const float* scale, int64_t nscale, const void* bias,
                   void* y, int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
-  using namespace sp;
-  clear_error();
-  if (!x || !w_e4m3 || !scale || !y) return set_error(SP_ERR_INVALID_ARG, "fp8 linear: null pointer");
-  if (nscale != 1 && nscale != N)
-    return set_error(SP_ERR_SHAPE, "fp8 linear: scale count %lld must be 1 or N", (long long)nscale);
-  if (int rc = check_ql_shape(M, N, K, dtype)) return rc;
-  if (int rc = require_sm100()) return rc;
-  QlParams p{M, N, K, nullptr, scale, nscale, static_cast<const __nv_bfloat16*>(bias),
-             static_cast<__nv_bfloat16*>(y)};
-  return launch_qlinear<W_FP8>(x, w_e4m3, p, static_cast<cudaStream_t>(stream));
+  return sp::ql_entry<sp::W_FP8>("fp8 linear", x, w_e4m3, nullptr, scale, nscale, bias, y, M, N, K,
+                                 dtype, sp::QlEpilogue{}, stream);
+}
+
+int sp_fp8_linear_gated(const void* x, const void* w_e4m3, const float* scale, int64_t nscale,
+                        const void* bias, const void* gate, const void* residual, void* y,
+                        int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
+  return sp::ql_entry<sp::W_FP8>("fp8 linear", x, w_e4m3, nullptr, scale, nscale, bias, y, M, N, K,
+                                 dtype, sp::gated(gate, residual), stream);
+}
+
+int sp_fp8_linear_rope(const void* x, const void* w_e4m3, const float* scale, int64_t nscale,
+                       const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                       const float* rope_cos_sin, int64_t rope_positions, int64_t rope_cols,
+                       int64_t head_dim, int64_t pos_offset, int64_t pos_div, int64_t pos_mod,
+                       int dtype, void* stream) {
+  return sp::ql_entry<sp::W_FP8>(
+      "fp8 linear", x, w_e4m3, nullptr, scale, nscale, bias, y, M, N, K, dtype,
+      sp::roped(ldy, rope_cos_sin, rope_positions, rope_cols, head_dim, pos_offset, pos_div,
+                pos_mod),
+      stream);
 }
 
 }  // extern "C"

@@ -31,8 +31,8 @@ import torch.nn.functional as F
 
 from .attention import flash_attention
 from .glu import swiglu
-from .layernorm import layer_norm
-from .quantized_matmul import GpuQuantizedLinear
+from .layernorm import layer_norm_modulate
+from .quantized_matmul import GpuQuantizedLinear, RopeEpilogue, rope_pair_table
 
 
 @dataclass(frozen=True)
@@ -107,8 +107,12 @@ class _Attn:
                                      self.qkv.bias[h:])
         self.H, self.D = cfg.num_heads, cfg.head_dim
 
-    def forward(self, x, cos, sin, cross=None):
+    def forward(self, x, cos, sin, cross=None, gate=None, residual=None, out=None):
+        """proj(attention(x)); with gate [h] and residual: residual + gate * proj(...), the
+        gated residual add done in the projection's epilogue."""
         b, s, _ = x.shape
+        if _epilogue_fusable(x):
+            return self._forward_joint(x, cos, sin, cross, gate, residual, out)
         qkv = self.qkv(x).view(b, s, 3, self.H, self.D)
         q = apply_rope(qkv[:, :, 0].transpose(1, 2), cos, sin)
         k = apply_rope(qkv[:, :, 1].transpose(1, 2), cos, sin)
@@ -120,7 +124,24 @@ class _Attn:
             v = torch.cat([v, kv[:, :, 1].transpose(1, 2)], dim=2)
         o = torch.empty((b, s, self.H, self.D), dtype=x.dtype, device=x.device)
         flash_attention(q, k, v, out=o.transpose(1, 2))
-        return self.proj(o.view(b, s, self.H * self.D))
+        return self.proj(o.view(b, s, self.H * self.D), out=out, gate=gate, residual=residual)
+
+    def _forward_joint(self, x, cos, sin, cross, gate, residual, out):
+        """One prompt: the qkv GEMM writes q, k, v with RoPE applied in its epilogue into a
+        joint [s + c, 3h] buffer whose last c rows receive the cross stream's k, v from the
+        kv GEMM, so attention reads K = [k_self; k_cross] and V likewise in place (no
+        rotation or concatenation passes)."""
+        _, s, h = x.shape
+        c = cross.shape[1] if cross is not None else 0
+        buf = torch.empty((1, s + c, 3 * h), dtype=x.dtype, device=x.device)
+        self.qkv(x, out=buf[:, :s], rope=RopeEpilogue(_rope_pairs(cos, sin), 2 * h, self.D))
+        if c:
+            self.kv(cross, out=buf[:, s:, h:])
+        heads = lambda t: t.unflatten(-1, (self.H, self.D)).transpose(1, 2)  # noqa: E731
+        o = torch.empty((1, s, self.H, self.D), dtype=x.dtype, device=x.device)
+        flash_attention(heads(buf[:, :s, :h]), heads(buf[:, :, h:2 * h]), heads(buf[:, :, 2 * h:]),
+                        out=o.transpose(1, 2))
+        return self.proj(o.view(1, s, h), out=out, gate=gate, residual=residual)
 
 
 class _SwiGlu:
@@ -135,15 +156,41 @@ class _SwiGlu:
         self.down = _q8_linear(seed + 2, h, i, device, scale_range=cfg.weight_scale)
         self.i = i
 
-    def forward(self, x):
-        return self.down(swiglu(self.gate_up(x)))  # silu(gate) * up, one pass
+    def forward(self, x, gate=None, residual=None, out=None):
+        # silu(gate) * up in one pass; the optional gated residual add runs in down's epilogue
+        return self.down(swiglu(self.gate_up(x)), out=out, gate=gate, residual=residual)
 
 
-def _ln(x):
-    # LayerNorm::new(hidden): gamma 1, beta 0, unbiased variance (layernorm.rs:63-73)
-    n = x.shape[-1]
-    one = torch.ones(n, dtype=x.dtype, device=x.device)
-    return layer_norm(x, one, torch.zeros_like(one), 1e-5, True)
+def _ln(x, scale=None, shift=None):
+    # LayerNorm::new(hidden) (gamma 1, beta 0, unbiased variance, layernorm.rs:63-73), with
+    # the blocks' `(1 + scale) * x + shift` modulation fused when scale / shift are given
+    return layer_norm_modulate(x, scale, shift, 1e-5, True)
+
+
+def _rope_pairs(cos, sin):
+    """The f32 (cos, sin) pair table of the RoPE epilogue for these [positions, head_dim]
+    tables: the one FluxB200 attached (built from f32 angles), else derived once and kept on
+    the `cos` tensor."""
+    t = getattr(cos, "_sp_rope_pairs", None)
+    if t is None:
+        t = rope_pair_table(cos, sin)
+        cos._sp_rope_pairs = t
+    return t
+
+
+def _epilogue_fusable(r):
+    # the GEMM epilogue takes one gate vector and a contiguous bf16 residual
+    return r.shape[0] == 1 and r.dtype == torch.bfloat16 and r.is_contiguous()
+
+
+def _gated_add(r, gate, branch, in_place=False):
+    """r + gate * branch(): `gate` is the modulation's [b, 1, h] slice.  For one prompt
+    (b == 1) the add runs in the branch's last GEMM epilogue (in place on `r` when
+    `in_place`, which callers use only on a tensor this block created); otherwise as
+    torch element-wise ops."""
+    if _epilogue_fusable(r):
+        return branch(gate=gate.reshape(-1), residual=r, out=r if in_place else None)
+    return r + gate * branch()
 
 
 class FluxDoubleBlockB200:
@@ -158,13 +205,13 @@ class FluxDoubleBlockB200:
         b = img.shape[0]
         m = self.modulation(cond).view(b, 1, 6, self.h)
         shift, scale, gate = m[:, :, 0], m[:, :, 1], m[:, :, 2]
-        x = (1 + scale) * _ln(img) + shift
-        img = img + gate * self.img_attn.forward(x, cos, sin, txt)
-        img = img + gate * self.img_ffn.forward(_ln(img))
+        x = _ln(img, scale, shift)
+        img = _gated_add(img, gate, lambda **kw: self.img_attn.forward(x, cos, sin, txt, **kw))
+        img = _gated_add(img, gate, lambda **kw: self.img_ffn.forward(_ln(img), **kw), True)
         shift, scale, gate = m[:, :, 3], m[:, :, 4], m[:, :, 5]
-        x = (1 + scale) * _ln(txt) + shift
-        txt = txt + gate * self.txt_attn.forward(x, cos, sin, img)
-        txt = txt + gate * self.txt_ffn.forward(_ln(txt))
+        x = _ln(txt, scale, shift)
+        txt = _gated_add(txt, gate, lambda **kw: self.txt_attn.forward(x, cos, sin, img, **kw))
+        txt = _gated_add(txt, gate, lambda **kw: self.txt_ffn.forward(_ln(txt), **kw), True)
         return img, txt
 
 
@@ -180,9 +227,9 @@ class FluxSingleBlockB200:
         b = x.shape[0]
         m = self.modulation(cond).view(b, 1, 3, self.h)
         shift, scale, gate = m[:, :, 0], m[:, :, 1], m[:, :, 2]
-        xn = (1 + scale) * _ln(x) + shift
-        x = x + gate * self.attn.forward(xn, cos, sin)
-        return x + gate * self.ffn.forward(_ln(x))
+        xn = _ln(x, scale, shift)
+        x = _gated_add(x, gate, lambda **kw: self.attn.forward(xn, cos, sin, **kw))
+        return _gated_add(x, gate, lambda **kw: self.ffn.forward(_ln(x), **kw), True)
 
 
 class FluxB200:
@@ -211,6 +258,8 @@ class FluxB200:
         cos, sin = rope_tables(cfg.head_dim, cfg.max_seq_len)
         self.cos = torch.from_numpy(cos).to(self.device, torch.bfloat16)
         self.sin = torch.from_numpy(sin).to(self.device, torch.bfloat16)
+        # the GEMM-epilogue RoPE reads f32 (cos, sin) pairs of the unrounded angles
+        self.cos._sp_rope_pairs = rope_pair_table(torch.from_numpy(cos), torch.from_numpy(sin)).to(self.device)
         self.tfreq = torch.from_numpy(flux_timestep_freqs(cfg.time_dim)).to(self.device)
         self.gfreq = torch.from_numpy(flux_timestep_freqs(cfg.guidance_dim)).to(self.device)
 
@@ -240,7 +289,7 @@ class FluxB200:
         x = x[:, : ph * pw]
         m = self.final_mod(cond).view(B, 1, 2 * cfg.hidden_size)
         shift, scale = m[..., : cfg.hidden_size], m[..., cfg.hidden_size:]
-        out = self.final_proj((1 + scale) * _ln(x) + shift)
+        out = self.final_proj(_ln(x, scale, shift))
         # unpatchify (dit.rs:327-345)
         out = out.reshape(B, ph, pw, C, ps, ps).permute(0, 3, 4, 5, 1, 2)
         return out.reshape(B, C, Hh, Ww)

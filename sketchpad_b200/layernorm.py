@@ -31,6 +31,41 @@ def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: f
     return y
 
 
+def layer_norm_modulate(x: torch.Tensor, scale: torch.Tensor | None = None,
+                        shift: torch.Tensor | None = None, eps: float = 1e-5,
+                        unbiased: bool = True, out=None) -> torch.Tensor:
+    """LN(x) * (1 + scale) + shift over x [b, s, n] with LN = LayerNorm::new (gamma 1, beta 0)
+    and scale / shift of shape [b, 1, n] (any strides whose last dim is contiguous: slices of
+    the modulation output), one pass (crates/sketchpad-dit/src/flux.rs:479-481)."""
+    dev = require_cuda(x, scale, shift, out)
+    xx = x.contiguous()
+    b, n = xx.shape[0], xx.shape[-1]
+    rows = xx.numel() // n
+    stride = None
+    ops = []
+    for v in (scale, shift):
+        if v is None:
+            ops.append(None)
+            continue
+        if v.dtype != xx.dtype:
+            raise ValueError("scale / shift must have x's dtype")
+        v2 = v.reshape(v.shape[0], -1) if v.dim() > 1 else v.reshape(1, -1)
+        if v2.shape != (b, n) and not (v2.shape == (1, n) and b == 1):
+            raise ValueError(f"scale / shift must hold one [{n}] vector per batch entry")
+        if v2.stride(-1) != 1:
+            raise ValueError("scale / shift rows must be contiguous")
+        s = v2.stride(0) if b > 1 else 0
+        if stride is not None and s != stride:
+            raise ValueError("scale and shift must share the batch stride")
+        stride = s
+        ops.append(v2)
+    y = out if out is not None else torch.empty_like(xx)
+    _lib.call("sp_layernorm_modulate", ptr(xx), ptr(ops[0]), ptr(ops[1]), ptr(y), rows, n,
+              rows // b, stride or 0, float(eps), 1 if unbiased else 0, dtype_code(xx.dtype),
+              stream_ptr(dev))
+    return y
+
+
 class LayerNorm:
     """sketchpad_core::layernorm::LayerNorm { weight, bias, eps }."""
 
@@ -48,4 +83,4 @@ class LayerNorm:
     __call__ = forward
 
 
-__all__ = ["LayerNorm", "layer_norm"]
+__all__ = ["LayerNorm", "layer_norm", "layer_norm_modulate"]

@@ -114,8 +114,14 @@ class Fp8Linear:
                     config: Fp8Config = Fp8Config()):
         return cls(quantize_fp8(weight, config), bias)
 
-    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        dev = require_cuda(x, self.weight.data)
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
+                gate: Optional[torch.Tensor] = None,
+                residual: Optional[torch.Tensor] = None, rope=None) -> torch.Tensor:
+        """x @ dequant(W)^T + b; with gate / residual: residual + gate * (x @ W^T + b); with
+        `rope` (a RopeEpilogue) the rotary embedding of its columns, and `out` may be a
+        column slice of a wider buffer."""
+        dev = require_cuda(x, self.weight.data, gate, residual,
+                           None if rope is None else rope.table)
         N, K = self.weight.shape
         lead = x.shape[:-1]
         xx = x.reshape(-1, K)
@@ -123,13 +129,30 @@ class Fp8Linear:
             xx = xx.to(torch.bfloat16)
         xx = xx.contiguous()
         M = xx.shape[0]
-        y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=dev)
         b = self.bias
         if b is not None and b.dtype != torch.bfloat16:
             b = b.to(torch.bfloat16)
-        _lib.call("sp_fp8_linear", ptr(xx), ptr(self.weight.data), ptr(self.weight.scale),
-                  self.weight.scale.numel(), ptr(b), ptr(y), M, N, K, _lib.SP_BF16,
-                  stream_ptr(dev))
+        if rope is not None or (out is not None and not out.is_contiguous()):
+            from .quantized_matmul import _NO_ROPE, _output_rows
+            if gate is not None or residual is not None:
+                raise ValueError("the rope / strided-output epilogue takes no gate or residual")
+            y, ldy = _output_rows(out, M, N, dev)
+            r = rope.args() if rope is not None else _NO_ROPE
+            _lib.call("sp_fp8_linear_rope", ptr(xx), ptr(self.weight.data),
+                      ptr(self.weight.scale), self.weight.scale.numel(), ptr(b), ptr(y), ldy, M,
+                      N, K, *r, _lib.SP_BF16, stream_ptr(dev))
+            return y if out is not None else y.reshape(*lead, N)
+        y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        if gate is None and residual is None:
+            _lib.call("sp_fp8_linear", ptr(xx), ptr(self.weight.data), ptr(self.weight.scale),
+                      self.weight.scale.numel(), ptr(b), ptr(y), M, N, K, _lib.SP_BF16,
+                      stream_ptr(dev))
+        else:
+            from .quantized_matmul import _epilogue_operands
+            g, r = _epilogue_operands(gate, residual, M, N)
+            _lib.call("sp_fp8_linear_gated", ptr(xx), ptr(self.weight.data),
+                      ptr(self.weight.scale), self.weight.scale.numel(), ptr(b), ptr(g), ptr(r),
+                      ptr(y), M, N, K, _lib.SP_BF16, stream_ptr(dev))
         y = y.reshape(*lead, N)
         return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
 

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import ctypes
 import enum
+from dataclasses import dataclass
 from typing import Optional
 
 import numpy as np
@@ -58,6 +59,67 @@ def repack_q8_0(gguf: torch.Tensor, out_features: int, in_features: int):
     return q, s
 
 
+@dataclass(frozen=True)
+class RopeEpilogue:
+    """Rotary embedding applied in a projection GEMM's epilogue (rope.rs:145-170): columns
+    [0, cols) are head_dim-wide heads whose (even, odd) pairs rotate by the angle of position
+    ((row + pos_offset) // pos_div) % pos_mod.  `table` is f32 [positions, head_dim/2, 2] of
+    (cos, sin), from `rope_pair_table`."""
+
+    table: torch.Tensor
+    cols: int
+    head_dim: int
+    pos_offset: int = 0
+    pos_div: int = 1
+    pos_mod: Optional[int] = None
+
+    def args(self):
+        mod = self.pos_mod if self.pos_mod is not None else self.table.shape[0]
+        return (ptr(self.table), self.table.shape[0], self.cols, self.head_dim, self.pos_offset,
+                self.pos_div, mod)
+
+
+_NO_ROPE = (ptr(None), 0, 0, 0, 0, 1, 1)  # table, positions, cols, head_dim, off, div, mod
+
+
+def rope_pair_table(cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """[positions, head_dim] cos / sin tables (each value repeated for its pair, rope.rs:60-94)
+    -> f32 [positions, head_dim/2, 2] (cos, sin) pairs for RopeEpilogue."""
+    return torch.stack((cos[:, ::2].float(), sin[:, ::2].float()), dim=-1).contiguous()
+
+
+def _output_rows(out, M, N, dev):
+    """The GEMM output as rows of N values `ldy` apart (a column slice of a wider buffer is
+    fine: the DiT attention writes its cross-stream k/v next to the self stream's)."""
+    if out is None:
+        return torch.empty((M, N), dtype=torch.bfloat16, device=dev), N
+    if out.dtype != torch.bfloat16:
+        raise ValueError("out must be bf16")
+    try:
+        o2 = out.view(M, N)
+    except RuntimeError as e:
+        raise ValueError("out must be rows of the output width with a uniform row stride") from e
+    if o2.stride(1) != 1:
+        raise ValueError("out rows must be contiguous")
+    return out, o2.stride(0)
+
+
+def _epilogue_operands(gate, residual, M, N):
+    """bf16 gate [N] and residual [M, N] (contiguous rows) for the gated-residual epilogue."""
+    g = None
+    if gate is not None:
+        g = gate.reshape(-1)
+        if g.numel() != N:
+            raise ValueError(f"gate must hold {N} values")
+        g = (g if g.dtype == torch.bfloat16 else g.to(torch.bfloat16)).contiguous()
+    r = None
+    if residual is not None:
+        if residual.dtype != torch.bfloat16 or residual.numel() != M * N or not residual.is_contiguous():
+            raise ValueError("residual must be a contiguous bf16 tensor of the output's shape")
+        r = residual
+    return g, r
+
+
 class GpuQuantizedLinear:
     """quantized_matmul.rs:655-767 for Q8_0: output = input @ weight.T (+ optional bias)."""
 
@@ -83,22 +145,45 @@ class GpuQuantizedLinear:
         return dequantize_q8_0(self.q, self.scale, self.out_features, self.in_features,
                                dtype or torch.float32)
 
-    def forward(self, input: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """[..., in_features] -> [..., out_features] via the fused dequant-GEMM (bf16)."""
-        dev = require_cuda(input, self.q)
+    def forward(self, input: torch.Tensor, out: Optional[torch.Tensor] = None,
+                gate: Optional[torch.Tensor] = None,
+                residual: Optional[torch.Tensor] = None,
+                rope: Optional[RopeEpilogue] = None) -> torch.Tensor:
+        """[..., in_features] -> [..., out_features] via the fused dequant-GEMM (bf16).
+
+        With gate ([out_features]) and/or residual ([..., out_features], bf16, may be `out`),
+        returns residual + gate * (input . W^T + bias) from the GEMM epilogue; with `rope`,
+        the rotary embedding of its columns (and `out` may be a column slice of a wider
+        buffer)."""
+        dev = require_cuda(input, self.q, gate, residual, None if rope is None else rope.table)
         lead = input.shape[:-1]
         x = input.reshape(-1, self.in_features)
         if x.dtype != torch.bfloat16:
             x = x.to(torch.bfloat16)
         x = x.contiguous()
         M = x.shape[0]
-        y = out if out is not None else torch.empty((M, self.out_features), dtype=torch.bfloat16,
-                                                    device=dev)
         b = self.bias
         if b is not None and b.dtype != torch.bfloat16:
             b = b.to(torch.bfloat16)
-        _lib.call("sp_q8_0_linear", ptr(x), ptr(self.q), ptr(self.scale), ptr(b), ptr(y), M,
-                  self.out_features, self.in_features, _lib.SP_BF16, stream_ptr(dev))
+        if rope is not None or (out is not None and not out.is_contiguous()):
+            if gate is not None or residual is not None:
+                raise ValueError("the rope / strided-output epilogue takes no gate or residual")
+            y, ldy = _output_rows(out, M, self.out_features, dev)
+            r = rope.args() if rope is not None else _NO_ROPE
+            _lib.call("sp_q8_0_linear_rope", ptr(x), ptr(self.q), ptr(self.scale), ptr(b), ptr(y),
+                      ldy, M, self.out_features, self.in_features, *r, _lib.SP_BF16,
+                      stream_ptr(dev))
+            return y if out is not None else y.reshape(*lead, self.out_features)
+        y = out if out is not None else torch.empty((M, self.out_features), dtype=torch.bfloat16,
+                                                    device=dev)
+        if gate is None and residual is None:
+            _lib.call("sp_q8_0_linear", ptr(x), ptr(self.q), ptr(self.scale), ptr(b), ptr(y), M,
+                      self.out_features, self.in_features, _lib.SP_BF16, stream_ptr(dev))
+        else:
+            g, r = _epilogue_operands(gate, residual, M, self.out_features)
+            _lib.call("sp_q8_0_linear_gated", ptr(x), ptr(self.q), ptr(self.scale), ptr(b),
+                      ptr(g), ptr(r), ptr(y), M, self.out_features, self.in_features,
+                      _lib.SP_BF16, stream_ptr(dev))
         y = y.reshape(*lead, self.out_features)
         return y if input.dtype == torch.bfloat16 else y.to(input.dtype)
 

@@ -32,8 +32,9 @@ import torch.nn.functional as F
 
 from .attention import flash_attention
 from .flux import apply_rope, rope_tables
+from .quantized_matmul import RopeEpilogue, rope_pair_table
 from .glu import swiglu
-from .layernorm import layer_norm
+from .layernorm import layer_norm_modulate
 from .quantization import Fp8Format, Fp8Linear, Fp8Tensor
 from .ulysses import head_to_seq, seq_to_head
 
@@ -77,10 +78,15 @@ def fp8_linear_synthetic(seed: int, n: int, k: int, device, bias: bool) -> Fp8Li
     return Fp8Linear(Fp8Tensor(t.data, scale, Fp8Format.E4M3, (n, k)), b)
 
 
-def _ln(x):
-    n = x.shape[-1]
-    one = torch.ones(n, dtype=x.dtype, device=x.device)
-    return layer_norm(x, one, torch.zeros_like(one), 1e-5, True)
+def _ln(x, scale=None, shift=None):
+    # LayerNorm::new(hidden) (gamma 1, beta 0, unbiased variance, layernorm.rs:63-73), with
+    # the blocks' `(1 + scale) * x + shift` modulation fused when scale / shift are given
+    return layer_norm_modulate(x, scale, shift, 1e-5, True)
+
+
+def _rope_fusable(x):
+    # the GEMM epilogue writes bf16
+    return x.dtype == torch.bfloat16
 
 
 class WanBlockB200:
@@ -103,13 +109,26 @@ class WanBlockB200:
         tc, ts = rope_tables(cfg.head_dim, cfg.max_temporal_len)
         f = lambda a: torch.from_numpy(a).to(device, rope_dtype)  # noqa: E731
         self.s_cos, self.s_sin, self.t_cos, self.t_sin = f(sc), f(ss), f(tc), f(ts)
+        # f32 (cos, sin) pairs of the unrounded angles for the qkv GEMMs' RoPE epilogue
+        pairs = lambda c, s_: rope_pair_table(torch.from_numpy(c), torch.from_numpy(s_)).to(device)  # noqa: E731
+        self.s_pairs, self.t_pairs = pairs(sc, ss), pairs(tc, ts)
 
     # attention over the full token sequence of this rank's head group (Ulysses) -----------
-    def _self_attn(self, xn, qkv_lin, out_lin, nt, nhw, temporal):
+    def _self_attn(self, xn, qkv_lin, out_lin, nt, nhw, temporal, residual, out=None):
         cfg, P = self.cfg, self.P
         b, s_loc, _ = xn.shape
         H, D = cfg.num_heads, cfg.head_dim
-        qkv = qkv_lin(xn).view(b, s_loc, 3, H, D)
+        # RoPE in the qkv GEMM's epilogue, by each row's global token index (this rank holds
+        # tokens [rank * s_loc, (rank + 1) * s_loc) of every sequence); spatial position =
+        # token % (h*w), temporal position = token // (h*w) (frame-major tokens)
+        fused = _rope_fusable(xn) and (b == 1 or P == 1)
+        if fused:
+            off = dist.get_rank(self.group) * s_loc if P > 1 else 0
+            rope = (RopeEpilogue(self.t_pairs, 2 * H * D, D, off, nhw, nt) if temporal
+                    else RopeEpilogue(self.s_pairs, 2 * H * D, D, off, 1, nhw))
+            qkv = qkv_lin(xn, rope=rope).view(b, s_loc, 3, H, D)
+        else:
+            qkv = qkv_lin(xn).view(b, s_loc, 3, H, D)
         if P > 1:
             parts = [seq_to_head(qkv[:, :, j].contiguous(), self.group) for j in range(3)]
             hh = H // P
@@ -124,15 +143,22 @@ class WanBlockB200:
             q, k, v = (p.reshape(b, nt, nhw, hh, D).permute(0, 2, 3, 1, 4).reshape(b * nhw, hh, nt, D)
                        for p in parts)
             cos, sin = self.t_cos, self.t_sin
-        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
-        o = flash_attention(q.contiguous(), k.contiguous(), v.contiguous())
+        if not fused:
+            q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        # attention writes [b, t, h*w, heads, D] directly (strided output view)
+        ob = torch.empty((b, nt, nhw, hh, D), dtype=xn.dtype, device=xn.device)
         if not temporal:
-            o = o.transpose(1, 2).reshape(b, nt * nhw, hh, D)
+            flash_attention(q, k, v, out=ob.view(b * nt, nhw, hh, D).transpose(1, 2))
+        elif b == 1:
+            flash_attention(q, k, v, out=ob[0].permute(1, 2, 0, 3))
         else:
-            o = o.reshape(b, nhw, hh, nt, D).permute(0, 3, 1, 2, 4).reshape(b, nt * nhw, hh, D)
+            o = flash_attention(q, k, v)
+            ob.copy_(o.view(b, nhw, hh, nt, D).permute(0, 3, 1, 2, 4))
+        o = ob.view(b, nt * nhw, hh, D)
         if P > 1:
-            o = head_to_seq(o.contiguous(), self.group)
-        return out_lin(o.reshape(b, s_loc, H * D))
+            o = head_to_seq(o, self.group)
+        # residual + to_out(o), the add done in the GEMM epilogue
+        return out_lin(o.reshape(b, s_loc, H * D), out=out, residual=residual)
 
     def forward(self, x, cond, context, nt: int, nh: int, nw: int):
         """x: [b, S/P, hidden] (this rank's tokens), cond: [b, hidden], context: [b, 512, hidden]."""
@@ -140,11 +166,13 @@ class WanBlockB200:
         b = x.shape[0]
         m = self.modulation(cond).view(b, 8, 1, cfg.hidden_size)
         nhw = nh * nw
-        xn = (1 + m[:, 1]) * _ln(x) + m[:, 0]
-        x = x + self._self_attn(xn, self.s_qkv, self.s_out, nt, nhw, temporal=False)
-        xn = (1 + m[:, 3]) * _ln(x) + m[:, 2]
-        x = x + self._self_attn(xn, self.t_qkv, self.t_out, nt, nhw, temporal=True)
-        xn = (1 + m[:, 5]) * _ln(x) + m[:, 4]
+        xn = _ln(x, m[:, 1], m[:, 0])
+        # the residual adds run in each branch's last GEMM epilogue: out of place for the
+        # first (x belongs to the caller), in place on this block's own tensor afterwards
+        x = self._self_attn(xn, self.s_qkv, self.s_out, nt, nhw, False, x.contiguous())
+        xn = _ln(x, m[:, 3], m[:, 2])
+        x = self._self_attn(xn, self.t_qkv, self.t_out, nt, nhw, True, x, out=x)
+        xn = _ln(x, m[:, 5], m[:, 4])
         H, D = cfg.num_heads, cfg.head_dim
         s_loc = x.shape[1]
         q = self.c_q(xn).view(b, s_loc, H, D).transpose(1, 2)
@@ -152,10 +180,11 @@ class WanBlockB200:
         o = torch.empty((b, s_loc, H, D), dtype=x.dtype, device=x.device)
         flash_attention(q, kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2),
                         out=o.transpose(1, 2))
-        x = x + self.c_out(o.view(b, s_loc, H * D))
-        xn = (1 + m[:, 7]) * _ln(x) + m[:, 6]
+        x = self.c_out(o.view(b, s_loc, H * D), out=x, residual=x)
+        xn = _ln(x, m[:, 7], m[:, 6])
         # one expert: softmax over a single router logit is exactly 1 (wan.rs:576-601)
-        return x + self.down(swiglu(self.gate_up(xn)))  # silu(gate) * up, one pass
+        # silu(gate) * up in one pass; the residual add in down's epilogue
+        return self.down(swiglu(self.gate_up(xn)), out=x, residual=x)
 
 
 def wan_block_flops(cfg: WanConfig = WanConfig(), nt=21, nhw=3600, ctx=512) -> dict:

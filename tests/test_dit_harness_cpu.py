@@ -5,6 +5,7 @@ plain torch ops (CPU, fp32), so this checks only the harness against the oracle'
 independent restatement (crates/sketchpad-dit/src/flux.rs:325-607, wan.rs:351-601); the
 GPU tests check the kernels."""
 import numpy as np
+import pytest
 import torch
 import torch.nn.functional as F
 
@@ -19,11 +20,39 @@ from oracle import dit as OD
 TOL_WIRING = 1e-4  # fp32 torch stand-ins vs fp32 oracle: summation order only
 
 
-def _q8_forward(self, x, out=None):
+def _rope_epilogue(y, rope):
+    # RopeEpilogue on rows of y [M, N]: pairs (x0, x1) -> (x0 c - x1 s, x1 c + x0 s)
+    M = y.shape[0]
+    tab = rope.table.float()
+    mod = rope.pos_mod if rope.pos_mod is not None else tab.shape[0]
+    pos = ((torch.arange(M) + rope.pos_offset) // rope.pos_div) % mod
+    cs = tab[pos]  # [M, D/2, 2]
+    heads = y[:, : rope.cols].reshape(M, -1, rope.head_dim // 2, 2)
+    x0, x1 = heads[..., 0], heads[..., 1]
+    c, s = cs[:, None, :, 0], cs[:, None, :, 1]
+    rot = torch.stack((x0 * c - x1 * s, x1 * c + x0 * s), dim=-1).reshape(M, rope.cols)
+    return torch.cat([rot, y[:, rope.cols:]], dim=1)
+
+
+def _epilogue(y, out, gate, residual, rope=None):
+    # the GEMM epilogue's residual + gate * rope(y), written into `out` when given
+    if rope is not None:
+        y = _rope_epilogue(y.reshape(-1, y.shape[-1]), rope).reshape(y.shape)
+    if gate is not None:
+        y = y * gate.float().reshape(-1)
+    if residual is not None:
+        y = y + residual.float().reshape(y.shape)
+    if out is None:
+        return y
+    return out.copy_(y.reshape(out.shape))
+
+
+def _q8_forward(self, x, out=None, gate=None, residual=None, rope=None):
     q = self.q.float()
     s = self.scale.view(torch.float16).float().t().repeat_interleave(32, dim=1)  # [N, K]
     y = x.float() @ (q * s).t()
-    return y + self.bias.float() if self.bias is not None else y
+    y = y + self.bias.float() if self.bias is not None else y
+    return _epilogue(y, out, gate, residual, rope)
 
 
 def _e4m3(w):
@@ -36,15 +65,26 @@ def _fp8_quantize(t, cfg):
     return QZ.Fp8Tensor(data, torch.full((1,), float(cfg.scale)), QZ.Fp8Format.E4M3, tuple(t.shape))
 
 
-def _fp8_forward(self, x, out=None):
+def _fp8_forward(self, x, out=None, gate=None, residual=None, rope=None):
     w = self.weight.data.view(torch.float8_e4m3fn).float() * self.weight.scale.view(-1, 1)
     y = x.float() @ w.t()
-    return y + self.bias.float() if self.bias is not None else y
+    y = y + self.bias.float() if self.bias is not None else y
+    return _epilogue(y, out, gate, residual, rope)
 
 
 def _ln(x, w, b, eps, unbiased, out=None):
     xf = x.float()
     return (xf - xf.mean(-1, keepdim=True)) / torch.sqrt(xf.var(-1, keepdim=True, unbiased=unbiased) + eps) * w + b
+
+
+def _ln_mod(x, scale=None, shift=None, eps=1e-5, unbiased=True, out=None):
+    n = x.shape[-1]
+    y = _ln(x, torch.ones(n), torch.zeros(n), eps, unbiased)
+    if scale is not None:
+        y = y * (1 + scale.float())
+    if shift is not None:
+        y = y + shift.float()
+    return y
 
 
 def _sdpa(q, k, v, out=None):
@@ -63,16 +103,20 @@ def _patch(monkeypatch):
     monkeypatch.setattr(QZ.Fp8Linear, "forward", _fp8_forward)
     monkeypatch.setattr(QZ.Fp8Linear, "__call__", _fp8_forward)
     monkeypatch.setattr(QZ, "quantize_fp8", _fp8_quantize)
-    monkeypatch.setattr(FX, "layer_norm", _ln)
-    monkeypatch.setattr(WN, "layer_norm", _ln)
+    monkeypatch.setattr(FX, "layer_norm_modulate", _ln_mod)
+    monkeypatch.setattr(WN, "layer_norm_modulate", _ln_mod)
     monkeypatch.setattr(FX, "flash_attention", _sdpa)
     monkeypatch.setattr(WN, "flash_attention", _sdpa)
     monkeypatch.setattr(FX, "swiglu", _swiglu)
     monkeypatch.setattr(WN, "swiglu", _swiglu)
 
 
-def test_flux_blocks_wiring_match_oracle(monkeypatch):
+@pytest.mark.parametrize("epilogue", [False, True])
+def test_flux_blocks_wiring_match_oracle(monkeypatch, epilogue):
     _patch(monkeypatch)
+    # epilogue=True routes the gated residual adds through the GEMM-epilogue arguments
+    # (the bf16 batch-1 path on the GPU), False through torch element-wise ops
+    monkeypatch.setattr(FX, "_epilogue_fusable", lambda r: epilogue)
     cfg = SMALL_FLUX
     g = torch.Generator().manual_seed(0)
     img = torch.randn(1, 200, 256, generator=g)
@@ -96,8 +140,12 @@ def test_flux_blocks_wiring_match_oracle(monkeypatch):
     assert rel_err(to_np(gx), rx) < TOL_WIRING
 
 
-def test_wan_block_wiring_matches_oracle(monkeypatch):
+@pytest.mark.parametrize("epilogue", [False, True])
+def test_wan_block_wiring_matches_oracle(monkeypatch, epilogue):
     _patch(monkeypatch)
+    # epilogue=True applies RoPE through the qkv GEMMs' epilogue arguments (the bf16 path on
+    # the GPU), False through apply_rope
+    monkeypatch.setattr(WN, "_rope_fusable", lambda x: epilogue)
     cfg = SMALL_WAN
     nt, nh, nw = 3, 4, 6
     g = torch.Generator().manual_seed(1)
@@ -121,3 +169,50 @@ def test_oracle_rope_matches_reference_rotation():
     want = [1 * np.cos(a0) - 2 * np.sin(a0), 1 * np.sin(a0) + 2 * np.cos(a0),
             3 * np.cos(a1) - 4 * np.sin(a1), 3 * np.sin(a1) + 4 * np.cos(a1)]
     assert np.allclose(y, want, atol=1e-6)
+
+
+class _Setter:
+    # monkeypatch stand-in for spawned ranks (the process ends with the test)
+    @staticmethod
+    def setattr(obj, name, value):
+        setattr(obj, name, value)
+
+
+def _wan_ulysses_worker(rank, ws, port, result_dir):
+    import os
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    try:
+        _patch(_Setter())
+        WN._rope_fusable = lambda x: True  # RoPE by global token index in the qkv epilogue
+        cfg = SMALL_WAN
+        nt, nh, nw = 3, 4, 6
+        g = torch.Generator().manual_seed(1)
+        x = torch.randn(1, nt * nh * nw, 256, generator=g)
+        ctx = torch.randn(1, 40, 256, generator=g)
+        cond = torch.randn(1, 256, generator=g)
+        blk = WN.WanBlockB200(3, cfg, "cpu", group=dist.group.WORLD, rope_dtype=torch.float32)
+        s = x.shape[1] // ws
+        sl = slice(rank * s, (rank + 1) * s)
+        y = blk.forward(x[:, sl].contiguous(), cond, ctx, nt, nh, nw)
+        ref = OD.wan_block(x.numpy(), cond.numpy(), ctx.numpy(), wan_block_weights(blk), nt, nh,
+                           nw, 2, 128, OD.rope_tables(128, 64), OD.rope_tables(128, 8))
+        np.save(f"{result_dir}/err{rank}.npy", np.array([rel_err(to_np(y), ref[:, sl])]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_wan_block_ulysses_two_ranks_matches_oracle(tmp_path):
+    # sequence-parallel WanBlock (each rank 36 of 72 tokens, one head each): the epilogue RoPE
+    # positions count from the rank's first global token (36 -> spatial position 12)
+    import socket
+    import torch.multiprocessing as mp
+    sk = socket.socket()
+    sk.bind(("127.0.0.1", 0))
+    port = sk.getsockname()[1]
+    sk.close()
+    mp.spawn(_wan_ulysses_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    errs = [float(np.load(tmp_path / f"err{r}.npy")[0]) for r in range(2)]
+    assert max(errs) < TOL_WIRING

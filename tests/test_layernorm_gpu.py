@@ -36,3 +36,34 @@ def test_layernorm_add(rows, n, dtype):
     xs = to_np((x + a[None, :]).to(dtype))
     ref = oracle.layernorm(xs, to_np(w), to_np(b))
     assert rel_err(to_np(y), ref) < (TOL_F32 if dtype == torch.float32 else TOL_HALF)
+
+
+@pytest.mark.parametrize("b,s,n", [(1, 4608, 3072), (2, 300, 5120), (1, 77, 640), (3, 5, 24),
+                                   (2, 9, 6000)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_layernorm_modulate(b, s, n, dtype):
+    # LN::new(x) * (1 + scale) + shift with scale / shift sliced out of a modulation output
+    # [b, 1, k, n] like the Flux blocks (flux.rs:479-481); (2, 9, 6000) takes the generic path
+    from sketchpad_b200 import layer_norm_modulate
+    g = torch.Generator().manual_seed(b * s + n)
+    x = (torch.randn(b, s, n, generator=g) * 2 + 0.3).to(dtype)
+    m = (torch.randn(b, 1, 3, n, generator=g) * 0.3).to(dtype)
+    shift, scale = m[:, :, 0], m[:, :, 1]
+    md = m.cuda()
+    y = layer_norm_modulate(x.cuda(), md[:, :, 1], md[:, :, 0])
+    ones = np.ones(n, np.float32)
+    ln = oracle.layernorm(to_np(x).reshape(b * s, n), ones, np.zeros(n, np.float32))
+    ref = ln.reshape(b, s, n) * (1 + to_np(scale)) + to_np(shift)
+    assert rel_err(to_np(y), ref) < (TOL_F32 if dtype == torch.float32 else TOL_HALF)
+    # neither vector: plain LayerNorm::new
+    y0 = layer_norm_modulate(x.cuda())
+    assert rel_err(to_np(y0).reshape(b * s, n), ln) < (TOL_F32 if dtype == torch.float32 else TOL_HALF)
+
+
+def test_layernorm_modulate_rejects_mismatched_vectors():
+    from sketchpad_b200 import layer_norm_modulate
+    x = torch.zeros(2, 4, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        layer_norm_modulate(x, torch.zeros(3, 1, 64, device="cuda", dtype=torch.bfloat16))
+    with pytest.raises(ValueError):
+        layer_norm_modulate(x, torch.zeros(2, 1, 64, device="cuda"))  # f32 vs bf16

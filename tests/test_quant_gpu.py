@@ -157,3 +157,142 @@ def test_fp8_synthetic_bytes_roundtrip():
     exp = np.array(exp, np.float32)
     ok = ~np.isnan(exp)
     assert np.array_equal(got[ok], exp[ok]) and np.all(np.isnan(got[~ok]))
+
+
+def _epilogue_ref(mm, gate, residual):
+    # residual + gate * (x . W^T + b): Flux's `img + gate * proj(..)` (flux.rs:486-560) and
+    # Wan's `x + to_out(..)` (wan.rs:430-470) in f32
+    out = mm if gate is None else mm * gate[None, :]
+    return out if residual is None else out + residual
+
+
+@pytest.mark.parametrize("M,N,K", [(200, 256, 128), (4608, 3072, 3072), (77, 1536, 640)])
+@pytest.mark.parametrize("mode", ["gate+residual", "residual", "gate", "in_place"])
+def test_q8_0_linear_gated_residual_epilogue(M, N, K, mode):
+    raw = make_q8_0_synthetic(N, K, seed=N + K)
+    g = torch.Generator(device="cpu").manual_seed(M)
+    bias = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+    lin = GpuQuantizedLinear.from_bytes(raw, GpuQuantType.Q8_0, N, K, bias=bias.cuda())
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    gate = (torch.randn(N, generator=g)).to(torch.bfloat16) if mode != "residual" else None
+    res = (torch.randn(M, N, generator=g) * 4).to(torch.bfloat16) if mode != "gate" else None
+    rd = res.cuda() if res is not None else None
+    y = lin.forward(x.cuda(), gate=None if gate is None else gate.cuda(), residual=rd,
+                    out=rd if mode == "in_place" else None)
+    torch.cuda.synchronize()
+    if mode == "in_place":
+        assert y.data_ptr() == rd.data_ptr()
+    rows = slice(0, min(M, 256))
+    mm = oracle.q8_0_matmul(np.frombuffer(raw, np.uint8), N, K, to_np(x[rows])) + to_np(bias)
+    ref = _epilogue_ref(mm, None if gate is None else to_np(gate),
+                        None if res is None else to_np(res[rows]))
+    assert rel_err(to_np(y[rows]), ref) < TOL_HALF
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 160, 320), (2048, 5120, 5120)])
+@pytest.mark.parametrize("in_place", [False, True])
+def test_fp8_linear_residual_epilogue(M, N, K, in_place):
+    g = torch.Generator(device="cpu").manual_seed(M + N)
+    w = torch.randn(N, K, generator=g) * 0.02
+    bias = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+    lin = Fp8Linear.from_weight(w.cuda(), bias.cuda(), Fp8Config.e4m3().with_per_channel(True))
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    gate = torch.randn(N, generator=g).to(torch.bfloat16)
+    res = (torch.randn(M, N, generator=g) * 4).to(torch.bfloat16)
+    rd = res.cuda()
+    y = lin.forward(x.cuda(), gate=gate.cuda(), residual=rd, out=rd if in_place else None)
+    torch.cuda.synchronize()
+    wdq = to_np(lin.weight.dequantize())
+    rows = slice(0, min(M, 256))
+    ref = _epilogue_ref(oracle.linear_nt(to_np(x[rows]), wdq, to_np(bias)), to_np(gate),
+                        to_np(res[rows]))
+    assert rel_err(to_np(y[rows]), ref) < TOL_HALF
+
+
+def test_gated_epilogue_rejects_bad_operands():
+    lin = GpuQuantizedLinear.from_bytes(make_q8_0_synthetic(64, 64, seed=1), GpuQuantType.Q8_0,
+                                        64, 64)
+    x = torch.randn(8, 64, device="cuda").to(torch.bfloat16)
+    with pytest.raises(ValueError, match="gate"):
+        lin.forward(x, gate=torch.ones(32, device="cuda"))
+    with pytest.raises(ValueError, match="residual"):
+        lin.forward(x, residual=torch.zeros(8, 64, device="cuda"))  # f32
+    with pytest.raises(ValueError, match="residual"):
+        lin.forward(x, residual=torch.zeros(64, 8, device="cuda", dtype=torch.bfloat16).t())
+
+
+def _rope_ref(y, cos, sin, cols, D, off, div, mod):
+    # rope.rs:145-170 per row of y [M, N] at position ((row + off) // div) % mod
+    M = y.shape[0]
+    pos = ((np.arange(M) + off) // div) % mod
+    out = y.copy()
+    h = y[:, :cols].reshape(M, cols // D, D)
+    c, s = cos[pos][:, None, :], sin[pos][:, None, :]
+    rot = np.stack((-h[..., 1::2], h[..., 0::2]), axis=-1).reshape(h.shape)
+    out[:, :cols] = (h * c + rot * s).reshape(M, cols)
+    return out
+
+
+@pytest.mark.parametrize("M,N,K,D,off,div,mod", [
+    (4608, 9216, 3072, 128, 0, 1, 4608),   # Flux qkv: q and k of 24 heads rotated
+    (300, 384, 256, 64, 36, 24, 3),        # Wan temporal-style positions with a rank offset
+    (77, 256, 128, 128, 5, 1, 40)])
+def test_q8_0_linear_rope_epilogue_strided(M, N, K, D, off, div, mod):
+    from sketchpad_b200.flux import rope_tables
+    from sketchpad_b200.quantized_matmul import RopeEpilogue, rope_pair_table
+    raw = make_q8_0_synthetic(N, K, seed=N + 7)
+    g = torch.Generator(device="cpu").manual_seed(M + 3)
+    bias = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+    lin = GpuQuantizedLinear.from_bytes(raw, GpuQuantType.Q8_0, N, K, bias=bias.cuda())
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    cos, sin = rope_tables(D, max(mod, 8))
+    cols = (2 * N // 3) // D * D
+    # output rows N wide inside a buffer 16 columns wider (row stride N + 16), at column 8
+    buf = torch.full((M, N + 16), 7.0, dtype=torch.bfloat16, device="cuda")
+    rope = RopeEpilogue(rope_pair_table(torch.from_numpy(cos), torch.from_numpy(sin)).cuda(),
+                        cols, D, off, div, mod)
+    lin.forward(x.cuda(), out=buf[:, 8:8 + N], rope=rope)
+    torch.cuda.synchronize()
+    b = to_np(buf)
+    assert np.all(b[:, :8] == 7.0) and np.all(b[:, 8 + N:] == 7.0)  # nothing outside the slice
+    rows = slice(0, min(M, 256))
+    mm = oracle.q8_0_matmul(np.frombuffer(raw, np.uint8), N, K, to_np(x[rows])) + to_np(bias)
+    ref = _rope_ref(mm, cos, sin, cols, D, off, div, mod)
+    assert rel_err(b[rows, 8:8 + N], ref) < TOL_HALF
+    if M > 256:  # the last rows' positions
+        mm = oracle.q8_0_matmul(np.frombuffer(raw, np.uint8), N, K, to_np(x[-64:])) + to_np(bias)
+        ref = _rope_ref(mm, cos, sin, cols, D, off + M - 64, div, mod)
+        assert rel_err(b[-64:, 8:8 + N], ref) < TOL_HALF
+
+
+def test_fp8_linear_rope_epilogue():
+    from sketchpad_b200.flux import rope_tables
+    from sketchpad_b200.quantized_matmul import RopeEpilogue, rope_pair_table
+    M, N, K, D = 512, 3 * 640, 640, 128
+    g = torch.Generator(device="cpu").manual_seed(9)
+    w = torch.randn(N, K, generator=g) * 0.02
+    bias = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+    lin = Fp8Linear.from_weight(w.cuda(), bias.cuda(), Fp8Config.e4m3().with_per_channel(True))
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    cos, sin = rope_tables(D, 100)
+    rope = RopeEpilogue(rope_pair_table(torch.from_numpy(cos), torch.from_numpy(sin)).cuda(),
+                        2 * 640, D, 0, 1, 100)
+    y = lin.forward(x.cuda(), rope=rope)
+    torch.cuda.synchronize()
+    wdq = to_np(lin.weight.dequantize())
+    rows = slice(0, 256)
+    ref = _rope_ref(oracle.linear_nt(to_np(x[rows]), wdq, to_np(bias)), cos, sin, 2 * 640, D,
+                    0, 1, 100)
+    assert rel_err(to_np(y[rows]), ref) < TOL_HALF
+
+
+def test_rope_epilogue_rejects_bad_geometry():
+    from sketchpad_b200.quantized_matmul import RopeEpilogue
+    lin = GpuQuantizedLinear.from_bytes(make_q8_0_synthetic(64, 64, seed=1), GpuQuantType.Q8_0,
+                                        64, 64)
+    x = torch.randn(8, 64, device="cuda").to(torch.bfloat16)
+    tab = torch.zeros(4, 8, 2, device="cuda")
+    with pytest.raises(Exception, match="positions"):
+        lin.forward(x, rope=RopeEpilogue(tab, 32, 16, 0, 1, 5))  # mod > table rows
+    with pytest.raises(Exception, match="head_dim"):
+        lin.forward(x, rope=RopeEpilogue(tab, 36, 12, 0, 1, 4))  # 8 does not divide 12
