@@ -11,10 +11,11 @@
 //                k-tile's block scales, RAW_STAGES deep.
 //   warp 1       TMEM owner (512 columns: two 128 x 256 f32 accumulators) + MMA issuer.
 //   warps 2, 3   idle (the block is sized in whole warpgroups).
-//   warps 4..11  decoders: raw 8-bit tile -> bf16 tile in the UMMA K-major 128B-swizzled
+//   warps 4..19  decoders: raw 8-bit tile -> bf16 tile in the UMMA K-major 128B-swizzled
 //                layout (Q8_0: f16 block scale * int8; FP8: exact e4m3 -> bf16), CVT_STAGES
-//                deep; then the epilogue (warps 4-7 half 0, 8-11 half 1: TMEM -> per-channel
-//                scale, bias -> bf16 -> HBM).
+//                deep (16 warps: two per scheduler, so decode latency overlaps); then the
+//                epilogue, each warp one (TMEM lane quarter, M half, column half): TMEM ->
+//                per-channel scale, bias [, RoPE] [, gate, residual] -> bf16 -> HBM.
 #include <cstring>
 
 #include "common.cuh"
@@ -25,7 +26,7 @@ namespace sp {
 namespace {
 
 constexpr int kQBM = 256, kQHalf = 128, kQBN = 256, kQBK = 64;
-constexpr int kQThreads = 384, kQDecoders = 256, kQFirstDecoderWarp = 4;
+constexpr int kQThreads = 640, kQDecoders = 512, kQFirstDecoderWarp = 4;
 constexpr int kRawStages = 3, kCvtStages = 2;
 constexpr int kXBytes = kQBM * kQBK * 2;    // 32 KB
 constexpr int kWRawBytes = kQBN * kQBK;     // 16 KB
@@ -70,16 +71,31 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return r;
 }
 
-// 4 int8 (one u32) * f32 scale -> 2 x bf16x2 (exact int8 -> f32 via the 2^23 magic number).
+// packed f32x2 operands: two f32 in one 64-bit register pair
+__device__ __forceinline__ uint64_t pk2(uint32_t a, uint32_t b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_of(uint64_t v) {
+  uint32_t a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
+  return pack_bf16x2(__uint_as_float(a), __uint_as_float(b));
+}
+// 4 int8 (one u32) * f32 scale -> 2 x bf16x2 (exact int8 -> f32 via the 2^23 magic number),
+// two lanes per packed f32x2 instruction.
 __device__ __forceinline__ void q8x4_to_bf16(uint32_t w, float s, uint32_t& lo, uint32_t& hi) {
   const uint32_t u = w ^ 0x80808080u;  // int8 -> biased uint8 (q + 128)
-  const float kMagic = 8388736.0f;     // 2^23 + 128
-  const float f0 = __uint_as_float(prmt(u, 0x4B000000u, 0x7650)) - kMagic;
-  const float f1 = __uint_as_float(prmt(u, 0x4B000000u, 0x7651)) - kMagic;
-  const float f2 = __uint_as_float(prmt(u, 0x4B000000u, 0x7652)) - kMagic;
-  const float f3 = __uint_as_float(prmt(u, 0x4B000000u, 0x7653)) - kMagic;
-  lo = pack_bf16x2(f0 * s, f1 * s);
-  hi = pack_bf16x2(f2 * s, f3 * s);
+  const uint64_t magic = pk2(0x4B000080u, 0x4B000080u);  // 2^23 + 128
+  const uint64_t s2 = pk2(__float_as_uint(s), __float_as_uint(s));
+  uint64_t a = pk2(prmt(u, 0x4B000000u, 0x7650), prmt(u, 0x4B000000u, 0x7651));
+  uint64_t b = pk2(prmt(u, 0x4B000000u, 0x7652), prmt(u, 0x4B000000u, 0x7653));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(a) : "l"(a), "l"(magic));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(b) : "l"(b), "l"(magic));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(a) : "l"(a), "l"(s2));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(b) : "l"(b), "l"(s2));
+  lo = bf16x2_of(a);
+  hi = bf16x2_of(b);
 }
 
 // 4 e4m3 bytes -> 2 x bf16x2, exact: the e4m3 bit pattern is placed in bf16 position
@@ -245,14 +261,17 @@ __global__ void __launch_bounds__(kQThreads, 1)
     // ------------------------------------------------------------ epilogue
     if (__all_sync(0xffffffffu, ok) && mbar_wait_warp(acc_full, 0, abort_flag, WD_EPILOGUE_WAIT)) {
       tc_fence_after();
-      const int half = (warp - kQFirstDecoderWarp) >> 2;
+      // 16 warps: (lane quarter, M half, column half) each
+      const int dw = warp - kQFirstDecoderWarp;
+      const int half = (dw >> 2) & 1;
       const int quarter = warp & 3;  // the TMEM lane quarter this warp may access
+      const int cbeg = (dw >> 3) * (kQBN / 2);
       const int row = half * kQHalf + quarter * 32 + lane;
       const int64_t m = m0 + row;
       const uint32_t taddr = tmem + half * kQBN + ((uint32_t)(quarter * 32) << 16);
       const float2* rope_row =
           p.rope ? p.rope + ((m + p.rope_off) / p.rope_div % p.rope_mod) * p.rope_half : nullptr;
-      for (int c = 0; c < kQBN; c += 32) {
+      for (int c = cbeg; c < cbeg + kQBN / 2; c += 32) {
         uint32_t r[32];
         tmem_ld32(taddr + c, r);
         tmem_wait_ld();
