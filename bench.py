@@ -437,6 +437,16 @@ def _case_q8(torch, M, N, K):
     return (lambda: lin.forward(x, out=y)), 2.0 * M * N * K, "flop"
 
 
+def _case_kquant(torch, name, M, N, K):
+    from sketchpad_b200.quantized_matmul import (GpuQuantType, GpuQuantizedLinear,
+                                                 make_kquant_synthetic)
+    qt = GpuQuantType[name]
+    lin = GpuQuantizedLinear.from_bytes(make_kquant_synthetic(qt, N, K), qt, N, K)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    return (lambda: lin.forward(x, out=y)), 2.0 * M * N * K, "flop"
+
+
 def _case_fp8(torch, M, N, K):
     from sketchpad_b200.wan import fp8_linear_synthetic
     lin = fp8_linear_synthetic(0, N, K, "cuda", bias=True)
@@ -512,6 +522,10 @@ CASES = {
     "gn_nhwc_2x320x64x64_bf16": lambda t: _case_groupnorm_nhwc(t, 2, 320, 64, 64, t.bfloat16),
     "gn_nhwc_2x1280x16x16_bf16": lambda t: _case_groupnorm_nhwc(t, 2, 1280, 16, 16, t.bfloat16),
     "q8_0_4608x3072x3072": lambda t: _case_q8(t, 4608, 3072, 3072),
+    "q4_k_4608x3072x3072": lambda t: _case_kquant(t, "Q4K", 4608, 3072, 3072),
+    "q2_k_4608x3072x3072": lambda t: _case_kquant(t, "Q2K", 4608, 3072, 3072),
+    "q3_k_4608x3072x3072": lambda t: _case_kquant(t, "Q3K", 4608, 3072, 3072),
+    "q4_k_4608x12288x3072": lambda t: _case_kquant(t, "Q4K", 4608, 12288, 3072),
     "q8_0_4608x12288x3072": lambda t: _case_q8(t, 4608, 12288, 3072),
     "fp8_8192x13824x5120": lambda t: _case_fp8(t, 8192, 13824, 5120),
 }

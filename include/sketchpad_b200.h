@@ -161,6 +161,31 @@ int sp_q8_0_repack(const void* gguf, size_t nbytes, int64_t out_f, int64_t in_f,
  * crates/sketchpad-convert/src/gguf.rs:643-656 does (subnormal scales included). */
 int sp_q8_0_dequant(const void* q, const void* scale, int64_t out_f, int64_t in_f, void* out,
                     int out_dtype, void* stream);
+/* ------------------------------------------------------------------------------------
+ * GGUF K-quants (GpuQuantType::{Q4K, Q2K, Q3K}, quantized_matmul.rs:33-43): the CPU decode of
+ * crates/sketchpad-convert/src/gguf.rs:737-871 is the semantics (f16 d/dmin with subnormals).
+ * The format id is the GGML type id.  Repacked layout: qpack [N, K/2] bytes (value k of a row
+ * in the low nibble of byte k/2 for even k, high nibble for odd k; one 4-bit unsigned quant
+ * per value) and f32 factors a, b [K/sub, N] (k-block-major; sub = 32 for Q4_K, 16 for
+ * Q2_K/Q3_K): w[n, k] = a * (q - off) - b, off = 4 for Q3_K (b = 0), else 0, exactly the
+ * reference's f32 value.  K must be a multiple of 256.
+ * ------------------------------------------------------------------------------------ */
+typedef enum sp_kquant_format { SP_QK_Q2_K = 10, SP_QK_Q3_K = 11, SP_QK_Q4_K = 12 } sp_kquant_format;
+/* Host repack of nbytes of row-major GGUF super-blocks (out_f rows of in_f/256 blocks):
+ * qpack_host [out_f * in_f/2], a_host and b_host [in_f/sub * out_f]. */
+int sp_kquant_repack_host(int fmt, const uint8_t* gguf_host, size_t nbytes, int64_t out_f,
+                          int64_t in_f, uint8_t* qpack_host, float* a_host, float* b_host);
+/* Dequantize to [out_f, in_f] of out_dtype (replaces dequantize_q4k / dequantize_q2k /
+ * dequantize_q3k, quantized_matmul.rs:410-520); SP_F32 is bit-exact with the CPU decode. */
+int sp_kquant_dequant(int fmt, const void* qpack, const float* a, const float* b, int64_t out_f,
+                      int64_t in_f, void* out, int out_dtype, void* stream);
+/* y[M,N] = x[M,K] . dequant(W)[N,K]^T (+ bias[N]), the K-quant decode inside the GEMM
+ * mainloop (GpuQuantizedLinear::forward for Q4K/Q2K/Q3K, quantized_matmul.rs:752-766).
+ * x, y, bias bf16; qpack/a/b as above. */
+int sp_kquant_linear(int fmt, const void* x, const void* qpack, const float* a, const float* b,
+                     const void* bias, void* y, int64_t M, int64_t N, int64_t K, int dtype,
+                     void* stream);
+
 /* y[M,N] = x[M,K] . dequant(W)[N,K]^T (+ bias[N]); the dequantization happens inside the
  * GEMM mainloop (replaces GpuQuantizedLinear::forward, quantized_matmul.rs:752-766).
  * x, y, bias: SP_BF16.  K % 64 == 0, N % 16 == 0.  bias may be NULL.  x, q, scale and y

@@ -57,6 +57,7 @@ def lib():
                                        _i64, ctypes.c_int, ctypes.c_float, ctypes.c_int]
             L.or_q8_0_dequantize.argtypes = [_u8p, _i64, _f32p]
             L.or_q8_0_matmul.argtypes = [_u8p, _i64, _i64, _f32p, _i64, _f32p]
+            L.or_kquant_dequantize.argtypes = [ctypes.c_int, _u8p, _i64, _f32p]
             L.or_fp8_quantize_scalar.argtypes = [ctypes.c_float, ctypes.c_int]
             L.or_fp8_quantize_scalar.restype = ctypes.c_float
             L.or_fp8_quantize.argtypes = [_f32p, _i64, _i64, ctypes.c_int, ctypes.c_int,
@@ -141,6 +142,21 @@ def q8_0_dequantize(data: np.ndarray, n_elements: int) -> np.ndarray:
     out = np.empty(nb * 32, np.float32)
     _check(lib().or_q8_0_dequantize(d.ctypes.data_as(_u8p), nb, out.ctypes.data_as(_f32p)),
            "q8_0_dequantize")
+    return out
+
+
+KQUANT_BLOCK_BYTES = {10: 84, 11: 110, 12: 144}  # GGML type id -> bytes per 256 values
+
+
+def kquant_dequantize(fmt: int, data: np.ndarray, n_elements: int) -> np.ndarray:
+    """Q2_K (10) / Q3_K (11) / Q4_K (12) super-blocks -> f32 (gguf.rs:737-871)."""
+    d = np.ascontiguousarray(data, dtype=np.uint8)
+    nb = n_elements // 256
+    if d.size < nb * KQUANT_BLOCK_BYTES[fmt]:
+        raise ValueError("k-quant data shorter than n_elements")
+    out = np.empty(nb * 256, np.float32)
+    _check(lib().or_kquant_dequantize(int(fmt), d.ctypes.data_as(_u8p), nb,
+                                      out.ctypes.data_as(_f32p)), "kquant_dequantize")
     return out
 
 

@@ -277,6 +277,79 @@ int or_q8_0_dequantize(const uint8_t* data, int64_t nblocks, float* out) {
   return 0;
 }
 
+// K-quant super-blocks of 256 values, the reference's CPU decode
+// (crates/sketchpad-convert/src/gguf.rs:737-871).  Products are evaluated left to right in
+// f32 as the Rust expressions are (`d * sc * q - dmin * m`, `d * scale * raw`).
+// fmt: 10 = Q2_K (84 B), 11 = Q3_K (110 B), 12 = Q4_K (144 B).
+int or_kquant_dequantize(int fmt, const uint8_t* data, int64_t nblocks, float* out) {
+  if (!data || !out || nblocks < 0 || fmt < 10 || fmt > 12) return -1;
+  const int bytes = fmt == 12 ? 144 : (fmt == 10 ? 84 : 110);
+#pragma omp parallel for schedule(static) num_threads(nthreads())
+  for (int64_t bi = 0; bi < nblocks; ++bi) {
+    const uint8_t* blk = data + bi * bytes;
+    float* o = out + bi * 256;
+    if (fmt == 12) {  // gguf.rs:821-852, scales/mins gguf.rs:854-871
+      const float d = half_to_float((uint16_t)(blk[0] | (blk[1] << 8)));
+      const float dmin = half_to_float((uint16_t)(blk[2] | (blk[3] << 8)));
+      const uint8_t* sb = blk + 4;
+      const uint8_t* qs = blk + 16;
+      uint8_t scales[8], mins[8];
+      for (int i = 0; i < 4; ++i) {
+        scales[i] = sb[i] & 63;
+        mins[i] = sb[i + 4] & 63;
+      }
+      for (int i = 4; i < 8; ++i) {
+        scales[i] = (uint8_t)((sb[i + 4] & 0x0F) | ((sb[i - 4] >> 6) << 4));
+        mins[i] = (uint8_t)((sb[i + 4] >> 4) | ((sb[i] >> 6) << 4));
+      }
+      for (int j = 0; j < 8; ++j) {
+        const float sc = (float)scales[j], m = (float)mins[j];
+        for (int i = 0; i < 16; ++i) {
+          const uint8_t byte = qs[j * 16 + i];
+          const float lo = (float)(byte & 0x0F), hi = (float)((byte >> 4) & 0x0F);
+          const float dsc = d * sc, dm = dmin * m;
+          o[j * 32 + i] = dsc * lo - dm;
+          o[j * 32 + i + 16] = dsc * hi - dm;
+        }
+      }
+    } else if (fmt == 10) {  // gguf.rs:737-758
+      const uint8_t* sb = blk;
+      const uint8_t* qs = blk + 16;
+      const float d = half_to_float((uint16_t)(blk[80] | (blk[81] << 8)));
+      const float dmin = half_to_float((uint16_t)(blk[82] | (blk[83] << 8)));
+      for (int i = 0; i < 256; ++i) {
+        const int ib = i / 16;
+        const float sc = (float)(sb[ib] & 0x0F), m = (float)((sb[ib] >> 4) & 0x0F);
+        const float q = (float)((qs[i / 4] >> (2 * (i % 4))) & 0x3);
+        const float dsc = d * sc, dm = dmin * m;
+        o[i] = dsc * q - dm;
+      }
+    } else {  // Q3_K, gguf.rs:760-819
+      const uint8_t* hmask = blk;
+      const uint8_t* qs = blk + 32;
+      const uint8_t* sr = blk + 96;
+      const float d = half_to_float((uint16_t)(blk[108] | (blk[109] << 8)));
+      const uint32_t w0 = (uint32_t)sr[0] | ((uint32_t)sr[1] << 8) | ((uint32_t)sr[2] << 16) |
+                          ((uint32_t)sr[3] << 24);
+      const uint32_t w1 = (uint32_t)sr[4] | ((uint32_t)sr[5] << 8) | ((uint32_t)sr[6] << 16) |
+                          ((uint32_t)sr[7] << 24);
+      const uint32_t utmp[4] = {w0 & 0x3f3f3f3fu, w1 & 0x3f3f3f3fu, (w0 >> 6) & 0x3f3f3f3fu,
+                                (w1 >> 6) & 0x3f3f3f3fu};
+      int scales[16];
+      for (int i = 0; i < 4; ++i)
+        for (int b = 0; b < 4; ++b) scales[i * 4 + b] = (int)((utmp[i] >> (b * 8)) & 0xFF) - 32;
+      for (int i = 0; i < 256; ++i) {
+        const int low2 = (qs[i / 4] >> (2 * (i % 4))) & 0x3;
+        const int hbit = (hmask[i / 8] >> (i % 8)) & 1;
+        const int raw = (low2 | (hbit << 2)) - 4;
+        const float ds = d * (float)scales[i / 16];
+        o[i] = ds * (float)raw;
+      }
+    }
+  }
+  return 0;
+}
+
 // crates/sketchpad-llm/src/quantized.rs:70-92 (QuantizedTensor::matmul_f32): row dequant into
 // a buffer, then for every token a sequential f32 dot (Iterator::sum folds from -0.0).
 int or_q8_0_matmul(const uint8_t* data, int64_t N, int64_t K, const float* x, int64_t M,

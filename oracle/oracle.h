@@ -56,6 +56,8 @@ int or_attention(const float* q, const float* k, const float* v, const float* ma
 /* Q8_0 block decode, crates/sketchpad-convert/src/gguf.rs:643-656.
  * data: nblocks * 34 bytes (f16 LE scale + 32 int8); out: nblocks*32 floats. */
 int or_q8_0_dequantize(const uint8_t* data, int64_t nblocks, float* out);
+// K-quant super-blocks (fmt = GGML type id: 10 Q2_K, 11 Q3_K, 12 Q4_K) -> 256 f32 values each.
+int or_kquant_dequantize(int fmt, const uint8_t* data, int64_t nblocks, float* out);
 /* Q8_0 row-dequant matmul, crates/sketchpad-llm/src/quantized.rs:70-92 / :421-446:
  * y[M,N] = x[M,K] . W[N,K]^T, each dot a sequential f32 sum (Rust Iterator::sum). */
 int or_q8_0_matmul(const uint8_t* data, int64_t N, int64_t K, const float* x, int64_t M,

@@ -33,7 +33,21 @@ constexpr int kWRawBytes = kQBN * kQBK;     // 16 KB
 constexpr int kScBytes = 2 * kQBN * 2;      // 1 KB: two k-blocks x 256 rows of f16
 constexpr int kWCvtBytes = kQBN * kQBK * 2; // 32 KB
 
-enum WFormat : int { W_Q8_0 = 0, W_FP8 = 1 };
+enum WFormat : int { W_Q8_0 = 0, W_FP8 = 1, W_Q4K = 2, W_Q2K = 3, W_Q3K = 4 };
+
+// K-quant formats: one 4-bit quant per value (32 bytes per row of a k-tile), f32 factors a, b
+// per sub-block of kSub values; w = a * (q - kOff) - b.
+template <int WF>
+struct KqFmt {
+  static constexpr bool kIsK = WF >= W_Q4K;
+  enum : int {
+    kSub = WF == W_Q4K ? 32 : 16,
+    kOff = WF == W_Q3K ? 4 : 0,
+    kFactorRows = kQBK / kSub,              // sub-blocks per k-tile
+    kQBytes = kQBN * kQBK / 2,              // 8 KB of nibbles
+    kFactorBytes = kFactorRows * kQBN * 4,  // one factor array
+  };
+};
 
 struct QlSmem {
   static constexpr int kX = 0;
@@ -51,6 +65,8 @@ struct QlParams {
   const uint16_t* q8_scale;  // Q8_0: [K/32, N] f16 bits (loaded by TMA)
   const float* fp8_scale;    // FP8: [N] or [1]
   int64_t nscale;
+  const float* kq_a;         // K-quants: factors a, b [K/sub, N] (loaded by TMA)
+  const float* kq_b;
   const __nv_bfloat16* bias;  // [N] or null
   __nv_bfloat16* y;           // [M, ldy]: columns [0, N) written
   // epilogue y = residual + gate[n] * rope(x.W^T + bias): the DiT blocks' gated residual
@@ -98,6 +114,34 @@ __device__ __forceinline__ void q8x4_to_bf16(uint32_t w, float s, uint32_t& lo, 
   hi = bf16x2_of(b);
 }
 
+// 8 nibbles (values 0..7 of a group in k order: byte j holds values 2j, 2j+1 in its low and
+// high nibble) -> 4 x bf16x2 of a * (q - off) - b, the product and difference each rounded
+// in f32 (packed f32x2, no contraction) as the reference's decode computes them.
+__device__ __forceinline__ void k4x8_to_bf16(uint32_t w, float a, float b, int off, uint32_t& o0,
+                                             uint32_t& o1, uint32_t& o2, uint32_t& o3) {
+  const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+  const uint32_t u0 = prmt(lo, hi, 0x5140);  // values 0..3 as bytes
+  const uint32_t u1 = prmt(lo, hi, 0x7362);  // values 4..7
+  const float m = 8388608.0f + (float)off;   // 2^23 + off: q - off exactly
+  const uint64_t magic = pk2(__float_as_uint(m), __float_as_uint(m));
+  const uint64_t a2 = pk2(__float_as_uint(a), __float_as_uint(a));
+  const uint64_t b2 = pk2(__float_as_uint(b), __float_as_uint(b));
+  uint64_t v[4] = {pk2(prmt(u0, 0x4B000000u, 0x7650), prmt(u0, 0x4B000000u, 0x7651)),
+                   pk2(prmt(u0, 0x4B000000u, 0x7652), prmt(u0, 0x4B000000u, 0x7653)),
+                   pk2(prmt(u1, 0x4B000000u, 0x7650), prmt(u1, 0x4B000000u, 0x7651)),
+                   pk2(prmt(u1, 0x4B000000u, 0x7652), prmt(u1, 0x4B000000u, 0x7653))};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(v[i]) : "l"(v[i]), "l"(magic));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(v[i]) : "l"(v[i]), "l"(a2));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(v[i]) : "l"(v[i]), "l"(b2));
+  }
+  o0 = bf16x2_of(v[0]);
+  o1 = bf16x2_of(v[1]);
+  o2 = bf16x2_of(v[2]);
+  o3 = bf16x2_of(v[3]);
+}
+
 // 4 e4m3 bytes -> 2 x bf16x2, exact: the e4m3 bit pattern is placed in bf16 position
 // (exponent bias 7 instead of 127) and multiplied by 2^120; e4m3 subnormals land on bf16
 // subnormals and are scaled exactly as well.
@@ -114,8 +158,12 @@ __device__ __forceinline__ void e4m3x4_to_bf16(uint32_t w, uint32_t& lo, uint32_
 template <int WF>
 __global__ void __launch_bounds__(kQThreads, 1)
     qlinear_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
-                   const __grid_constant__ CUtensorMap tms, const QlParams p) {
+                   const __grid_constant__ CUtensorMap tms, const __grid_constant__ CUtensorMap tmb,
+                   const QlParams p) {
   using L = QlSmem;
+  using KF = KqFmt<WF>;
+  // K-quants: a raw stage holds the nibble tile, then factor arrays a and b
+  static_assert(KF::kQBytes + 2 * KF::kFactorBytes <= kWRawBytes, "k-quant raw stage");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -161,8 +209,11 @@ __global__ void __launch_bounds__(kQThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmx);
       tma_prefetch_desc(&tmw);
-      if constexpr (WF == W_Q8_0) tma_prefetch_desc(&tms);
-      constexpr uint32_t kTx = kXBytes + kWRawBytes + (WF == W_Q8_0 ? kScBytes : 0);
+      if constexpr (WF == W_Q8_0 || KF::kIsK) tma_prefetch_desc(&tms);
+      if constexpr (KF::kIsK) tma_prefetch_desc(&tmb);
+      constexpr uint32_t kTx =
+          kXBytes + (KF::kIsK ? KF::kQBytes + 2 * KF::kFactorBytes
+                              : kWRawBytes + (WF == W_Q8_0 ? kScBytes : 0));
       int issued = 0;
       for (int kt = 0; kt < ktiles; ++kt) {
         const int st = kt % kRawStages;
@@ -170,7 +221,15 @@ __global__ void __launch_bounds__(kQThreads, 1)
         if (kt >= kRawStages && !mbar_wait(&raw_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) break;
         mbar_arrive_expect_tx(&raw_full[st], kTx);
         tma_load_2d(smem + L::kX + st * kXBytes, &tmx, &raw_full[st], kt * kQBK, m0);
-        tma_load_2d(smem + L::kWRaw + st * kWRawBytes, &tmw, &raw_full[st], kt * kQBK, n0);
+        if constexpr (KF::kIsK) {
+          uint8_t* rw = smem + L::kWRaw + st * kWRawBytes;
+          tma_load_2d(rw, &tmw, &raw_full[st], kt * (kQBK / 2), n0);
+          tma_load_2d(rw + KF::kQBytes, &tms, &raw_full[st], n0, kt * KF::kFactorRows);
+          tma_load_2d(rw + KF::kQBytes + KF::kFactorBytes, &tmb, &raw_full[st], n0,
+                      kt * KF::kFactorRows);
+        } else {
+          tma_load_2d(smem + L::kWRaw + st * kWRawBytes, &tmw, &raw_full[st], kt * kQBK, n0);
+        }
         if constexpr (WF == W_Q8_0)
           tma_load_2d(smem + L::kSc + st * kScBytes, &tms, &raw_full[st], n0, kt * (kQBK / 32));
         issued = kt + 1;
@@ -231,8 +290,18 @@ __global__ void __launch_bounds__(kQThreads, 1)
       for (int it = 0; it < (kQBN * 4) / kQDecoders; ++it) {
         const int task = t + it * kQDecoders;
         const int row = task >> 2, ch = task & 3;  // 16 weights: k = 16*ch .. 16*ch+15
-        const uint4 w = *reinterpret_cast<const uint4*>(raw + row * 64 + ch * 16);
         uint32_t o[8];
+        if constexpr (KF::kIsK) {
+          // 16 nibbles (8 bytes); rows past N read TMA zero fill: a = b = 0, weights 0
+          const uint2 w = *reinterpret_cast<const uint2*>(raw + row * 32 + ch * 8);
+          const float* fa = reinterpret_cast<const float*>(raw + KF::kQBytes);
+          const int sb = (ch * 16) / KF::kSub;
+          const float a = fa[sb * kQBN + row];
+          const float b = fa[KF::kFactorRows * kQBN + sb * kQBN + row];
+          k4x8_to_bf16(w.x, a, b, KF::kOff, o[0], o[1], o[2], o[3]);
+          k4x8_to_bf16(w.y, a, b, KF::kOff, o[4], o[5], o[6], o[7]);
+        } else {
+        const uint4 w = *reinterpret_cast<const uint4*>(raw + row * 64 + ch * 16);
         if constexpr (WF == W_Q8_0) {
           // rows past N read TMA zero fill: scale 0, weights 0
           const float s = __half2float(sc[(ch >> 1) * kQBN + row]);
@@ -245,6 +314,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
           e4m3x4_to_bf16(w.y, o[2], o[3]);
           e4m3x4_to_bf16(w.z, o[4], o[5]);
           e4m3x4_to_bf16(w.w, o[6], o[7]);
+        }
         }
         // bf16 row of 64 = eight 16-byte chunks; this task fills chunks 2*ch and 2*ch+1
         uint8_t* rowp = cvt + row * 128;
@@ -335,8 +405,12 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
       (WF == W_Q8_0 && !aligned(p.q8_scale, 16)))
     return set_error(SP_ERR_ALIGN,
                      "quantized linear: x, weights, scales and y must be 16-byte aligned");
-  CUtensorMap mx, mw, ms;
+  using KF = KqFmt<WF>;
+  if (KF::kIsK && (!aligned(p.kq_a, 16) || !aligned(p.kq_b, 16)))
+    return set_error(SP_ERR_ALIGN, "quantized linear: k-quant factors must be 16-byte aligned");
+  CUtensorMap mx, mw, ms, mb;
   std::memset(&ms, 0, sizeof(ms));
+  std::memset(&mb, 0, sizeof(mb));
   {
     const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
     const uint64_t strides[1] = {(uint64_t)p.K * 2};
@@ -345,7 +419,25 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
                               CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   }
-  {
+  if (KF::kIsK) {
+    // nibbles [N, K/2] bytes: a k-tile of 64 values is 32 bytes of each of 256 rows
+    const uint64_t dims[2] = {(uint64_t)(p.K / 2), (uint64_t)p.N};
+    const uint64_t strides[1] = {(uint64_t)(p.K / 2)};
+    const uint32_t box[2] = {kQBK / 2, kQBN};
+    if (int rc = encode_tiled(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w8, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+    // factors a, b [K/sub, N] f32: one box = the k-tile's sub-blocks x 256 rows
+    const uint64_t fdims[2] = {(uint64_t)p.N, (uint64_t)(p.K / KF::kSub)};
+    const uint64_t fstrides[1] = {(uint64_t)p.N * 4};
+    const uint32_t fbox[2] = {kQBN, (uint32_t)KF::kFactorRows};
+    if (int rc = encode_tiled(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.kq_a, fdims, fstrides,
+                              fbox, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+    if (int rc = encode_tiled(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.kq_b, fdims, fstrides,
+                              fbox, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+  } else {
     const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
     const uint64_t strides[1] = {(uint64_t)p.K};
     const uint32_t box[2] = {kQBK, kQBN};
@@ -373,7 +465,7 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
     }
   }
   dim3 grid((unsigned)((p.M + kQBM - 1) / kQBM), (unsigned)((p.N + kQBN - 1) / kQBN));
-  kern<<<grid, kQThreads, QlSmem::kAlloc, s>>>(mx, mw, ms, p);
+  kern<<<grid, kQThreads, QlSmem::kAlloc, s>>>(mx, mw, ms, mb, p);
   return check_launch("quantized linear");
 }
 
@@ -404,10 +496,17 @@ struct QlEpilogue {
 template <int WF>
 int ql_entry(const char* what, const void* x, const void* w, const void* q8_scale,
              const float* fp8_scale, int64_t nscale, const void* bias, void* y, int64_t M,
-             int64_t N, int64_t K, int dtype, const QlEpilogue& e, void* stream) {
+             int64_t N, int64_t K, int dtype, const QlEpilogue& e, void* stream,
+             const float* kq_a = nullptr, const float* kq_b = nullptr) {
   clear_error();
-  if (!x || !w || (!q8_scale && !fp8_scale) || !y)
+  const bool have_scales = WF == W_Q8_0 ? q8_scale != nullptr
+                           : WF == W_FP8 ? fp8_scale != nullptr
+                                         : (kq_a != nullptr && kq_b != nullptr);
+  if (!x || !w || !have_scales || !y)
     return set_error(SP_ERR_INVALID_ARG, "%s: null pointer", what);
+  if (KqFmt<WF>::kIsK && K % 256)
+    return set_error(SP_ERR_SHAPE, "%s: K=%lld must be a multiple of 256 (k-quant super-blocks)",
+                     what, (long long)K);
   if (WF == W_FP8 && nscale != 1 && nscale != N)
     return set_error(SP_ERR_SHAPE, "%s: scale count %lld must be 1 or N", what, (long long)nscale);
   if (int rc = check_ql_shape(M, N, K, dtype)) return rc;
@@ -429,7 +528,7 @@ int ql_entry(const char* what, const void* x, const void* w, const void* q8_scal
     if (!aligned(e.rope, 8)) return set_error(SP_ERR_ALIGN, "%s: rope table must be 8-byte aligned", what);
   }
   if (int rc = require_sm100()) return rc;
-  QlParams p{M, N, K, static_cast<const uint16_t*>(q8_scale), fp8_scale, nscale,
+  QlParams p{M, N, K, static_cast<const uint16_t*>(q8_scale), fp8_scale, nscale, kq_a, kq_b,
              static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
              static_cast<const __nv_bfloat16*>(e.gate), static_cast<const __nv_bfloat16*>(e.residual),
              ldy, reinterpret_cast<const float2*>(e.rope), e.pos_off, e.pos_div, e.pos_mod,
@@ -485,6 +584,26 @@ int sp_q8_0_linear_rope(const void* x, const void* q, const void* scale, const v
       sp::roped(ldy, rope_cos_sin, rope_positions, rope_cols, head_dim, pos_offset, pos_div,
                 pos_mod),
       stream);
+}
+
+int sp_kquant_linear(int fmt, const void* x, const void* qpack, const float* a, const float* b,
+                     const void* bias, void* y, int64_t M, int64_t N, int64_t K, int dtype,
+                     void* stream) {
+  using namespace sp;
+  switch (fmt) {
+    case SP_QK_Q4_K:
+      return ql_entry<W_Q4K>("q4_k linear", x, qpack, nullptr, nullptr, 0, bias, y, M, N, K,
+                             dtype, QlEpilogue{}, stream, a, b);
+    case SP_QK_Q2_K:
+      return ql_entry<W_Q2K>("q2_k linear", x, qpack, nullptr, nullptr, 0, bias, y, M, N, K,
+                             dtype, QlEpilogue{}, stream, a, b);
+    case SP_QK_Q3_K:
+      return ql_entry<W_Q3K>("q3_k linear", x, qpack, nullptr, nullptr, 0, bias, y, M, N, K,
+                             dtype, QlEpilogue{}, stream, a, b);
+    default:
+      clear_error();
+      return set_error(SP_ERR_DTYPE, "k-quant linear: unknown format %d", fmt);
+  }
 }
 
 int sp_fp8_linear(const void* x, const void* w_e4m3, const float* scale, int64_t nscale, const void* bias,

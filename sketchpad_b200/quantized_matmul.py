@@ -1,12 +1,15 @@
-"""Q8_0 (GGUF) linear layers with the dequantization fused into the GEMM mainloop.
+"""GGUF-quantized linear layers (Q8_0, Q4_K, Q2_K, Q3_K) with the dequantization fused into
+the GEMM mainloop.
 
 Host mirror of crates/sketchpad-cubecl/src/quantized_matmul.rs:
-  :33    GpuQuantType (Q8_0 is the format on this path; Q4_K/Q2_K/Q3_K are not built)
-  :376   dequantize_q8_0(packed, out_features, in_features)
+  :33    GpuQuantType {Q8_0, Q4K, Q2K, Q3K}
+  :376   dequantize_q8_0(packed, out_features, in_features); :410-520 the K-quant dequants
   :655   GpuQuantizedLinear { from_bytes :670, dequantize :705, forward_burn :726, forward :752 }
-Weights stay quantized in HBM (planar int8 + f16 block scales, a lossless repack of the
-34-byte GGUF blocks).  `dequantize()` in f32 is bit-exact with the CPU decode
-(crates/sketchpad-convert/src/gguf.rs:643-656); `forward` decodes to bf16 inside the GEMM.
+Weights stay quantized in HBM, repacked losslessly: Q8_0 as planar int8 + f16 block scales;
+the K-quants as one 4-bit quant per value + two f32 factors per sub-block (see
+include/sketchpad_b200.h).  `dequantize()` in f32 is bit-exact with the CPU decode
+(crates/sketchpad-convert/src/gguf.rs:643-656 for Q8_0, :737-871 for the K-quants);
+`forward` decodes to bf16 inside the GEMM.
 """
 from __future__ import annotations
 
@@ -24,6 +27,41 @@ from ._torch import dtype_code, ptr, require_cuda, stream_ptr
 
 class GpuQuantType(enum.Enum):
     Q8_0 = "q8_0"
+    Q4K = "q4_k"
+    Q2K = "q2_k"
+    Q3K = "q3_k"
+
+
+# GGML type id, bytes per 256-value super-block, values per factor sub-block
+_KQ = {GpuQuantType.Q4K: (12, 144, 32), GpuQuantType.Q2K: (10, 84, 16),
+       GpuQuantType.Q3K: (11, 110, 16)}
+
+
+def repack_kquant_host(data, quant_type: GpuQuantType, out_features: int, in_features: int):
+    """GGUF K-quant bytes -> (qpack uint8 [out, in/2], a f32 [in/sub, out], b f32 [in/sub, out])
+    on the host (the layout of sp_kquant_repack_host)."""
+    fmt, _, sub = _KQ[quant_type]
+    buf = np.frombuffer(bytes(data), np.uint8) if not isinstance(data, np.ndarray) else \
+        np.ascontiguousarray(data, dtype=np.uint8)
+    qp = np.empty((out_features, in_features // 2), np.uint8)
+    a = np.empty((in_features // sub, out_features), np.float32)
+    b = np.empty_like(a)
+    _lib.call("sp_kquant_repack_host", fmt, buf.ctypes.data_as(ctypes.c_void_p), buf.size,
+              out_features, in_features, qp.ctypes.data_as(ctypes.c_void_p),
+              a.ctypes.data_as(ctypes.c_void_p), b.ctypes.data_as(ctypes.c_void_p))
+    return qp, a, b
+
+
+def dequantize_kquant(quant_type: GpuQuantType, qpack: torch.Tensor, a: torch.Tensor,
+                      b: torch.Tensor, out_features: int, in_features: int,
+                      dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """dequantize_q4k / dequantize_q2k / dequantize_q3k (quantized_matmul.rs:410-520) from the
+    repacked form; f32 output is bit-exact with the CPU decode."""
+    dev = require_cuda(qpack, a, b)
+    out = torch.empty((out_features, in_features), dtype=dtype, device=dev)
+    _lib.call("sp_kquant_dequant", _KQ[quant_type][0], ptr(qpack), ptr(a), ptr(b), out_features,
+              in_features, ptr(out), dtype_code(dtype), stream_ptr(dev))
+    return out
 
 
 def repack_q8_0_host(data: bytes | np.ndarray, out_features: int, in_features: int):
@@ -121,12 +159,19 @@ def _epilogue_operands(gate, residual, M, N):
 
 
 class GpuQuantizedLinear:
-    """quantized_matmul.rs:655-767 for Q8_0: output = input @ weight.T (+ optional bias)."""
+    """quantized_matmul.rs:655-767: output = input @ weight.T (+ optional bias).
+
+    Q8_0: q int8 [out, in], scale f16 bits [in/32, out].  K-quants: q = qpack uint8
+    [out, in/2], scale = a and kmin = b, f32 [in/sub, out]."""
 
     def __init__(self, q: torch.Tensor, scale: torch.Tensor, out_features: int, in_features: int,
-                 dtype: torch.dtype = torch.bfloat16, bias: Optional[torch.Tensor] = None):
-        self.q, self.scale = q, scale
-        self.quant_type = GpuQuantType.Q8_0
+                 dtype: torch.dtype = torch.bfloat16, bias: Optional[torch.Tensor] = None,
+                 quant_type: GpuQuantType = GpuQuantType.Q8_0,
+                 kmin: Optional[torch.Tensor] = None):
+        self.q, self.scale, self.kmin = q, scale, kmin
+        self.quant_type = quant_type
+        if quant_type != GpuQuantType.Q8_0 and kmin is None:
+            raise ValueError("k-quant layers need both factor arrays (scale = a, kmin = b)")
         self.out_features, self.in_features = out_features, in_features
         self.dtype = dtype
         self.bias = bias
@@ -134,14 +179,22 @@ class GpuQuantizedLinear:
     @classmethod
     def from_bytes(cls, data, quant_type: GpuQuantType, out_features: int, in_features: int,
                    device="cuda", dtype: torch.dtype = torch.bfloat16, bias=None):
-        """Upload raw GGUF bytes (little-endian Q8_0 blocks), repacked losslessly."""
+        """Upload raw GGUF bytes (little-endian Q8_0 blocks or K-quant super-blocks), repacked
+        losslessly."""
+        if quant_type in _KQ:
+            qp, a, b = repack_kquant_host(data, quant_type, out_features, in_features)
+            t = lambda v: torch.from_numpy(v).to(device)  # noqa: E731
+            return cls(t(qp), t(a), out_features, in_features, dtype, bias, quant_type, t(b))
         if quant_type != GpuQuantType.Q8_0:
-            raise ValueError(f"{quant_type} is not supported (Q8_0 only)")
+            raise ValueError(f"{quant_type} is not supported")
         q, s = repack_q8_0_host(data, out_features, in_features)
         return cls(torch.from_numpy(q).to(device), torch.from_numpy(s.view(np.int16)).to(device),
                    out_features, in_features, dtype, bias)
 
     def dequantize(self, dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        if self.quant_type in _KQ:
+            return dequantize_kquant(self.quant_type, self.q, self.scale, self.kmin,
+                                     self.out_features, self.in_features, dtype or torch.float32)
         return dequantize_q8_0(self.q, self.scale, self.out_features, self.in_features,
                                dtype or torch.float32)
 
@@ -165,6 +218,18 @@ class GpuQuantizedLinear:
         b = self.bias
         if b is not None and b.dtype != torch.bfloat16:
             b = b.to(torch.bfloat16)
+        if self.quant_type in _KQ:
+            if gate is not None or residual is not None or rope is not None:
+                raise ValueError("k-quant layers have the plain (bias) epilogue only")
+            y = out if out is not None else torch.empty((M, self.out_features),
+                                                        dtype=torch.bfloat16, device=dev)
+            if y.dtype != torch.bfloat16 or not y.is_contiguous() or y.numel() != M * self.out_features:
+                raise ValueError("out must be a contiguous bf16 tensor of the output's shape")
+            _lib.call("sp_kquant_linear", _KQ[self.quant_type][0], ptr(x), ptr(self.q),
+                      ptr(self.scale), ptr(self.kmin), ptr(b), ptr(y), M, self.out_features,
+                      self.in_features, _lib.SP_BF16, stream_ptr(dev))
+            y = y.reshape(*lead, self.out_features)
+            return y if input.dtype == torch.bfloat16 else y.to(input.dtype)
         if rope is not None or (out is not None and not out.is_contiguous()):
             if gate is not None or residual is not None:
                 raise ValueError("the rope / strided-output epilogue takes no gate or residual")
@@ -206,6 +271,24 @@ def q8_0_quantize_reference(w: np.ndarray) -> bytes:
     return out.tobytes()
 
 
+def make_kquant_synthetic(quant_type: GpuQuantType, out_features: int, in_features: int,
+                          seed: int = 0) -> bytes:
+    """Random K-quant super-blocks: every quant / scale / mask byte uniform, d and dmin f16
+    ~ U(0.0005, 0.005) (normal f16 values), so decoded weights are O(0.1)."""
+    fmt, nbytes, _ = _KQ[quant_type]
+    rng = np.random.default_rng(seed)
+    nb = out_features * in_features // 256
+    blocks = rng.integers(0, 256, (nb, nbytes), dtype=np.uint8)
+    f16 = lambda: rng.uniform(0.0005, 0.005, nb).astype(np.float16).view(np.uint8).reshape(-1, 2)  # noqa: E731
+    if quant_type == GpuQuantType.Q4K:
+        blocks[:, 0:2], blocks[:, 2:4] = f16(), f16()
+    elif quant_type == GpuQuantType.Q2K:
+        blocks[:, 80:82], blocks[:, 82:84] = f16(), f16()
+    else:
+        blocks[:, 108:110] = f16()
+    return blocks.tobytes()
+
+
 def make_q8_0_synthetic(out_features: int, in_features: int, seed: int = 0) -> bytes:
     """BASELINE config 4's weights: int8 ~ U[-127,127], f16 scale ~ U(0.001, 0.02)."""
     rng = np.random.default_rng(seed)
@@ -217,4 +300,5 @@ def make_q8_0_synthetic(out_features: int, in_features: int, seed: int = 0) -> b
 
 
 __all__ = ["GpuQuantType", "GpuQuantizedLinear", "dequantize_q8_0", "repack_q8_0",
-           "repack_q8_0_host", "q8_0_quantize_reference", "make_q8_0_synthetic"]
+           "repack_q8_0_host", "q8_0_quantize_reference", "make_q8_0_synthetic",
+           "repack_kquant_host", "dequantize_kquant", "make_kquant_synthetic"]

@@ -296,3 +296,53 @@ def test_rope_epilogue_rejects_bad_geometry():
         lin.forward(x, rope=RopeEpilogue(tab, 32, 16, 0, 1, 5))  # mod > table rows
     with pytest.raises(Exception, match="head_dim"):
         lin.forward(x, rope=RopeEpilogue(tab, 36, 12, 0, 1, 4))  # 8 does not divide 12
+
+
+_KQ_CASES = [("Q4K", 12), ("Q2K", 10), ("Q3K", 11)]
+
+
+@pytest.mark.parametrize("name,fmt", _KQ_CASES)
+@pytest.mark.parametrize("N,K", [(64, 512), (300, 1024)])
+def test_kquant_dequant_bit_exact(name, fmt, N, K):
+    from sketchpad_b200.quantized_matmul import make_kquant_synthetic
+    qt = GpuQuantType[name]
+    raw = make_kquant_synthetic(qt, N, K, seed=fmt + N)
+    lin = GpuQuantizedLinear.from_bytes(raw, qt, N, K)
+    got = to_np(lin.dequantize())
+    ref = oracle.kquant_dequantize(fmt, np.frombuffer(raw, np.uint8), N * K).reshape(N, K)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("name,fmt", _KQ_CASES)
+@pytest.mark.parametrize("M,N,K", [(200, 256, 512), (4608, 3072, 3072), (77, 48, 256)])
+def test_kquant_linear_vs_oracle(name, fmt, M, N, K):
+    from sketchpad_b200.quantized_matmul import make_kquant_synthetic
+    qt = GpuQuantType[name]
+    raw = make_kquant_synthetic(qt, N, K, seed=M + fmt)
+    g = torch.Generator(device="cpu").manual_seed(M)
+    bias = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+    lin = GpuQuantizedLinear.from_bytes(raw, qt, N, K, bias=bias.cuda())
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    y = lin.forward(x.cuda())
+    torch.cuda.synchronize()
+    w = oracle.kquant_dequantize(fmt, np.frombuffer(raw, np.uint8), N * K).reshape(N, K)
+    rows = slice(0, min(M, 256))
+    ref = oracle.linear_nt(to_np(x[rows]), w, to_np(bias))
+    assert rel_err(to_np(y[rows]), ref) < TOL_HALF
+    if M > 256:
+        ref_tail = oracle.linear_nt(to_np(x[-64:]), w, to_np(bias))
+        assert rel_err(to_np(y[-64:]), ref_tail) < TOL_HALF
+
+
+def test_kquant_linear_rejects_bad_shapes():
+    from sketchpad_b200 import _lib
+    from sketchpad_b200.quantized_matmul import make_kquant_synthetic
+    lin = GpuQuantizedLinear.from_bytes(make_kquant_synthetic(GpuQuantType.Q4K, 16, 256),
+                                        GpuQuantType.Q4K, 16, 256)
+    with pytest.raises(ValueError, match="epilogue"):
+        lin.forward(torch.zeros(4, 256, device="cuda", dtype=torch.bfloat16),
+                    gate=torch.ones(16, device="cuda", dtype=torch.bfloat16))
+    x = torch.zeros(4, 192, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(_lib.SketchpadError, match="multiple of 256"):
+        _lib.call("sp_kquant_linear", 12, x.data_ptr(), lin.q.data_ptr(), lin.scale.data_ptr(),
+                  lin.kmin.data_ptr(), None, x.data_ptr(), 4, 16, 192, _lib.SP_BF16, None)
