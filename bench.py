@@ -455,6 +455,21 @@ def _case_fp8(torch, M, N, K):
     return (lambda: lin.forward(x, out=y)), 2.0 * M * N * K, "flop"
 
 
+def _case_denoise_loop(torch, kind, steps):
+    from sketchpad_b200.denoise import Sd1xDenoiseLoop
+    from sketchpad_b200.samplers import DdimSampler, DpmPlusPlusSampler, NoiseSchedule
+    from sketchpad_b200.unet import UNetB200, make_unet_params, unet_flops
+    net = UNetB200(make_unet_params(device="cuda", seed=0), device="cuda")
+    sch = NoiseSchedule.sd1x()
+    smp = DdimSampler(sch, steps) if kind == "ddim" else DpmPlusPlusSampler(sch, steps)
+    loop = Sd1xDenoiseLoop(net, smp, guidance=7.5)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    lat = torch.randn(1, 4, 64, 64, device="cuda", generator=g)
+    cu = torch.randn(1, 77, 768, device="cuda", generator=g)
+    cc = torch.randn(1, 77, 768, device="cuda", generator=g)
+    return (lambda: loop(lat, cu, cc)), steps * unet_flops()["total"], "flop"
+
+
 def _case_unet_step(torch):
     from sketchpad_b200.unet import UNetB200, make_unet_params, unet_flops
     net = UNetB200(make_unet_params(device="cuda", seed=0), device="cuda")
@@ -508,6 +523,8 @@ def _case_wan_block(torch):
 
 CASES = {
     "unet_step_eager": _case_unet_step,
+    "sd1x_ddim_loop_20": lambda t: _case_denoise_loop(t, "ddim", 20),
+    "sd1x_dpmpp2m_loop_20": lambda t: _case_denoise_loop(t, "dpmpp_2m", 20),
     "flux_double_4096x512": lambda t: _case_flux_block(t, False),
     "flux_single_4608": lambda t: _case_flux_block(t, True),
     "flux_step": _case_flux_step,

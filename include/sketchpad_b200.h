@@ -280,6 +280,27 @@ int sp_layernorm_modulate(const void* x, const void* scale, const void* shift, v
                           int64_t rows, int64_t n, int64_t rows_per_group, int64_t mod_stride,
                           float eps, int unbiased, int dtype, void* stream);
 
+/* ------------------------------------------------------------------------------------
+ * Denoising-loop latent update fused with classifier-free guidance (one pass over the
+ * latent).  eps = eps_uncond + (eps_cond - eps_uncond) * guidance (apply_guidance,
+ * crates/sketchpad-samplers/src/ddim.rs:158-164); eps_cond NULL means eps = eps_uncond.
+ * x, eps_*, noise, out: n elements of `dtype`, f32 arithmetic in the reference's order;
+ * out may be x.  The scalars are the host values of the reference's step.
+ * ------------------------------------------------------------------------------------ */
+/* DdimSampler::step (ddim.rs:72-133): out = (x - eps*sqrt_one_minus_at)/sqrt_at * sqrt_at_prev
+ * + dir_xt * eps (+ noise * sigma when noise is non-NULL, eta > 0). */
+int sp_cfg_ddim_step(const void* x, const void* eps_uncond, const void* eps_cond, const void* noise,
+                     void* out, int64_t n, float guidance, float sqrt_one_minus_at, float sqrt_at,
+                     float sqrt_at_prev, float dir_xt, float sigma, int dtype, void* stream);
+/* DpmPlusPlusSampler::step (crates/sketchpad-samplers/src/dpm.rs:101-171): denoised = x - eps
+ * * sigma; out = x * sigma_ratio + d * one_minus_exp_neg_h with d = denoised (first order) or
+ * denoised * one_plus_coeff - prev_denoised * coeff (second order).  prev_denoised (f32, n;
+ * may be NULL for a first-order-only call) receives this step's denoised. */
+int sp_cfg_dpmpp_2m_step(const void* x, const void* eps_uncond, const void* eps_cond,
+                         float* prev_denoised, void* out, int64_t n, float guidance, float sigma,
+                         float sigma_ratio, float one_minus_exp_neg_h, float one_plus_coeff,
+                         float coeff, int second_order, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

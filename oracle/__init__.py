@@ -269,3 +269,36 @@ def conv2d(x, w, b=None, stride: int = 1, pad: int = 0):
     _check(lib().or_conv2d(px, pw, pb, y.ctypes.data_as(_f32p), B, Cin, H, W, Cout, kh, kw,
                            stride, pad), "conv2d")
     return y
+
+
+# ---- denoising-loop latent updates (numpy f32, one rounding per operation, reference order)
+def _guided(eps_u, eps_c, g):
+    # crates/sketchpad-samplers/src/ddim.rs:158-164: uncond + (cond - uncond) * scale
+    u = np.asarray(eps_u, np.float32)
+    if eps_c is None:
+        return u
+    return u + (np.asarray(eps_c, np.float32) - u) * np.float32(g)
+
+
+def ddim_step(x, eps_u, eps_c, guidance, sqrt_one_minus_at, sqrt_at, sqrt_at_prev, dir_xt,
+              noise=None, sigma=0.0):
+    """crates/sketchpad-samplers/src/ddim.rs:96-133 with the step's scalars given."""
+    f = np.float32
+    eps = _guided(eps_u, eps_c, guidance)
+    px0 = (np.asarray(x, f) - eps * f(sqrt_one_minus_at)) / f(sqrt_at)
+    prev = px0 * f(sqrt_at_prev) + f(dir_xt) * eps
+    if noise is not None:
+        prev = prev + np.asarray(noise, f) * f(sigma)
+    return prev
+
+
+def dpmpp_2m_step(x, eps_u, eps_c, guidance, sigma, ratio, one_minus_exp_neg_h, prev=None,
+                  one_plus_coeff=1.0, coeff=0.0):
+    """crates/sketchpad-samplers/src/dpm.rs:126-165: returns (next latent, denoised)."""
+    f = np.float32
+    eps = _guided(eps_u, eps_c, guidance)
+    xv = np.asarray(x, f)
+    den = xv - eps * f(sigma)
+    d = den if prev is None else den * f(one_plus_coeff) - np.asarray(prev, f) * f(coeff)
+    return xv * f(ratio) + d * f(one_minus_exp_neg_h), den
+

@@ -57,6 +57,9 @@ SIGNATURES = {
     "sp_fp8_linear": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "sp_fp8_linear_gated": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int,
                                    _vp]),
+    "sp_cfg_ddim_step": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _f, _f, _f, _f, _f, _f, _int, _vp]),
+    "sp_cfg_dpmpp_2m_step": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _f, _f, _f, _f, _f, _f, _int,
+                                    _int, _vp]),
     "sp_kquant_repack_host": (_int, [_int, _vp, _sz, _i64, _i64, _vp, _vp, _vp]),
     "sp_kquant_dequant": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _vp, _int, _vp]),
     "sp_kquant_linear": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),

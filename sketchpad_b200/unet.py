@@ -22,7 +22,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass, field
-from typing import Dict, List
+from typing import Dict, List, Optional
 
 import numpy as np
 import torch
@@ -482,7 +482,8 @@ class UNetStepGraph:
     inputs, replays, and returns the static output (copy it before the next call)."""
 
     def __init__(self, net: UNetB200, batch: int = 2, hw: int = 64, ctx_len: int = 77,
-                 warmup: int = 2, time_attention: bool = False):
+                 warmup: int = 2, time_attention: bool = False,
+                 out_dtype: Optional[torch.dtype] = None):
         dev = net.device
         cfg = net.cfg
         self.net = net
@@ -506,6 +507,8 @@ class UNetStepGraph:
         try:
             with torch.cuda.graph(self.graph):
                 self.out = net(self.x, self.t, self.ctx)
+                if out_dtype is not None and self.out.dtype != out_dtype:
+                    self.out = self.out.to(out_dtype)  # captured with the step
         finally:
             if time_attention:
                 self.attn_events = net.attn_events
