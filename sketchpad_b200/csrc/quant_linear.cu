@@ -16,6 +16,7 @@
 //                deep (16 warps: two per scheduler, so decode latency overlaps); then the
 //                epilogue, each warp one (TMEM lane quarter, M half, column half): TMEM ->
 //                per-channel scale, bias [, RoPE] [, gate, residual] -> bf16 -> HBM.
+#include <algorithm>
 #include <cstring>
 
 #include "common.cuh"
@@ -79,6 +80,10 @@ struct QlParams {
   const float2* rope;             // [positions, head_dim / 2] or null
   int64_t rope_off, rope_div, rope_mod;
   int rope_cols, rope_half;
+  // split-K (grid.z = splits > 1): CTA z sums k-tiles [z * kt_per_split, ...) and writes its
+  // raw f32 partial to ws[z][M][N]; a reduce pass sums them in order and runs the epilogue
+  float* ws;
+  int splits, kt_per_split;
 };
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -155,6 +160,63 @@ __device__ __forceinline__ void e4m3x4_to_bf16(uint32_t w, uint32_t& lo, uint32_
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(hi) : "r"(tb), "r"(k2p120));
 }
 
+// Epilogue of 8 consecutive accumulator values of row m, columns n .. n+7: FP8 per-channel
+// scale, bias, optional RoPE, optional gate and residual, bf16 store.
+template <int WF>
+__device__ __forceinline__ void ql_finish8(const QlParams& p, float (&v)[8], int64_t m, int64_t n,
+                                           const float2* rope_row) {
+  uint4 rv = make_uint4(0, 0, 0, 0);
+  if (p.residual) rv = *reinterpret_cast<const uint4*>(p.residual + m * p.ldy + n);
+  const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    if constexpr (WF == W_FP8) v[e] *= p.fp8_scale[p.nscale == 1 ? 0 : n + e];
+    if (p.bias) v[e] += __bfloat162float(p.bias[n + e]);
+  }
+  if (rope_row && n < p.rope_cols) {
+    // x*cos + rotate_half(x)*sin, rotate_half([x0, x1]) = [-x1, x0]; 8 | head_dim, so the
+    // group's 4 pairs sit in one head
+    const float2* cs = rope_row + (int)(n % (2 * p.rope_half)) / 2;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 t = cs[e];
+      const float x0 = v[2 * e], x1 = v[2 * e + 1];
+      v[2 * e] = x0 * t.x - x1 * t.y;
+      v[2 * e + 1] = x1 * t.x + x0 * t.y;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    if (p.gate) v[e] *= __bfloat162float(p.gate[n + e]);
+    if (p.residual) v[e] += __bfloat162float(re[e]);
+  }
+  *reinterpret_cast<uint4*>(p.y + m * p.ldy + n) =
+      make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                 pack_bf16x2(v[6], v[7]));
+}
+
+// Split-K reduce: out[m, n..n+7] = epilogue(sum over z of ws[z][m][n..n+7]), z in order, one
+// thread per 8 outputs.
+template <int WF>
+__global__ void __launch_bounds__(256) ql_splitk_reduce_kernel(const QlParams p) {
+  const int64_t groups = p.M * (p.N / 8);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < groups;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / (p.N / 8), n = (i - m * (p.N / 8)) * 8;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int z = 0; z < p.splits; ++z) {
+      const float* src = p.ws + ((int64_t)z * p.M + m) * p.N + n;
+      const float4 a = *reinterpret_cast<const float4*>(src);
+      const float4 b = *reinterpret_cast<const float4*>(src + 4);
+      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+      v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+    }
+    const float2* rope_row =
+        p.rope ? p.rope + ((m + p.rope_off) / p.rope_div % p.rope_mod) * p.rope_half : nullptr;
+    ql_finish8<WF>(p, v, m, n, rope_row);
+  }
+}
+
 template <int WF>
 __global__ void __launch_bounds__(kQThreads, 1)
     qlinear_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
@@ -180,7 +242,9 @@ __global__ void __launch_bounds__(kQThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * kQBM;
   const int n0 = blockIdx.y * kQBN;
-  const int ktiles = (int)(p.K / kQBK);
+  // this CTA's k-tiles (all of them without split-K); kt below counts from 0
+  const int kbase = (int)blockIdx.z * p.kt_per_split;
+  const int ktiles = min((int)(p.K / kQBK) - kbase, p.kt_per_split);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRawStages; ++s) {
@@ -220,18 +284,18 @@ __global__ void __launch_bounds__(kQThreads, 1)
         const uint32_t ph = (kt / kRawStages) & 1;
         if (kt >= kRawStages && !mbar_wait(&raw_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) break;
         mbar_arrive_expect_tx(&raw_full[st], kTx);
-        tma_load_2d(smem + L::kX + st * kXBytes, &tmx, &raw_full[st], kt * kQBK, m0);
+        tma_load_2d(smem + L::kX + st * kXBytes, &tmx, &raw_full[st], (kbase + kt) * kQBK, m0);
         if constexpr (KF::kIsK) {
           uint8_t* rw = smem + L::kWRaw + st * kWRawBytes;
-          tma_load_2d(rw, &tmw, &raw_full[st], kt * (kQBK / 2), n0);
-          tma_load_2d(rw + KF::kQBytes, &tms, &raw_full[st], n0, kt * KF::kFactorRows);
+          tma_load_2d(rw, &tmw, &raw_full[st], (kbase + kt) * (kQBK / 2), n0);
+          tma_load_2d(rw + KF::kQBytes, &tms, &raw_full[st], n0, (kbase + kt) * KF::kFactorRows);
           tma_load_2d(rw + KF::kQBytes + KF::kFactorBytes, &tmb, &raw_full[st], n0,
-                      kt * KF::kFactorRows);
+                      (kbase + kt) * KF::kFactorRows);
         } else {
-          tma_load_2d(smem + L::kWRaw + st * kWRawBytes, &tmw, &raw_full[st], kt * kQBK, n0);
+          tma_load_2d(smem + L::kWRaw + st * kWRawBytes, &tmw, &raw_full[st], (kbase + kt) * kQBK, n0);
         }
         if constexpr (WF == W_Q8_0)
-          tma_load_2d(smem + L::kSc + st * kScBytes, &tms, &raw_full[st], n0, kt * (kQBK / 32));
+          tma_load_2d(smem + L::kSc + st * kScBytes, &tms, &raw_full[st], n0, (kbase + kt) * (kQBK / 32));
         issued = kt + 1;
       }
       if (*abort_flag)
@@ -348,43 +412,27 @@ __global__ void __launch_bounds__(kQThreads, 1)
         if (m >= p.M) continue;
         const int64_t nb = n0 + c;
         if (nb >= p.N) continue;
-        __nv_bfloat16* dst = p.y + m * p.ldy + nb;
-        const __nv_bfloat16* res = p.residual ? p.residual + m * p.ldy + nb : nullptr;
+        if (p.splits > 1) {  // raw partial sums; the reduce pass applies the epilogue
+          float* wdst = p.ws + ((int64_t)blockIdx.z * p.M + m) * p.N + nb;
+#pragma unroll
+          for (int g = 0; g < 32; g += 8) {
+            if (nb + g >= p.N) break;  // N % 16 == 0, so groups of 8 are whole
+            *reinterpret_cast<float4*>(wdst + g) =
+                make_float4(__uint_as_float(r[g]), __uint_as_float(r[g + 1]),
+                            __uint_as_float(r[g + 2]), __uint_as_float(r[g + 3]));
+            *reinterpret_cast<float4*>(wdst + g + 4) =
+                make_float4(__uint_as_float(r[g + 4]), __uint_as_float(r[g + 5]),
+                            __uint_as_float(r[g + 6]), __uint_as_float(r[g + 7]));
+          }
+          continue;
+        }
 #pragma unroll
         for (int g = 0; g < 32; g += 8) {
           if (nb + g >= p.N) break;  // N % 16 == 0, so groups of 8 are whole
-          uint4 rv = make_uint4(0, 0, 0, 0);
-          if (res) rv = *reinterpret_cast<const uint4*>(res + g);
-          const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rv);
           float v[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int64_t n = nb + g + e;
-            float a = __uint_as_float(r[g + e]);
-            if constexpr (WF == W_FP8) a *= p.fp8_scale[p.nscale == 1 ? 0 : n];
-            if (p.bias) a += __bfloat162float(p.bias[n]);
-            v[e] = a;
-          }
-          if (rope_row && nb + g < p.rope_cols) {
-            // x*cos + rotate_half(x)*sin, rotate_half([x0, x1]) = [-x1, x0]; 8 | head_dim, so
-            // the group's 4 pairs sit in one head
-            const float2* cs = rope_row + (int)((nb + g) % (2 * p.rope_half)) / 2;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 t = cs[e];
-              const float x0 = v[2 * e], x1 = v[2 * e + 1];
-              v[2 * e] = x0 * t.x - x1 * t.y;
-              v[2 * e + 1] = x1 * t.x + x0 * t.y;
-            }
-          }
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            if (p.gate) v[e] *= __bfloat162float(p.gate[nb + g + e]);
-            if (res) v[e] += __bfloat162float(re[e]);
-          }
-          *reinterpret_cast<uint4*>(dst + g) =
-              make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
-                         pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+          for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[g + e]);
+          ql_finish8<WF>(p, v, m, nb + g, rope_row);
         }
       }
     }
@@ -464,8 +512,38 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
       return set_error(SP_ERR_LAUNCH, "quantized linear: smem attribute failed: %s", cudaGetErrorString(e));
     }
   }
-  dim3 grid((unsigned)((p.M + kQBM - 1) / kQBM), (unsigned)((p.N + kQBN - 1) / kQBN));
-  kern<<<grid, kQThreads, QlSmem::kAlloc, s>>>(mx, mw, ms, mb, p);
+  const int tiles_m = (int)((p.M + kQBM - 1) / kQBM), tiles_n = (int)((p.N + kQBN - 1) / kQBN);
+  // Split-K when the tile grid leaves most SMs idle (the text-stream and modulation GEMMs of
+  // the DiT blocks): each split's CTAs write f32 partials to stream-ordered scratch, and one
+  // reduce pass sums them in a fixed order and runs the epilogue.  Scratch that cannot be had
+  // means no split.
+  QlParams q = p;
+  const int ktotal = (int)(p.K / kQBK), tiles = tiles_m * tiles_n, sms = num_sms();
+  int splits = 1;
+  if (2 * tiles <= sms && ktotal >= 8) splits = std::min(std::min(8, sms / tiles), ktotal / 4);
+  void* ws = nullptr;
+  if (splits > 1) {
+    q.kt_per_split = (ktotal + splits - 1) / splits;
+    splits = (ktotal + q.kt_per_split - 1) / q.kt_per_split;  // no empty split
+    const size_t bytes = (size_t)splits * (size_t)p.M * (size_t)p.N * sizeof(float);
+    if (cudaMallocAsync(&ws, bytes, s) != cudaSuccess) {
+      cudaGetLastError();
+      ws = nullptr;
+      splits = 1;
+      q.kt_per_split = ktotal;
+    }
+  }
+  q.ws = static_cast<float*>(ws);
+  q.splits = splits;
+  dim3 grid((unsigned)tiles_m, (unsigned)tiles_n, (unsigned)splits);
+  kern<<<grid, kQThreads, QlSmem::kAlloc, s>>>(mx, mw, ms, mb, q);
+  if (splits > 1) {
+    const int64_t groups = p.M * (p.N / 8);
+    const unsigned rblocks = (unsigned)std::min<int64_t>((groups + 255) / 256, 8LL * sms);
+    ql_splitk_reduce_kernel<WF><<<rblocks, 256, 0, s>>>(q);
+    const cudaError_t e = cudaFreeAsync(ws, s);
+    if (e != cudaSuccess) return set_error(SP_ERR_LAUNCH, "quantized linear: scratch free failed");
+  }
   return check_launch("quantized linear");
 }
 
@@ -532,7 +610,7 @@ int ql_entry(const char* what, const void* x, const void* w, const void* q8_scal
              static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
              static_cast<const __nv_bfloat16*>(e.gate), static_cast<const __nv_bfloat16*>(e.residual),
              ldy, reinterpret_cast<const float2*>(e.rope), e.pos_off, e.pos_div, e.pos_mod,
-             (int)e.rope_cols, (int)(e.head_dim / 2)};
+             (int)e.rope_cols, (int)(e.head_dim / 2), nullptr, 1, (int)(K / kQBK)};
   return launch_qlinear<WF>(x, w, p, static_cast<cudaStream_t>(stream));
 }
 

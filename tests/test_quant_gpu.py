@@ -166,7 +166,8 @@ def _epilogue_ref(mm, gate, residual):
     return out if residual is None else out + residual
 
 
-@pytest.mark.parametrize("M,N,K", [(200, 256, 128), (4608, 3072, 3072), (77, 1536, 640)])
+@pytest.mark.parametrize("M,N,K", [(200, 256, 128), (4608, 3072, 3072), (77, 1536, 640),
+                                   (512, 3072, 12288)])  # the last two run split-K
 @pytest.mark.parametrize("mode", ["gate+residual", "residual", "gate", "in_place"])
 def test_q8_0_linear_gated_residual_epilogue(M, N, K, mode):
     raw = make_q8_0_synthetic(N, K, seed=N + K)
@@ -236,7 +237,8 @@ def _rope_ref(y, cos, sin, cols, D, off, div, mod):
 @pytest.mark.parametrize("M,N,K,D,off,div,mod", [
     (4608, 9216, 3072, 128, 0, 1, 4608),   # Flux qkv: q and k of 24 heads rotated
     (300, 384, 256, 64, 36, 24, 3),        # Wan temporal-style positions with a rank offset
-    (77, 256, 128, 128, 5, 1, 40)])
+    (77, 256, 128, 128, 5, 1, 40),
+    (77, 512, 2048, 128, 3, 1, 100)])     # small grid: split-K, the epilogue in the reduce pass
 def test_q8_0_linear_rope_epilogue_strided(M, N, K, D, off, div, mod):
     from sketchpad_b200.flux import rope_tables
     from sketchpad_b200.quantized_matmul import RopeEpilogue, rope_pair_table
@@ -346,3 +348,21 @@ def test_kquant_linear_rejects_bad_shapes():
     with pytest.raises(_lib.SketchpadError, match="multiple of 256"):
         _lib.call("sp_kquant_linear", 12, x.data_ptr(), lin.q.data_ptr(), lin.scale.data_ptr(),
                   lin.kmin.data_ptr(), None, x.data_ptr(), 4, 16, 192, _lib.SP_BF16, None)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 18432, 3072), (512, 3072, 12288), (3, 9216, 3072)])
+def test_splitk_small_grid_linear_vs_oracle(M, N, K):
+    # the DiT modulation (M = 1) and text-stream (M = 512) GEMMs: tile grids of 24-72 CTAs,
+    # run as split-K with the deterministic reduce; two calls give identical bytes
+    raw = make_q8_0_synthetic(N, K, seed=N + M)
+    g = torch.Generator(device="cpu").manual_seed(M + 1)
+    bias = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+    lin = GpuQuantizedLinear.from_bytes(raw, GpuQuantType.Q8_0, N, K, bias=bias.cuda())
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    y1, y2 = lin.forward(x), lin.forward(x)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    rows = slice(0, min(M, 64))
+    ref = oracle.q8_0_matmul(np.frombuffer(raw, np.uint8), N, K, to_np(x[rows])) + to_np(bias)
+    assert rel_err(to_np(y1[rows]), ref) < TOL_HALF
+
