@@ -230,6 +230,17 @@ int sp_fp8_linear(const void* x, const void* w_e4m3, const float* scale, int64_t
 int sp_fp8_linear_gated(const void* x, const void* w_e4m3, const float* scale, int64_t nscale,
                         const void* bias, const void* gate, const void* residual, void* y,
                         int64_t M, int64_t N, int64_t K, int dtype, void* stream);
+/* The feed-forward gate in the GEMM epilogue: W's rows interleaved as (first-half row j,
+ * second-half row j) of the stacked [2F, K] gate/up (or value/gate) weight, so the GEMM's
+ * columns 2j, 2j+1 are (lo, hi) and y[M, N/2] (row stride N/2) gets lo * gelu(hi)
+ * (SP_GLU_GEGLU, crates/sketchpad-unet/src/blocks.rs:446-458) or silu(lo) * hi
+ * (SP_GLU_SWIGLU, crates/sketchpad-core/src/glu.rs:91-96; crates/sketchpad-dit/src/wan.rs:
+ * 330-337) from the f32 accumulators — no [M, 2F] intermediate in HBM. */
+int sp_q8_0_linear_glu(const void* x, const void* q, const void* scale, const void* bias, void* y,
+                       int64_t M, int64_t N, int64_t K, int glu_kind, int dtype, void* stream);
+int sp_fp8_linear_glu(const void* x, const void* w_e4m3, const float* scale, int64_t nscale,
+                      const void* bias, void* y, int64_t M, int64_t N, int64_t K, int glu_kind,
+                      int dtype, void* stream);
 /* The attention projection GEMM of the DiT blocks with its rotary embedding done in the
  * epilogue, written into a strided output:
  *   y[m, n] (row stride ldy >= N, ldy % 8 == 0) = rope(x . W^T + bias)[m, n]

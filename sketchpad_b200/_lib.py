@@ -63,6 +63,9 @@ SIGNATURES = {
     "sp_kquant_repack_host": (_int, [_int, _vp, _sz, _i64, _i64, _vp, _vp, _vp]),
     "sp_kquant_dequant": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _vp, _int, _vp]),
     "sp_kquant_linear": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "sp_q8_0_linear_glu": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp]),
+    "sp_fp8_linear_glu": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _int,
+                                 _vp]),
     "sp_q8_0_linear_rope": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64,
                                    _i64, _i64, _i64, _i64, _i64, _int, _vp]),
     "sp_fp8_linear_rope": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp,

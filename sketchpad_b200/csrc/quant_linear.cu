@@ -84,6 +84,10 @@ struct QlParams {
   // raw f32 partial to ws[z][M][N]; a reduce pass sums them in order and runs the epilogue
   float* ws;
   int splits, kt_per_split;
+  // GLU epilogue (-1: none): weight rows interleaved as (first-half row j, second-half row j),
+  // so columns 2j, 2j+1 of x.W^T + b are (lo, hi) and y[m, j] = lo * gelu(hi) (SP_GLU_GEGLU)
+  // or silu(lo) * hi (SP_GLU_SWIGLU); y holds N/2 columns, ldy apart
+  int glu;
 };
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -160,11 +164,33 @@ __device__ __forceinline__ void e4m3x4_to_bf16(uint32_t w, uint32_t& lo, uint32_
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(hi) : "r"(tb), "r"(k2p120));
 }
 
+__device__ __forceinline__ float ql_gelu_erf(float g) {
+  return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
+}
+// x * sigmoid(x) with an IEEE division, as the reference's silu
+__device__ __forceinline__ float ql_silu(float g) { return g / (1.0f + expf(-g)); }
+
 // Epilogue of 8 consecutive accumulator values of row m, columns n .. n+7: FP8 per-channel
-// scale, bias, optional RoPE, optional gate and residual, bf16 store.
+// scale, bias, then either the GLU (4 outputs at column n/2) or optional RoPE, gate and
+// residual, bf16 store.
 template <int WF>
 __device__ __forceinline__ void ql_finish8(const QlParams& p, float (&v)[8], int64_t m, int64_t n,
                                            const float2* rope_row) {
+  if (p.glu >= 0) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if constexpr (WF == W_FP8) v[e] *= p.fp8_scale[p.nscale == 1 ? 0 : n + e];
+      if (p.bias) v[e] += __bfloat162float(p.bias[n + e]);
+    }
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      o[j] = p.glu == SP_GLU_GEGLU ? v[2 * j] * ql_gelu_erf(v[2 * j + 1])
+                                   : ql_silu(v[2 * j]) * v[2 * j + 1];
+    *reinterpret_cast<uint2*>(p.y + m * p.ldy + n / 2) =
+        make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+    return;
+  }
   uint4 rv = make_uint4(0, 0, 0, 0);
   if (p.residual) rv = *reinterpret_cast<const uint4*>(p.residual + m * p.ldy + n);
   const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rv);
@@ -569,6 +595,7 @@ struct QlEpilogue {
   int64_t ldy = 0;  // 0: N
   const float* rope = nullptr;
   int64_t rope_positions = 0, rope_cols = 0, head_dim = 0, pos_off = 0, pos_div = 1, pos_mod = 1;
+  int glu = -1;
 };
 
 template <int WF>
@@ -588,8 +615,12 @@ int ql_entry(const char* what, const void* x, const void* w, const void* q8_scal
   if (WF == W_FP8 && nscale != 1 && nscale != N)
     return set_error(SP_ERR_SHAPE, "%s: scale count %lld must be 1 or N", what, (long long)nscale);
   if (int rc = check_ql_shape(M, N, K, dtype)) return rc;
-  const int64_t ldy = e.ldy ? e.ldy : N;
-  if (ldy < N || ldy % 8)
+  if (e.glu >= 0 && (e.glu > SP_GLU_SWIGLU || e.gate || e.residual || e.rope))
+    return set_error(SP_ERR_INVALID_ARG, "%s: the GLU epilogue takes no gate, residual or rope",
+                     what);
+  const int64_t out_cols = e.glu >= 0 ? N / 2 : N;
+  const int64_t ldy = e.ldy ? e.ldy : out_cols;
+  if (ldy < out_cols || ldy % 8)
     return set_error(SP_ERR_SHAPE, "%s: row stride %lld must be >= N and a multiple of 8", what,
                      (long long)ldy);
   if (e.residual && !aligned(e.residual, 16))
@@ -610,7 +641,7 @@ int ql_entry(const char* what, const void* x, const void* w, const void* q8_scal
              static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
              static_cast<const __nv_bfloat16*>(e.gate), static_cast<const __nv_bfloat16*>(e.residual),
              ldy, reinterpret_cast<const float2*>(e.rope), e.pos_off, e.pos_div, e.pos_mod,
-             (int)e.rope_cols, (int)(e.head_dim / 2), nullptr, 1, (int)(K / kQBK)};
+             (int)e.rope_cols, (int)(e.head_dim / 2), nullptr, 1, (int)(K / kQBK), e.glu};
   return launch_qlinear<WF>(x, w, p, static_cast<cudaStream_t>(stream));
 }
 
@@ -682,6 +713,23 @@ int sp_kquant_linear(int fmt, const void* x, const void* qpack, const float* a, 
       clear_error();
       return set_error(SP_ERR_DTYPE, "k-quant linear: unknown format %d", fmt);
   }
+}
+
+int sp_q8_0_linear_glu(const void* x, const void* q, const void* scale, const void* bias, void* y,
+                       int64_t M, int64_t N, int64_t K, int glu_kind, int dtype, void* stream) {
+  sp::QlEpilogue e;
+  e.glu = glu_kind < 0 ? SP_GLU_SWIGLU + 1 : glu_kind;  // negative kinds are rejected
+  return sp::ql_entry<sp::W_Q8_0>("q8_0 linear", x, q, scale, nullptr, 0, bias, y, M, N, K, dtype,
+                                  e, stream);
+}
+
+int sp_fp8_linear_glu(const void* x, const void* w_e4m3, const float* scale, int64_t nscale,
+                      const void* bias, void* y, int64_t M, int64_t N, int64_t K, int glu_kind,
+                      int dtype, void* stream) {
+  sp::QlEpilogue e;
+  e.glu = glu_kind < 0 ? SP_GLU_SWIGLU + 1 : glu_kind;
+  return sp::ql_entry<sp::W_FP8>("fp8 linear", x, w_e4m3, nullptr, scale, nscale, bias, y, M, N, K,
+                                 dtype, e, stream);
 }
 
 int sp_fp8_linear(const void* x, const void* w_e4m3, const float* scale, int64_t nscale, const void* bias,

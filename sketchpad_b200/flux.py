@@ -30,9 +30,9 @@ import torch
 import torch.nn.functional as F
 
 from .attention import flash_attention
-from .glu import swiglu
 from .layernorm import layer_norm_modulate
-from .quantized_matmul import GpuQuantizedLinear, RopeEpilogue, rope_pair_table
+from .quantized_matmul import (GLU_SWIGLU, GpuQuantizedLinear, RopeEpilogue, interleave_rows,
+                               rope_pair_table)
 
 
 @dataclass(frozen=True)
@@ -149,16 +149,18 @@ class _SwiGlu:
         h, i = cfg.hidden_size, cfg.intermediate
         gate = _q8_linear(seed, i, h, device, scale_range=cfg.weight_scale)
         up = _q8_linear(seed + 1, i, h, device, scale_range=cfg.weight_scale)
-        # gate and up share x: one GEMM over the stacked rows
-        self.gate_up = GpuQuantizedLinear(torch.cat([gate.q, up.q]),
-                                          torch.cat([gate.scale, up.scale], dim=1),
-                                          2 * i, h, torch.bfloat16, torch.cat([gate.bias, up.bias]))
+        # gate and up share x: one GEMM over their rows interleaved (gate j, up j), whose
+        # epilogue forms silu(gate) * up (no [M, 2I] intermediate)
+        self.gate_up = GpuQuantizedLinear(interleave_rows(gate.q, up.q),
+                                          interleave_rows(gate.scale, up.scale, dim=1),
+                                          2 * i, h, torch.bfloat16,
+                                          interleave_rows(gate.bias, up.bias))
         self.down = _q8_linear(seed + 2, h, i, device, scale_range=cfg.weight_scale)
         self.i = i
 
     def forward(self, x, gate=None, residual=None, out=None):
-        # silu(gate) * up in one pass; the optional gated residual add runs in down's epilogue
-        return self.down(swiglu(self.gate_up(x)), out=out, gate=gate, residual=residual)
+        # silu(gate) * up in gate_up's epilogue; the optional gated residual add in down's
+        return self.down(self.gate_up(x, glu=GLU_SWIGLU), out=out, gate=gate, residual=residual)
 
 
 def _ln(x, scale=None, shift=None):

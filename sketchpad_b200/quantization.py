@@ -116,7 +116,8 @@ class Fp8Linear:
 
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
                 gate: Optional[torch.Tensor] = None,
-                residual: Optional[torch.Tensor] = None, rope=None) -> torch.Tensor:
+                residual: Optional[torch.Tensor] = None, rope=None,
+                glu: Optional[int] = None) -> torch.Tensor:
         """x @ dequant(W)^T + b; with gate / residual: residual + gate * (x @ W^T + b); with
         `rope` (a RopeEpilogue) the rotary embedding of its columns, and `out` may be a
         column slice of a wider buffer."""
@@ -132,6 +133,16 @@ class Fp8Linear:
         b = self.bias
         if b is not None and b.dtype != torch.bfloat16:
             b = b.to(torch.bfloat16)
+        if glu is not None:  # rows interleaved (first-half j, second-half j): y [.., N/2]
+            if gate is not None or residual is not None or rope is not None:
+                raise ValueError("the GLU epilogue takes no gate, residual or rope")
+            y = out if out is not None else torch.empty((M, N // 2), dtype=torch.bfloat16, device=dev)
+            if y.dtype != torch.bfloat16 or not y.is_contiguous() or y.numel() != M * (N // 2):
+                raise ValueError("out must be a contiguous bf16 tensor of [..., N / 2]")
+            _lib.call("sp_fp8_linear_glu", ptr(xx), ptr(self.weight.data), ptr(self.weight.scale),
+                      self.weight.scale.numel(), ptr(b), ptr(y), M, N, K, int(glu), _lib.SP_BF16,
+                      stream_ptr(dev))
+            return y.reshape(*lead, N // 2)
         if rope is not None or (out is not None and not out.is_contiguous()):
             from .quantized_matmul import _NO_ROPE, _output_rows
             if gate is not None or residual is not None:

@@ -142,6 +142,15 @@ def _output_rows(out, M, N, dev):
     return out, o2.stride(0)
 
 
+GLU_GEGLU, GLU_SWIGLU = 0, 1  # sp_glu_kind
+
+
+def interleave_rows(first: torch.Tensor, second: torch.Tensor, dim: int = 0) -> torch.Tensor:
+    """Stack two equally shaped halves row-interleaved along `dim` ((first j, second j), ...),
+    the weight layout of the GLU epilogue: [F, ...] + [F, ...] -> [2F, ...]."""
+    return torch.stack((first, second), dim=dim + 1).flatten(dim, dim + 1)
+
+
 def _epilogue_operands(gate, residual, M, N):
     """bf16 gate [N] and residual [M, N] (contiguous rows) for the gated-residual epilogue."""
     g = None
@@ -201,13 +210,14 @@ class GpuQuantizedLinear:
     def forward(self, input: torch.Tensor, out: Optional[torch.Tensor] = None,
                 gate: Optional[torch.Tensor] = None,
                 residual: Optional[torch.Tensor] = None,
-                rope: Optional[RopeEpilogue] = None) -> torch.Tensor:
+                rope: Optional[RopeEpilogue] = None, glu: Optional[int] = None) -> torch.Tensor:
         """[..., in_features] -> [..., out_features] via the fused dequant-GEMM (bf16).
 
         With gate ([out_features]) and/or residual ([..., out_features], bf16, may be `out`),
         returns residual + gate * (input . W^T + bias) from the GEMM epilogue; with `rope`,
         the rotary embedding of its columns (and `out` may be a column slice of a wider
-        buffer)."""
+        buffer); with `glu` (GLU_SWIGLU / GLU_GEGLU, rows interleaved by `interleave_rows`),
+        the gated [..., out_features / 2] feed-forward activation."""
         dev = require_cuda(input, self.q, gate, residual, None if rope is None else rope.table)
         lead = input.shape[:-1]
         x = input.reshape(-1, self.in_features)
@@ -218,6 +228,18 @@ class GpuQuantizedLinear:
         b = self.bias
         if b is not None and b.dtype != torch.bfloat16:
             b = b.to(torch.bfloat16)
+        if glu is not None:
+            if self.quant_type != GpuQuantType.Q8_0 or gate is not None or residual is not None \
+                    or rope is not None:
+                raise ValueError("the GLU epilogue is for Q8_0 layers without gate/residual/rope")
+            half = self.out_features // 2
+            y = out if out is not None else torch.empty((M, half), dtype=torch.bfloat16, device=dev)
+            if y.dtype != torch.bfloat16 or not y.is_contiguous() or y.numel() != M * half:
+                raise ValueError("out must be a contiguous bf16 tensor of [..., out_features / 2]")
+            _lib.call("sp_q8_0_linear_glu", ptr(x), ptr(self.q), ptr(self.scale), ptr(b), ptr(y),
+                      M, self.out_features, self.in_features, int(glu), _lib.SP_BF16,
+                      stream_ptr(dev))
+            return y.reshape(*lead, half)
         if self.quant_type in _KQ:
             if gate is not None or residual is not None or rope is not None:
                 raise ValueError("k-quant layers have the plain (bias) epilogue only")

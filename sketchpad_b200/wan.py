@@ -32,8 +32,7 @@ import torch.nn.functional as F
 
 from .attention import flash_attention
 from .flux import apply_rope, rope_tables
-from .quantized_matmul import RopeEpilogue, rope_pair_table
-from .glu import swiglu
+from .quantized_matmul import GLU_SWIGLU, RopeEpilogue, interleave_rows, rope_pair_table
 from .layernorm import layer_norm_modulate
 from .quantization import Fp8Format, Fp8Linear, Fp8Tensor
 from .ulysses import head_to_seq, seq_to_head
@@ -98,8 +97,9 @@ class WanBlockB200:
         self.t_qkv, self.t_out = L(3, 3 * h, h), L(4, h, h)
         self.c_q, self.c_kv, self.c_out = L(5, h, h), L(6, 2 * h, h), L(7, h, h)
         gate, up = L(8, i, h, False), L(9, i, h, False)
-        self.gate_up = Fp8Linear(Fp8Tensor(torch.cat([gate.weight.data, up.weight.data]),
-                                           torch.cat([gate.weight.scale, up.weight.scale]),
+        # rows interleaved (gate j, up j): silu(gate) * up in the GEMM epilogue
+        self.gate_up = Fp8Linear(Fp8Tensor(interleave_rows(gate.weight.data, up.weight.data),
+                                           interleave_rows(gate.weight.scale, up.weight.scale),
                                            Fp8Format.E4M3, (2 * i, h)), None)
         self.down = L(10, h, i, False)
         self.modulation = L(11, 8 * h, h)
@@ -183,8 +183,8 @@ class WanBlockB200:
         x = self.c_out(o.view(b, s_loc, H * D), out=x, residual=x)
         xn = _ln(x, m[:, 7], m[:, 6])
         # one expert: softmax over a single router logit is exactly 1 (wan.rs:576-601)
-        # silu(gate) * up in one pass; the residual add in down's epilogue
-        return self.down(swiglu(self.gate_up(xn)), out=x, residual=x)
+        # silu(gate) * up in gate_up's epilogue; the residual add in down's
+        return self.down(self.gate_up(xn, glu=GLU_SWIGLU), out=x, residual=x)
 
 
 def wan_block_flops(cfg: WanConfig = WanConfig(), nt=21, nhw=3600, ctx=512) -> dict:

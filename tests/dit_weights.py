@@ -4,7 +4,7 @@ import numpy as np
 
 import sketchpad_b200.flux as FX
 import sketchpad_b200.wan as WN
-from helpers import fp8_linear_f32, q8_linear_f32, split_rows
+from helpers import fp8_linear_f32, q8_linear_f32, split_interleaved
 
 # Reduced widths with the real head_dim 128.  Q8_0 block scales ~ U(1e-4, 4e-4) give weights
 # of std ~0.02 (like the Wan FP8 weights), so attention logits stay O(1).  With the config-4
@@ -22,7 +22,7 @@ def flux_block_weights(blk, single: bool):
         ("txt_attn.", blk.txt_attn, "txt_ffn.", blk.txt_ffn)]
     for ap, attn, fp, ffn in streams:
         W[ap + "qkv"], W[ap + "proj"] = q8_linear_f32(attn.qkv), q8_linear_f32(attn.proj)
-        W[fp + "gate"], W[fp + "up"] = split_rows(q8_linear_f32(ffn.gate_up), ffn.i)
+        W[fp + "gate"], W[fp + "up"] = split_interleaved(q8_linear_f32(ffn.gate_up))
         W[fp + "down"] = q8_linear_f32(ffn.down)
     return W
 
@@ -33,7 +33,7 @@ def wan_block_weights(blk):
          "temporal.to_qkv": fp8_linear_f32(blk.t_qkv), "temporal.to_out": fp8_linear_f32(blk.t_out),
          "cross.to_q": fp8_linear_f32(blk.c_q), "cross.to_kv": fp8_linear_f32(blk.c_kv),
          "cross.to_out": fp8_linear_f32(blk.c_out), "expert0.down": fp8_linear_f32(blk.down)}
-    W["expert0.gate"], W["expert0.up"] = split_rows(fp8_linear_f32(blk.gate_up), blk.cfg.intermediate)
+    W["expert0.gate"], W["expert0.up"] = split_interleaved(fp8_linear_f32(blk.gate_up))
     # one expert: the router's softmax is exactly 1 whatever its weights are
     h = blk.cfg.hidden_size
     W["router"] = (np.random.default_rng(5).standard_normal((1, h)).astype(np.float32) * 0.02,

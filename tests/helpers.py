@@ -52,3 +52,10 @@ def split_rows(wb, i):
     """Split a stacked (W, b) pair at output row i (gate/up share one GEMM in the harness)."""
     w, b = wb
     return (w[:i], None if b is None else b[:i]), (w[i:], None if b is None else b[i:])
+
+
+def split_interleaved(wb):
+    """Split a row-interleaved (W, b) pair (first-half row j at 2j, second-half row j at
+    2j+1: the GLU-epilogue layout) into its two halves."""
+    w, b = wb
+    return (w[0::2], None if b is None else b[0::2]), (w[1::2], None if b is None else b[1::2])

@@ -47,11 +47,19 @@ def _epilogue(y, out, gate, residual, rope=None):
     return out.copy_(y.reshape(out.shape))
 
 
-def _q8_forward(self, x, out=None, gate=None, residual=None, rope=None):
+def _glu(y, glu):
+    # the GLU epilogue on row-interleaved columns (lo = even, hi = odd)
+    lo, hi = y[..., 0::2], y[..., 1::2]
+    return F.silu(lo) * hi if glu == 1 else lo * F.gelu(hi)
+
+
+def _q8_forward(self, x, out=None, gate=None, residual=None, rope=None, glu=None):
     q = self.q.float()
     s = self.scale.view(torch.float16).float().t().repeat_interleave(32, dim=1)  # [N, K]
     y = x.float() @ (q * s).t()
     y = y + self.bias.float() if self.bias is not None else y
+    if glu is not None:
+        return _glu(y, glu)
     return _epilogue(y, out, gate, residual, rope)
 
 
@@ -65,10 +73,12 @@ def _fp8_quantize(t, cfg):
     return QZ.Fp8Tensor(data, torch.full((1,), float(cfg.scale)), QZ.Fp8Format.E4M3, tuple(t.shape))
 
 
-def _fp8_forward(self, x, out=None, gate=None, residual=None, rope=None):
+def _fp8_forward(self, x, out=None, gate=None, residual=None, rope=None, glu=None):
     w = self.weight.data.view(torch.float8_e4m3fn).float() * self.weight.scale.view(-1, 1)
     y = x.float() @ w.t()
     y = y + self.bias.float() if self.bias is not None else y
+    if glu is not None:
+        return _glu(y, glu)
     return _epilogue(y, out, gate, residual, rope)
 
 
@@ -92,11 +102,6 @@ def _sdpa(q, k, v, out=None):
     return out.copy_(o) if out is not None else o
 
 
-def _swiglu(h):
-    f = h.shape[-1] // 2
-    return F.silu(h[..., :f]) * h[..., f:]
-
-
 def _patch(monkeypatch):
     monkeypatch.setattr(QM.GpuQuantizedLinear, "forward", _q8_forward)
     monkeypatch.setattr(QM.GpuQuantizedLinear, "__call__", _q8_forward)
@@ -107,8 +112,6 @@ def _patch(monkeypatch):
     monkeypatch.setattr(WN, "layer_norm_modulate", _ln_mod)
     monkeypatch.setattr(FX, "flash_attention", _sdpa)
     monkeypatch.setattr(WN, "flash_attention", _sdpa)
-    monkeypatch.setattr(FX, "swiglu", _swiglu)
-    monkeypatch.setattr(WN, "swiglu", _swiglu)
 
 
 @pytest.mark.parametrize("epilogue", [False, True])

@@ -366,3 +366,48 @@ def test_splitk_small_grid_linear_vs_oracle(M, N, K):
     ref = oracle.q8_0_matmul(np.frombuffer(raw, np.uint8), N, K, to_np(x[rows])) + to_np(bias)
     assert rel_err(to_np(y1[rows]), ref) < TOL_HALF
 
+
+
+@pytest.mark.parametrize("kind", ["swiglu", "geglu"])
+@pytest.mark.parametrize("M,F,K", [(200, 128, 256), (4096, 1536, 3072), (77, 640, 2048)])
+def test_q8_0_linear_glu_epilogue(kind, M, F, K):
+    # gate/up (value/gate) rows interleaved; y = silu(lo) * hi or lo * gelu(hi) from the f32
+    # accumulators (glu.rs:91-96, blocks.rs:446-458); (77, 640, 2048) runs split-K
+    from sketchpad_b200.quantized_matmul import GLU_GEGLU, GLU_SWIGLU, interleave_rows
+    raw_a, raw_b = make_q8_0_synthetic(F, K, seed=F + 1), make_q8_0_synthetic(F, K, seed=F + 2)
+    g = torch.Generator(device="cpu").manual_seed(M)
+    ba = (torch.randn(F, generator=g) * 0.1).to(torch.bfloat16)
+    bb = (torch.randn(F, generator=g) * 0.1).to(torch.bfloat16)
+    la = GpuQuantizedLinear.from_bytes(raw_a, GpuQuantType.Q8_0, F, K)
+    lb = GpuQuantizedLinear.from_bytes(raw_b, GpuQuantType.Q8_0, F, K)
+    lin = GpuQuantizedLinear(interleave_rows(la.q, lb.q), interleave_rows(la.scale, lb.scale, dim=1),
+                             2 * F, K, torch.bfloat16, interleave_rows(ba, bb).cuda())
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    y = lin.forward(x.cuda(), glu=GLU_SWIGLU if kind == "swiglu" else GLU_GEGLU)
+    torch.cuda.synchronize()
+    assert y.shape == (M, F)
+    rows = slice(0, min(M, 128))
+    lo = oracle.q8_0_matmul(np.frombuffer(raw_a, np.uint8), F, K, to_np(x[rows])) + to_np(ba)
+    hi = oracle.q8_0_matmul(np.frombuffer(raw_b, np.uint8), F, K, to_np(x[rows])) + to_np(bb)
+    ref = (oracle.activation(lo, "silu") * hi if kind == "swiglu"
+           else lo * oracle.activation(hi, "gelu"))
+    assert rel_err(to_np(y[rows]), ref) < TOL_HALF
+
+
+def test_fp8_linear_glu_epilogue():
+    from sketchpad_b200.quantized_matmul import GLU_SWIGLU, interleave_rows
+    M, F, K = 300, 640, 640
+    g = torch.Generator(device="cpu").manual_seed(4)
+    wa, wb = torch.randn(F, K, generator=g) * 0.02, torch.randn(F, K, generator=g) * 0.02
+    la = Fp8Linear.from_weight(wa.cuda(), None, Fp8Config.e4m3().with_per_channel(True))
+    lb = Fp8Linear.from_weight(wb.cuda(), None, Fp8Config.e4m3().with_per_channel(True))
+    lin = Fp8Linear(Fp8Tensor(interleave_rows(la.weight.data, lb.weight.data),
+                              interleave_rows(la.weight.scale, lb.weight.scale),
+                              Fp8Format.E4M3, (2 * F, K)), None)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    y = lin.forward(x.cuda(), glu=GLU_SWIGLU)
+    torch.cuda.synchronize()
+    rows = slice(0, 128)
+    lo = oracle.linear_nt(to_np(x[rows]), to_np(la.weight.dequantize()))
+    hi = oracle.linear_nt(to_np(x[rows]), to_np(lb.weight.dequantize()))
+    assert rel_err(to_np(y[rows]), oracle.activation(lo, "silu") * hi) < TOL_HALF
