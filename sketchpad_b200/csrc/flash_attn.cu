@@ -532,6 +532,136 @@ int launch_fa(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& m
 }  // namespace
 }  // namespace sp
 
+namespace sp {
+namespace {
+
+// ---------------------------------------------------------------------------------------
+// Short sequences (Sq, Skv <= 32, D = Dv in {64, 128}, no mask, not causal): one warp per
+// (batch, head).  Wan's temporal attention runs 144,000 such problems of 21 tokens, where
+// 128-row tensor-core tiles would be 84 % padding and per-CTA setup dominates.  Lane j holds
+// key j in registers (f32); the warp's Q and V rows sit in shared memory.  Per query: lane j
+// forms q . k_j, the warp takes max and sum by shuffles (exp2 with the scale folded in, as
+// the tiled kernel does), and lane l accumulates output dims [l*D/32, (l+1)*D/32).
+// ---------------------------------------------------------------------------------------
+constexpr int kShortWarps = 4;
+constexpr int kShortMax = 32;
+
+struct ShortArgs {
+  int64_t BH, H, Sq, Skv;
+  int64_t qs0, qs1, qs2, ks0, ks1, ks2, vs0, vs1, vs2, os0, os1, os2;
+  float scale_log2;
+  int out_dtype;
+};
+
+template <typename T>
+__device__ __forceinline__ float sh_f32(T v);
+template <>
+__device__ __forceinline__ float sh_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float sh_f32<__half>(__half v) { return __half2float(v); }
+
+template <typename T, int DH>
+__global__ void __launch_bounds__(kShortWarps * 32) attn_short_kernel(const T* __restrict__ q,
+                                                                      const T* __restrict__ k,
+                                                                      const T* __restrict__ v,
+                                                                      void* out, ShortArgs a) {
+  constexpr int kChunks = DH / 8;  // 16-byte chunks per row
+  constexpr int kDpl = DH / 32;    // output dims per lane
+  extern __shared__ uint4 sh_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t pb = (int64_t)blockIdx.x * kShortWarps + warp;
+  if (pb >= a.BH) return;  // warp-uniform
+  T* sq = reinterpret_cast<T*>(sh_raw) + (int64_t)warp * 2 * kShortMax * DH;
+  T* sv = sq + kShortMax * DH;
+  const int64_t b = pb / a.H, h = pb - b * a.H;
+  const T* qp = q + b * a.qs0 + h * a.qs1;
+  const T* kp = k + b * a.ks0 + h * a.ks1;
+  const T* vp = v + b * a.vs0 + h * a.vs1;
+  const int Sq = (int)a.Sq, Skv = (int)a.Skv;
+  for (int e = lane; e < Sq * kChunks; e += 32) {
+    const int r = e / kChunks, c = e - r * kChunks;
+    reinterpret_cast<uint4*>(sq + r * DH)[c] = *reinterpret_cast<const uint4*>(qp + r * a.qs2 + c * 8);
+  }
+  for (int e = lane; e < Skv * kChunks; e += 32) {
+    const int r = e / kChunks, c = e - r * kChunks;
+    reinterpret_cast<uint4*>(sv + r * DH)[c] = *reinterpret_cast<const uint4*>(vp + r * a.vs2 + c * 8);
+  }
+  float kf[DH];
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (lane < Skv) u = *reinterpret_cast<const uint4*>(kp + lane * a.ks2 + c * 8);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) kf[c * 8 + t] = sh_f32<T>(e[t]);
+  }
+  __syncwarp();
+  for (int i = 0; i < Sq; ++i) {
+    const T* qr = sq + i * DH;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int d = 0; d < DH; d += 2) {
+      s0 = fmaf(sh_f32<T>(qr[d]), kf[d], s0);  // broadcast reads: every lane the same word
+      s1 = fmaf(sh_f32<T>(qr[d + 1]), kf[d + 1], s1);
+    }
+    const float x = lane < Skv ? (s0 + s1) * a.scale_log2 : -INFINITY;
+    float m = x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float pe = lane < Skv ? ex2_approx(x - m) : 0.f;
+    float l = pe;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    float acc[kDpl];
+#pragma unroll
+    for (int t = 0; t < kDpl; ++t) acc[t] = 0.f;
+    for (int j = 0; j < Skv; ++j) {
+      const float pj = __shfl_sync(0xffffffffu, pe, j);
+      const T* vr = sv + j * DH + lane * kDpl;
+#pragma unroll
+      for (int t = 0; t < kDpl; ++t) acc[t] = fmaf(pj, sh_f32<T>(vr[t]), acc[t]);
+    }
+    const float inv_l = 1.0f / l;
+    const int64_t ob = b * a.os0 + h * a.os1 + (int64_t)i * a.os2 + lane * kDpl;
+    if (a.out_dtype == SP_F32) {
+      float* o = static_cast<float*>(out) + ob;
+#pragma unroll
+      for (int t = 0; t < kDpl; ++t) o[t] = acc[t] * inv_l;
+    } else if (a.out_dtype == SP_BF16) {
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + ob;
+#pragma unroll
+      for (int t = 0; t < kDpl; ++t) o[t] = __float2bfloat16_rn(acc[t] * inv_l);
+    } else {
+      __half* o = static_cast<__half*>(out) + ob;
+#pragma unroll
+      for (int t = 0; t < kDpl; ++t) o[t] = __float2half_rn(acc[t] * inv_l);
+    }
+  }
+}
+
+template <typename T, int DH>
+int launch_attn_short(const void* q, const void* k, const void* v, void* out, const ShortArgs& a,
+                      cudaStream_t s) {
+  auto kern = attn_short_kernel<T, DH>;
+  const int smem = kShortWarps * 2 * kShortMax * DH * (int)sizeof(T);
+  static unsigned long long attr_set = 0;
+  if (smem > 48 * 1024 && first_time_on_device(&attr_set)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+      __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
+      return set_error(SP_ERR_LAUNCH, "flash_attn: short-sequence smem attribute: %s",
+                       cudaGetErrorString(e));
+    }
+  }
+  const unsigned grid = (unsigned)((a.BH + kShortWarps - 1) / kShortWarps);
+  kern<<<grid, kShortWarps * 32, smem, s>>>(static_cast<const T*>(q), static_cast<const T*>(k),
+                                            static_cast<const T*>(v), out, a);
+  return check_launch("flash_attn short");
+}
+
+}  // namespace
+}  // namespace sp
+
 extern "C" int sp_flash_attn_fwd(const void* q, const void* k, const void* v, const float* mask,
                                  int64_t mask_row_stride, void* out, int64_t B, int64_t H,
                                  int64_t Sq, int64_t Skv, int64_t D, int64_t Dv,
@@ -565,6 +695,23 @@ extern "C" int sp_flash_attn_fwd(const void* q, const void* k, const void* v, co
   if (int rc = require_sm100()) return rc;
 
   const int in_f16 = dtype_in == SP_F16;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float sc0 = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
+  if (!mask && !causal && Sq <= kShortMax && Skv <= kShortMax && D == Dv && (D == 64 || D == 128) &&
+      q_strides[3] == 1 && k_strides[3] == 1 && v_strides[3] == 1 && aligned(q, 16) &&
+      aligned(k, 16) && aligned(v, 16) && q_strides[2] % 8 == 0 && k_strides[2] % 8 == 0 &&
+      v_strides[2] % 8 == 0 && (o_strides[2] * oes) % 16 == 0) {
+    const ShortArgs a{B * H, H, Sq, Skv,
+                      q_strides[0], q_strides[1], q_strides[2],
+                      k_strides[0], k_strides[1], k_strides[2],
+                      v_strides[0], v_strides[1], v_strides[2],
+                      o_strides[0], o_strides[1], o_strides[2], sc0 * kLog2e, dtype_out};
+    if (in_f16)
+      return D == 64 ? launch_attn_short<__half, 64>(q, k, v, out, a, s)
+                     : launch_attn_short<__half, 128>(q, k, v, out, a, s);
+    return D == 64 ? launch_attn_short<__nv_bfloat16, 64>(q, k, v, out, a, s)
+                   : launch_attn_short<__nv_bfloat16, 128>(q, k, v, out, a, s);
+  }
   CUtensorMap mq, mk, mv;
   if (int rc = make_qkv_map(&mq, q, in_f16, Sq, H, B, (int)D, q_strides, "q")) return rc;
   if (int rc = make_qkv_map(&mk, k, in_f16, Skv, H, B, (int)D, k_strides, "k")) return rc;
@@ -593,7 +740,6 @@ extern "C" int sp_flash_attn_fwd(const void* q, const void* k, const void* v, co
   p.os2 = o_strides[2];
   p.out_dtype = dtype_out;
   p.in_f16 = in_f16;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool qk2 = D > 64, v2 = Dv > 64;
   if (!qk2 && !v2) return launch_fa<1, 1, 4>(mq, mk, mv, p, B, s);  // 160 KB smem
   if (qk2 && v2) return launch_fa<2, 2, 2>(mq, mk, mv, p, B, s);     // 192 KB smem

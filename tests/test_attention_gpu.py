@@ -120,3 +120,31 @@ def test_setup_errors():
         flash_attention(q, q, q)  # head dim not a multiple of 8
     with pytest.raises(AttentionSetupError):
         flash_attention(rnd((1, 1, 16, 64), 30), rnd((1, 2, 16, 64), 31), rnd((1, 2, 16, 64), 32))
+
+
+@pytest.mark.parametrize("B,H,Sq,Skv,D,dtype,out_dtype", [
+    (3, 40, 21, 21, 128, torch.bfloat16, None),       # Wan temporal attention shape
+    (2, 5, 7, 32, 64, torch.float16, None),
+    (1, 3, 32, 1, 128, torch.bfloat16, torch.float32),
+    (4, 2, 1, 17, 64, torch.bfloat16, None)])
+def test_short_sequence_path(B, H, Sq, Skv, D, dtype, out_dtype):
+    # Sq, Skv <= 32, no mask: the one-warp-per-(batch, head) kernel
+    q, k, v = rnd((B, H, Sq, D), 40, dtype), rnd((B, H, Skv, D), 41, dtype), rnd((B, H, Skv, D), 42, dtype)
+    opts = FlashAttentionOptions(out_dtype=out_dtype)
+    out = flash_attention(q, k, v, opts)
+    torch.cuda.synchronize()
+    assert out.dtype == (out_dtype or dtype)
+    check(q, k, v, out, tol=1e-2 if out_dtype == torch.float32 else TOL_HALF)
+
+
+def test_short_sequence_strided_temporal_views():
+    # the Wan temporal layout: [t, hw, heads, D] viewed as [hw, heads, t, D] (no copies), and
+    # the output written through the same kind of view
+    T, HW, Hh, D = 21, 48, 4, 128
+    base = [rnd((1, T, HW, Hh, D), 50 + i) for i in range(3)]
+    q, k, v = (t[0].permute(1, 2, 0, 3) for t in base)  # [HW, Hh, T, D] strided
+    ob = torch.empty((T, HW, Hh, D), dtype=torch.bfloat16, device="cuda")
+    out = ob.permute(1, 2, 0, 3)
+    flash_attention(q, k, v, out=out)
+    torch.cuda.synchronize()
+    check(q, k, v, out, heads=[(0, 0), (HW - 1, Hh - 1), (17, 2)])
