@@ -85,6 +85,43 @@ int current_device() {
   return dev;
 }
 
+// The library's stream-ordered scratch pool for this device (split-K partials): freed blocks
+// stay in the pool (release threshold = max), so the per-call allocate / free pair is cheap
+// after the first call of a size.  Created once per device; null if the pool cannot be made.
+cudaMemPool_t scratch_pool() {
+  static cudaMemPool_t pools[64] = {};
+  static int state[64] = {};  // 0 none, 1 creating, 2 ready, 3 failed
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return nullptr;
+  int st = __atomic_load_n(&state[dev], __ATOMIC_ACQUIRE);
+  if (st == 2) return pools[dev];
+  if (st == 3) return nullptr;
+  int expected = 0;
+  if (__atomic_compare_exchange_n(&state[dev], &expected, 1, false, __ATOMIC_ACQ_REL,
+                                  __ATOMIC_ACQUIRE)) {
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) == cudaSuccess) {
+      uint64_t keep = ~0ull;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+      pools[dev] = pool;
+      __atomic_store_n(&state[dev], 2, __ATOMIC_RELEASE);
+      return pool;
+    }
+    cudaGetLastError();
+    __atomic_store_n(&state[dev], 3, __ATOMIC_RELEASE);
+    return nullptr;
+  }
+  // another thread is creating it: wait (bounded by the creation itself)
+  while ((st = __atomic_load_n(&state[dev], __ATOMIC_ACQUIRE)) == 1) {
+  }
+  return st == 2 ? pools[dev] : nullptr;
+}
+
 bool first_time_on_device(unsigned long long* flag_bits) {
   const int dev = current_device();
   if (dev < 0 || dev >= 64) return true;

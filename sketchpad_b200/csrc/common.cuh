@@ -42,6 +42,7 @@ int current_device();
 // True once per (flag, device): lets a launcher set a kernel attribute the first time it
 // runs on a device instead of on every call.
 bool first_time_on_device(unsigned long long* flag_bits);
+cudaMemPool_t scratch_pool();
 
 // cuTensorMapEncodeTiled obtained through cudaGetDriverEntryPoint (no libcuda link).
 int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, const void* base,

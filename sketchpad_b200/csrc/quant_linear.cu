@@ -546,13 +546,30 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
   QlParams q = p;
   const int ktotal = (int)(p.K / kQBK), tiles = tiles_m * tiles_n, sms = num_sms();
   int splits = 1;
-  if (2 * tiles <= sms && ktotal >= 8) splits = std::min(std::min(8, sms / tiles), ktotal / 4);
+  if (2 * tiles <= sms && ktotal >= 8) {
+    splits = std::min(std::min(8, sms / tiles), ktotal / 4);
+  } else if (ktotal >= 128) {
+    // long K with a badly quantised last wave (e.g. 192 tiles on 148 SMs: 65 % busy): split
+    // 2-4 ways when that fills the waves better; the f32 partials (S x M x N x 4 bytes, written
+    // and read once) cost little next to K >= 8192 of MMA work
+    auto eff = [&](int sp) {
+      const int ctas = tiles * sp;
+      return (double)ctas / ((double)((ctas + sms - 1) / sms) * sms);
+    };
+    double best = eff(1);
+    for (int sp = 2; sp <= 4; ++sp)
+      if (eff(sp) > best + 0.1) {
+        best = eff(sp);
+        splits = sp;
+      }
+  }
   void* ws = nullptr;
   if (splits > 1) {
     q.kt_per_split = (ktotal + splits - 1) / splits;
     splits = (ktotal + q.kt_per_split - 1) / q.kt_per_split;  // no empty split
     const size_t bytes = (size_t)splits * (size_t)p.M * (size_t)p.N * sizeof(float);
-    if (cudaMallocAsync(&ws, bytes, s) != cudaSuccess) {
+    cudaMemPool_t pool = scratch_pool();
+    if (!pool || cudaMallocFromPoolAsync(&ws, bytes, pool, s) != cudaSuccess) {
       cudaGetLastError();
       ws = nullptr;
       splits = 1;
