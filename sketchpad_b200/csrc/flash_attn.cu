@@ -28,6 +28,8 @@
 // (o_done) after computing its exponentials, just before it rescales O_t and writes P_t.
 // Q, K, V tiles in shared memory are 128 rows x 64 elements (128 B) boxes with the 128B
 // swizzle: the canonical K-major layout for Q and K, MN-major for V.
+#include <type_traits>
+
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -538,10 +540,9 @@ namespace {
 // ---------------------------------------------------------------------------------------
 // Short sequences (Sq, Skv <= 32, D = Dv in {64, 128}, no mask, not causal): one warp per
 // (batch, head).  Wan's temporal attention runs 144,000 such problems of 21 tokens, where
-// 128-row tensor-core tiles would be 84 % padding and per-CTA setup dominates.  Lane j holds
-// key j in registers (f32); the warp's Q and V rows sit in shared memory.  Per query: lane j
-// forms q . k_j, the warp takes max and sum by shuffles (exp2 with the scale folded in, as
-// the tiled kernel does), and lane l accumulates output dims [l*D/32, (l+1)*D/32).
+// 128-row tensor-core tiles would be 84 % padding and per-CTA setup dominates.  The warp
+// works on 32-row tiles with mma.sync m16n8k16 (f32 accumulate), the softmax in exp2 with
+// the scale folded in, as the tiled kernel does.
 // ---------------------------------------------------------------------------------------
 constexpr int kShortWarps = 4;
 constexpr int kShortMax = 32;
@@ -553,97 +554,214 @@ struct ShortArgs {
   int out_dtype;
 };
 
-template <typename T>
-__device__ __forceinline__ float sh_f32(T v);
-template <>
-__device__ __forceinline__ float sh_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
-template <>
-__device__ __forceinline__ float sh_f32<__half>(__half v) { return __half2float(v); }
+// The warp's Q, K and V rows are copied to shared memory by cp.async (rows past Sq / Skv
+// zero filled), S = Q K^T is formed as 16 x 8 tiles over K = DH with ldmatrix fragments,
+// P = softmax(S) stays in registers as the A operand of O = P V (the S accumulator layout is
+// the A fragment layout of the next product), and V's B fragments come from its row-major
+// rows by ldmatrix.trans.  The bf16/f16 output is staged in the Q rows of the finished tile
+// and written back as 16-byte rows.  Padded keys get -inf before the softmax.
+// Fragment layouts (PTX mma.m16n8k16, g = lane / 4, t = lane % 4): A a0 = A[g][2t..2t+1],
+// a1 = A[g+8][2t..], a2 = A[g][2t+8..], a3 = A[g+8][2t+8..]; B b0 = B[2t..2t+1][g],
+// b1 = B[2t+8..2t+9][g]; C c0,c1 = C[g][2t..2t+1], c2,c3 = C[g+8][2t..2t+1].
+constexpr int kSmRow = 8;  // padding elements per shared row: 8 rows of a fragment hit 32 banks
 
-template <typename T, int DH>
-__global__ void __launch_bounds__(kShortWarps * 32) attn_short_kernel(const T* __restrict__ q,
-                                                                      const T* __restrict__ k,
-                                                                      const T* __restrict__ v,
-                                                                      void* out, ShortArgs a) {
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  if constexpr (std::is_same<T, __half>::value)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// 16-byte global -> shared copy; src_bytes = 0 writes 16 zero bytes and reads nothing
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (std::is_same<T, __half>::value) return pack_f16x2(lo, hi);
+  else return pack_bf16x2(lo, hi);
+}
+
+template <int OUT>
+__device__ __forceinline__ uint32_t pack_out2(float lo, float hi) {
+  if constexpr (OUT == SP_F16) return pack_f16x2(lo, hi);
+  else return pack_bf16x2(lo, hi);
+}
+
+template <typename T, int DH, int OUT>
+__global__ void __launch_bounds__(kShortWarps * 32) attn_short_mma_kernel(const T* __restrict__ q,
+                                                                          const T* __restrict__ k,
+                                                                          const T* __restrict__ v,
+                                                                          void* out, ShortArgs a) {
+  constexpr int RS = DH + kSmRow;  // row stride of the Q / K / V rows in shared memory (elements)
   constexpr int kChunks = DH / 8;  // 16-byte chunks per row
-  constexpr int kDpl = DH / 32;    // output dims per lane
+  constexpr int kRowsBytes = kShortMax * RS * 2;
   extern __shared__ uint4 sh_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
   const int64_t pb = (int64_t)blockIdx.x * kShortWarps + warp;
   if (pb >= a.BH) return;  // warp-uniform
-  T* sq = reinterpret_cast<T*>(sh_raw) + (int64_t)warp * 2 * kShortMax * DH;
-  T* sv = sq + kShortMax * DH;
+  T* sq = reinterpret_cast<T*>(sh_raw) + (int64_t)warp * 3 * kShortMax * RS;
+  const uint32_t sq_a = (uint32_t)__cvta_generic_to_shared(sq);
+  const uint32_t sk_a = sq_a + kRowsBytes, sv_a = sk_a + kRowsBytes;
   const int64_t b = pb / a.H, h = pb - b * a.H;
   const T* qp = q + b * a.qs0 + h * a.qs1;
   const T* kp = k + b * a.ks0 + h * a.ks1;
   const T* vp = v + b * a.vs0 + h * a.vs1;
   const int Sq = (int)a.Sq, Skv = (int)a.Skv;
-  for (int e = lane; e < Sq * kChunks; e += 32) {
+#pragma unroll 4
+  for (int e = lane; e < kShortMax * kChunks; e += 32) {
     const int r = e / kChunks, c = e - r * kChunks;
-    reinterpret_cast<uint4*>(sq + r * DH)[c] = *reinterpret_cast<const uint4*>(qp + r * a.qs2 + c * 8);
+    const uint32_t so = (uint32_t)(r * RS + c * 8) * 2;
+    const bool rq = r < Sq, rkv = r < Skv;
+    cp_async16(sq_a + so, rq ? qp + r * a.qs2 + c * 8 : qp, rq ? 16 : 0);
+    cp_async16(sk_a + so, rkv ? kp + r * a.ks2 + c * 8 : kp, rkv ? 16 : 0);
+    cp_async16(sv_a + so, rkv ? vp + r * a.vs2 + c * 8 : vp, rkv ? 16 : 0);
   }
-  for (int e = lane; e < Skv * kChunks; e += 32) {
-    const int r = e / kChunks, c = e - r * kChunks;
-    reinterpret_cast<uint4*>(sv + r * DH)[c] = *reinterpret_cast<const uint4*>(vp + r * a.vs2 + c * 8);
-  }
-  float kf[DH];
-#pragma unroll
-  for (int c = 0; c < kChunks; ++c) {
-    uint4 u = make_uint4(0, 0, 0, 0);
-    if (lane < Skv) u = *reinterpret_cast<const uint4*>(kp + lane * a.ks2 + c * 8);
-    const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-    for (int t = 0; t < 8; ++t) kf[c * 8 + t] = sh_f32<T>(e[t]);
-  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncwarp();
-  for (int i = 0; i < Sq; ++i) {
-    const T* qr = sq + i * DH;
-    float s0 = 0.f, s1 = 0.f;
+  // ldmatrix lane addressing: lane l supplies row (l & 7) of matrix (l >> 3)
+  const int mi = lane >> 3, rr = lane & 7;
+  const bool kv_hi = Skv > 16;  // keys 16..31 present (second S tile pair, second PV k-step)
+  for (int mt = 0; mt < 2; ++mt) {
+    if (mt * 16 >= Sq) break;
+    float sacc[4][4];
 #pragma unroll
-    for (int d = 0; d < DH; d += 2) {
-      s0 = fmaf(sh_f32<T>(qr[d]), kf[d], s0);  // broadcast reads: every lane the same word
-      s1 = fmaf(sh_f32<T>(qr[d + 1]), kf[d + 1], s1);
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sacc[nt][i] = 0.f;
+    // S = Q K^T: rows 16mt .. 16mt+15, keys 0..31 (the upper 16 only when present)
+#pragma unroll
+    for (int ks = 0; ks < DH / 16; ++ks) {
+      uint32_t af[4], kb[4];
+      ldsm_x4(af, sq_a + (uint32_t)((mt * 16 + (mi & 1) * 8 + rr) * RS + ks * 16 + (mi >> 1) * 8) * 2);
+      ldsm_x4(kb, sk_a + (uint32_t)(((mi >> 1) * 8 + rr) * RS + ks * 16 + (mi & 1) * 8) * 2);
+      mma16816<T>(sacc[0], af, kb[0], kb[1]);
+      mma16816<T>(sacc[1], af, kb[2], kb[3]);
+      if (kv_hi) {
+        ldsm_x4(kb, sk_a + (uint32_t)((16 + (mi >> 1) * 8 + rr) * RS + ks * 16 + (mi & 1) * 8) * 2);
+        mma16816<T>(sacc[2], af, kb[0], kb[1]);
+        mma16816<T>(sacc[3], af, kb[2], kb[3]);
+      }
     }
-    const float x = lane < Skv ? (s0 + s1) * a.scale_log2 : -INFINITY;
-    float m = x;
+    // softmax over keys for rows g and g+8 of the tile; the 4 lanes of a row hold 8 keys each
+    float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float pe = lane < Skv ? ex2_approx(x - m) : 0.f;
-    float l = pe;
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    float acc[kDpl];
+      for (int i = 0; i < 4; ++i) {
+        const int key = nt * 8 + 2 * t + (i & 1);
+        const float x = key < Skv ? sacc[nt][i] * a.scale_log2 : -INFINITY;
+        sacc[nt][i] = x;
+        if (i < 2) mx0 = fmaxf(mx0, x);
+        else mx1 = fmaxf(mx1, x);
+      }
 #pragma unroll
-    for (int t = 0; t < kDpl; ++t) acc[t] = 0.f;
-    for (int j = 0; j < Skv; ++j) {
-      const float pj = __shfl_sync(0xffffffffu, pe, j);
-      const T* vr = sv + j * DH + lane * kDpl;
-#pragma unroll
-      for (int t = 0; t < kDpl; ++t) acc[t] = fmaf(pj, sh_f32<T>(vr[t]), acc[t]);
+    for (int o = 1; o <= 2; o <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
     }
-    const float inv_l = 1.0f / l;
-    const int64_t ob = b * a.os0 + h * a.os1 + (int64_t)i * a.os2 + lane * kDpl;
-    if (a.out_dtype == SP_F32) {
-      float* o = static_cast<float*>(out) + ob;
+    float l0 = 0.f, l1 = 0.f;
 #pragma unroll
-      for (int t = 0; t < kDpl; ++t) o[t] = acc[t] * inv_l;
-    } else if (a.out_dtype == SP_BF16) {
-      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + ob;
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int t = 0; t < kDpl; ++t) o[t] = __float2bfloat16_rn(acc[t] * inv_l);
-    } else {
-      __half* o = static_cast<__half*>(out) + ob;
+      for (int i = 0; i < 4; ++i) {
+        const float pe = ex2_approx(sacc[nt][i] - (i < 2 ? mx0 : mx1));
+        sacc[nt][i] = pe;
+        if (i < 2) l0 += pe;
+        else l1 += pe;
+      }
 #pragma unroll
-      for (int t = 0; t < kDpl; ++t) o[t] = __float2half_rn(acc[t] * inv_l);
+    for (int o = 1; o <= 2; o <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+    // P as A fragments: k-step kk covers keys 16kk .. 16kk+15 = S tiles 2kk, 2kk+1
+    uint32_t pf[2][4];
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      pf[kk][0] = pack2<T>(sacc[2 * kk][0], sacc[2 * kk][1]);
+      pf[kk][1] = pack2<T>(sacc[2 * kk][2], sacc[2 * kk][3]);
+      pf[kk][2] = pack2<T>(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
+      pf[kk][3] = pack2<T>(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
+    }
+    const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+    const int r0 = mt * 16 + g, r1 = r0 + 8;
+    __syncwarp();  // every lane's Q fragments of this tile are read: its rows take the output
+    // O = P V, 16 output columns (two 8-column tiles) per step
+#pragma unroll 2
+    for (int np = 0; np < DH / 16; ++np) {
+      float oa[4] = {0.f, 0.f, 0.f, 0.f}, ob[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t vb[4];
+      ldsm_x4_trans(vb, sv_a + (uint32_t)(((mi & 1) * 8 + rr) * RS + np * 16 + (mi >> 1) * 8) * 2);
+      mma16816<T>(oa, pf[0], vb[0], vb[1]);
+      mma16816<T>(ob, pf[0], vb[2], vb[3]);
+      if (kv_hi) {
+        ldsm_x4_trans(vb, sv_a + (uint32_t)((16 + (mi & 1) * 8 + rr) * RS + np * 16 + (mi >> 1) * 8) * 2);
+        mma16816<T>(oa, pf[1], vb[0], vb[1]);
+        mma16816<T>(ob, pf[1], vb[2], vb[3]);
+      }
+      const int col = np * 16 + 2 * t;
+      if constexpr (OUT == SP_F32) {
+        float* o = static_cast<float*>(out) + b * a.os0 + h * a.os1 + col;
+        if (r0 < Sq) {
+          *reinterpret_cast<float2*>(o + (int64_t)r0 * a.os2) = make_float2(oa[0] * inv0, oa[1] * inv0);
+          *reinterpret_cast<float2*>(o + (int64_t)r0 * a.os2 + 8) = make_float2(ob[0] * inv0, ob[1] * inv0);
+        }
+        if (r1 < Sq) {
+          *reinterpret_cast<float2*>(o + (int64_t)r1 * a.os2) = make_float2(oa[2] * inv1, oa[3] * inv1);
+          *reinterpret_cast<float2*>(o + (int64_t)r1 * a.os2 + 8) = make_float2(ob[2] * inv1, ob[3] * inv1);
+        }
+      } else {
+        uint32_t* s0 = reinterpret_cast<uint32_t*>(sq + r0 * RS + col);
+        uint32_t* s1 = reinterpret_cast<uint32_t*>(sq + r1 * RS + col);
+        s0[0] = pack_out2<OUT>(oa[0] * inv0, oa[1] * inv0);
+        s0[4] = pack_out2<OUT>(ob[0] * inv0, ob[1] * inv0);
+        s1[0] = pack_out2<OUT>(oa[2] * inv1, oa[3] * inv1);
+        s1[4] = pack_out2<OUT>(ob[2] * inv1, ob[3] * inv1);
+      }
+    }
+  }
+  if constexpr (OUT != SP_F32) {
+    __syncwarp();
+    uint16_t* o = static_cast<uint16_t*>(out) + b * a.os0 + h * a.os1;
+    for (int e = lane; e < Sq * kChunks; e += 32) {
+      const int r = e / kChunks, c = e - r * kChunks;
+      *reinterpret_cast<uint4*>(o + r * a.os2 + c * 8) =
+          *reinterpret_cast<const uint4*>(sq + r * RS + c * 8);
     }
   }
 }
 
-template <typename T, int DH>
-int launch_attn_short(const void* q, const void* k, const void* v, void* out, const ShortArgs& a,
-                      cudaStream_t s) {
-  auto kern = attn_short_kernel<T, DH>;
-  const int smem = kShortWarps * 2 * kShortMax * DH * (int)sizeof(T);
+template <typename T, int DH, int OUT>
+int launch_attn_short_mma(const void* q, const void* k, const void* v, void* out,
+                          const ShortArgs& a, cudaStream_t s) {
+  auto kern = attn_short_mma_kernel<T, DH, OUT>;
+  const int smem = kShortWarps * 3 * kShortMax * (DH + kSmRow) * (int)sizeof(T);
   static unsigned long long attr_set = 0;
   if (smem > 48 * 1024 && first_time_on_device(&attr_set)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -656,8 +774,19 @@ int launch_attn_short(const void* q, const void* k, const void* v, void* out, co
   const unsigned grid = (unsigned)((a.BH + kShortWarps - 1) / kShortWarps);
   kern<<<grid, kShortWarps * 32, smem, s>>>(static_cast<const T*>(q), static_cast<const T*>(k),
                                             static_cast<const T*>(v), out, a);
-  return check_launch("flash_attn short");
+  return check_launch("flash_attn short (mma)");
 }
+
+template <typename T, int DH>
+int launch_attn_short_out(const void* q, const void* k, const void* v, void* out,
+                          const ShortArgs& a, cudaStream_t s) {
+  switch (a.out_dtype) {
+    case SP_F32: return launch_attn_short_mma<T, DH, SP_F32>(q, k, v, out, a, s);
+    case SP_F16: return launch_attn_short_mma<T, DH, SP_F16>(q, k, v, out, a, s);
+    default: return launch_attn_short_mma<T, DH, SP_BF16>(q, k, v, out, a, s);
+  }
+}
+
 
 }  // namespace
 }  // namespace sp
@@ -699,18 +828,20 @@ extern "C" int sp_flash_attn_fwd(const void* q, const void* k, const void* v, co
   const float sc0 = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
   if (!mask && !causal && Sq <= kShortMax && Skv <= kShortMax && D == Dv && (D == 64 || D == 128) &&
       q_strides[3] == 1 && k_strides[3] == 1 && v_strides[3] == 1 && aligned(q, 16) &&
-      aligned(k, 16) && aligned(v, 16) && q_strides[2] % 8 == 0 && k_strides[2] % 8 == 0 &&
-      v_strides[2] % 8 == 0 && (o_strides[2] * oes) % 16 == 0) {
+      aligned(k, 16) && aligned(v, 16) && q_strides[0] % 8 == 0 && q_strides[1] % 8 == 0 &&
+      q_strides[2] % 8 == 0 && k_strides[0] % 8 == 0 && k_strides[1] % 8 == 0 &&
+      k_strides[2] % 8 == 0 && v_strides[0] % 8 == 0 && v_strides[1] % 8 == 0 &&
+      v_strides[2] % 8 == 0) {
     const ShortArgs a{B * H, H, Sq, Skv,
                       q_strides[0], q_strides[1], q_strides[2],
                       k_strides[0], k_strides[1], k_strides[2],
                       v_strides[0], v_strides[1], v_strides[2],
                       o_strides[0], o_strides[1], o_strides[2], sc0 * kLog2e, dtype_out};
     if (in_f16)
-      return D == 64 ? launch_attn_short<__half, 64>(q, k, v, out, a, s)
-                     : launch_attn_short<__half, 128>(q, k, v, out, a, s);
-    return D == 64 ? launch_attn_short<__nv_bfloat16, 64>(q, k, v, out, a, s)
-                   : launch_attn_short<__nv_bfloat16, 128>(q, k, v, out, a, s);
+      return D == 64 ? launch_attn_short_out<__half, 64>(q, k, v, out, a, s)
+                     : launch_attn_short_out<__half, 128>(q, k, v, out, a, s);
+    return D == 64 ? launch_attn_short_out<__nv_bfloat16, 64>(q, k, v, out, a, s)
+                   : launch_attn_short_out<__nv_bfloat16, 128>(q, k, v, out, a, s);
   }
   CUtensorMap mq, mk, mv;
   if (int rc = make_qkv_map(&mq, q, in_f16, Sq, H, B, (int)D, q_strides, "q")) return rc;

@@ -126,7 +126,10 @@ def test_setup_errors():
     (3, 40, 21, 21, 128, torch.bfloat16, None),       # Wan temporal attention shape
     (2, 5, 7, 32, 64, torch.float16, None),
     (1, 3, 32, 1, 128, torch.bfloat16, torch.float32),
-    (4, 2, 1, 17, 64, torch.bfloat16, None)])
+    (4, 2, 1, 17, 64, torch.bfloat16, None),
+    (3, 4, 16, 16, 128, torch.float16, torch.bfloat16),  # one 16-row tile, one key half
+    (2, 3, 32, 9, 64, torch.bfloat16, torch.float16),
+    (2, 2, 17, 31, 128, torch.float16, torch.float32)])
 def test_short_sequence_path(B, H, Sq, Skv, D, dtype, out_dtype):
     # Sq, Skv <= 32, no mask: the one-warp-per-(batch, head) kernel
     q, k, v = rnd((B, H, Sq, D), 40, dtype), rnd((B, H, Skv, D), 41, dtype), rnd((B, H, Skv, D), 42, dtype)
