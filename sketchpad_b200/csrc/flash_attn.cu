@@ -63,13 +63,6 @@ struct FaParams {
   int in_f16;  // 1 if inputs are f16 (P is then f16 too), 0 for bf16
 };
 
-__device__ __forceinline__ float mask_score(const FaParams& p, int kv, int qi, float raw) {
-  const bool valid = kv < p.Skv && !(p.causal && kv > qi);
-  float x = raw;
-  if (p.mask && valid && qi < p.Sq) x += p.mask[(int64_t)qi * p.mask_stride + kv] * p.inv_scale;
-  return valid ? x : -INFINITY;
-}
-
 template <int NBQ, int NBV, int STAGES>
 struct FaSmem {
   static constexpr int kQ = 0;                                // two tiles x NBQ boxes
@@ -98,11 +91,6 @@ __device__ __forceinline__ float exp2_fma(float x) {
   const float p = fmaf(fmaf(fmaf(0.055171624f, f, 0.24261113f), f, 0.69326098f), f, 0.99992806f);
   return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
 }
-
-// Raw score of key kv for query qi after masking: tail keys and causal positions -> -inf,
-// the additive mask applied in raw units (x_log2 = (s + mask / scale) * scale * log2 e).
-struct FaParams;
-__device__ __forceinline__ float mask_score(const FaParams& p, int kv, int qi, float raw);
 
 // Pairs of columns (out of every 16) whose exponentials use exp2_fma on unmasked tiles.
 constexpr uint32_t kPolyPairs = 0;  // none: measured slower than MUFU-only on B200 (issue-bound)
@@ -338,11 +326,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&s_free[t]);  // S_t may now be overwritten by S_t(j+1)
       }
       if (need_mask) {
+        if (p.mask == nullptr && !p.causal) {
+          // only the key tail: columns at and past Skv - kv0 get -inf
+          const int lim = (int)p.Skv - kv0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+          for (int q = 0; q < 4; ++q)
 #pragma unroll
-          for (int c = 0; c < 32; ++c)
-            r[q][c] = float_bits(mask_score(p, kv0 + q * 32 + c, qi, __uint_as_float(r[q][c])));
+            for (int c = 0; c < 32; ++c)
+              if (q * 32 + c >= lim) r[q][c] = float_bits(-INFINITY);
+        } else {
+          // tail keys and causal positions -> -inf; the additive mask is applied in raw units
+          // (x_log2 = (s + mask / scale) * scale * log2 e)
+          const int lim = (int)p.Skv - kv0;
+          const int clim = p.causal ? qi - kv0 + 1 : lim;  // causal: keys <= qi
+          const float* mrow =
+              (p.mask && qi < p.Sq) ? p.mask + (int64_t)qi * p.mask_stride + kv0 : nullptr;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const int col = q * 32 + c;
+              const bool valid = col < lim && col < clim;
+              float x = __uint_as_float(r[q][c]);
+              if (mrow && valid) x += mrow[col] * p.inv_scale;
+              r[q][c] = float_bits(valid ? x : -INFINITY);
+            }
+        }
       }
       float mx;
       {
