@@ -407,6 +407,17 @@ def _case_attention(torch, B, H, Sq, Skv, D):
     return (lambda: flash_attention(q, k, v, out=o)), 4.0 * B * H * Sq * Skv * D, "flop"
 
 
+def _case_attention_short(torch, HW, H, T, D):
+    # Wan's temporal attention: [T, HW, H, D] activations viewed as [HW, H, T, D] (strided)
+    from sketchpad_b200 import flash_attention
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q, k, v = (torch.randn(T, HW, H, D, device="cuda", generator=g, dtype=torch.bfloat16)
+               .permute(1, 2, 0, 3) for _ in range(3))
+    o = torch.empty(T, HW, H, D, device="cuda", dtype=torch.bfloat16).permute(1, 2, 0, 3)
+    # HBM bytes: q, k, v read once, o written once
+    return (lambda: flash_attention(q, k, v, out=o)), 4.0 * T * HW * H * D * 2, "byte"
+
+
 def _case_groupnorm(torch, B, C, Hh, W, dt):
     from sketchpad_b200 import groupnorm_bytes, groupnorm_silu
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -533,6 +544,8 @@ CASES = {
     "attn_2x8x4096x40": lambda t: _case_attention(t, 2, 8, 4096, 4096, 40),
     "attn_2x10x1024x64": lambda t: _case_attention(t, 2, 10, 1024, 1024, 64),
     "attn_cross_2x8x4096x77x40": lambda t: _case_attention(t, 2, 8, 4096, 77, 40),
+    "attn_short_3600x40x21x128": lambda t: _case_attention_short(t, 3600, 40, 21, 128),
+    "attn_short_900x40x21x128": lambda t: _case_attention_short(t, 900, 40, 21, 128),
     "gn_8x512x128x128_f32": lambda t: _case_groupnorm(t, 8, 512, 128, 128, t.float32),
     "gn_8x512x128x128_f16": lambda t: _case_groupnorm(t, 8, 512, 128, 128, t.float16),
     "gn_2x320x64x64_f32": lambda t: _case_groupnorm(t, 2, 320, 64, 64, t.float32),
