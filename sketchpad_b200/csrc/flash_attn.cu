@@ -61,6 +61,7 @@ struct FaParams {
   int64_t os0, os1, os2;  // output element strides (b, h, s); innermost is 1
   int out_dtype;
   int in_f16;  // 1 if inputs are f16 (P is then f16 too), 0 for bf16
+  int single;  // 1: one query tile per CTA (grids that would leave SMs idle), 0: two
 };
 
 template <int NBQ, int NBV, int STAGES>
@@ -133,12 +134,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int q0 = qt * 2 * kBM;
+  // query tiles of this CTA: two, or one when the grid of tile pairs would leave SMs idle
+  const int ntq = p.single ? 1 : 2;
+  const int q0 = qt * ntq * kBM;
 
   // KV tiles this pair of query tiles needs (causal: keys <= last query of tile 1).
   int n_tiles = p.n_kv_tiles;
   if (p.causal) {
-    const int last_q = min((int)p.Sq - 1, q0 + 2 * kBM - 1);
+    const int last_q = min((int)p.Sq - 1, q0 + ntq * kBM - 1);
     n_tiles = min(n_tiles, last_q / kBN + 1);
   }
 
@@ -175,8 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmq);
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
-      mbar_arrive_expect_tx(q_full, 2 * NBQ * kBox);
-      for (int t = 0; t < 2; ++t)
+      mbar_arrive_expect_tx(q_full, ntq * NBQ * kBox);
+      for (int t = 0; t < ntq; ++t)
         for (int blk = 0; blk < NBQ; ++blk)
           tma_load_4d(smem + L::kQ + (t * NBQ + blk) * kBox, &tmq, q_full, blk * 64, q0 + t * kBM,
                       h, b);
@@ -244,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       if (ok && n_tiles > 0) {
         issue_qk(0, 0);
-        issue_qk(1, 0);
+        if (ntq == 2) issue_qk(1, 0);
         umma_commit(&k_empty[0]);
       }
       for (int j = 0; ok && j < n_tiles; ++j) {
@@ -257,18 +260,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait(&s_free[0], j & 1, abort_flag, WD_MMA_WAIT)) break;
             tc_fence_after();
             issue_qk(0, j + 1);
-            if (!mbar_wait(&s_free[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
-            tc_fence_after();
-            issue_qk(1, j + 1);
+            if (ntq == 2) {
+              if (!mbar_wait(&s_free[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
+              tc_fence_after();
+              issue_qk(1, j + 1);
+            }
             umma_commit(&k_empty[st1]);
           }
           if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
           if (!mbar_wait(&p_full[0], j & 1, abort_flag, WD_MMA_WAIT)) break;
           tc_fence_after();
           issue_pv(0, j);
-          if (!mbar_wait(&p_full[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
-          tc_fence_after();
-          issue_pv(1, j);
+          if (ntq == 2) {
+            if (!mbar_wait(&p_full[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
+            tc_fence_after();
+            issue_pv(1, j);
+          }
           umma_commit(&v_empty[st]);
           continue;
         }
@@ -281,12 +288,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           issue_qk(0, j + 1);
         }
-        if (!mbar_wait(&p_full[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
-        tc_fence_after();
-        issue_pv(1, j);
+        if (ntq == 2) {
+          if (!mbar_wait(&p_full[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
+          tc_fence_after();
+          issue_pv(1, j);
+        }
         umma_commit(&v_empty[st]);
         if (more) {
-          issue_qk(1, j + 1);
+          if (ntq == 2) issue_qk(1, j + 1);
           umma_commit(&k_empty[st1]);
         }
       }
@@ -294,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(drain);
       mbar_wait(drain, 0, nullptr, WD_MMA_WAIT);
     }
-  } else if (warp < 8) {
+  } else if (warp < 4 * ntq) {
     // ------------------------------------------------------------------ softmax + epilogue
     const int t = warp >> 2;       // query tile of this warpgroup
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
@@ -535,7 +544,8 @@ int launch_fa(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& m
                        fa.maxDynamicSharedSizeBytes);
     }
   }
-  dim3 grid((unsigned)((p.Sq + 2 * kBM - 1) / (2 * kBM)), (unsigned)p.H, (unsigned)B);
+  const int tiles = p.single ? 1 : 2;
+  dim3 grid((unsigned)((p.Sq + tiles * kBM - 1) / (tiles * kBM)), (unsigned)p.H, (unsigned)B);
   kern<<<grid, kThreads, L::kAlloc, s>>>(mq, mk, mv, p);
   return check_launch("flash_attn");
 }
@@ -880,6 +890,8 @@ extern "C" int sp_flash_attn_fwd(const void* q, const void* k, const void* v, co
   p.os2 = o_strides[2];
   p.out_dtype = dtype_out;
   p.in_f16 = in_f16;
+  // one query tile per CTA when the grid of tile pairs would not cover the SMs
+  p.single = (Sq + 2 * kBM - 1) / (2 * kBM) * H * B < num_sms() ? 1 : 0;
   const bool qk2 = D > 64, v2 = Dv > 64;
   if (!qk2 && !v2) return launch_fa<1, 1, 4>(mq, mk, mv, p, B, s);  // 160 KB smem
   if (qk2 && v2) return launch_fa<2, 2, 2>(mq, mk, mv, p, B, s);     // 192 KB smem
