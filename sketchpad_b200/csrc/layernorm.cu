@@ -51,32 +51,6 @@ struct LnArgs {
   int modulate;
 };
 
-// gamma / beta of one row's columns c .. c+VE-1 (16-byte vectors; w and b 16-byte aligned)
-template <typename T>
-__device__ __forceinline__ void ln_affine(const LnArgs<T>& a, const T* wr, const T* br, int vi,
-                                          float* g, float* bb) {
-  constexpr int VE = 16 / sizeof(T);
-  if (wr) {
-    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr) + vi);
-    const T* e = reinterpret_cast<const T*>(&wv);
-    const float base = a.modulate ? 1.f : 0.f;
-#pragma unroll
-    for (int t = 0; t < VE; ++t) g[t] = base + ln_to_f32(e[t]);
-  } else {
-#pragma unroll
-    for (int t = 0; t < VE; ++t) g[t] = 1.f;
-  }
-  if (br) {
-    const uint4 bv = __ldg(reinterpret_cast<const uint4*>(br) + vi);
-    const T* e = reinterpret_cast<const T*>(&bv);
-#pragma unroll
-    for (int t = 0; t < VE; ++t) bb[t] = ln_to_f32(e[t]);
-  } else {
-#pragma unroll
-    for (int t = 0; t < VE; ++t) bb[t] = 0.f;
-  }
-}
-
 // VPL = 16-byte vectors per lane; row length n = nvec * (16 / sizeof(T)), nvec <= 32 * VPL.
 template <typename T, int VPL>
 __global__ void __launch_bounds__(kLnWarps * 32) ln_reg_kernel(const LnArgs<T> a) {
@@ -87,12 +61,20 @@ __global__ void __launch_bounds__(kLnWarps * 32) ln_reg_kernel(const LnArgs<T> a
   const int n = a.n;
   const int nvec = n / VE;
   const uint4* xv = reinterpret_cast<const uint4*>(a.x + row * n);
-  uint4 buf[VPL];
+  // gamma / beta rows are loaded together with x, so their latency overlaps the statistics
+  const int64_t goff = a.modulate ? (row / a.rows_per_group) * a.mod_stride : 0;
+  const T* wr = a.w ? a.w + goff : nullptr;
+  const T* br = a.b ? a.b + goff : nullptr;
+  uint4 buf[VPL], wbuf[VPL], bbuf[VPL];
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int vi = lane + 32 * j;
-    if (vi < nvec) buf[j] = __ldg(xv + vi);
+    if (vi < nvec) {
+      buf[j] = __ldg(xv + vi);
+      if (wr) wbuf[j] = __ldg(reinterpret_cast<const uint4*>(wr) + vi);
+      if (br) bbuf[j] = __ldg(reinterpret_cast<const uint4*>(br) + vi);
+    }
   }
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
@@ -126,16 +108,20 @@ __global__ void __launch_bounds__(kLnWarps * 32) ln_reg_kernel(const LnArgs<T> a
   }
   const float var = ln_warp_sum(ss) / (float)(a.unbiased ? n - 1 : n);
   const float rstd = rsqrtf(var + a.eps);
-  const int64_t goff = a.modulate ? (row / a.rows_per_group) * a.mod_stride : 0;
-  const T* wr = a.w ? a.w + goff : nullptr;
-  const T* br = a.b ? a.b + goff : nullptr;
   uint4* yv = reinterpret_cast<uint4*>(a.y + row * n);
+  const float gbase = a.modulate ? 1.f : 0.f;
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int vi = lane + 32 * j;
     if (vi < nvec) {
       float g[VE], bb[VE];
-      ln_affine(a, wr, br, vi, g, bb);
+      const T* we = reinterpret_cast<const T*>(&wbuf[j]);
+      const T* be = reinterpret_cast<const T*>(&bbuf[j]);
+#pragma unroll
+      for (int t = 0; t < VE; ++t) {
+        g[t] = wr ? gbase + ln_to_f32(we[t]) : 1.f;
+        bb[t] = br ? ln_to_f32(be[t]) : 0.f;
+      }
       const T* e = reinterpret_cast<const T*>(&buf[j]);
       uint4 o;
       T* oe = reinterpret_cast<T*>(&o);
