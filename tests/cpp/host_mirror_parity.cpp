@@ -1,0 +1,114 @@
+// Runs the C++ host mirror (include/sketchpad_b200.hpp) on seeded inputs and writes every
+// input and output to the file named by argv[1] as raw little-endian arrays, in this order:
+//   attention   q, k, v (bf16 bits [1,2,200,64], [1,2,77,64] x2), out (f32 [1,2,200,64])
+//   groupnorm   x (f32 [2,64,16,16]), gamma, beta (f32 [64]), y (f32, NCHW)
+//   Q8_0 linear GGUF bytes (128 rows x 256), x (bf16 bits [64,256]), y (bf16 bits [64,128])
+// The test compares the outputs with the CPU oracle.  Needs a B200.
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "sketchpad_b200.hpp"
+
+namespace sp = sketchpad_b200;
+
+static uint64_t g_state = 0x9E3779B97F4A7C15ull;
+static float uniform() {  // [0, 1)
+  g_state = g_state * 6364136223846793005ull + 1442695040888963407ull;
+  return (float)((g_state >> 40) & 0xFFFFFF) / 16777216.0f;
+}
+static float normal() {
+  const float u1 = uniform() + 1e-7f, u2 = uniform();
+  return std::sqrt(-2.0f * std::log(u1)) * std::cos(6.2831853f * u2);
+}
+static uint16_t to_bf16_bits(float f) {  // round to nearest even (finite inputs)
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+template <typename T>
+static void upload(void* dst, const std::vector<T>& src) {
+  if (cudaMemcpy(dst, src.data(), src.size() * sizeof(T), cudaMemcpyHostToDevice) != cudaSuccess)
+    throw std::runtime_error("upload failed");
+}
+template <typename T>
+static std::vector<T> download(const sp::Tensor& t) {
+  std::vector<T> h((size_t)t.view.numel());
+  if (cudaMemcpy(h.data(), t.view.data, h.size() * sizeof(T), cudaMemcpyDeviceToHost) != cudaSuccess)
+    throw std::runtime_error("download failed");
+  return h;
+}
+template <typename T>
+static void put(FILE* f, const std::vector<T>& v) {
+  std::fwrite(v.data(), sizeof(T), v.size(), f);
+}
+
+int main(int argc, char** argv) {
+  if (argc != 2) return 2;
+  FILE* f = std::fopen(argv[1], "wb");
+  if (!f) return 2;
+  try {
+    // ---- attention: bf16 in, f32 out, 77 keys (a key tail)
+    std::vector<uint16_t> hq(1 * 2 * 200 * 64), hk(1 * 2 * 77 * 64), hv(1 * 2 * 77 * 64);
+    for (auto* a : {&hq, &hk, &hv})
+      for (auto& e : *a) e = to_bf16_bits(normal());
+    sp::Tensor q = sp::empty(sp::DType::BF16, {1, 2, 200, 64});
+    sp::Tensor k = sp::empty(sp::DType::BF16, {1, 2, 77, 64});
+    sp::Tensor v = sp::empty(sp::DType::BF16, {1, 2, 77, 64});
+    upload(q.view.data, hq);
+    upload(k.view.data, hk);
+    upload(v.view.data, hv);
+    sp::Tensor o = sp::flash_attention(q.view, k.view, v.view,
+                                       sp::FlashAttentionOptions{}.with_dtype(sp::DType::F32));
+    put(f, hq);
+    put(f, hk);
+    put(f, hv);
+    put(f, download<float>(o));
+
+    // ---- GroupNorm + SiLU, f32 NCHW, 32 groups
+    std::vector<float> hx(2 * 64 * 16 * 16), hg(64), hb(64);
+    for (auto& e : hx) e = normal() * 3.f + 0.5f;
+    for (auto& e : hg) e = 1.f + 0.1f * normal();
+    for (auto& e : hb) e = 0.1f * normal();
+    sp::Tensor x = sp::empty(sp::DType::F32, {2, 64, 16, 16});
+    sp::Tensor g = sp::empty(sp::DType::F32, {64});
+    sp::Tensor b = sp::empty(sp::DType::F32, {64});
+    upload(x.view.data, hx);
+    upload(g.view.data, hg);
+    upload(b.view.data, hb);
+    sp::Tensor y = sp::groupnorm_silu(x.view, g.view, b.view);
+    put(f, hx);
+    put(f, hg);
+    put(f, hb);
+    put(f, download<float>(y));
+
+    // ---- Q8_0 linear: 128 x 256 weights from GGUF bytes, no bias
+    const int N = 128, K = 256, M = 64;
+    std::vector<uint8_t> gguf((size_t)N * (K / 32) * 34);
+    for (size_t blk = 0; blk < gguf.size() / 34; ++blk) {
+      const uint16_t scale = 0x1C00 + (uint16_t)(uniform() * 512);  // f16 in [2^-8, 2^-7)
+      gguf[blk * 34] = (uint8_t)(scale & 0xFF);
+      gguf[blk * 34 + 1] = (uint8_t)(scale >> 8);
+      for (int i = 0; i < 32; ++i) gguf[blk * 34 + 2 + i] = (uint8_t)(int8_t)(uniform() * 254.f - 127.f);
+    }
+    std::vector<uint16_t> hxq((size_t)M * K);
+    for (auto& e : hxq) e = to_bf16_bits(normal());
+    sp::GpuQuantizedLinear lin = sp::GpuQuantizedLinear::from_bytes(gguf.data(), gguf.size(), N, K);
+    sp::Tensor xq = sp::empty(sp::DType::BF16, {M, K});
+    upload(xq.view.data, hxq);
+    sp::Tensor yq = lin.forward(xq.view);
+    put(f, gguf);
+    put(f, hxq);
+    put(f, download<uint16_t>(yq));
+  } catch (const std::exception& e) {
+    std::fprintf(stderr, "error: %s\n", e.what());
+    std::fclose(f);
+    return 1;
+  }
+  std::fclose(f);
+  std::printf("ok\n");
+  return 0;
+}
