@@ -13,6 +13,7 @@
 //       crates/sketchpad-cubecl/src/quantized_matmul.rs:376-408, :655-767
 //   quantize_fp8 / Fp8Tensor::dequantize / Fp8Linear::forward
 //       crates/sketchpad-core/src/quantization.rs:435-447, :495-577, :601-609
+//   layer_norm (LayerNorm::forward, crates/sketchpad-core/src/layernorm.rs:63-73)
 // Like the reference, each operator allocates its output on the device and hands it to the
 // caller (Tensor owns the memory).  Every launch is asynchronous on the given stream.
 // Link with libsketchpad_b200.so and the CUDA runtime.
@@ -244,6 +245,22 @@ inline Tensor groupnorm_silu(const TensorView& x, const TensorView& weight,
 inline Tensor groupnorm(const TensorView& x, const TensorView& weight, const TensorView& bias,
                         const GroupNormSiLuOptions& opts = {}, cudaStream_t stream = nullptr) {
   return detail::groupnorm_act(x, weight, bias, opts, SP_ACT_NONE, stream);
+}
+
+// ------------------------------------------------------------------------------------------
+// LayerNorm (crates/sketchpad-core/src/layernorm.rs:63-73: burn's unbiased variance)
+// ------------------------------------------------------------------------------------------
+inline Tensor layer_norm(const TensorView& x, const TensorView& gamma, const TensorView& beta,
+                         float eps = 1e-5f, bool unbiased = true, cudaStream_t stream = nullptr) {
+  if (x.rank() < 1 || !x.is_contiguous())
+    throw std::invalid_argument("layer_norm: x must be a contiguous [..., n] tensor");
+  const int64_t n = x.shape.back();
+  if (gamma.numel() != n || beta.numel() != n || gamma.dtype != x.dtype || beta.dtype != x.dtype)
+    throw std::invalid_argument("layer_norm: gamma and beta must be [n] of the input dtype");
+  Tensor y = empty(x.dtype, x.shape);
+  check(sp_layernorm(x.data, gamma.data, beta.data, y.view.data, x.numel() / n, n, eps,
+                     unbiased ? 1 : 0, (int)x.dtype, stream));
+  return y;
 }
 
 // ------------------------------------------------------------------------------------------

@@ -49,6 +49,10 @@ int main() {
   ok &= throws<std::invalid_argument>("groupnorm weight length",
                                       [&] { sp::groupnorm_silu(x, w_short, w_short); });
 
+  ok &= throws<std::invalid_argument>("layer_norm gamma length", [&] {
+    sp::layer_norm(sp::TensorView::contiguous(nullptr, bf, {8, 320}), w_short, w_short);
+  });
+
   std::vector<uint8_t> bytes(34 * 4);
   ok &= throws<std::invalid_argument>("Q8_0 in_features not a multiple of 32", [&] {
     sp::GpuQuantizedLinear::from_bytes(bytes.data(), bytes.size(), 4, 48);

@@ -3,6 +3,9 @@
 //   attention   q, k, v (bf16 bits [1,2,200,64], [1,2,77,64] x2), out (f32 [1,2,200,64])
 //   groupnorm   x (f32 [2,64,16,16]), gamma, beta (f32 [64]), y (f32, NCHW)
 //   Q8_0 linear GGUF bytes (128 rows x 256), x (bf16 bits [64,256]), y (bf16 bits [64,128])
+//   LayerNorm   x (f32 [64,320]), gamma, beta (f32 [320]), y (f32)
+//   FP8 linear  w (f32 [128,256], quantized per channel), x (bf16 bits [64,256]),
+//               y (bf16 bits [64,128])
 // The test compares the outputs with the CPU oracle.  Needs a B200.
 #include <cmath>
 #include <cstdint>
@@ -103,6 +106,34 @@ int main(int argc, char** argv) {
     put(f, gguf);
     put(f, hxq);
     put(f, download<uint16_t>(yq));
+
+    // ---- LayerNorm, f32 [64, 320], unbiased variance
+    std::vector<float> hl(64 * 320), hlg(320), hlb(320);
+    for (auto& e : hl) e = normal() * 2.f + 0.3f;
+    for (auto& e : hlg) e = 1.f + 0.1f * normal();
+    for (auto& e : hlb) e = 0.1f * normal();
+    sp::Tensor lx = sp::empty(sp::DType::F32, {64, 320});
+    sp::Tensor lg = sp::empty(sp::DType::F32, {320});
+    sp::Tensor lb = sp::empty(sp::DType::F32, {320});
+    upload(lx.view.data, hl);
+    upload(lg.view.data, hlg);
+    upload(lb.view.data, hlb);
+    sp::Tensor ly = sp::layer_norm(lx.view, lg.view, lb.view);
+    put(f, hl);
+    put(f, hlg);
+    put(f, hlb);
+    put(f, download<float>(ly));
+
+    // ---- FP8 e4m3 linear, per-channel scales
+    std::vector<float> hw((size_t)N * K);
+    for (auto& e : hw) e = 0.05f * normal();
+    sp::Tensor w = sp::empty(sp::DType::F32, {N, K});
+    upload(w.view.data, hw);
+    sp::Fp8Linear fp8(sp::quantize_fp8(w.view));
+    sp::Tensor yf = fp8.forward(xq.view);
+    put(f, hw);
+    put(f, hxq);
+    put(f, download<uint16_t>(yf));
   } catch (const std::exception& e) {
     std::fprintf(stderr, "error: %s\n", e.what());
     std::fclose(f);

@@ -4,8 +4,9 @@ for compiled callers, with the reference's names and error behaviour.
   * setup errors (CPU): attention shape / dtype / mask errors raise AttentionSetupError
     (attention.rs:97-104 returns Err there), GroupNorm and the quantized layers reject bad
     shapes before any device call;
-  * parity (GPU): attention with a 77-key tail, GroupNorm+SiLU f32 and a Q8_0 linear run
-    through the C++ operators on seeded inputs, checked against the CPU oracle.
+  * parity (GPU): attention with a 77-key tail, GroupNorm+SiLU f32, LayerNorm f32, a Q8_0 and
+    an FP8 linear run through the C++ operators on seeded inputs, checked against the CPU
+    oracle.
 """
 import os
 import shutil
@@ -80,5 +81,17 @@ def test_cpp_mirror_parity(tmp_path):
     gguf = take(np.uint8, 128 * (256 // 32) * 34)
     xq = _bf16(take(np.uint16, 64 * 256)).reshape(64, 256)
     yq = _bf16(take(np.uint16, 64 * 128)).reshape(64, 128)
-    assert pos == len(buf)
     assert rel_err(yq, oracle.q8_0_matmul(gguf, 128, 256, xq)) < TOL_HALF
+    # LayerNorm f32 [64, 320]
+    lx = take(np.float32, 64 * 320).reshape(64, 320)
+    lg = take(np.float32, 320)
+    lb = take(np.float32, 320)
+    ly = take(np.float32, 64 * 320).reshape(64, 320)
+    assert rel_err(ly, oracle.layernorm(lx, lg, lb, 1e-5)) < TOL_F32
+    # FP8 linear, per-channel e4m3 weights
+    w = take(np.float32, 128 * 256).reshape(128, 256)
+    xf = _bf16(take(np.uint16, 64 * 256)).reshape(64, 256)
+    yf = _bf16(take(np.uint16, 64 * 128)).reshape(64, 128)
+    assert pos == len(buf)
+    data, sc = oracle.fp8_quantize(w)
+    assert rel_err(yf, oracle.linear_nt(xf, oracle.fp8_dequantize(data, sc))) < TOL_HALF
