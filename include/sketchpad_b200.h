@@ -92,6 +92,12 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
                      int64_t C, int64_t H, int64_t W, const int64_t x_strides[4], int64_t groups,
                      float eps, int act, int dtype, void* workspace, size_t workspace_bytes,
                      void* stream);
+/* The element strides sp_groupnorm_act writes y with for this x: channels-last when x is
+ * dense channels-last (dimensions of size 1 ignored, C == 1 counts as NCHW), else contiguous
+ * NCHW.  Callers that allocate y (the reference allocates it inside groupnorm_silu,
+ * groupnorm_silu.rs:287) use this to label it.  SP_ERR_INVALID_ARG on non-positive sizes. */
+int sp_groupnorm_act_output_strides(int64_t B, int64_t C, int64_t H, int64_t W,
+                                    const int64_t x_strides[4], int64_t y_strides[4]);
 
 /* GroupNorm (+ SiLU) of x + x_add[b, c]: the ResBlock's time-embedding add (h + temb[:, :,
  * None, None]) followed by its second GroupNorm(+SiLU), as ResBlockCubeCL::forward does in two

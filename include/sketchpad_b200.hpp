@@ -100,6 +100,7 @@ struct TensorView {
   }
   size_t rank() const { return shape.size(); }
   bool is_contiguous() const {
+    if (strides.size() != shape.size()) return false;
     int64_t want = 1;
     for (int i = (int)shape.size() - 1; i >= 0; --i) {
       if (shape[i] > 1 && strides[i] != want) return false;
@@ -140,11 +141,22 @@ inline void strides4(const TensorView& t, int64_t out[4]) {
   for (int i = 0; i < 4; ++i) out[i] = t.strides[i];
 }
 
+// A hand-built view must carry one stride per dimension before any stride is read.
+inline bool well_formed(const TensorView& t) { return t.strides.size() == t.shape.size(); }
+
+// Argument and layout problems are setup errors (AttentionSetupError in the reference);
+// launch failures and a missing sm_100 device keep their status as SketchpadError.
+inline bool is_setup_status(int rc) {
+  return rc == SP_ERR_INVALID_ARG || rc == SP_ERR_SHAPE || rc == SP_ERR_DTYPE || rc == SP_ERR_ALIGN;
+}
+
 inline Tensor flash(const TensorView& q, const TensorView& k, const TensorView& v,
                     const TensorView* mask, const FlashAttentionOptions& opts,
                     std::optional<float> scale, cudaStream_t stream) {
   if (q.rank() != 4 || k.rank() != 4 || v.rank() != 4)
     throw AttentionSetupError("query, key and value must be [batch, heads, seq, dim]");
+  if (!well_formed(q) || !well_formed(k) || !well_formed(v) || (mask && !well_formed(*mask)))
+    throw AttentionSetupError("every view needs one stride per dimension");
   const int64_t B = q.shape[0], H = q.shape[1], Sq = q.shape[2], D = q.shape[3];
   const int64_t Skv = k.shape[2], Dv = v.shape[3];
   if (k.shape[0] != B || k.shape[1] != H || k.shape[3] != D || v.shape[0] != B ||
@@ -173,7 +185,10 @@ inline Tensor flash(const TensorView& q, const TensorView& k, const TensorView& 
   const int rc = sp_flash_attn_fwd(q.data, k.data, v.data, m, mstride, out.view.data, B, H, Sq, Skv,
                                    D, Dv, qs, ks, vs, os, (int)q.dtype, (int)od,
                                    opts.causal ? 1 : 0, scale.value_or(0.f), stream);
-  if (rc != SP_OK) throw AttentionSetupError(sp_last_error());
+  if (rc != SP_OK) {
+    if (is_setup_status(rc)) throw AttentionSetupError(sp_last_error());
+    check(rc);
+  }
   return out;
 }
 }  // namespace detail
@@ -207,17 +222,19 @@ namespace detail {
 inline Tensor groupnorm_act(const TensorView& x, const TensorView& weight, const TensorView& bias,
                             const GroupNormSiLuOptions& opts, int act, cudaStream_t stream) {
   if (x.rank() != 4) throw std::invalid_argument("groupnorm: input must be [batch, channels, h, w]");
+  if (!well_formed(x)) throw std::invalid_argument("groupnorm: input needs one stride per dimension");
   const int64_t B = x.shape[0], C = x.shape[1], H = x.shape[2], W = x.shape[3];
   if (opts.num_groups <= 0 || C % opts.num_groups != 0)
     throw std::invalid_argument("groupnorm: channels must be divisible by num_groups");
   if (weight.numel() != C || bias.numel() != C || weight.dtype != x.dtype || bias.dtype != x.dtype)
     throw std::invalid_argument("groupnorm: weight and bias must be [channels] of the input dtype");
-  int64_t xs[4];
+  int64_t xs[4], ys[4];
   strides4(x, xs);
-  // y follows x: dense channels-last stays channels-last, anything else becomes NCHW
-  const bool nhwc = xs[1] == 1 && xs[3] == C && xs[2] == W * C && xs[0] == H * W * C;
+  // y follows x as the library decides it (dense channels-last stays channels-last, size-1
+  // dimensions ignored; anything else becomes NCHW): ask the library, do not guess
+  check(sp_groupnorm_act_output_strides(B, C, H, W, xs, ys));
   Tensor y = empty(x.dtype, {B, C, H, W});
-  if (nhwc) y.view.strides = {H * W * C, 1, W * C, C};
+  y.view.strides = {ys[0], ys[1], ys[2], ys[3]};
   const size_t ws_bytes =
       sp_groupnorm_act_workspace_size(B, C, H, W, xs, opts.num_groups, (int)x.dtype);
   void* ws = nullptr;  // stream-ordered: allocated and freed on `stream`
@@ -270,9 +287,11 @@ class GpuQuantizedLinear {
  public:
   // GpuQuantizedLinear::from_bytes for Q8_0: GGUF bytes on the host ([out_f rows of in_f/32
   // blocks of 34 bytes]), repacked losslessly into the planar device layout.  bias: [out_f]
-  // bf16 on the device, or none.
+  // bf16 on the device, or none.  The upload runs on `stream` and is complete when this
+  // returns, so kernels later queued on any stream (non-blocking ones included) see it.
   static GpuQuantizedLinear from_bytes(const uint8_t* gguf, size_t nbytes, int64_t out_f,
-                                       int64_t in_f, std::optional<TensorView> bias = std::nullopt) {
+                                       int64_t in_f, std::optional<TensorView> bias = std::nullopt,
+                                       cudaStream_t stream = nullptr) {
     if (out_f <= 0 || in_f <= 0 || in_f % 32 != 0)
       throw std::invalid_argument("Q8_0: in_features must be a positive multiple of 32");
     if (nbytes != (size_t)(out_f * (in_f / 32) * 34))
@@ -287,9 +306,16 @@ class GpuQuantizedLinear {
     l.in_f_ = in_f;
     l.q_ = std::make_shared<DeviceBuffer>(q.size());
     l.scale_ = std::make_shared<DeviceBuffer>(sc.size() * 2);
-    if (cudaMemcpy(l.q_->get(), q.data(), q.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(l.scale_->get(), sc.data(), sc.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+    // pageable sources: wait for the copies before q / sc go out of scope (a plain
+    // cudaMemcpy may return before its DMA lands, unordered with non-blocking streams)
+    if (cudaMemcpyAsync(l.q_->get(), q.data(), q.size(), cudaMemcpyHostToDevice, stream) !=
+            cudaSuccess ||
+        cudaMemcpyAsync(l.scale_->get(), sc.data(), sc.size() * 2, cudaMemcpyHostToDevice,
+                        stream) != cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess) {
+      cudaGetLastError();
       throw SketchpadError(SP_ERR_LAUNCH, "Q8_0: weight upload failed");
+    }
     l.bias_ = bias;
     return l;
   }
@@ -328,7 +354,8 @@ class GpuQuantizedLinear {
 // dequantize_q8_0 (:376-408): GGUF bytes on the host -> [out_f, in_f] of out_dtype.
 inline Tensor dequantize_q8_0(const uint8_t* gguf, size_t nbytes, int64_t out_f, int64_t in_f,
                               DType out_dtype = DType::F32, cudaStream_t stream = nullptr) {
-  return GpuQuantizedLinear::from_bytes(gguf, nbytes, out_f, in_f).dequantize(out_dtype, stream);
+  return GpuQuantizedLinear::from_bytes(gguf, nbytes, out_f, in_f, std::nullopt, stream)
+      .dequantize(out_dtype, stream);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -363,9 +390,14 @@ inline Fp8Tensor quantize_fp8(const TensorView& w, bool per_channel = true,
   int mode = per_channel ? SP_FP8_PER_CHANNEL : SP_FP8_PER_TENSOR;
   if (given_scale) {
     mode = SP_FP8_GIVEN_SCALE;
-    if (cudaMemcpy(t.scale->get(), &*given_scale, sizeof(float), cudaMemcpyHostToDevice) !=
-        cudaSuccess)
+    // ordered on `stream` ahead of sp_fp8_quantize; synchronised because the source is a
+    // host value that does not outlive this call
+    if (cudaMemcpyAsync(t.scale->get(), &*given_scale, sizeof(float), cudaMemcpyHostToDevice,
+                        stream) != cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess) {
+      cudaGetLastError();
       throw SketchpadError(SP_ERR_LAUNCH, "quantize_fp8: scale upload failed");
+    }
   }
   check(sp_fp8_quantize(static_cast<const float*>(w.data), t.N, t.K, mode, t.bytes->get(),
                         static_cast<float*>(t.scale->get()), stream));

@@ -38,6 +38,7 @@ SIGNATURES = {
     "sp_flash_attn_fwd": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
                                  _i64, _i64p, _i64p, _i64p, _i64p, _int, _int, _int, _f, _vp]),
     "sp_groupnorm_act_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64p, _i64, _int]),
+    "sp_groupnorm_act_output_strides": (_int, [_i64, _i64, _i64, _i64, _i64p, _i64p]),
     "sp_groupnorm_act": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p, _i64, _f,
                                 _int, _int, _vp, _sz, _vp]),
     "sp_groupnorm_add_act": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p,

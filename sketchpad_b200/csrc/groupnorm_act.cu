@@ -977,6 +977,15 @@ size_t sp_groupnorm_act_workspace_size(int64_t B, int64_t C, int64_t H, int64_t 
   return (pl.cluster_path || pl.stream_path) ? 0 : sp::general_workspace_bytes(B, C, H, W, groups);
 }
 
+int sp_groupnorm_act_output_strides(int64_t B, int64_t C, int64_t H, int64_t W,
+                                    const int64_t x_strides[4], int64_t y_strides[4]) {
+  sp::clear_error();
+  if (!y_strides || B <= 0 || C <= 0 || H <= 0 || W <= 0)
+    return sp::set_error(SP_ERR_INVALID_ARG, "groupnorm output strides: bad arguments");
+  sp::output_strides(B, C, H, W, x_strides, y_strides);
+  return SP_OK;
+}
+
 int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y, int64_t B,
                      int64_t C, int64_t H, int64_t W, const int64_t x_strides[4], int64_t groups,
                      float eps, int act, int dtype, void* workspace, size_t workspace_bytes,

@@ -66,6 +66,30 @@ int main() {
   ok &= throws<std::invalid_argument>("FP8 weights dtype", [&] {
     sp::quantize_fp8(sp::TensorView::contiguous(nullptr, bf, {64, 64}));
   });
+  // a hand-built view with fewer strides than dimensions is a setup error, not a read past
+  // the end of the stride vector
+  sp::TensorView qshort = q;
+  qshort.strides.resize(2);
+  ok &= throws<sp::AttentionSetupError>("short query strides",
+                                        [&] { sp::flash_attention(qshort, k, v); });
+  sp::TensorView xshort = x;
+  xshort.strides.clear();
+  ok &= throws<std::invalid_argument>("missing groupnorm strides", [&] { sp::groupnorm_silu(xshort, w, w); });
+
+  // the output layout comes from the library: channels-last with B == 1 stays channels-last
+  // whatever the batch stride; C == 1 and NCHW inputs give NCHW
+  {
+    int64_t ys[4];
+    const int64_t nhwc_b1[4] = {12345, 1, 16 * 64, 64};
+    ok &= sp_groupnorm_act_output_strides(1, 64, 16, 16, nhwc_b1, ys) == SP_OK && ys[1] == 1 &&
+          ys[3] == 64 && ys[2] == 16 * 64;
+    const int64_t nchw[4] = {64 * 256, 256, 16, 1};
+    ok &= sp_groupnorm_act_output_strides(2, 64, 16, 16, nchw, ys) == SP_OK && ys[3] == 1 &&
+          ys[1] == 256;
+    ok &= sp_groupnorm_act_output_strides(2, 64, 16, 16, nullptr, ys) == SP_OK && ys[3] == 1;
+    ok &= sp_groupnorm_act_output_strides(0, 64, 16, 16, nullptr, ys) == SP_ERR_INVALID_ARG;
+    if (!ok) std::printf("FAIL groupnorm output strides\n");
+  }
   if (!ok) return 1;
   std::printf("ok\n");
   return 0;

@@ -6,6 +6,9 @@
 //   LayerNorm   x (f32 [64,320]), gamma, beta (f32 [320]), y (f32)
 //   FP8 linear  w (f32 [128,256], quantized per channel), x (bf16 bits [64,256]),
 //               y (bf16 bits [64,128])
+//   groupnorm   channels-last x [1,64,16,16] whose batch stride is not H*W*C (any stride
+//               is valid for a size-1 batch): x, gamma, beta (f32), y (f32) -- x and y
+//               gathered to NCHW order through each tensor's own strides
 // The test compares the outputs with the CPU oracle.  Needs a B200.
 #include <cmath>
 #include <cstdint>
@@ -43,6 +46,18 @@ static std::vector<T> download(const sp::Tensor& t) {
   if (cudaMemcpy(h.data(), t.view.data, h.size() * sizeof(T), cudaMemcpyDeviceToHost) != cudaSuccess)
     throw std::runtime_error("download failed");
   return h;
+}
+// the elements of a 4-D tensor in NCHW order, read through its strides
+static std::vector<float> gather_nchw(const sp::Tensor& t, const std::vector<float>& mem) {
+  const auto& sh = t.view.shape;
+  const auto& st = t.view.strides;
+  std::vector<float> out;
+  for (int64_t a = 0; a < sh[0]; ++a)
+    for (int64_t b = 0; b < sh[1]; ++b)
+      for (int64_t c = 0; c < sh[2]; ++c)
+        for (int64_t d = 0; d < sh[3]; ++d)
+          out.push_back(mem[(size_t)(a * st[0] + b * st[1] + c * st[2] + d * st[3])]);
+  return out;
 }
 template <typename T>
 static void put(FILE* f, const std::vector<T>& v) {
@@ -134,6 +149,30 @@ int main(int argc, char** argv) {
     put(f, hw);
     put(f, hxq);
     put(f, download<uint16_t>(yf));
+
+    // ---- GroupNorm + SiLU, channels-last B = 1 with an unusual batch stride: the library
+    // writes y channels-last (size-1 dimensions do not decide the layout) and the mirror
+    // must label y with the strides the library used
+    {
+      const int64_t C = 64, H = 16, W = 16;
+      std::vector<float> mem((size_t)(C * H * W));
+      for (auto& e : mem) e = normal() * 3.f + 0.5f;
+      sp::Tensor xb = sp::empty(sp::DType::F32, {1, C, H, W});
+      upload(xb.view.data, mem);
+      xb.view.strides = {7 * C * H * W + 3, 1, W * C, C};  // channels-last, odd batch stride
+      std::vector<float> g2(C), b2(C);
+      for (auto& e : g2) e = 1.f + 0.1f * normal();
+      for (auto& e : b2) e = 0.1f * normal();
+      sp::Tensor gg = sp::empty(sp::DType::F32, {C});
+      sp::Tensor bb = sp::empty(sp::DType::F32, {C});
+      upload(gg.view.data, g2);
+      upload(bb.view.data, b2);
+      sp::Tensor yb = sp::groupnorm_silu(xb.view, gg.view, bb.view);
+      put(f, gather_nchw(xb, mem));
+      put(f, g2);
+      put(f, b2);
+      put(f, gather_nchw(yb, download<float>(yb)));
+    }
   } catch (const std::exception& e) {
     std::fprintf(stderr, "error: %s\n", e.what());
     std::fclose(f);

@@ -23,11 +23,16 @@ CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 
 
 def _compile(name, tmp_path):
-    from sketchpad_b200 import build as _build
-    lib = _build.build()
     gxx = shutil.which("g++")
     if gxx is None or not os.path.isdir(os.path.join(CUDA, "include")):
         pytest.skip("g++ or the CUDA headers are not available")
+    from sketchpad_b200 import build as _build
+    try:
+        lib = _build.build()
+    except RuntimeError as exc:  # no nvcc on this machine: nothing to link against
+        if "nvcc not found" in str(exc):
+            pytest.skip(str(exc))
+        raise
     exe = str(tmp_path / name)
     libdir = os.path.dirname(lib)
     cmd = [gxx, "-std=c++17", "-O1", "-Wall", "-I" + os.path.join(ROOT, "include"),
@@ -92,6 +97,13 @@ def test_cpp_mirror_parity(tmp_path):
     w = take(np.float32, 128 * 256).reshape(128, 256)
     xf = _bf16(take(np.uint16, 64 * 256)).reshape(64, 256)
     yf = _bf16(take(np.uint16, 64 * 128)).reshape(64, 128)
-    assert pos == len(buf)
     data, sc = oracle.fp8_quantize(w)
     assert rel_err(yf, oracle.linear_nt(xf, oracle.fp8_dequantize(data, sc))) < TOL_HALF
+    # GroupNorm + SiLU, channels-last B = 1 with an unusual batch stride (gathered to NCHW
+    # through the strides the mirror labelled y with)
+    x1 = take(np.float32, 64 * 16 * 16).reshape(1, 64, 16, 16)
+    g1 = take(np.float32, 64)
+    b1 = take(np.float32, 64)
+    y1 = take(np.float32, 64 * 16 * 16).reshape(1, 64, 16, 16)
+    assert pos == len(buf)
+    assert rel_err(y1, oracle.groupnorm_act(x1, g1, b1, 32, 1e-5, True)) < TOL_F32
