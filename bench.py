@@ -205,6 +205,89 @@ def kernel_microbench(torch, peaks, reps=20):
     return out
 
 
+def ulysses_wan_block_bench(torch, dist, ws, rank, steps=4, warmup=3):
+    """The Wan block at full width (hidden 5120, 40 heads, FFN 13824, FP8 weights) over the
+    whole 21 x 45 x 80 = 75,600-token sequence, sequence-parallel (Ulysses) over the ws ranks
+    through the library's NCCL communicator (sp_ulysses_a2a): block ms (max over ranks), the
+    all-to-all ms inside it (CUDA events around each exchange, max over ranks), its share, and
+    the per-GPU bytes sent over NVLink per ms."""
+    from sketchpad_b200.comm import NcclComm
+    from sketchpad_b200.wan import WanBlockB200, WanConfig, wan_block_flops
+    cfg = WanConfig()
+    nt, nh, nw = 21, 45, 80
+    S = nt * nh * nw
+    comm = NcclComm.from_group(timeout=120.0)
+    try:
+        blk = WanBlockB200(0, cfg, "cuda", group=comm)
+        g = torch.Generator(device="cuda").manual_seed(7)
+        s = S // ws
+        x = torch.randn(1, S, cfg.hidden_size, device="cuda", generator=g).to(torch.bfloat16)
+        x = x[:, rank * s:(rank + 1) * s].contiguous()
+        ctx = torch.randn(1, 512, cfg.hidden_size, device="cuda", generator=g).to(torch.bfloat16)
+        cond = torch.randn(1, cfg.hidden_size, device="cuda", generator=g).to(torch.bfloat16)
+        with torch.inference_mode():
+            for _ in range(warmup):
+                blk.forward(x, cond, ctx, nt, nh, nw)
+            comm.wait(120.0)
+            dist.barrier()
+            torch.cuda.synchronize()
+            comm.events = []
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(steps):
+                blk.forward(x, cond, ctx, nt, nh, nw)
+            b.record()
+            comm.wait(120.0)
+            torch.cuda.synchronize()
+            block_ms = a.elapsed_time(b) / steps
+            ev, comm.events = comm.events, None
+            a2a_ms = sum(e0.elapsed_time(e1) for e0, e1, _ in ev) / steps
+            sent = sum(n for _, _, n in ev) / steps
+        t = torch.tensor([block_ms, a2a_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        block_ms, a2a_ms = float(t[0]), float(t[1])
+        return {"tokens": S, "ranks": ws, "block_ms": block_ms, "a2a_ms": a2a_ms,
+                "a2a_share": a2a_ms / block_ms, "a2a_per_block": len(ev) // steps,
+                "a2a_bytes_sent_per_gpu": sent, "a2a_gbs_per_gpu": sent / a2a_ms / 1e6,
+                "block_tflops_per_gpu": wan_block_flops(cfg)["total"] / ws / block_ms / 1e9,
+                "transport": "sp_ulysses_a2a (library NCCL communicator, grouped send/recv)",
+                "timing": "CUDA events around the block and each all-to-all; max over ranks"}
+    finally:
+        comm.destroy()
+
+
+def cfg_split_bench(torch, dist, ws, rank, net, steps=10, warmup=3):
+    """One CFG pair split over ranks 0 and 1 (the unconditional and the conditional
+    prediction, batch 1 each): the pair's step latency is the slower half plus the exchange
+    of the two noise predictions (an all-gather of 4x64x64 f32).  Every rank runs its batch-1
+    half; the latency reported is that of ranks 0 and 1 (max over all ranks)."""
+    from sketchpad_b200.unet import UNetStepGraph
+    graph = UNetStepGraph(net, batch=1, warmup=2)
+    g = torch.Generator(device="cuda").manual_seed(30 + rank)
+    graph.x.copy_(torch.randn(1, 4, 64, 64, device="cuda", generator=g))
+    graph.t.fill_(999.0)
+    graph.ctx.copy_(torch.randn(1, 77, 768, device="cuda", generator=g))
+    eps_all = torch.empty(ws, 1, 4, 64, 64, device="cuda")
+    with torch.inference_mode():
+        for _ in range(warmup):
+            dist.all_gather_into_tensor(eps_all, graph.replay().float())
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            dist.all_gather_into_tensor(eps_all, graph.replay().float())
+        b.record()
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    t = torch.tensor([ms], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del graph
+    return {"pair_step_ms": float(t[0]), "pairs_per_s": 1e3 / float(t[0]),
+            "split": "uncond on rank 0, cond on rank 1 (batch 1 each), eps all-gathered",
+            "timing": "CUDA events, max over ranks"}
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -340,10 +423,18 @@ def run_b200(args):
         d2h = yh.numel() * 2
 
     # max over ranks
+    ulysses = cfg_split = None
     if ws > 1:
         tt = torch.tensor([ms, e2e_ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms, e2e_ms = float(tt[0]), float(tt[1])
+        if not args.no_ulysses:
+            del graph
+            graph = None
+            torch.cuda.empty_cache()
+            if ws == 2:
+                cfg_split = cfg_split_bench(torch, dist, ws, rank, net)
+            ulysses = ulysses_wan_block_bench(torch, dist, ws, rank)
 
     kernels = None
     cpu = None
@@ -370,7 +461,7 @@ def run_b200(args):
             "e2e": {"value": ws * 1e3 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * args.steps,
-            "cuda_graph": graph is not None,
+            "cuda_graph": not args.no_graph,
             "roofline": {"kernel": "sp flash attention (all 32 launches of the step)",
                          "bound": "tensor", "achieved": achieved,
                          "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
@@ -387,6 +478,10 @@ def run_b200(args):
             "kernels": kernels,
             "cpu_baseline": cpu,
         }
+        if ulysses is not None:
+            line["ulysses_wan_block"] = ulysses
+        if cfg_split is not None:
+            line["cfg_split_pair"] = cfg_split
         line["clocks"] = clk.summary()
         print(json.dumps(line), flush=True)
     if ws > 1:
@@ -594,6 +689,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time eager steps, no CUDA graph")
+    ap.add_argument("--no-ulysses", action="store_true",
+                    help="N > 1: skip the sequence-parallel Wan block and CFG-split lines")
     ap.add_argument("--case", default=None, choices=sorted(CASES),
                     help="run one kernel workload only (for ncu captures); prints its timing")
     args = ap.parse_args()

@@ -32,7 +32,8 @@ typedef enum sp_status {
   SP_ERR_ALIGN = -4,       /* pointer/stride alignment the kernel cannot use */
   SP_ERR_LAUNCH = -5,      /* CUDA launch / driver call failed */
   SP_ERR_WORKSPACE = -6,   /* workspace missing or too small */
-  SP_ERR_DEVICE = -7       /* device is not sm_100 */
+  SP_ERR_DEVICE = -7,      /* device is not sm_100 */
+  SP_ERR_COMM = -8         /* NCCL missing or failed, or a communication deadline passed */
 } sp_status;
 
 typedef enum sp_dtype { SP_F32 = 0, SP_F16 = 1, SP_BF16 = 2 } sp_dtype;
@@ -317,6 +318,44 @@ int sp_cfg_dpmpp_2m_step(const void* x, const void* eps_uncond, const void* eps_
                          float* prev_denoised, void* out, int64_t n, float guidance, float sigma,
                          float sigma_ratio, float one_minus_exp_neg_h, float one_plus_coeff,
                          float coeff, int second_order, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Sequence-parallel (Ulysses) exchange of the long-video DiT, over NCCL.
+ * The reference runs Wan::forward on one device (crates/sketchpad-dit/src/wan.rs:720-757,
+ * blocks :489-573) and has no collectives; splitting its 75,600 tokens over P GPUs needs an
+ * all-to-all around each self-attention ([S/P tokens, H heads] <-> [S tokens, H/P heads]).
+ * NCCL is loaded at run time (libnccl.so.2; the copy already in the process, if any).
+ *
+ * Communicators are NON-BLOCKING (ncclConfig_t.blocking = 0): every call below returns once
+ * its work is enqueued, polling ncclCommGetAsyncError against a host deadline of timeout_s
+ * seconds; on an NCCL error or an expired deadline the communicator is aborted
+ * (ncclCommAbort: its kernels and proxy threads stop) and SP_ERR_COMM is returned, so a rank
+ * that never joins or stops answering ends the others' calls with an error, not a hang.
+ * ------------------------------------------------------------------------------------ */
+/* Size of an NCCL unique id (128 bytes) and a fresh one, made by one rank and passed to the
+ * others by any host channel. */
+size_t sp_nccl_unique_id_bytes(void);
+int sp_nccl_unique_id(void* id_out, size_t id_bytes);
+/* Joins rank `rank` of `nranks` to the communicator named by `id` on the current device. */
+int sp_nccl_comm_init(void** comm_out, int nranks, int rank, const void* id, double timeout_s);
+/* The communicator's asynchronous state (an ncclResult_t: 0 success, 7 in progress). */
+int sp_nccl_comm_poll(void* comm, int* nccl_status_out);
+/* Waits until `stream` has finished (cudaStreamQuery) while polling the communicator; aborts
+ * it and returns SP_ERR_COMM on an NCCL error or when timeout_s passes first. */
+int sp_nccl_wait(void* comm, void* stream, double timeout_s);
+int sp_nccl_comm_abort(void* comm);
+/* Finalizes (bounded by timeout_s, abort on expiry) and frees the communicator. */
+int sp_nccl_comm_destroy(void* comm, double timeout_s);
+/* All-to-all of P equal chunks: chunk p of `send` (count elements of dtype) goes to rank p,
+ * chunk p of `recv` comes from rank p; the rank's own chunk is a device copy.  send and recv
+ * hold P * count elements and must not alias.  For Ulysses, chunk p of the send buffer holds
+ * this rank's tokens for head group p, and the receive buffer is then [P ranks' tokens] x
+ * [this rank's heads] in global token order. */
+int sp_ulysses_a2a(const void* send, void* recv, int64_t count, int dtype, void* comm,
+                   void* stream, double timeout_s);
+/* All-gather of count elements per rank (the Wan velocity's token shards). */
+int sp_nccl_all_gather(const void* send, void* recv, int64_t count, int dtype, void* comm,
+                       void* stream, double timeout_s);
 
 #ifdef __cplusplus
 }

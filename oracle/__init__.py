@@ -53,6 +53,9 @@ def lib():
             L.or_f32_to_f16.argtypes = [_f32p, _u16p, _i64]
             L.or_groupnorm_act.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64,
                                            _i64, ctypes.c_float, ctypes.c_int]
+            L.or_groupnorm_act_dtype.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64,
+                                                 _i64, _i64, ctypes.c_float, ctypes.c_int,
+                                                 ctypes.c_int]
             L.or_attention.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64,
                                        _i64, ctypes.c_int, ctypes.c_float, ctypes.c_int]
             L.or_q8_0_dequantize.argtypes = [_u8p, _i64, _f32p]
@@ -105,14 +108,23 @@ def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
     return out
 
 
-def groupnorm_act(x, gamma, beta, num_groups: int = 32, eps: float = 1e-5, silu: bool = True):
+_GN_DTYPES = {None: 0, "f32": 0, "f16": 1, "bf16": 2}
+
+
+def groupnorm_act(x, gamma, beta, num_groups: int = 32, eps: float = 1e-5, silu: bool = True,
+                  dtype=None):
+    """GroupNorm(+SiLU) of groupnorm.rs:62-102.  dtype None/"f32": the f32 path; "f16" /
+    "bf16": x, gamma and beta are that dtype's values (given as f32) and the reference's
+    cast back before the affine, and its f16/bf16 affine, clamp and SiLU, are rounded as the
+    reference rounds them."""
     x, px = _f(x)
     g, pg = _f(gamma)
     b, pb = _f(beta)
     B, C, H, W = x.shape
     y = np.empty_like(x)
-    _check(lib().or_groupnorm_act(px, pg, pb, y.ctypes.data_as(_f32p), B, C, H, W, num_groups,
-                                  eps, 1 if silu else 0), "groupnorm_act")
+    _check(lib().or_groupnorm_act_dtype(px, pg, pb, y.ctypes.data_as(_f32p), B, C, H, W,
+                                        num_groups, eps, 1 if silu else 0, _GN_DTYPES[dtype]),
+           "groupnorm_act")
     return y
 
 

@@ -166,10 +166,40 @@ void or_f32_to_f16(const float* f, uint16_t* h, int64_t n) {
   for (int64_t i = 0; i < n; ++i) h[i] = float_to_half_rne(f[i]);
 }
 
-// crates/sketchpad-core/src/groupnorm.rs:62-102 (+ silu.rs:5-7)
-int or_groupnorm_act(const float* x, const float* gamma, const float* beta, float* y, int64_t B,
-                     int64_t C, int64_t H, int64_t W, int64_t G, float eps, int act) {
+// Rounding of an f32 value to the tensor dtype and back: 0 = f32 (no-op), 1 = f16 (the
+// `half` crate's f16::from_f32, round to nearest even), 2 = bf16 (half's bf16::from_f32,
+// round to nearest even).
+inline float bf16_round(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return f;  // nan stays nan
+  u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+  float r;
+  std::memcpy(&r, &u, 4);
+  return r;
+}
+inline float round_to_dtype(float v, int dtype) {
+  if (dtype == 1) return half_to_float(float_to_half_rne(v));
+  if (dtype == 2) return bf16_round(v);
+  return v;
+}
+
+// crates/sketchpad-core/src/groupnorm.rs:62-102 (+ silu.rs:5-7).  dtype is the tensor dtype
+// of x, weight and bias (0 f32, 1 f16, 2 bf16); their values arrive here as f32 (exact).
+//  * :68 clamp x to +-65000 (in the tensor dtype; exact for f16/bf16 inputs)
+//  * :76-87 f32 mean, biased variance (mean of squared deviations), (x - mean)/sqrt(var+eps)
+//  * :88 cast the normalised value back to the tensor dtype  <- rounding for f16/bf16
+//  * :95 x * weight + bias as two tensor ops in the tensor dtype, each rounded
+//  * :99 clamp +-65000
+//  * silu.rs:5-7 x * sigmoid(x): burn's sigmoid evaluates in f32 and casts back to the
+//    tensor dtype (burn-tensor 0.20.0-pre.6 ActivationOps::sigmoid default; burn is not
+//    vendored with the reference, so this step is restated from its published code), then
+//    the product is one more tensor op in the tensor dtype.
+int or_groupnorm_act_dtype(const float* x, const float* gamma, const float* beta, float* y,
+                           int64_t B, int64_t C, int64_t H, int64_t W, int64_t G, float eps,
+                           int act, int dtype) {
   if (!x || !gamma || !beta || !y || B <= 0 || C <= 0 || H <= 0 || W <= 0 || G <= 0) return -1;
+  if (dtype < 0 || dtype > 2) return -1;
   if (C % G != 0) return -2;  // the reference asserts channels % num_groups == 0
   const int64_t cg = C / G, hw = H * W, n = cg * hw;
 #pragma omp parallel for collapse(2) schedule(dynamic, 1) num_threads(nthreads())
@@ -193,16 +223,21 @@ int or_groupnorm_act(const float* x, const float* gamma, const float* beta, floa
         const float w = gamma[g * cg + c], bb = beta[g * cg + c];
         for (int64_t i = 0; i < hw; ++i) {
           const float d = clampf(xs[c * hw + i], -65000.f, 65000.f) - mean;
-          const float xn = d / denom;  // normalised in f32; the cast back to f32 is a no-op
-          float v = xn * w + bb;        // affine after the cast
+          const float xn = round_to_dtype(d / denom, dtype);  // x_f32.cast(original_dtype)
+          float v = round_to_dtype(round_to_dtype(xn * w, dtype) + bb, dtype);
           v = clampf(v, -65000.f, 65000.f);
-          if (act == 1) v = v * sigmoidf_ref(v);
+          if (act == 1) v = round_to_dtype(v * round_to_dtype(sigmoidf_ref(v), dtype), dtype);
           ys[c * hw + i] = v;
         }
       }
     }
   }
   return 0;
+}
+
+int or_groupnorm_act(const float* x, const float* gamma, const float* beta, float* y, int64_t B,
+                     int64_t C, int64_t H, int64_t W, int64_t G, float eps, int act) {
+  return or_groupnorm_act_dtype(x, gamma, beta, y, B, C, H, W, G, eps, act, 0);
 }
 
 // crates/sketchpad-unet/src/blocks.rs:393-401 (variant 0) and

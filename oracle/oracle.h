@@ -42,6 +42,12 @@ void or_f32_to_f16(const float* f, uint16_t* h, int64_t n);
  * act: 0 = none, 1 = silu. */
 int or_groupnorm_act(const float* x, const float* gamma, const float* beta, float* y,
                      int64_t B, int64_t C, int64_t H, int64_t W, int64_t G, float eps, int act);
+/* The same for f16 (dtype 1) / bf16 (dtype 2) tensors: the normalised value is cast back
+ * to the tensor dtype before the affine, and the affine, clamp and SiLU run as tensor ops in
+ * that dtype (groupnorm.rs:88-99), each rounded.  dtype 0 is or_groupnorm_act. */
+int or_groupnorm_act_dtype(const float* x, const float* gamma, const float* beta, float* y,
+                           int64_t B, int64_t C, int64_t H, int64_t W, int64_t G, float eps,
+                           int act, int dtype);
 
 /* Attention over [BH, S, D] contiguous heads.
  * variant 0: crates/sketchpad-unet/src/blocks.rs:393-401 (scores = QK^T * d^-1/2, explicit

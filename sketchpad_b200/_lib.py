@@ -18,6 +18,7 @@ SP_ACT_NONE, SP_ACT_SILU = 0, 1
 _STATUS = {
     -1: "invalid argument", -2: "unsupported shape", -3: "unsupported dtype",
     -4: "alignment", -5: "launch failure", -6: "workspace", -7: "device is not sm_100",
+    -8: "communication failure or deadline",
 }
 
 _lib = None
@@ -39,6 +40,15 @@ SIGNATURES = {
                                  _i64, _i64p, _i64p, _i64p, _i64p, _int, _int, _int, _f, _vp]),
     "sp_groupnorm_act_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64p, _i64, _int]),
     "sp_groupnorm_act_output_strides": (_int, [_i64, _i64, _i64, _i64, _i64p, _i64p]),
+    "sp_nccl_unique_id_bytes": (_sz, []),
+    "sp_nccl_unique_id": (_int, [_vp, _sz]),
+    "sp_nccl_comm_init": (_int, [ctypes.POINTER(_vp), _int, _int, _vp, ctypes.c_double]),
+    "sp_nccl_comm_poll": (_int, [_vp, ctypes.POINTER(_int)]),
+    "sp_nccl_wait": (_int, [_vp, _vp, ctypes.c_double]),
+    "sp_nccl_comm_abort": (_int, [_vp]),
+    "sp_nccl_comm_destroy": (_int, [_vp, ctypes.c_double]),
+    "sp_ulysses_a2a": (_int, [_vp, _vp, _i64, _int, _vp, _vp, ctypes.c_double]),
+    "sp_nccl_all_gather": (_int, [_vp, _vp, _i64, _int, _vp, _vp, ctypes.c_double]),
     "sp_groupnorm_act": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p, _i64, _f,
                                 _int, _int, _vp, _sz, _vp]),
     "sp_groupnorm_add_act": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64p,

@@ -106,6 +106,9 @@ class _Attn:
                                      torch.bfloat16,
                                      self.qkv.bias[h:])
         self.H, self.D = cfg.num_heads, cfg.head_dim
+        # a dict here receives this attention's bf16 inputs (q after RoPE, joint k and v) on
+        # every forward: parity tests feed them to the oracle to check the later stages alone
+        self.record = None
 
     def forward(self, x, cos, sin, cross=None, gate=None, residual=None, out=None):
         """proj(attention(x)); with gate [h] and residual: residual + gate * proj(...), the
@@ -137,6 +140,9 @@ class _Attn:
         self.qkv(x, out=buf[:, :s], rope=RopeEpilogue(_rope_pairs(cos, sin), 2 * h, self.D))
         if c:
             self.kv(cross, out=buf[:, s:, h:])
+        if self.record is not None:
+            self.record.update(q=buf[:, :s, :h].clone(), k=buf[:, :, h:2 * h].clone(),
+                               v=buf[:, :, 2 * h:].clone())
         heads = lambda t: t.unflatten(-1, (self.H, self.D)).transpose(1, 2)  # noqa: E731
         o = torch.empty((1, s, self.H, self.D), dtype=x.dtype, device=x.device)
         flash_attention(heads(buf[:, :s, :h]), heads(buf[:, :, h:2 * h]), heads(buf[:, :, 2 * h:]),
@@ -263,11 +269,12 @@ class FluxB200:
         # the GEMM-epilogue RoPE reads f32 (cos, sin) pairs of the unrounded angles
         self.cos._sp_rope_pairs = rope_pair_table(torch.from_numpy(cos), torch.from_numpy(sin)).to(self.device)
         self.tfreq = torch.from_numpy(flux_timestep_freqs(cfg.time_dim)).to(self.device)
+        self.act_dtype = torch.bfloat16  # activations entering the GEMMs
         self.gfreq = torch.from_numpy(flux_timestep_freqs(cfg.guidance_dim)).to(self.device)
 
     def _temb(self, t: float, freqs, l1, l2):
         a = freqs * t
-        e = torch.cat([torch.sin(a), torch.cos(a)])[None].to(torch.bfloat16)
+        e = torch.cat([torch.sin(a), torch.cos(a)])[None].to(self.act_dtype)
         return l2(F.silu(l1(e)))
 
     def forward(self, latents: torch.Tensor, timestep: float, txt_embeds: torch.Tensor,
@@ -277,9 +284,9 @@ class FluxB200:
         ps = cfg.patch_size
         ph, pw = Hh // ps, Ww // ps
         # PatchEmbed (dit.rs:299-315): reshape, swap_dims(2,4), swap_dims(3,5), reshape
-        x = latents.to(torch.bfloat16).reshape(B, C, ph, ps, pw, ps).permute(0, 1, 4, 5, 2, 3)
+        x = latents.to(self.act_dtype).reshape(B, C, ph, ps, pw, ps).permute(0, 1, 4, 5, 2, 3)
         img = self.img_embed(x.reshape(B, ph * pw, C * ps * ps))
-        txt = self.txt_embed(txt_embeds.to(torch.bfloat16))
+        txt = self.txt_embed(txt_embeds.to(self.act_dtype))
         cond = self._temb(timestep, self.tfreq, self.t1, self.t2)
         if guidance is not None:
             cond = cond + self._temb(guidance, self.gfreq, self.g1, self.g2)
@@ -292,8 +299,9 @@ class FluxB200:
         m = self.final_mod(cond).view(B, 1, 2 * cfg.hidden_size)
         shift, scale = m[..., : cfg.hidden_size], m[..., cfg.hidden_size:]
         out = self.final_proj(_ln(x, scale, shift))
-        # unpatchify (dit.rs:327-345)
-        out = out.reshape(B, ph, pw, C, ps, ps).permute(0, 3, 4, 5, 1, 2)
+        # unpatchify (dit.rs:326-345): reshape [B, ph, pw, C, ps, ps], swap_dims(2, 4),
+        # swap_dims(3, 5), reshape [B, C, H, W] -- the element order of the two swaps
+        out = out.reshape(B, ph, pw, C, ps, ps).permute(0, 1, 4, 5, 2, 3)
         return out.reshape(B, C, Hh, Ww)
 
     __call__ = forward

@@ -10,6 +10,7 @@ Follows rhi-zone/sketchpad crates/sketchpad-dit/src/wan.rs:
              temporal attention over T frames per position, text cross-attention, MoE FFN
   :576-601   forward_moe: softmax router, dense sum over experts (num_experts = 1 here, so
              the router weight is exactly 1 and the FFN is one SwiGLU expert)
+  :613-627   WanFinalLayer, :661-718 patchify / unpatchify, :720-757 Wan::forward
 Config 5: hidden 5120, 40 heads x 128, FFN 13824, 40 blocks, latent 16x21x90x160 with patch
 1x2x2 -> 21 frames x 45 x 80 = 75,600 tokens, text context 512 x 4096 (projected to hidden).
 
@@ -35,7 +36,7 @@ from .flux import apply_rope, rope_tables
 from .quantized_matmul import GLU_SWIGLU, RopeEpilogue, interleave_rows, rope_pair_table
 from .layernorm import layer_norm_modulate
 from .quantization import Fp8Format, Fp8Linear, Fp8Tensor
-from .ulysses import head_to_seq, seq_to_head
+from .ulysses import all_gather_tokens, head_to_seq, rank_of, seq_to_head_qkv, world_size
 
 
 @dataclass(frozen=True)
@@ -89,8 +90,10 @@ def _rope_fusable(x):
 
 
 class WanBlockB200:
-    def __init__(self, seed: int, cfg: WanConfig, device, group: Optional[dist.ProcessGroup] = None,
+    def __init__(self, seed: int, cfg: WanConfig, device, group=None,
                  rope_dtype: torch.dtype = torch.bfloat16):
+        """group: None (one device), a torch.distributed process group or an NcclComm
+        (sequence-parallel over its ranks)."""
         h, i = cfg.hidden_size, cfg.intermediate
         L = lambda s, n, k, b=True: fp8_linear_synthetic(seed + s, n, k, device, b)  # noqa: E731
         self.s_qkv, self.s_out = L(1, 3 * h, h), L(2, h, h)
@@ -104,7 +107,7 @@ class WanBlockB200:
         self.down = L(10, h, i, False)
         self.modulation = L(11, 8 * h, h)
         self.cfg, self.group = cfg, group
-        self.P = dist.get_world_size(group) if group is not None else 1
+        self.P = world_size(group) if group is not None else 1
         sc, ss = rope_tables(cfg.head_dim, cfg.max_spatial_len)
         tc, ts = rope_tables(cfg.head_dim, cfg.max_temporal_len)
         f = lambda a: torch.from_numpy(a).to(device, rope_dtype)  # noqa: E731
@@ -123,14 +126,16 @@ class WanBlockB200:
         # token % (h*w), temporal position = token // (h*w) (frame-major tokens)
         fused = _rope_fusable(xn) and (b == 1 or P == 1)
         if fused:
-            off = dist.get_rank(self.group) * s_loc if P > 1 else 0
+            off = rank_of(self.group) * s_loc if P > 1 else 0
             rope = (RopeEpilogue(self.t_pairs, 2 * H * D, D, off, nhw, nt) if temporal
                     else RopeEpilogue(self.s_pairs, 2 * H * D, D, off, 1, nhw))
             qkv = qkv_lin(xn, rope=rope).view(b, s_loc, 3, H, D)
         else:
             qkv = qkv_lin(xn).view(b, s_loc, 3, H, D)
         if P > 1:
-            parts = [seq_to_head(qkv[:, :, j].contiguous(), self.group) for j in range(3)]
+            # one exchange for q, k and v; they stay strided views of the receive buffer
+            qkv_h = seq_to_head_qkv(qkv, self.group)
+            parts = [qkv_h[:, :, j] for j in range(3)]
             hh = H // P
         else:
             parts = [qkv[:, :, j] for j in range(3)]
@@ -187,6 +192,92 @@ class WanBlockB200:
         return self.down(self.gate_up(xn, glu=GLU_SWIGLU), out=x, residual=x)
 
 
+class WanB200:
+    """Wan::forward (wan.rs:720-757) for one sample: patchify + video_embed, text_embed,
+    the timestep embedding (forward_scalar, wan.rs:213-221), the blocks, the final layer
+    (wan.rs:613-627) and unpatchify.  Every Linear is an FP8 Linear.
+
+    With a process group of P ranks the sample is sequence-parallel (Ulysses): every rank
+    patchifies the whole latent (a few MB) and embeds only its S/P tokens; the blocks
+    exchange heads and tokens around each self-attention; the final layer runs on the local
+    tokens and one all-gather of the [S/P, C*ps*ps] outputs (S*64*2 bytes in total) gives
+    every rank the whole velocity."""
+
+    def __init__(self, cfg: WanConfig = WanConfig(), device="cuda", seed: int = 0,
+                 num_blocks: Optional[int] = None, group=None):
+        if cfg.temporal_patch_size != 1:
+            raise ValueError("temporal_patch_size must be 1 (wan.rs:668)")
+        self.cfg, self.device, self.group = cfg, torch.device(device), group
+        self.P = world_size(group) if group is not None else 1
+        h = cfg.hidden_size
+        pd = cfg.in_channels * cfg.patch_size ** 2
+        L = lambda s, n, k: fp8_linear_synthetic(seed + s, n, k, device, True)  # noqa: E731
+        self.video_embed, self.text_embed = L(1, h, pd), L(2, h, cfg.text_dim)
+        self.t1, self.t2 = L(3, h, cfg.time_embed_dim), L(4, h, h)
+        nb = cfg.num_blocks if num_blocks is None else num_blocks
+        self.blocks = [WanBlockB200(seed + 100 + 20 * i, cfg, device, group) for i in range(nb)]
+        self.final_mod, self.final_proj = L(5, 2 * h, h), L(6, pd, h)
+        self.freqs = torch.from_numpy(wan_timestep_freqs(cfg.time_embed_dim)).to(self.device)
+        self.act_dtype = torch.bfloat16  # activations entering the GEMMs
+
+    def patchify(self, latents: torch.Tensor) -> torch.Tensor:
+        """wan.rs:661-689 before the projection: [B, C, T, H, W] -> [B, T*nh*nw, C*ps*ps]."""
+        B, C, T, Hh, Ww = latents.shape
+        ps = self.cfg.patch_size
+        nh, nw = Hh // ps, Ww // ps
+        x = latents.permute(0, 2, 1, 3, 4).reshape(B * T, C, nh, ps, nw, ps)
+        return x.permute(0, 2, 4, 1, 3, 5).reshape(B, T * nh * nw, C * ps * ps)
+
+    def unpatchify(self, x: torch.Tensor, nt: int, nh: int, nw: int, C: int) -> torch.Tensor:
+        """wan.rs:691-718: [B, T*nh*nw, C*ps*ps] -> [B, C, T, H, W]."""
+        B = x.shape[0]
+        ps = self.cfg.patch_size
+        y = x.reshape(B * nt, nh, nw, C, ps, ps).permute(0, 3, 1, 4, 2, 5)
+        return y.reshape(B, nt, C, nh * ps, nw * ps).permute(0, 2, 1, 3, 4).contiguous()
+
+    def time_embedding(self, t: float) -> torch.Tensor:
+        a = self.freqs * t
+        e = torch.cat([torch.sin(a), torch.cos(a)])[None].to(self.act_dtype)
+        return self.t2(F.silu(self.t1(e)))
+
+    def forward(self, latents: torch.Tensor, timestep: float, text_embeds: torch.Tensor) -> torch.Tensor:
+        cfg, P = self.cfg, self.P
+        B, C, T, Hh, Ww = latents.shape
+        ps = cfg.patch_size
+        nh, nw = Hh // ps, Ww // ps
+        x = self.patchify(latents.to(self.act_dtype))
+        S = x.shape[1]
+        if P > 1:
+            if S % P:
+                raise ValueError(f"tokens ({S}) must divide by the sequence-parallel size ({P})")
+            r = rank_of(self.group)
+            x = x[:, r * (S // P):(r + 1) * (S // P)]
+        x = self.video_embed(x.contiguous())
+        context = self.text_embed(text_embeds.to(self.act_dtype))
+        cond = self.time_embedding(timestep)
+        for blk in self.blocks:
+            x = blk.forward(x, cond, context, T, nh, nw)
+        h = cfg.hidden_size
+        m = self.final_mod(cond).view(B, 1, 2 * h)
+        out = self.final_proj(_ln(x, m[..., h:], m[..., :h]))
+        if P > 1:
+            out = all_gather_tokens(out, self.group)
+        return self.unpatchify(out, T, nh, nw, C)
+
+    __call__ = forward
+
+
+def wan_step_flops(cfg: WanConfig = WanConfig(), nt=21, nhw=3600, ctx=512, num_blocks=None) -> float:
+    """Algorithmic FLOPs of one Wan::forward: the blocks plus the embeddings and final layer."""
+    h = cfg.hidden_size
+    nb = cfg.num_blocks if num_blocks is None else num_blocks
+    S = nt * nhw
+    pd = cfg.in_channels * cfg.patch_size ** 2
+    extra = 2.0 * (S * pd * h + ctx * cfg.text_dim * h + cfg.time_embed_dim * h + h * h
+                   + 2 * h * h + S * h * pd)
+    return nb * wan_block_flops(cfg, nt, nhw, ctx)["total"] + extra
+
+
 def wan_block_flops(cfg: WanConfig = WanConfig(), nt=21, nhw=3600, ctx=512) -> dict:
     """Algorithmic FLOPs of one WanBlock over the whole (unsharded) sequence."""
     h, i, H, D = cfg.hidden_size, cfg.intermediate, cfg.num_heads, cfg.head_dim
@@ -197,5 +288,5 @@ def wan_block_flops(cfg: WanConfig = WanConfig(), nt=21, nhw=3600, ctx=512) -> d
     return {"linear": lin, "attention": att, "total": lin + att}
 
 
-__all__ = ["WanConfig", "WanBlockB200", "wan_block_flops", "wan_timestep_freqs",
-           "fp8_linear_synthetic"]
+__all__ = ["WanConfig", "WanB200", "WanBlockB200", "wan_block_flops", "wan_step_flops",
+           "wan_timestep_freqs", "fp8_linear_synthetic"]

@@ -43,3 +43,28 @@ def wan_block_weights(blk):
 
 SMALL_WAN = WN.WanConfig(hidden_size=256, num_heads=2, intermediate=512, max_spatial_len=64,
                          max_temporal_len=8)
+
+
+def flux_model_weights(net):
+    """(model-level weights, block_weights(kind, i)) of a FluxB200 for oracle.dit.flux_forward;
+    block weights are decoded when the oracle asks for them."""
+    W = {"img_embed": q8_linear_f32(net.img_embed), "txt_embed": q8_linear_f32(net.txt_embed),
+         "time.linear1": q8_linear_f32(net.t1), "time.linear2": q8_linear_f32(net.t2),
+         "guidance.linear1": q8_linear_f32(net.g1), "guidance.linear2": q8_linear_f32(net.g2),
+         "final.modulation": q8_linear_f32(net.final_mod),
+         "final.proj": q8_linear_f32(net.final_proj)}
+
+    def block(kind, i):
+        return flux_block_weights(net.double[i], False) if kind == "double" else \
+            flux_block_weights(net.single[i], True)
+    return W, block
+
+
+def wan_model_weights(net):
+    """(model-level weights, block_weights(i)) of a WanB200 for oracle.dit.wan_forward."""
+    W = {"video_embed": fp8_linear_f32(net.video_embed),
+         "text_embed": fp8_linear_f32(net.text_embed),
+         "time.linear1": fp8_linear_f32(net.t1), "time.linear2": fp8_linear_f32(net.t2),
+         "final.modulation": fp8_linear_f32(net.final_mod),
+         "final.proj": fp8_linear_f32(net.final_proj)}
+    return W, lambda i: wan_block_weights(net.blocks[i])

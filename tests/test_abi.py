@@ -74,3 +74,38 @@ def test_q8_0_host_repack_matches_oracle_decode():
     dec = oracle.f16_bits_to_f32(s.T).repeat(32, axis=1) * q.astype(np.float32)
     ref = oracle.q8_0_dequantize(buf, out_f * in_f).reshape(out_f, in_f)
     assert np.array_equal(dec.view(np.uint32), ref.view(np.uint32))
+
+
+def test_ulysses_a2a_and_comm_argument_errors_without_a_gpu():
+    # argument checks come before NCCL or the device is touched (include/sketchpad_b200.h)
+    L = _lib.load()
+    p = ctypes.c_void_p(256)
+    assert L.sp_ulysses_a2a(p, ctypes.c_void_p(512), 16, 2, None, None, 1.0) == -1  # no comm
+    assert L.sp_ulysses_a2a(p, ctypes.c_void_p(512), 0, 2, p, None, 1.0) == -1      # count
+    assert L.sp_ulysses_a2a(p, ctypes.c_void_p(512), 16, 9, p, None, 1.0) == -3     # dtype
+    assert L.sp_ulysses_a2a(p, p, 16, 2, p, None, 1.0) == -1                         # aliasing
+    assert b"alias" in L.sp_last_error()
+    assert L.sp_ulysses_a2a(p, ctypes.c_void_p(512), 16, 2, p, None, 0.0) == -1     # deadline
+    comm = ctypes.c_void_p()
+    uid = ctypes.create_string_buffer(128)
+    assert L.sp_nccl_comm_init(ctypes.byref(comm), 2, 2, uid, 1.0) == -1           # rank >= n
+    assert L.sp_nccl_comm_init(ctypes.byref(comm), 2, 0, None, 1.0) == -1          # no id
+    assert L.sp_nccl_comm_init(ctypes.byref(comm), 2, 0, uid, -1.0) == -1          # deadline
+    assert L.sp_nccl_wait(None, None, 1.0) == -1
+    assert L.sp_nccl_comm_abort(None) == -1
+    assert L.sp_nccl_comm_destroy(None, 1.0) == -1
+
+
+def test_nccl_unique_id_on_the_host():
+    # the id is made on the host (NCCL bootstrap, no device): 128 bytes, fresh each call
+    L = _lib.load()
+    n = L.sp_nccl_unique_id_bytes()
+    assert n == 128
+    assert L.sp_nccl_unique_id(ctypes.create_string_buffer(8), 8) == -1
+    a, b = ctypes.create_string_buffer(n), ctypes.create_string_buffer(n)
+    rc = L.sp_nccl_unique_id(a, n)
+    if rc == -8:  # no NCCL on this machine: the status says so
+        assert b"NCCL" in L.sp_last_error()
+        return
+    assert rc == 0 and L.sp_nccl_unique_id(b, n) == 0
+    assert a.raw != bytes(n) and a.raw != b.raw

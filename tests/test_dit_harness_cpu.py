@@ -13,7 +13,8 @@ import sketchpad_b200.flux as FX
 import sketchpad_b200.quantization as QZ
 import sketchpad_b200.quantized_matmul as QM
 import sketchpad_b200.wan as WN
-from dit_weights import SMALL_FLUX, SMALL_WAN, flux_block_weights, wan_block_weights
+from dit_weights import (SMALL_FLUX, SMALL_WAN, flux_block_weights, flux_model_weights,
+                         wan_block_weights, wan_model_weights)
 from helpers import rel_err, to_np
 from oracle import dit as OD
 
@@ -218,4 +219,109 @@ def test_wan_block_ulysses_two_ranks_matches_oracle(tmp_path):
     sk.close()
     mp.spawn(_wan_ulysses_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
     errs = [float(np.load(tmp_path / f"err{r}.npy")[0]) for r in range(2)]
+    assert max(errs) < TOL_WIRING
+
+
+def test_flux_model_wiring_matches_oracle(monkeypatch):
+    # Flux::forward (flux.rs:686-741): patch embed, text projection, scalar timestep
+    # embedding, 1 double + 1 single block, final layer and unpatchify -- the element orders
+    # of dit.rs:300-345 followed literally on both sides
+    _patch(monkeypatch)
+    cfg = SMALL_FLUX
+    net = FX.FluxB200(cfg, "cpu", seed=3, num_double=1, num_single=1)
+    net.act_dtype = torch.float32
+    net.cos, net.sin = (torch.from_numpy(t) for t in OD.rope_tables(cfg.head_dim, cfg.max_seq_len))
+    g = torch.Generator().manual_seed(4)
+    lat = torch.randn(1, 16, 16, 12, generator=g)
+    txt = torch.randn(1, 24, cfg.text_dim, generator=g)
+    with torch.no_grad():
+        y = net.forward(lat, 0.75, txt)
+    W, blocks = flux_model_weights(net)
+    W = {k: v for k, v in W.items() if not k.startswith("guidance.")}
+    cos, sin = OD.rope_tables(cfg.head_dim, cfg.max_seq_len)
+    ref = OD.flux_forward(lat.numpy(), 0.75, txt.numpy(), W, blocks, 1, 1, cfg.num_heads,
+                          cfg.head_dim, cfg.patch_size, cos, sin)
+    assert y.shape == ref.shape
+    assert rel_err(to_np(y), ref) < TOL_WIRING
+
+
+def test_wan_model_wiring_matches_oracle(monkeypatch):
+    # Wan::forward (wan.rs:720-757): patchify, text / time embeddings, 2 blocks, final layer,
+    # unpatchify
+    _patch(monkeypatch)
+    monkeypatch.setattr(WN, "_rope_fusable", lambda x: True)
+    cfg = SMALL_WAN
+    net = WN.WanB200(cfg, "cpu", seed=5, num_blocks=2)
+    net.act_dtype = torch.float32
+    for blk in net.blocks:
+        blk.s_cos, blk.s_sin, blk.t_cos, blk.t_sin = (
+            t.float() for t in (blk.s_cos, blk.s_sin, blk.t_cos, blk.t_sin))
+    g = torch.Generator().manual_seed(6)
+    lat = torch.randn(1, 16, 3, 8, 12, generator=g)
+    txt = torch.randn(1, 20, cfg.text_dim, generator=g)
+    with torch.no_grad():
+        y = net.forward(lat, 0.5, txt)
+    W, blocks = wan_model_weights(net)
+    ref = OD.wan_forward(lat.numpy(), 0.5, txt.numpy(), W, blocks, 2, cfg.num_heads,
+                         cfg.head_dim, cfg.patch_size, OD.rope_tables(128, cfg.max_spatial_len),
+                         OD.rope_tables(128, cfg.max_temporal_len))
+    assert y.shape == ref.shape == (1, 16, 3, 8, 12)
+    assert rel_err(to_np(y), ref) < TOL_WIRING
+
+
+def test_oracle_patchify_orders():
+    # dit.rs:300-345 / wan.rs:661-718: unpatchify inverts the patch embedding's element order
+    # (no projection), and the literal swap orders are not the "[B, ph, pw, C, ps, ps]" the
+    # reference's comments describe
+    x = np.arange(2 * 4 * 6 * 8, dtype=np.float32).reshape(2, 4, 6, 8)
+    p = OD.flux_patch_embed(x, 2)
+    assert p.shape == (2, 12, 16)
+    v = np.arange(1 * 4 * 3 * 6 * 8, dtype=np.float32).reshape(1, 4, 3, 6, 8)
+    pv = OD.wan_patchify(v, 2)
+    assert np.array_equal(OD.wan_unpatchify(pv, 3, 3, 4, 4, 2), v)
+    # wan's patch k of frame t holds pixels (2*i + a, 2*j + b) of every channel
+    assert np.array_equal(pv[0, 0, :4], [v[0, 0, 0, 0, 0], v[0, 0, 0, 0, 1], v[0, 0, 0, 1, 0],
+                                         v[0, 0, 0, 1, 1]])
+
+
+def _wan_model_ulysses_worker(rank, ws, port, result_dir):
+    import os
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    try:
+        _patch(_Setter())
+        WN._rope_fusable = lambda x: True
+        cfg = SMALL_WAN
+        net = WN.WanB200(cfg, "cpu", seed=7, num_blocks=1, group=dist.group.WORLD)
+        net.act_dtype = torch.float32
+        for blk in net.blocks:
+            blk.s_cos, blk.s_sin, blk.t_cos, blk.t_sin = (
+                t.float() for t in (blk.s_cos, blk.s_sin, blk.t_cos, blk.t_sin))
+        g = torch.Generator().manual_seed(8)
+        lat = torch.randn(1, 16, 3, 8, 12, generator=g)
+        txt = torch.randn(1, 20, cfg.text_dim, generator=g)
+        with torch.no_grad():
+            y = net.forward(lat, 0.25, txt)
+        W, blocks = wan_model_weights(net)
+        ref = OD.wan_forward(lat.numpy(), 0.25, txt.numpy(), W, blocks, 1, cfg.num_heads,
+                             cfg.head_dim, cfg.patch_size, OD.rope_tables(128, cfg.max_spatial_len),
+                             OD.rope_tables(128, cfg.max_temporal_len))
+        np.save(f"{result_dir}/merr{rank}.npy", np.array([rel_err(to_np(y), ref)]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_wan_model_ulysses_two_ranks_matches_oracle(tmp_path):
+    # the whole Wan::forward sequence-parallel over 2 gloo ranks: each rank embeds its 36 of
+    # 72 tokens; the all-gathered velocity matches the single-device oracle on every rank
+    import socket
+    import torch.multiprocessing as mp
+    sk = socket.socket()
+    sk.bind(("127.0.0.1", 0))
+    port = sk.getsockname()[1]
+    sk.close()
+    mp.spawn(_wan_model_ulysses_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    errs = [float(np.load(tmp_path / f"merr{r}.npy")[0]) for r in range(2)]
     assert max(errs) < TOL_WIRING

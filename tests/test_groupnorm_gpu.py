@@ -2,6 +2,9 @@
 
 Metric: rel_err = max|gpu - oracle| / max|oracle|; bars: 1e-3 (fp32), 2e-2 (fp16/bf16).
 Inputs follow BASELINE config 2: x ~ N(0,1)*3+0.5, gamma ~ N(1,0.1), beta ~ N(0,0.1), seed 0.
+For f16/bf16 tensors the oracle runs the reference's dtype path (groupnorm.rs:88-99): the
+normalised value cast back to the tensor dtype, then the affine, clamp and SiLU as f16/bf16
+tensor ops, each rounded.  The kernel keeps f32 through the affine and SiLU and rounds once.
 """
 import numpy as np
 import pytest
@@ -12,6 +15,11 @@ from sketchpad_b200 import GroupNormSiLuLayer, GroupNormSiLuOptions, groupnorm, 
 from helpers import TOL_F32, TOL_HALF, rel_err, to_np
 
 pytestmark = pytest.mark.gpu
+
+
+def dt(dtype):
+    """The oracle's dtype argument for a torch dtype (None = the f32 path)."""
+    return {torch.float32: None, torch.float16: "f16", torch.bfloat16: "bf16"}[dtype]
 
 SHAPES = [(2, 320, 64, 64), (2, 640, 32, 32), (2, 1280, 16, 16), (2, 512, 128, 128),
           (8, 320, 64, 64), (8, 640, 32, 32), (8, 1280, 16, 16), (8, 512, 128, 128)]
@@ -33,7 +41,8 @@ def test_groupnorm_silu_baseline_sweep(shape, dtype):
     xt = torch.from_numpy(x).cuda().to(dtype)
     # the oracle sees exactly the values the GPU sees
     ref = oracle.groupnorm_act(to_np(xt), to_np(torch.from_numpy(g).to(dtype)),
-                               to_np(torch.from_numpy(b).to(dtype)), 32, 1e-5, silu=True)
+                               to_np(torch.from_numpy(b).to(dtype)), 32, 1e-5, silu=True,
+                               dtype=dt(dtype))
     y = groupnorm_silu(xt, torch.from_numpy(g).cuda().to(dtype), torch.from_numpy(b).cuda().to(dtype))
     torch.cuda.synchronize()
     tol = TOL_F32 if dtype == torch.float32 else TOL_HALF
@@ -44,9 +53,10 @@ def test_groupnorm_silu_baseline_sweep(shape, dtype):
 def test_groupnorm_without_silu(dtype):
     x, g, b = make((2, 320, 64, 64), seed=1)
     xt = torch.from_numpy(x).cuda().to(dtype)
-    ref = oracle.groupnorm_act(to_np(xt), to_np(torch.from_numpy(g).to(dtype)),
-                               to_np(torch.from_numpy(b).to(dtype)), 32, 1e-5, silu=False)
-    y = groupnorm(xt, torch.from_numpy(g).cuda(), torch.from_numpy(b).cuda())
+    gg, bb = torch.from_numpy(g).to(dtype), torch.from_numpy(b).to(dtype)
+    ref = oracle.groupnorm_act(to_np(xt), to_np(gg), to_np(bb), 32, 1e-5, silu=False,
+                               dtype=dt(dtype))
+    y = groupnorm(xt, gg.cuda(), bb.cuda())
     tol = TOL_F32 if dtype == torch.float32 else TOL_HALF
     assert rel_err(to_np(y), ref) < tol
 
@@ -106,7 +116,8 @@ def test_groupnorm_channels_last(shape, dtype):
     x, g, b = make(shape, seed=7)
     xt = torch.from_numpy(x).cuda().to(dtype).to(memory_format=torch.channels_last)
     ref = oracle.groupnorm_act(to_np(xt), to_np(torch.from_numpy(g).to(dtype)),
-                               to_np(torch.from_numpy(b).to(dtype)), 32, 1e-5, silu=True)
+                               to_np(torch.from_numpy(b).to(dtype)), 32, 1e-5, silu=True,
+                               dtype=dt(dtype))
     y = groupnorm_silu(xt, torch.from_numpy(g).cuda().to(dtype), torch.from_numpy(b).cuda().to(dtype))
     assert y.is_contiguous(memory_format=torch.channels_last)
     tol = TOL_F32 if dtype == torch.float32 else TOL_HALF
@@ -119,15 +130,17 @@ def test_groupnorm_channels_last(shape, dtype):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_groupnorm_add_channels_last(shape, dtype):
     # ResBlock's norm2(h + temb[:, :, None, None]) in one pass: the oracle normalises the
-    # explicit sum (formed in f32 from the same rounded inputs)
+    # explicit sum, rounded to the tensor dtype as the reference's separate add is (the
+    # kernel keeps the sum in f32)
     x, g, b = make(shape, seed=11)
     B, C = shape[:2]
     t = np.random.default_rng(12).standard_normal((B, C)).astype(np.float32)
     xt = torch.from_numpy(x).cuda().to(dtype).to(memory_format=torch.channels_last)
     tt = torch.from_numpy(t).cuda().to(dtype)
-    xs = to_np(xt) + to_np(tt)[:, :, None, None]
+    xs = to_np(torch.from_numpy(to_np(xt) + to_np(tt)[:, :, None, None]).to(dtype))
     ref = oracle.groupnorm_act(xs, to_np(torch.from_numpy(g).to(dtype)),
-                               to_np(torch.from_numpy(b).to(dtype)), 32, 1e-5, silu=True)
+                               to_np(torch.from_numpy(b).to(dtype)), 32, 1e-5, silu=True,
+                               dtype=dt(dtype))
     y = groupnorm_silu(xt, torch.from_numpy(g).cuda().to(dtype), torch.from_numpy(b).cuda().to(dtype),
                        add=tt)
     assert y.is_contiguous(memory_format=torch.channels_last)
@@ -145,15 +158,17 @@ def test_groupnorm_channels_last_fallback_paths(shape, groups, dtype):
     x, g, b = make(shape, seed=13)
     xt = torch.from_numpy(x).cuda().to(dtype).to(memory_format=torch.channels_last)
     gt, bt = torch.from_numpy(g).to(dtype), torch.from_numpy(b).to(dtype)
-    ref = oracle.groupnorm_act(to_np(xt), to_np(gt), to_np(bt), groups, 1e-5, silu=True)
+    ref = oracle.groupnorm_act(to_np(xt), to_np(gt), to_np(bt), groups, 1e-5, silu=True,
+                               dtype=dt(dtype))
     t = torch.from_numpy(np.random.default_rng(14).standard_normal(shape[:2]).astype(np.float32))
     y = groupnorm_silu(xt, gt.cuda(), bt.cuda(), GroupNormSiLuOptions(groups, 1e-5))
     tol = TOL_F32 if dtype == torch.float32 else TOL_HALF
     assert rel_err(to_np(y), ref) < tol
     # and the folded time-embedding add on the same paths
     tt = t.to(dtype)
-    ref2 = oracle.groupnorm_act(to_np(xt) + to_np(tt)[:, :, None, None], to_np(gt), to_np(bt),
-                                groups, 1e-5, silu=True)
+    xs = to_np(torch.from_numpy(to_np(xt) + to_np(tt)[:, :, None, None]).to(dtype))
+    ref2 = oracle.groupnorm_act(xs, to_np(gt), to_np(bt), groups, 1e-5, silu=True,
+                                dtype=dt(dtype))
     y2 = groupnorm_silu(xt, gt.cuda(), bt.cuda(), GroupNormSiLuOptions(groups, 1e-5), add=tt.cuda())
     assert rel_err(to_np(y2), ref2) < tol
 

@@ -124,3 +124,35 @@ def test_f16_decode_all_bit_patterns():
     ok = ~np.isnan(ref)
     assert np.array_equal(f.view(np.uint32)[ok], ref.view(np.uint32)[ok])
     assert np.all(np.isnan(f[~ok]))
+
+
+@pytest.mark.parametrize("silu", [False, True])
+def test_groupnorm_f16_dtype_path(silu):
+    # groupnorm.rs:76-99 on an f16 tensor, restated with numpy float16 arithmetic (each f16
+    # op computes in f32 and rounds to nearest even, as the half crate does): f32 stats,
+    # normalise in f32, cast to f16, x * weight and + bias as f16 ops, clamp, then
+    # silu(x) = x * sigmoid(x) with sigmoid evaluated in f32 and cast to f16
+    rng = np.random.default_rng(21)
+    x16 = (rng.standard_normal((2, 8, 3, 5)) * 3 + 0.5).astype(np.float16)
+    g16 = (rng.standard_normal(8) * 0.1 + 1).astype(np.float16)
+    b16 = (rng.standard_normal(8) * 0.1).astype(np.float16)
+    xg = x16.astype(np.float64).reshape(2, 4, -1)
+    mean = xg.mean(axis=2, keepdims=True).astype(np.float32)
+    var = ((xg - mean) ** 2).mean(axis=2, keepdims=True).astype(np.float32)
+    xn = ((xg.astype(np.float32) - mean) / np.sqrt(var + np.float32(1e-5))).astype(np.float16)
+    xn = xn.reshape(2, 8, 3, 5)
+    v = xn * g16[None, :, None, None] + b16[None, :, None, None]  # f16 ops, each rounded
+    v = np.clip(v, -65000, 65000).astype(np.float16)
+    if silu:
+        sig = (1.0 / (1.0 + np.exp(-v.astype(np.float32)))).astype(np.float16)
+        v = v * sig
+    y = oracle.groupnorm_act(x16.astype(np.float32), g16.astype(np.float32),
+                             b16.astype(np.float32), 4, 1e-5, silu=silu, dtype="f16")
+    # every oracle value is an f16 value; allow one f16 ulp for f32 exp/sqrt rounding
+    assert np.array_equal(y.astype(np.float16).astype(np.float32), y)
+    ulp = np.spacing(np.abs(v).astype(np.float16)).astype(np.float32)
+    assert np.all(np.abs(y - v.astype(np.float32)) <= ulp)
+    # and it differs from the f32 path (the dtype round trips are real)
+    y32 = oracle.groupnorm_act(x16.astype(np.float32), g16.astype(np.float32),
+                               b16.astype(np.float32), 4, 1e-5, silu=silu)
+    assert not np.array_equal(y, y32)
