@@ -258,7 +258,9 @@ int sp_fp8_linear_glu(const void* x, const void* w_e4m3, const float* scale, int
  * (crates/sketchpad-dit/src/wan.rs:371-390).  (c, s) = rope_cos_sin[pos * head_dim/2 + pair]
  * as f32 pairs, pos = ((m + pos_offset) / pos_div) % pos_mod, pos_mod <= rope_positions
  * (the table's rows).  rope_cos_sin may be NULL (no rotation: a plain strided-output GEMM,
- * used to write the cross stream's k/v next to the self stream's in one buffer). */
+ * used to write the cross stream's k/v next to the self stream's in one buffer).  x and
+ * bias are bf16; dtype is y's type, SP_BF16 or SP_F16 (f16 attention inputs: 3 more
+ * mantissa bits for q and k, for activations inside f16's range). */
 int sp_q8_0_linear_rope(const void* x, const void* q, const void* scale, const void* bias, void* y,
                         int64_t ldy, int64_t M, int64_t N, int64_t K, const float* rope_cos_sin,
                         int64_t rope_positions, int64_t rope_cols, int64_t head_dim,

@@ -88,6 +88,9 @@ struct QlParams {
   // so columns 2j, 2j+1 of x.W^T + b are (lo, hi) and y[m, j] = lo * gelu(hi) (SP_GLU_GEGLU)
   // or silu(lo) * hi (SP_GLU_SWIGLU); y holds N/2 columns, ldy apart
   int glu;
+  // y's element type for the plain / rope epilogue: 0 bf16, 1 f16 (the attention inputs of
+  // long-sequence DiTs, where f16's 3 extra mantissa bits shrink the logit error 8x)
+  int y_f16;
 };
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -217,8 +220,10 @@ __device__ __forceinline__ void ql_finish8(const QlParams& p, float (&v)[8], int
     if (p.residual) v[e] += __bfloat162float(re[e]);
   }
   *reinterpret_cast<uint4*>(p.y + m * p.ldy + n) =
-      make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                 pack_bf16x2(v[6], v[7]));
+      p.y_f16 ? make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]),
+                           pack_f16x2(v[4], v[5]), pack_f16x2(v[6], v[7]))
+              : make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                           pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
 }
 
 // Split-K reduce: out[m, n..n+7] = epilogue(sum over z of ws[z][m][n..n+7]), z in order, one
@@ -613,6 +618,7 @@ struct QlEpilogue {
   const float* rope = nullptr;
   int64_t rope_positions = 0, rope_cols = 0, head_dim = 0, pos_off = 0, pos_div = 1, pos_mod = 1;
   int glu = -1;
+  bool out_dtype_free = false;  // the rope / strided-output entries: y may be bf16 or f16
 };
 
 template <int WF>
@@ -631,7 +637,8 @@ int ql_entry(const char* what, const void* x, const void* w, const void* q8_scal
                      what, (long long)K);
   if (WF == W_FP8 && nscale != 1 && nscale != N)
     return set_error(SP_ERR_SHAPE, "%s: scale count %lld must be 1 or N", what, (long long)nscale);
-  if (int rc = check_ql_shape(M, N, K, dtype)) return rc;
+  const bool y_f16 = e.out_dtype_free && dtype == SP_F16;
+  if (int rc = check_ql_shape(M, N, K, y_f16 ? SP_BF16 : dtype)) return rc;
   if (e.glu >= 0 && (e.glu > SP_GLU_SWIGLU || e.gate || e.residual || e.rope))
     return set_error(SP_ERR_INVALID_ARG, "%s: the GLU epilogue takes no gate, residual or rope",
                      what);
@@ -658,7 +665,8 @@ int ql_entry(const char* what, const void* x, const void* w, const void* q8_scal
              static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
              static_cast<const __nv_bfloat16*>(e.gate), static_cast<const __nv_bfloat16*>(e.residual),
              ldy, reinterpret_cast<const float2*>(e.rope), e.pos_off, e.pos_div, e.pos_mod,
-             (int)e.rope_cols, (int)(e.head_dim / 2), nullptr, 1, (int)(K / kQBK), e.glu};
+             (int)e.rope_cols, (int)(e.head_dim / 2), nullptr, 1, (int)(K / kQBK), e.glu,
+             y_f16 ? 1 : 0};
   return launch_qlinear<WF>(x, w, p, static_cast<cudaStream_t>(stream));
 }
 
@@ -680,6 +688,7 @@ QlEpilogue roped(int64_t ldy, const float* rope, int64_t positions, int64_t cols
   e.pos_off = off;
   e.pos_div = div;
   e.pos_mod = mod;
+  e.out_dtype_free = true;
   return e;
 }
 }  // namespace

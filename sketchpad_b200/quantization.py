@@ -117,7 +117,7 @@ class Fp8Linear:
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
                 gate: Optional[torch.Tensor] = None,
                 residual: Optional[torch.Tensor] = None, rope=None,
-                glu: Optional[int] = None) -> torch.Tensor:
+                glu: Optional[int] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
         """x @ dequant(W)^T + b; with gate / residual: residual + gate * (x @ W^T + b); with
         `rope` (a RopeEpilogue) the rotary embedding of its columns, and `out` may be a
         column slice of a wider buffer."""
@@ -143,15 +143,16 @@ class Fp8Linear:
                       self.weight.scale.numel(), ptr(b), ptr(y), M, N, K, int(glu), _lib.SP_BF16,
                       stream_ptr(dev))
             return y.reshape(*lead, N // 2)
-        if rope is not None or (out is not None and not out.is_contiguous()):
+        f16_out = out_dtype == torch.float16 or (out is not None and out.dtype == torch.float16)
+        if rope is not None or f16_out or (out is not None and not out.is_contiguous()):
             from .quantized_matmul import _NO_ROPE, _output_rows
             if gate is not None or residual is not None:
                 raise ValueError("the rope / strided-output epilogue takes no gate or residual")
-            y, ldy = _output_rows(out, M, N, dev)
+            y, ldy = _output_rows(out, M, N, dev, torch.float16 if f16_out else torch.bfloat16)
             r = rope.args() if rope is not None else _NO_ROPE
             _lib.call("sp_fp8_linear_rope", ptr(xx), ptr(self.weight.data),
                       ptr(self.weight.scale), self.weight.scale.numel(), ptr(b), ptr(y), ldy, M,
-                      N, K, *r, _lib.SP_BF16, stream_ptr(dev))
+                      N, K, *r, _lib.SP_F16 if f16_out else _lib.SP_BF16, stream_ptr(dev))
             return y if out is not None else y.reshape(*lead, N)
         y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=dev)
         if gate is None and residual is None:

@@ -126,13 +126,16 @@ def rope_pair_table(cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     return torch.stack((cos[:, ::2].float(), sin[:, ::2].float()), dim=-1).contiguous()
 
 
-def _output_rows(out, M, N, dev):
+def _output_rows(out, M, N, dev, dtype=torch.bfloat16):
     """The GEMM output as rows of N values `ldy` apart (a column slice of a wider buffer is
-    fine: the DiT attention writes its cross-stream k/v next to the self stream's)."""
+    fine: the DiT attention writes its cross-stream k/v next to the self stream's).  dtype:
+    bf16, or f16 for attention inputs that need its finer rounding."""
+    if dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("the strided-output epilogue writes bf16 or f16")
     if out is None:
-        return torch.empty((M, N), dtype=torch.bfloat16, device=dev), N
-    if out.dtype != torch.bfloat16:
-        raise ValueError("out must be bf16")
+        return torch.empty((M, N), dtype=dtype, device=dev), N
+    if out.dtype != dtype:
+        raise ValueError(f"out must be {dtype}")
     try:
         o2 = out.view(M, N)
     except RuntimeError as e:
@@ -210,7 +213,8 @@ class GpuQuantizedLinear:
     def forward(self, input: torch.Tensor, out: Optional[torch.Tensor] = None,
                 gate: Optional[torch.Tensor] = None,
                 residual: Optional[torch.Tensor] = None,
-                rope: Optional[RopeEpilogue] = None, glu: Optional[int] = None) -> torch.Tensor:
+                rope: Optional[RopeEpilogue] = None, glu: Optional[int] = None,
+                out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
         """[..., in_features] -> [..., out_features] via the fused dequant-GEMM (bf16).
 
         With gate ([out_features]) and/or residual ([..., out_features], bf16, may be `out`),
@@ -252,14 +256,16 @@ class GpuQuantizedLinear:
                       self.in_features, _lib.SP_BF16, stream_ptr(dev))
             y = y.reshape(*lead, self.out_features)
             return y if input.dtype == torch.bfloat16 else y.to(input.dtype)
-        if rope is not None or (out is not None and not out.is_contiguous()):
+        f16_out = out_dtype == torch.float16 or (out is not None and out.dtype == torch.float16)
+        if rope is not None or f16_out or (out is not None and not out.is_contiguous()):
             if gate is not None or residual is not None:
                 raise ValueError("the rope / strided-output epilogue takes no gate or residual")
-            y, ldy = _output_rows(out, M, self.out_features, dev)
+            ydt = torch.float16 if f16_out else torch.bfloat16
+            y, ldy = _output_rows(out, M, self.out_features, dev, ydt)
             r = rope.args() if rope is not None else _NO_ROPE
             _lib.call("sp_q8_0_linear_rope", ptr(x), ptr(self.q), ptr(self.scale), ptr(b), ptr(y),
-                      ldy, M, self.out_features, self.in_features, *r, _lib.SP_BF16,
-                      stream_ptr(dev))
+                      ldy, M, self.out_features, self.in_features, *r,
+                      _lib.SP_F16 if f16_out else _lib.SP_BF16, stream_ptr(dev))
             return y if out is not None else y.reshape(*lead, self.out_features)
         y = out if out is not None else torch.empty((M, self.out_features), dtype=torch.bfloat16,
                                                     device=dev)

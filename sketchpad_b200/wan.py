@@ -52,6 +52,11 @@ class WanConfig:
     time_embed_dim: int = 256
     max_spatial_len: int = 3600
     max_temporal_len: int = 21
+    # dtype of the attention inputs q, k, v written by the projection epilogues: f16 keeps
+    # 3 more mantissa bits than bf16, so at full width (logits of order 10) the softmax
+    # weights move ~8x less than with bf16 q and k; the DiT's q / k / v stay far inside f16's
+    # range.  The residual stream and every other activation stay bf16.
+    attn_dtype: torch.dtype = torch.float16
 
     @property
     def head_dim(self):
@@ -129,7 +134,7 @@ class WanBlockB200:
             off = rank_of(self.group) * s_loc if P > 1 else 0
             rope = (RopeEpilogue(self.t_pairs, 2 * H * D, D, off, nhw, nt) if temporal
                     else RopeEpilogue(self.s_pairs, 2 * H * D, D, off, 1, nhw))
-            qkv = qkv_lin(xn, rope=rope).view(b, s_loc, 3, H, D)
+            qkv = qkv_lin(xn, rope=rope, out_dtype=cfg.attn_dtype).view(b, s_loc, 3, H, D)
         else:
             qkv = qkv_lin(xn).view(b, s_loc, 3, H, D)
         if P > 1:
@@ -180,8 +185,9 @@ class WanBlockB200:
         xn = _ln(x, m[:, 5], m[:, 4])
         H, D = cfg.num_heads, cfg.head_dim
         s_loc = x.shape[1]
-        q = self.c_q(xn).view(b, s_loc, H, D).transpose(1, 2)
-        kv = self.c_kv(context).view(b, context.shape[1], 2, H, D)
+        adt = cfg.attn_dtype if _rope_fusable(xn) else None
+        q = self.c_q(xn, out_dtype=adt).view(b, s_loc, H, D).transpose(1, 2)
+        kv = self.c_kv(context, out_dtype=adt).view(b, context.shape[1], 2, H, D)
         o = torch.empty((b, s_loc, H, D), dtype=x.dtype, device=x.device)
         flash_attention(q, kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2),
                         out=o.transpose(1, 2))

@@ -54,7 +54,8 @@ def _glu(y, glu):
     return F.silu(lo) * hi if glu == 1 else lo * F.gelu(hi)
 
 
-def _q8_forward(self, x, out=None, gate=None, residual=None, rope=None, glu=None):
+def _q8_forward(self, x, out=None, gate=None, residual=None, rope=None, glu=None,
+                out_dtype=None):
     q = self.q.float()
     s = self.scale.view(torch.float16).float().t().repeat_interleave(32, dim=1)  # [N, K]
     y = x.float() @ (q * s).t()
@@ -74,7 +75,9 @@ def _fp8_quantize(t, cfg):
     return QZ.Fp8Tensor(data, torch.full((1,), float(cfg.scale)), QZ.Fp8Format.E4M3, tuple(t.shape))
 
 
-def _fp8_forward(self, x, out=None, gate=None, residual=None, rope=None, glu=None):
+def _fp8_forward(self, x, out=None, gate=None, residual=None, rope=None, glu=None,
+                 out_dtype=None):
+    # out_dtype (f16 attention inputs on the GPU) is ignored: the wiring runs in f32
     w = self.weight.data.view(torch.float8_e4m3fn).float() * self.weight.scale.view(-1, 1)
     y = x.float() @ w.t()
     y = y + self.bias.float() if self.bias is not None else y

@@ -280,12 +280,18 @@ def test_fp8_linear_rope_epilogue():
     rope = RopeEpilogue(rope_pair_table(torch.from_numpy(cos), torch.from_numpy(sin)).cuda(),
                         2 * 640, D, 0, 1, 100)
     y = lin.forward(x.cuda(), rope=rope)
+    # the same product written as f16 (the attention-input dtype of the Wan harness)
+    y16 = lin.forward(x.cuda(), rope=rope, out_dtype=torch.float16)
     torch.cuda.synchronize()
+    assert y16.dtype == torch.float16
     wdq = to_np(lin.weight.dequantize())
     rows = slice(0, 256)
     ref = _rope_ref(oracle.linear_nt(to_np(x[rows]), wdq, to_np(bias)), cos, sin, 2 * 640, D,
                     0, 1, 100)
     assert rel_err(to_np(y[rows]), ref) < TOL_HALF
+    # f16's rounding is 8x finer than bf16's: the error shrinks accordingly
+    e16 = rel_err(to_np(y16[rows]), ref)
+    assert e16 < 2e-3 and e16 < rel_err(to_np(y[rows]), ref)
 
 
 def test_rope_epilogue_rejects_bad_geometry():
