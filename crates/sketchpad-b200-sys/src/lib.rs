@@ -48,6 +48,25 @@ pub const SP_FP8_PER_TENSOR: c_int = 0;
 pub const SP_FP8_PER_CHANNEL: c_int = 1;
 pub const SP_FP8_GIVEN_SCALE: c_int = 2;
 
+// sp_container
+pub const SP_CONTAINER_GGUF: c_int = 1;
+pub const SP_CONTAINER_SAFETENSORS: c_int = 2;
+
+// sp_tensor_type (GGUF block types: SP_T_GGML_BASE + ggml type id)
+pub const SP_T_F32: c_int = 0;
+pub const SP_T_F16: c_int = 1;
+pub const SP_T_BF16: c_int = 2;
+pub const SP_T_F8_E4M3: c_int = 3;
+pub const SP_T_F8_E5M2: c_int = 4;
+pub const SP_T_F64: c_int = 5;
+pub const SP_T_I8: c_int = 6;
+pub const SP_T_U8: c_int = 7;
+pub const SP_T_I16: c_int = 8;
+pub const SP_T_I32: c_int = 9;
+pub const SP_T_I64: c_int = 10;
+pub const SP_T_BOOL: c_int = 11;
+pub const SP_T_GGML_BASE: c_int = 100;
+
 extern "C" {
     // -- library, errors, device watchdog
     pub fn sp_abi_version() -> c_int;
@@ -87,7 +106,7 @@ extern "C" {
         c: i64, h: i64, w: i64, x_strides: *const i64, groups: i64, eps: c_float, act: c_int,
         dtype: c_int, stream: *mut c_void
     ) -> c_int;
-    // -- fusions around the path (GLU gates, residual adds, LayerNorms)
+    // -- fusions around the path (GLU gates, residual adds)
     pub fn sp_glu_gate(
         x: *const c_void, y: *mut c_void, rows: i64, f: i64, x_row_stride: i64,
         y_row_stride: i64, kind: c_int, dtype: c_int, stream: *mut c_void
@@ -133,7 +152,7 @@ extern "C" {
         dtype: c_int, stream: *mut c_void
     ) -> c_int;
     // -- FP8 e4m3 weights: quantize_fp8 / Fp8Tensor::dequantize / Fp8Linear::forward
-    //    (crates/sketchpad-core/src/quantization.rs:495, :435, :601)
+    //    (crates/sketchpad-core/src/quantization.rs:495, :435, :601), GLU and RoPE epilogues
     pub fn sp_fp8_quantize(
         w: *const c_float, n: i64, k: i64, scale_mode: c_int, w_e4m3: *mut c_void,
         scale: *mut c_float, stream: *mut c_void
@@ -221,6 +240,25 @@ extern "C" {
     pub fn sp_nccl_all_gather(
         send: *const c_void, recv: *mut c_void, count: i64, dtype: c_int, comm: *mut c_void,
         stream: *mut c_void, timeout_s: c_double
+    ) -> c_int;
+    // -- weight files: GGUF v3 (crates/sketchpad-convert/src/gguf.rs:351-470) and
+    //    safetensors (crates/sketchpad-convert/src/loader.rs:60-90), host only
+    pub fn sp_model_open(path: *const c_char, file_out: *mut *mut c_void) -> c_int;
+    pub fn sp_model_close(file: *mut c_void) -> c_int;
+    pub fn sp_model_info(
+        file: *mut c_void, container_out: *mut c_int, tensor_count_out: *mut i64,
+        meta_count_out: *mut i64
+    ) -> c_int;
+    pub fn sp_model_meta_key(
+        file: *mut c_void, index: i64, name_out: *mut c_char, name_cap: usize
+    ) -> c_int;
+    pub fn sp_model_tensor_info(
+        file: *mut c_void, index: i64, name_out: *mut c_char, name_cap: usize,
+        type_out: *mut c_int, ndims_out: *mut c_int, dims_out: *mut i64, nbytes_out: *mut u64
+    ) -> c_int;
+    pub fn sp_model_find(file: *mut c_void, name: *const c_char, index_out: *mut i64) -> c_int;
+    pub fn sp_model_tensor_data(
+        file: *mut c_void, index: i64, data_out: *mut *const u8
     ) -> c_int;
 
 }

@@ -650,3 +650,83 @@ impl Drop for UlyssesComm {
         }
     }
 }
+
+// ------------------------------------------------------------------------------------------
+// Weight files (crates/sketchpad-convert/src/gguf.rs:351-470, loader.rs:60-90)
+// ------------------------------------------------------------------------------------------
+/// One tensor of a GGUF or safetensors file: `sp_tensor_type`, row-major shape, byte size.
+#[derive(Debug, Clone)]
+pub struct TensorInfo {
+    pub name: String,
+    pub type_code: c_int,
+    pub shape: Vec<usize>,
+    pub nbytes: usize,
+    index: i64,
+}
+
+/// A GGUF v3 or safetensors file, memory-mapped by the library (host only).
+pub struct ModelFile {
+    handle: *mut c_void,
+    pub container: c_int,
+    pub tensors: Vec<TensorInfo>,
+}
+unsafe impl Send for ModelFile {}
+
+impl ModelFile {
+    pub fn open(path: &str) -> Result<Self, SketchpadError> {
+        let cpath = std::ffi::CString::new(path).expect("path without NUL");
+        let mut handle = core::ptr::null_mut();
+        check(unsafe { sys::sp_model_open(cpath.as_ptr(), &mut handle) })?;
+        let (mut container, mut nt, mut nm) = (0, 0i64, 0i64);
+        let mut file = ModelFile { handle, container: 0, tensors: Vec::new() };
+        check(unsafe { sys::sp_model_info(handle, &mut container, &mut nt, &mut nm) })?;
+        file.container = container;
+        let mut name = vec![0 as core::ffi::c_char; 4096];
+        for i in 0..nt {
+            let (mut t, mut nd, mut nb) = (0, 0, 0u64);
+            let mut dims = [0i64; 8];
+            check(unsafe {
+                sys::sp_model_tensor_info(handle, i, name.as_mut_ptr(), name.len(), &mut t, &mut nd,
+                                          dims.as_mut_ptr(), &mut nb)
+            })?;
+            let n = unsafe { CStr::from_ptr(name.as_ptr()) }.to_string_lossy().into_owned();
+            file.tensors.push(TensorInfo { name: n, type_code: t, index: i, nbytes: nb as usize,
+                                           shape: dims[..nd as usize].iter().map(|&d| d as usize).collect() });
+        }
+        Ok(file)
+    }
+
+    pub fn info(&self, name: &str) -> Option<&TensorInfo> {
+        self.tensors.iter().find(|t| t.name == name)
+    }
+
+    /// The tensor's bytes inside the map (GgufFile::tensor_raw_data, gguf.rs:448-470).
+    pub fn raw(&self, info: &TensorInfo) -> &[u8] {
+        let mut p: *const u8 = core::ptr::null();
+        check(unsafe { sys::sp_model_tensor_data(self.handle, info.index, &mut p) })
+            .expect("tensor data");
+        // SAFETY: the library maps nbytes at p for as long as the file is open
+        unsafe { core::slice::from_raw_parts(p, info.nbytes) }
+    }
+
+    /// A GpuQuantizedLinear over a 2-D GGUF Q8_0 / Q4_K / Q2_K / Q3_K weight.
+    pub fn quantized_linear(&self, name: &str, client: &ComputeClient) -> GpuQuantizedLinear {
+        let info = self.info(name).unwrap_or_else(|| panic!("tensor '{name}' not found"));
+        let qt = match info.type_code - sys::SP_T_GGML_BASE {
+            8 => GpuQuantType::Q8_0,
+            10 => GpuQuantType::Q2K,
+            11 => GpuQuantType::Q3K,
+            12 => GpuQuantType::Q4K,
+            t => panic!("tensor '{name}': ggml type {t} has no fused GPU path"),
+        };
+        assert_eq!(info.shape.len(), 2, "tensor '{name}' is not 2-D");
+        GpuQuantizedLinear::from_bytes(self.raw(info), qt, info.shape[0], info.shape[1], client,
+                                       DType::BF16)
+    }
+}
+
+impl Drop for ModelFile {
+    fn drop(&mut self) {
+        unsafe { sys::sp_model_close(self.handle) };
+    }
+}

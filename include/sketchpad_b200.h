@@ -359,6 +359,39 @@ int sp_ulysses_a2a(const void* send, void* recv, int64_t count, int dtype, void*
 int sp_nccl_all_gather(const void* send, void* recv, int64_t count, int dtype, void* comm,
                        void* stream, double timeout_s);
 
+/* ------------------------------------------------------------------------------------
+ * Weight files (host only, no GPU): GGUF v3 as crates/sketchpad-convert/src/gguf.rs:351-470
+ * reads it (version 3 only, tensor data at the header end rounded up to 32 bytes, shapes
+ * reversed to row-major) and safetensors as crates/sketchpad-convert/src/loader.rs:60-90
+ * reads it (8-byte header length, JSON header, data_offsets after it), with F8_E4M3 /
+ * F8_E5M2 tensors accepted as well.  The file is memory-mapped read-only; tensor bytes are
+ * returned as pointers into the map, valid until sp_model_close.  GGUF Q8_0 / Q2_K / Q3_K /
+ * Q4_K bytes go to sp_q8_0_repack_host / sp_kquant_repack_host unchanged.
+ * ------------------------------------------------------------------------------------ */
+typedef enum sp_container { SP_CONTAINER_GGUF = 1, SP_CONTAINER_SAFETENSORS = 2 } sp_container;
+/* Tensor element types: the sp_dtype values, then the other safetensors dtypes, then GGUF's
+ * block-quantized types as SP_T_GGML_BASE + the ggml type id (Q8_0 = 108, Q2_K = 110, Q3_K =
+ * 111, Q4_K = 112, ...). */
+typedef enum sp_tensor_type {
+  SP_T_F32 = 0, SP_T_F16 = 1, SP_T_BF16 = 2, SP_T_F8_E4M3 = 3, SP_T_F8_E5M2 = 4, SP_T_F64 = 5,
+  SP_T_I8 = 6, SP_T_U8 = 7, SP_T_I16 = 8, SP_T_I32 = 9, SP_T_I64 = 10, SP_T_BOOL = 11,
+  SP_T_GGML_BASE = 100
+} sp_tensor_type;
+/* Opens a GGUF (by its magic) or safetensors file; SP_ERR_INVALID_ARG / SP_ERR_DTYPE /
+ * SP_ERR_SHAPE on a malformed file, an unknown type or offsets outside the file. */
+int sp_model_open(const char* path, void** file_out);
+int sp_model_close(void* file);
+int sp_model_info(void* file, int* container_out, int64_t* tensor_count_out,
+                  int64_t* meta_count_out);
+int sp_model_meta_key(void* file, int64_t index, char* name_out, size_t name_cap);
+/* Name, sp_tensor_type, rank and row-major dims (up to 8, unused entries 0) and byte size of
+ * tensor `index` (file order). */
+int sp_model_tensor_info(void* file, int64_t index, char* name_out, size_t name_cap,
+                         int* type_out, int* ndims_out, int64_t dims_out[8],
+                         uint64_t* nbytes_out);
+int sp_model_find(void* file, const char* name, int64_t* index_out);
+int sp_model_tensor_data(void* file, int64_t index, const uint8_t** data_out);
+
 #ifdef __cplusplus
 }
 #endif

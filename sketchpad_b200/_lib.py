@@ -40,6 +40,14 @@ SIGNATURES = {
                                  _i64, _i64p, _i64p, _i64p, _i64p, _int, _int, _int, _f, _vp]),
     "sp_groupnorm_act_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64p, _i64, _int]),
     "sp_groupnorm_act_output_strides": (_int, [_i64, _i64, _i64, _i64, _i64p, _i64p]),
+    "sp_model_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "sp_model_close": (_int, [_vp]),
+    "sp_model_info": (_int, [_vp, ctypes.POINTER(_int), ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
+    "sp_model_meta_key": (_int, [_vp, _i64, ctypes.c_char_p, _sz]),
+    "sp_model_tensor_info": (_int, [_vp, _i64, ctypes.c_char_p, _sz, ctypes.POINTER(_int),
+                                    ctypes.POINTER(_int), _i64p, ctypes.POINTER(ctypes.c_uint64)]),
+    "sp_model_find": (_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_i64)]),
+    "sp_model_tensor_data": (_int, [_vp, _i64, ctypes.POINTER(ctypes.POINTER(ctypes.c_uint8))]),
     "sp_nccl_unique_id_bytes": (_sz, []),
     "sp_nccl_unique_id": (_int, [_vp, _sz]),
     "sp_nccl_comm_init": (_int, [ctypes.POINTER(_vp), _int, _int, _vp, ctypes.c_double]),

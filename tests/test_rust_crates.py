@@ -21,7 +21,9 @@ C_TO_RUST = {
     "const float*": "*const c_float", "float*": "*mut c_float", "const uint8_t*": "*const u8",
     "uint8_t*": "*mut u8", "int8_t*": "*mut i8", "uint16_t*": "*mut u16",
     "void**": "*mut *mut c_void", "int*": "*mut c_int", "const char*": "*const c_char",
-    "const int64_t[4]": "*const i64", "int64_t[4]": "*mut i64",
+    "const int64_t[4]": "*const i64", "int64_t[4]": "*mut i64", "int64_t[8]": "*mut i64",
+    "char*": "*mut c_char", "int64_t*": "*mut i64", "uint64_t*": "*mut u64",
+    "const uint8_t**": "*mut *const u8",
 }
 
 
@@ -33,8 +35,8 @@ def header_functions():
         a = " ".join(args.split())
         types = []
         for p in ([] if a == "void" else a.split(",")):
-            m = re.match(r"\s*(.*?)\s*(\w+)\s*(\[4\])?\s*$", p)
-            types.append(" ".join(m.group(1).split()) + ("[4]" if m.group(3) else ""))
+            m = re.match(r"\s*(.*?)\s*(\w+)\s*(\[\d\])?\s*$", p)
+            types.append(" ".join(m.group(1).split()) + (m.group(3) or ""))
         out[name] = (" ".join(ret.split()), types)
     return out
 
