@@ -127,8 +127,8 @@ def cpu_unet_step_time(max_seconds: float = 60.0, min_steps: int = 1, max_steps:
     return sum(times) / len(times), len(times), oracle.get_threads()
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one (2,8,4096,40) attention launch, from the
-# ncu capture summarised in profiles/flash_attn_fwd_2x8x4096x40_bf16.md
+# dram__bytes_read.sum + dram__bytes_write.sum of one (2,8,4096,40) attention launch (ncu
+# capture of `bench.py --case attn_2x8x4096x40`): Q, K and V read once, O left in L2
 ATTN_D40_TRAFFIC_BYTES = 15_822_592
 
 
@@ -473,7 +473,7 @@ def run_b200(args):
                          # (the step's dominant attention shape): Q+K+V read once, O left
                          # in L2 -- equal to the algorithmic input bytes (15.7 MB)
                          "traffic": ATTN_D40_TRAFFIC_BYTES,
-                         "traffic_case": "(2,8,4096,40) launch, profiles/flash_attn_fwd_2x8x4096x40_bf16.md"},
+                         "traffic_case": "one (2,8,4096,40) launch, ncu dram read + write"},
             "achieved_step_tflops": flops["total"] / ms / 1e9,
             "kernels": kernels,
             "cpu_baseline": cpu,
@@ -490,7 +490,7 @@ def run_b200(args):
 
 
 # ------------------------------------------------------------------------------------------
-# Single-kernel cases (what the committed ncu summaries under profiles/ capture)
+# Single-kernel cases (the workloads the ncu captures run)
 # ------------------------------------------------------------------------------------------
 def _case_attention(torch, B, H, Sq, Skv, D):
     from sketchpad_b200 import flash_attention

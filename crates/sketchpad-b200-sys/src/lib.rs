@@ -73,13 +73,17 @@ extern "C" {
     pub fn sp_last_error() -> *const c_char;
     pub fn sp_watchdog_read_and_clear(stream: *mut c_void, code_out: *mut c_int) -> c_int;
     // -- flash attention: sketchpad_cubecl::flash_attention / flash_attention_masked
-    //    (crates/sketchpad-cubecl/src/attention.rs:97, :119)
+    //    (crates/sketchpad-cubecl/src/attention.rs:97, :119); a bounded-wait check
     pub fn sp_flash_attn_fwd(
         q: *const c_void, k: *const c_void, v: *const c_void, mask: *const c_float,
         mask_row_stride: i64, out: *mut c_void, b: i64, h: i64, sq: i64, skv: i64, d: i64,
         dv: i64, q_strides: *const i64, k_strides: *const i64, v_strides: *const i64,
         o_strides: *const i64, dtype_in: c_int, dtype_out: c_int, causal: c_int,
         scale: c_float, stream: *mut c_void
+    ) -> c_int;
+    pub fn sp_flash_attn_fwd_wait_test(
+        q: *const c_void, k: *const c_void, v: *const c_void, out: *mut c_void, b: i64, h: i64,
+        s: i64, d: i64, skip_kv_tile: c_int, wait_budget_cycles: i64, stream: *mut c_void
     ) -> c_int;
     // -- GroupNorm (+ SiLU): sketchpad_cubecl::groupnorm_silu / groupnorm
     //    (crates/sketchpad-cubecl/src/groupnorm_silu.rs:232, :323)

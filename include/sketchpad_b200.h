@@ -70,6 +70,18 @@ int sp_flash_attn_fwd(const void* q, const void* k, const void* v, const float* 
                       const int64_t o_strides[4], int dtype_in, int dtype_out, int causal,
                       float scale, void* stream);
 
+/* Failure-handling check (no reference counterpart): sp_flash_attn_fwd on contiguous bf16
+ * q, k, v, out [B,H,S,D] (S > 32) whose TMA producer never loads key/value tile
+ * `skip_kv_tile`, with every bounded device wait given `wait_budget_cycles` (>= 1e6 SM
+ * cycles) instead of the ~2 s default.  The waits for the missing tile run out, the kernel
+ * records the code in the device watchdog word (sp_watchdog_read_and_clear), lets its copies
+ * in flight land, frees its tensor memory and returns; out is left unspecified.  Lets a test
+ * make a device wait expire without faulting or hanging the GPU and check that the context
+ * stays usable. */
+int sp_flash_attn_fwd_wait_test(const void* q, const void* k, const void* v, void* out, int64_t B,
+                                int64_t H, int64_t S, int64_t D, int skip_kv_tile,
+                                int64_t wait_budget_cycles, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * GroupNorm (+ SiLU), single pass over HBM.
  * Replaces sketchpad_cubecl::groupnorm_silu / groupnorm

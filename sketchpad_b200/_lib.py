@@ -38,6 +38,8 @@ SIGNATURES = {
     "sp_watchdog_read_and_clear": (_int, [_vp, ctypes.POINTER(_int)]),
     "sp_flash_attn_fwd": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _i64,
                                  _i64, _i64p, _i64p, _i64p, _i64p, _int, _int, _int, _f, _vp]),
+    "sp_flash_attn_fwd_wait_test": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int,
+                                           _i64, _vp]),
     "sp_groupnorm_act_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64p, _i64, _int]),
     "sp_groupnorm_act_output_strides": (_int, [_i64, _i64, _i64, _i64, _i64p, _i64p]),
     "sp_model_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),

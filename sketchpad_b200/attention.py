@@ -66,7 +66,8 @@ def _flash(query, key, value, mask, options: FlashAttentionOptions, scale, out):
             f"shape mismatch q{tuple(query.shape)} k{tuple(key.shape)} v{tuple(value.shape)}")
     compute = query.dtype if query.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
     q, k, v = (_prep(t, compute) for t in (query, key, value))
-    out_dtype = options.out_dtype or query.dtype
+    # the output dtype: the options', else a given out's (bf16 / f16 / f32), else the query's
+    out_dtype = options.out_dtype or (out.dtype if out is not None else query.dtype)
     if out is None:
         out = torch.empty((B, H, Sq, Dv), dtype=out_dtype, device=dev)
     elif out.shape != (B, H, Sq, Dv) or out.dtype != out_dtype:

@@ -62,6 +62,11 @@ struct FaParams {
   int out_dtype;
   int in_f16;  // 1 if inputs are f16 (P is then f16 too), 0 for bf16
   int single;  // 1: one query tile per CTA (grids that would leave SMs idle), 0: two
+  // bounded waits: budget of each mbarrier wait in SM cycles; a tile index >= 0 here is
+  // never loaded (sp_flash_attn_fwd_wait_test), so the waits for it expire and the CTA
+  // takes its abort path
+  long long wait_budget;
+  int skip_kv_tile;
 };
 
 template <int NBQ, int NBV, int STAGES>
@@ -80,22 +85,6 @@ struct FaSmem {
 
 __device__ __forceinline__ uint32_t float_bits(float f) { return __float_as_uint(f); }
 
-// 2^x on the FMA pipe (for x <= 8; x < -125 flushes to ~2^-125): x = n + f with n = rint(x)
-// from the 1.5*2^23 rounding trick, 2^f on [-1/2, 1/2] by a degree-3 polynomial fitted for
-// this kernel (relative error <= 7.5e-5, far below the 16-bit rounding of P), and n added
-// to the exponent field.  Used for part of each row so the MUFU unit is not the only
-// source of exponentials.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -125.0f);
-  const float j = __fadd_rn(x, 12582912.0f);
-  const float f = __fsub_rn(x, __fsub_rn(j, 12582912.0f));
-  const float p = fmaf(fmaf(fmaf(0.055171624f, f, 0.24261113f), f, 0.69326098f), f, 0.99992806f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
-}
-
-// Pairs of columns (out of every 16) whose exponentials use exp2_fma on unmasked tiles.
-constexpr uint32_t kPolyPairs = 0;  // none: measured slower than MUFU-only on B200 (issue-bound)
-
 // TMEM column offsets inside one tile's 256 columns
 template <int NBV>
 struct FaTmem {
@@ -104,7 +93,11 @@ struct FaTmem {
   static constexpr uint32_t kO = NBV == 1 ? 192 : 128;
 };
 
-template <int NBQ, int NBV, int STAGES>
+// ONES (Dv < the padded width, e.g. the UNet's D = 40): the first padding column of every V
+// stage is set to 1 before the PV product, so O's column Dv accumulates sum_k P[k] -- the
+// softmax row sum, taken on the tensor core from exactly the rounded P it multiplies V by,
+// and rescaled with O.  The softmax warps then keep no running sum.
+template <int NBQ, int NBV, int STAGES, bool ONES>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const FaParams p) {
@@ -187,13 +180,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % STAGES;
         const uint32_t ph = (j / STAGES) & 1;
-        if (j >= STAGES && !mbar_wait(&k_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) break;
+        if (j >= STAGES && !mbar_wait(&k_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT, p.wait_budget)) break;
+        if (j == p.skip_kv_tile) continue;  // test hook: this tile's barriers never complete
         mbar_arrive_expect_tx(&k_full[st], NBQ * kBox);
         for (int blk = 0; blk < NBQ; ++blk)
           tma_load_4d(smem + L::kK + (st * NBQ + blk) * kBox, &tmk, &k_full[st], blk * 64,
                       j * kBN, h, b);
         issued_k = j + 1;
-        if (j >= STAGES && !mbar_wait(&v_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) break;
+        if (j >= STAGES && !mbar_wait(&v_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT, p.wait_budget)) break;
         mbar_arrive_expect_tx(&v_full[st], NBV * kBox);
         for (int blk = 0; blk < NBV; ++blk)
           tma_load_4d(smem + L::kV + (st * NBV + blk) * kBox, &tmv, &v_full[st], blk * 64,
@@ -202,11 +196,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (*abort_flag) {
         // Let every copy still in flight land before the CTA can exit (bounded).
-        mbar_wait(q_full, 0, nullptr, WD_TMA_WAIT);
+        mbar_wait(q_full, 0, nullptr, WD_TMA_WAIT, p.wait_budget);
         for (int j = max(0, issued_k - STAGES); j < issued_k; ++j)
-          mbar_wait(&k_full[j % STAGES], (j / STAGES) & 1, nullptr, WD_TMA_WAIT);
+          mbar_wait(&k_full[j % STAGES], (j / STAGES) & 1, nullptr, WD_TMA_WAIT, p.wait_budget);
         for (int j = max(0, issued_v - STAGES); j < issued_v; ++j)
-          mbar_wait(&v_full[j % STAGES], (j / STAGES) & 1, nullptr, WD_TMA_WAIT);
+          mbar_wait(&v_full[j % STAGES], (j / STAGES) & 1, nullptr, WD_TMA_WAIT, p.wait_budget);
       }
     }
   } else if (warp == 9) {
@@ -230,6 +224,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&s_full[t]);
       };
+      // V stage st: column Dv of each of the 128 key rows <- 1 (its 16-byte chunk holds only
+      // padding columns, Dv % 8 == 0; 128B swizzle: chunk c of row r sits at c ^ (r & 7)),
+      // then a proxy fence so the tensor core's async-proxy reads see the stores
+      auto ones_column = [&](int st) {
+        if constexpr (ONES) {
+          uint8_t* vb = smem + L::kV + st * NBV * kBox;
+          const int chunk = p.Dv >> 3;
+#pragma unroll 8
+          for (int r = 0; r < kBN; ++r)
+            *reinterpret_cast<uint4*>(vb + r * 128 + ((chunk ^ (r & 7)) << 4)) =
+                make_uint4(p.in_f16 ? 0x3C00u : 0x3F80u, 0u, 0u, 0u);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        }
+      };
       // O_t += P_t V_j, P_t from TMEM (8 columns per 16 keys)
       auto issue_pv = [&](int t, int j) {
         const uint32_t v_base = smem_u32(smem + L::kV + (j % STAGES) * NBV * kBox);
@@ -242,8 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&o_done[t]);
       };
 
-      bool ok = mbar_wait(q_full, 0, abort_flag, WD_MMA_WAIT) &&
-                (n_tiles == 0 || mbar_wait(&k_full[0], 0, abort_flag, WD_MMA_WAIT));
+      bool ok = mbar_wait(q_full, 0, abort_flag, WD_MMA_WAIT, p.wait_budget) &&
+                (n_tiles == 0 || mbar_wait(&k_full[0], 0, abort_flag, WD_MMA_WAIT, p.wait_budget));
       tc_fence_after();
       if (ok && n_tiles > 0) {
         issue_qk(0, 0);
@@ -256,40 +264,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st1 = (j + 1) % STAGES;
         if constexpr (kEarlyQK) {
           if (more) {
-            if (!mbar_wait(&k_full[st1], ((j + 1) / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
-            if (!mbar_wait(&s_free[0], j & 1, abort_flag, WD_MMA_WAIT)) break;
+            if (!mbar_wait(&k_full[st1], ((j + 1) / STAGES) & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
+            if (!mbar_wait(&s_free[0], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
             tc_fence_after();
             issue_qk(0, j + 1);
             if (ntq == 2) {
-              if (!mbar_wait(&s_free[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
+              if (!mbar_wait(&s_free[1], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
               tc_fence_after();
               issue_qk(1, j + 1);
             }
             umma_commit(&k_empty[st1]);
           }
-          if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
-          if (!mbar_wait(&p_full[0], j & 1, abort_flag, WD_MMA_WAIT)) break;
+          if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
+          ones_column(st);
+          if (!mbar_wait(&p_full[0], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
           tc_fence_after();
           issue_pv(0, j);
           if (ntq == 2) {
-            if (!mbar_wait(&p_full[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
+            if (!mbar_wait(&p_full[1], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
             tc_fence_after();
             issue_pv(1, j);
           }
           umma_commit(&v_empty[st]);
           continue;
         }
-        if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
-        if (!mbar_wait(&p_full[0], j & 1, abort_flag, WD_MMA_WAIT)) break;
+        if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
+        if (!mbar_wait(&p_full[0], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
         tc_fence_after();
         issue_pv(0, j);
         if (more) {
-          if (!mbar_wait(&k_full[st1], ((j + 1) / STAGES) & 1, abort_flag, WD_MMA_WAIT)) break;
+          if (!mbar_wait(&k_full[st1], ((j + 1) / STAGES) & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
           tc_fence_after();
           issue_qk(0, j + 1);
         }
         if (ntq == 2) {
-          if (!mbar_wait(&p_full[1], j & 1, abort_flag, WD_MMA_WAIT)) break;
+          if (!mbar_wait(&p_full[1], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
           tc_fence_after();
           issue_pv(1, j);
         }
@@ -301,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Drain: every MMA issued above has completed once this commit arrives.
       umma_commit(drain);
-      mbar_wait(drain, 0, nullptr, WD_MMA_WAIT);
+      mbar_wait(drain, 0, nullptr, WD_MMA_WAIT, p.wait_budget);
     }
   } else if (warp < 4 * ntq) {
     // ------------------------------------------------------------------ softmax + epilogue
@@ -315,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
 
     for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait_warp(&s_full[t], j & 1, abort_flag, WD_SOFTMAX_WAIT)) {
+      if (!mbar_wait_warp(&s_full[t], j & 1, abort_flag, WD_SOFTMAX_WAIT, p.wait_budget)) {
         ok = false;
         break;
       }
@@ -402,49 +411,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Aliased layout: S_t(j)'s commit followed PV_t(j-1), so O is final here.
       if constexpr (!kEarlyQK) rescale_o();
 
-      // exp2, row sum, 16-bit P (column c holds keys 2c, 2c+1).  Unmasked tiles may send
-      // some exponentials to the FMA pipe (kPolyPairs); masked tiles use MUFU only, so -inf
-      // scores give exactly 0.
+      // exp2 (MUFU), row sum (unless the tensor core forms it, ONES), 16-bit P (column c
+      // holds keys 2c, 2c+1); -inf scores of masked tiles give exactly 0
       float rs0 = 0.f, rs1 = 0.f;
       uint32_t pk[4][16];
-      if (!need_mask) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 4; ++q) {
 #pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const float x0 = fmaf(__uint_as_float(r[q][2 * u]), sl2, -m_ref);
-            const float x1 = fmaf(__uint_as_float(r[q][2 * u + 1]), sl2, -m_ref);
-            float e0, e1;
-            if ((kPolyPairs >> u) & 1u) {  // resolved at compile time
-              e0 = exp2_fma(x0);
-              e1 = exp2_fma(x1);
-            } else {
-              e0 = ex2_approx(x0);
-              e1 = ex2_approx(x1);
-            }
+        for (int u = 0; u < 16; ++u) {
+          const float e0 = ex2_approx(fmaf(__uint_as_float(r[q][2 * u]), sl2, -m_ref));
+          const float e1 = ex2_approx(fmaf(__uint_as_float(r[q][2 * u + 1]), sl2, -m_ref));
+          if constexpr (!ONES) {
             rs0 += e0;
             rs1 += e1;
-            pk[q][u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
           }
-          if constexpr (!kEarlyQK) tmem_st16(lane_addr + TM::kP + q * 16, pk[q]);
+          pk[q][u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
         }
-      } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const float e0 = ex2_approx(fmaf(__uint_as_float(r[q][2 * u]), sl2, -m_ref));
-            const float e1 = ex2_approx(fmaf(__uint_as_float(r[q][2 * u + 1]), sl2, -m_ref));
-            rs0 += e0;
-            rs1 += e1;
-            pk[q][u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
-          }
-          if constexpr (!kEarlyQK) tmem_st16(lane_addr + TM::kP + q * 16, pk[q]);
-        }
+        if constexpr (!kEarlyQK) tmem_st16(lane_addr + TM::kP + q * 16, pk[q]);
       }
       if constexpr (kEarlyQK) {
         // PV_t(j-1) must be done before P_t is rewritten and O rescaled
-        if (j >= 1 && !mbar_wait_warp(&o_done[t], (j - 1) & 1, abort_flag, WD_SOFTMAX_WAIT)) {
+        if (j >= 1 && !mbar_wait_warp(&o_done[t], (j - 1) & 1, abort_flag, WD_SOFTMAX_WAIT, p.wait_budget)) {
           ok = false;
           break;
         }
@@ -463,9 +450,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- epilogue: O / l -> global
     const int last = n_tiles - 1;
     if (ok && n_tiles > 0 &&
-        mbar_wait_warp(&o_done[t], last & 1, abort_flag, WD_EPILOGUE_WAIT)) {
+        mbar_wait_warp(&o_done[t], last & 1, abort_flag, WD_EPILOGUE_WAIT, p.wait_budget)) {
       tc_fence_after();
-      const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
+      float l_fin = l_run;
+      if constexpr (ONES) {  // the row sum accumulated in O's column Dv
+        uint32_t rl[16];
+        tmem_ld16(lane_addr + TM::kO + (p.Dv & ~15), rl);
+        tmem_wait_ld();
+        l_fin = __uint_as_float(rl[p.Dv & 15]);
+      }
+      const float inv_l = l_fin > 0.f ? 1.0f / l_fin : 0.f;
       const bool row_ok = qi < p.Sq;
       const int64_t obase = (int64_t)b * p.os0 + (int64_t)h * p.os1 + (int64_t)qi * p.os2;
       for (int c = 0; c < p.dv_pad; c += 16) {
@@ -524,11 +518,11 @@ int make_qkv_map(CUtensorMap* m, const void* base, int in_f16, int64_t S, int64_
                       4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int NBQ, int NBV, int STAGES>
+template <int NBQ, int NBV, int STAGES, bool ONES = false>
 int launch_fa(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
               const FaParams& p, int64_t B, cudaStream_t s) {
   using L = FaSmem<NBQ, NBV, STAGES>;
-  auto kern = fa_fwd_kernel<NBQ, NBV, STAGES>;
+  auto kern = fa_fwd_kernel<NBQ, NBV, STAGES, ONES>;
   static_assert(L::kAlloc <= 232448, "flash_attn smem budget");
   static unsigned long long attr_set = 0;
   if (first_time_on_device(&attr_set)) {
@@ -810,15 +804,14 @@ int launch_attn_short_out(const void* q, const void* k, const void* v, void* out
 }  // namespace
 }  // namespace sp
 
-extern "C" int sp_flash_attn_fwd(const void* q, const void* k, const void* v, const float* mask,
-                                 int64_t mask_row_stride, void* out, int64_t B, int64_t H,
-                                 int64_t Sq, int64_t Skv, int64_t D, int64_t Dv,
-                                 const int64_t q_strides[4], const int64_t k_strides[4],
-                                 const int64_t v_strides[4], const int64_t o_strides[4],
-                                 int dtype_in, int dtype_out, int causal, float scale,
-                                 void* stream) {
-  using namespace sp;
-  clear_error();
+namespace sp {
+namespace {
+int flash_attn_impl(const void* q, const void* k, const void* v, const float* mask,
+                    int64_t mask_row_stride, void* out, int64_t B, int64_t H, int64_t Sq,
+                    int64_t Skv, int64_t D, int64_t Dv, const int64_t q_strides[4],
+                    const int64_t k_strides[4], const int64_t v_strides[4],
+                    const int64_t o_strides[4], int dtype_in, int dtype_out, int causal,
+                    float scale, void* stream, long long wait_budget, int skip_kv_tile) {
   if (!q || !k || !v || !out || !q_strides || !k_strides || !v_strides || !o_strides)
     return set_error(SP_ERR_INVALID_ARG, "flash_attn: null pointer argument");
   if (B <= 0 || H <= 0 || Sq <= 0 || Skv <= 0 || D <= 0 || Dv <= 0)
@@ -892,9 +885,44 @@ extern "C" int sp_flash_attn_fwd(const void* q, const void* k, const void* v, co
   p.in_f16 = in_f16;
   // one query tile per CTA when the grid of tile pairs would not cover the SMs
   p.single = (Sq + 2 * kBM - 1) / (2 * kBM) * H * B < num_sms() ? 1 : 0;
+  p.wait_budget = wait_budget;
+  p.skip_kv_tile = skip_kv_tile;
   const bool qk2 = D > 64, v2 = Dv > 64;
-  if (!qk2 && !v2) return launch_fa<1, 1, 4>(mq, mk, mv, p, B, s);  // 160 KB smem
+  if (!qk2 && !v2) {  // 160 KB smem; the row sum on the tensor core when V has a spare column
+    if (Dv < p.dv_pad) return launch_fa<1, 1, 4, true>(mq, mk, mv, p, B, s);
+    return launch_fa<1, 1, 4>(mq, mk, mv, p, B, s);
+  }
   if (qk2 && v2) return launch_fa<2, 2, 2>(mq, mk, mv, p, B, s);     // 192 KB smem
   if (qk2) return launch_fa<2, 1, 3>(mq, mk, mv, p, B, s);           // 208 KB smem
   return launch_fa<1, 2, 3>(mq, mk, mv, p, B, s);                    // 176 KB smem
+}
+}  // namespace
+}  // namespace sp
+
+extern "C" int sp_flash_attn_fwd(const void* q, const void* k, const void* v, const float* mask,
+                                 int64_t mask_row_stride, void* out, int64_t B, int64_t H,
+                                 int64_t Sq, int64_t Skv, int64_t D, int64_t Dv,
+                                 const int64_t q_strides[4], const int64_t k_strides[4],
+                                 const int64_t v_strides[4], const int64_t o_strides[4],
+                                 int dtype_in, int dtype_out, int causal, float scale,
+                                 void* stream) {
+  sp::clear_error();
+  return sp::flash_attn_impl(q, k, v, mask, mask_row_stride, out, B, H, Sq, Skv, D, Dv,
+                             q_strides, k_strides, v_strides, o_strides, dtype_in, dtype_out,
+                             causal, scale, stream, sp::kWaitBudgetCycles, -1);
+}
+
+extern "C" int sp_flash_attn_fwd_wait_test(const void* q, const void* k, const void* v, void* out,
+                                           int64_t B, int64_t H, int64_t S, int64_t D,
+                                           int skip_kv_tile, int64_t wait_budget_cycles,
+                                           void* stream) {
+  sp::clear_error();
+  if (S <= sp::kShortMax || skip_kv_tile < 0 || skip_kv_tile >= (S + sp::kBN - 1) / sp::kBN ||
+      wait_budget_cycles < 1000000 || wait_budget_cycles > sp::kWaitBudgetCycles)
+    return sp::set_error(SP_ERR_INVALID_ARG,
+                         "wait test: needs S > %d, a key tile index in range and a budget in "
+                         "[1e6, %lld] cycles", sp::kShortMax, (long long)sp::kWaitBudgetCycles);
+  const int64_t st[4] = {H * S * D, S * D, D, 1};
+  return sp::flash_attn_impl(q, k, v, nullptr, 0, out, B, H, S, S, D, D, st, st, st, st, SP_BF16,
+                             SP_BF16, 0, 0.f, stream, wait_budget_cycles, skip_kv_tile);
 }

@@ -70,7 +70,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait on the phase with the given parity.  `abort` (shared) lets the other roles of
 // the CTA stop waiting once any wait has expired.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int code) {
+                                          int code, long long budget = kWaitBudgetCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   uint32_t spins = 0;
@@ -78,7 +78,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 255u) == 0) {
       if (abort && *abort) return false;
-      if (clock64() - t0 > kWaitBudgetCycles) {
+      if (clock64() - t0 > budget) {
         atomicCAS(&g_watchdog, 0, code);
         if (abort) *abort = 1;
         return false;
@@ -90,8 +90,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Warp-uniform bounded wait: every lane of the (converged) warp gets the same answer, so
 // warp-collective tcgen05 instructions that follow are never reached by only part of a warp.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                               int code) {
-  const bool ok = mbar_wait(bar, parity, abort, code);
+                                               int code, long long budget = kWaitBudgetCycles) {
+  const bool ok = mbar_wait(bar, parity, abort, code, budget);
   return __all_sync(0xffffffffu, ok);
 }
 

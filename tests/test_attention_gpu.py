@@ -152,3 +152,39 @@ def test_short_sequence_strided_temporal_views():
     flash_attention(q, k, v, out=out)
     torch.cuda.synchronize()
     check(q, k, v, out, heads=[(0, 0), (HW - 1, Hh - 1), (17, 2)])
+
+
+def test_bounded_wait_expires_and_the_context_stays_usable():
+    # Failure handling without a GPU fault: the producer never loads key tile 3, so the
+    # waits for it (MMA issuer, softmax warps) run out their 20 M-cycle budget; the kernel
+    # records the code in the device watchdog word, drains its copies, frees TMEM and
+    # returns.  A normal launch right after on the same context must match the oracle.
+    import ctypes
+    import time
+
+    from sketchpad_b200 import _lib
+    from sketchpad_b200._torch import ptr, stream_ptr
+    L = _lib.load()
+    B, H, S, D = 1, 2, 1024, 64
+    q, k, v = rnd((B, H, S, D), 31), rnd((B, H, S, D), 32), rnd((B, H, S, D), 33)
+    out = torch.empty_like(q)
+    code = ctypes.c_int(-1)
+    dev = q.device
+    assert L.sp_watchdog_read_and_clear(stream_ptr(dev), ctypes.byref(code)) == 0  # clear
+    t0 = time.monotonic()
+    rc = L.sp_flash_attn_fwd_wait_test(ptr(q), ptr(k), ptr(v), ptr(out), B, H, S, D, 3,
+                                       20_000_000, stream_ptr(dev))
+    assert rc == 0, L.sp_last_error()
+    assert L.sp_watchdog_read_and_clear(stream_ptr(dev), ctypes.byref(code)) == 0
+    elapsed = time.monotonic() - t0
+    assert code.value in (1, 2, 3, 4), code.value  # WD_TMA / MMA / SOFTMAX / EPILOGUE wait
+    assert elapsed < 10.0
+    assert torch.cuda.synchronize() is None  # no sticky error on the context
+    o2 = flash_attention(q, k, v)
+    torch.cuda.synchronize()
+    check(q, k, v, o2, heads=[(0, 0), (0, 1)])
+    assert L.sp_watchdog_read_and_clear(stream_ptr(dev), ctypes.byref(code)) == 0
+    assert code.value == 0
+    # the argument checks of the test entry
+    assert L.sp_flash_attn_fwd_wait_test(ptr(q), ptr(k), ptr(v), ptr(out), B, H, S, D, 99,
+                                         20_000_000, stream_ptr(dev)) == -1
