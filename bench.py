@@ -627,6 +627,22 @@ def _case_wan_block(torch):
     return (lambda: blk.forward(x, cond, ctx, 21, 45, 80)), wan_block_flops(cfg)["total"], "flop"
 
 
+def _case_wan_step(torch):
+    """Wan::forward at config 5 on one GPU: 40 FP8 blocks over 21 x 45 x 80 = 75,600 tokens,
+    512 text tokens of width 4096, patchify / embeddings / final layer / unpatchify."""
+    from sketchpad_b200.wan import WanB200, WanConfig, wan_step_flops
+    cfg = WanConfig()
+    net = WanB200(cfg, "cuda", seed=0)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    lat = torch.randn(1, 16, 21, 90, 160, device="cuda", generator=g)
+    txt = torch.randn(1, 512, cfg.text_dim, device="cuda", generator=g).to(torch.bfloat16)
+
+    def step():
+        with torch.inference_mode():
+            net.forward(lat, 0.5, txt)
+    return step, wan_step_flops(cfg), "flop"
+
+
 CASES = {
     "unet_step_eager": _case_unet_step,
     "sd1x_ddim_loop_20": lambda t: _case_denoise_loop(t, "ddim", 20),
@@ -635,6 +651,7 @@ CASES = {
     "flux_single_4608": lambda t: _case_flux_block(t, True),
     "flux_step": _case_flux_step,
     "wan_block_21x45x80": _case_wan_block,
+    "wan_step_21x45x80": _case_wan_step,
     "attn_8x24x4608x128": lambda t: _case_attention(t, 8, 24, 4608, 4608, 128),
     "attn_2x8x4096x40": lambda t: _case_attention(t, 2, 8, 4096, 4096, 40),
     "attn_2x10x1024x64": lambda t: _case_attention(t, 2, 10, 1024, 1024, 64),

@@ -93,11 +93,7 @@ struct FaTmem {
   static constexpr uint32_t kO = NBV == 1 ? 192 : 128;
 };
 
-// ONES (Dv < the padded width, e.g. the UNet's D = 40): the first padding column of every V
-// stage is set to 1 before the PV product, so O's column Dv accumulates sum_k P[k] -- the
-// softmax row sum, taken on the tensor core from exactly the rounded P it multiplies V by,
-// and rescaled with O.  The softmax warps then keep no running sum.
-template <int NBQ, int NBV, int STAGES, bool ONES>
+template <int NBQ, int NBV, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmv, const FaParams p) {
@@ -224,20 +220,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&s_full[t]);
       };
-      // V stage st: column Dv of each of the 128 key rows <- 1 (its 16-byte chunk holds only
-      // padding columns, Dv % 8 == 0; 128B swizzle: chunk c of row r sits at c ^ (r & 7)),
-      // then a proxy fence so the tensor core's async-proxy reads see the stores
-      auto ones_column = [&](int st) {
-        if constexpr (ONES) {
-          uint8_t* vb = smem + L::kV + st * NBV * kBox;
-          const int chunk = p.Dv >> 3;
-#pragma unroll 8
-          for (int r = 0; r < kBN; ++r)
-            *reinterpret_cast<uint4*>(vb + r * 128 + ((chunk ^ (r & 7)) << 4)) =
-                make_uint4(p.in_f16 ? 0x3C00u : 0x3F80u, 0u, 0u, 0u);
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        }
-      };
       // O_t += P_t V_j, P_t from TMEM (8 columns per 16 keys)
       auto issue_pv = [&](int t, int j) {
         const uint32_t v_base = smem_u32(smem + L::kV + (j % STAGES) * NBV * kBox);
@@ -276,7 +258,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_commit(&k_empty[st1]);
           }
           if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
-          ones_column(st);
           if (!mbar_wait(&p_full[0], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
           tc_fence_after();
           issue_pv(0, j);
@@ -411,24 +392,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Aliased layout: S_t(j)'s commit followed PV_t(j-1), so O is final here.
       if constexpr (!kEarlyQK) rescale_o();
 
-      // exp2 (MUFU), row sum (unless the tensor core forms it, ONES), 16-bit P (column c
-      // holds keys 2c, 2c+1); -inf scores of masked tiles give exactly 0
+      // exp2 (MUFU), row sum, 16-bit P (column c holds keys 2c, 2c+1); -inf scores of
+      // masked tiles give exactly 0.  x = s * scale - m_ref is one fused multiply-add while
+      // m_ref is the ROUNDED product max * scale, so the row maximum's x can exceed 0 by half
+      // an ulp of m_ref: harmless for ordinary logits, but past |m_ref| ~ 2^24 that is more
+      // than 1, and with logits of 1e13 and up (activations in the millions) ex2 overflows to
+      // inf.  Rows with such a reference clamp x at 0 (their maximum's true value).
       float rs0 = 0.f, rs1 = 0.f;
       uint32_t pk[4][16];
+      auto exps = [&](auto clamp) {
+        constexpr bool kClamp = decltype(clamp)::value;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 4; ++q) {
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          const float e0 = ex2_approx(fmaf(__uint_as_float(r[q][2 * u]), sl2, -m_ref));
-          const float e1 = ex2_approx(fmaf(__uint_as_float(r[q][2 * u + 1]), sl2, -m_ref));
-          if constexpr (!ONES) {
+          for (int u = 0; u < 16; ++u) {
+            float x0 = fmaf(__uint_as_float(r[q][2 * u]), sl2, -m_ref);
+            float x1 = fmaf(__uint_as_float(r[q][2 * u + 1]), sl2, -m_ref);
+            if constexpr (kClamp) {
+              x0 = fminf(x0, 0.f);
+              x1 = fminf(x1, 0.f);
+            }
+            const float e0 = ex2_approx(x0), e1 = ex2_approx(x1);
             rs0 += e0;
             rs1 += e1;
+            pk[q][u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
           }
-          pk[q][u] = p.in_f16 ? pack_f16x2(e0, e1) : pack_bf16x2(e0, e1);
+          if constexpr (!kEarlyQK) tmem_st16(lane_addr + TM::kP + q * 16, pk[q]);
         }
-        if constexpr (!kEarlyQK) tmem_st16(lane_addr + TM::kP + q * 16, pk[q]);
-      }
+      };
+      if (__any_sync(0xffffffffu, fabsf(m_ref) > 1.0e6f))
+        exps(std::true_type{});
+      else
+        exps(std::false_type{});
       if constexpr (kEarlyQK) {
         // PV_t(j-1) must be done before P_t is rewritten and O rescaled
         if (j >= 1 && !mbar_wait_warp(&o_done[t], (j - 1) & 1, abort_flag, WD_SOFTMAX_WAIT, p.wait_budget)) {
@@ -452,14 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && n_tiles > 0 &&
         mbar_wait_warp(&o_done[t], last & 1, abort_flag, WD_EPILOGUE_WAIT, p.wait_budget)) {
       tc_fence_after();
-      float l_fin = l_run;
-      if constexpr (ONES) {  // the row sum accumulated in O's column Dv
-        uint32_t rl[16];
-        tmem_ld16(lane_addr + TM::kO + (p.Dv & ~15), rl);
-        tmem_wait_ld();
-        l_fin = __uint_as_float(rl[p.Dv & 15]);
-      }
-      const float inv_l = l_fin > 0.f ? 1.0f / l_fin : 0.f;
+      const float inv_l = l_run > 0.f ? 1.0f / l_run : 0.f;
       const bool row_ok = qi < p.Sq;
       const int64_t obase = (int64_t)b * p.os0 + (int64_t)h * p.os1 + (int64_t)qi * p.os2;
       for (int c = 0; c < p.dv_pad; c += 16) {
@@ -518,11 +506,11 @@ int make_qkv_map(CUtensorMap* m, const void* base, int in_f16, int64_t S, int64_
                       4, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int NBQ, int NBV, int STAGES, bool ONES = false>
+template <int NBQ, int NBV, int STAGES>
 int launch_fa(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
               const FaParams& p, int64_t B, cudaStream_t s) {
   using L = FaSmem<NBQ, NBV, STAGES>;
-  auto kern = fa_fwd_kernel<NBQ, NBV, STAGES, ONES>;
+  auto kern = fa_fwd_kernel<NBQ, NBV, STAGES>;
   static_assert(L::kAlloc <= 232448, "flash_attn smem budget");
   static unsigned long long attr_set = 0;
   if (first_time_on_device(&attr_set)) {
@@ -888,10 +876,7 @@ int flash_attn_impl(const void* q, const void* k, const void* v, const float* ma
   p.wait_budget = wait_budget;
   p.skip_kv_tile = skip_kv_tile;
   const bool qk2 = D > 64, v2 = Dv > 64;
-  if (!qk2 && !v2) {  // 160 KB smem; the row sum on the tensor core when V has a spare column
-    if (Dv < p.dv_pad) return launch_fa<1, 1, 4, true>(mq, mk, mv, p, B, s);
-    return launch_fa<1, 1, 4>(mq, mk, mv, p, B, s);
-  }
+  if (!qk2 && !v2) return launch_fa<1, 1, 4>(mq, mk, mv, p, B, s);  // 160 KB smem
   if (qk2 && v2) return launch_fa<2, 2, 2>(mq, mk, mv, p, B, s);     // 192 KB smem
   if (qk2) return launch_fa<2, 1, 3>(mq, mk, mv, p, B, s);           // 208 KB smem
   return launch_fa<1, 2, 3>(mq, mk, mv, p, B, s);                    // 176 KB smem

@@ -188,3 +188,17 @@ def test_bounded_wait_expires_and_the_context_stays_usable():
     # the argument checks of the test entry
     assert L.sp_flash_attn_fwd_wait_test(ptr(q), ptr(k), ptr(v), ptr(out), B, H, S, D, 99,
                                          20_000_000, stream_ptr(dev)) == -1
+
+
+def test_huge_logits_stay_finite():
+    # logits of ~1e11 (activations in the millions, like the config-4 Flux text stream): the
+    # softmax reference is the rounded product max * scale, whose half ulp exceeds 128 past
+    # 2^31, so without the clamp the row maximum's exponent could overflow ex2 to inf
+    B, H, S, D = 1, 2, 512, 128
+    q = rnd((B, H, S, D), 41) * 3.0e4
+    k = rnd((B, H, S, D), 42) * 3.0e6
+    v = rnd((B, H, S, D), 43)
+    out = flash_attention(q, k, v)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    check(q, k, v, out, heads=[(0, 0), (0, 1)])
