@@ -120,7 +120,7 @@ extern "C" {
         c: i64, dtype: c_int, stream: *mut c_void
     ) -> c_int;
     // -- Q8_0 / K-quant weights: dequantize_q8_0 and GpuQuantizedLinear
-    //    (crates/sketchpad-cubecl/src/quantized_matmul.rs:376, :655-767)
+    //    (crates/sketchpad-cubecl/src/quantized_matmul.rs:376, :655-767); bf16 linears
     pub fn sp_q8_0_repack_host(
         gguf_host: *const u8, nbytes: usize, out_f: i64, in_f: i64, q_host: *mut i8,
         scale_host: *mut u16
@@ -154,6 +154,19 @@ extern "C" {
         x: *const c_void, q: *const c_void, scale: *const c_void, bias: *const c_void,
         gate: *const c_void, residual: *const c_void, y: *mut c_void, m: i64, n: i64, k: i64,
         dtype: c_int, stream: *mut c_void
+    ) -> c_int;
+    pub fn sp_bf16_linear(
+        x: *const c_void, w: *const c_void, bias: *const c_void, y: *mut c_void, m: i64,
+        n: i64, k: i64, dtype: c_int, stream: *mut c_void
+    ) -> c_int;
+    pub fn sp_bf16_linear_gated(
+        x: *const c_void, w: *const c_void, bias: *const c_void, gate: *const c_void,
+        residual: *const c_void, y: *mut c_void, m: i64, n: i64, k: i64, dtype: c_int,
+        stream: *mut c_void
+    ) -> c_int;
+    pub fn sp_bf16_linear_glu(
+        x: *const c_void, w: *const c_void, bias: *const c_void, y: *mut c_void, m: i64,
+        n: i64, k: i64, glu_kind: c_int, dtype: c_int, stream: *mut c_void
     ) -> c_int;
     // -- FP8 e4m3 weights: quantize_fp8 / Fp8Tensor::dequantize / Fp8Linear::forward
     //    (crates/sketchpad-core/src/quantization.rs:495, :435, :601), GLU and RoPE epilogues

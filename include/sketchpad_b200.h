@@ -220,6 +220,23 @@ int sp_q8_0_linear_gated(const void* x, const void* q, const void* scale, const 
                          const void* gate, const void* residual, void* y, int64_t M, int64_t N,
                          int64_t K, int dtype, void* stream);
 
+/* y[M,N] = x[M,K] . W[N,K]^T (+ bias[N]) with plain bf16 weights on the same tcgen05 GEMM
+ * (TMA loads the weight tiles straight into the MMA layout; no decode): the UNet's attention
+ * projections, proj_in / proj_out and feed-forward (crates/sketchpad-unet/src/blocks.rs
+ * :213-231, :292-305, :446-458), which the reference runs as burn Linear matmuls.  x, W,
+ * bias, y bf16; K % 64 == 0, N % 16 == 0; 16-byte aligned.  _gated: y = residual + gate[n] *
+ * (x.W^T + bias[n]) (gate and residual may be NULL; residual may equal y: the UNet's
+ * in-place residual accumulation).  _glu: W's rows interleaved (first-half row j,
+ * second-half row j), y [M, N/2] = lo * gelu(hi) (SP_GLU_GEGLU, the UNet feed-forward) or
+ * silu(lo) * hi (SP_GLU_SWIGLU). */
+int sp_bf16_linear(const void* x, const void* w, const void* bias, void* y, int64_t M, int64_t N,
+                   int64_t K, int dtype, void* stream);
+int sp_bf16_linear_gated(const void* x, const void* w, const void* bias, const void* gate,
+                         const void* residual, void* y, int64_t M, int64_t N, int64_t K,
+                         int dtype, void* stream);
+int sp_bf16_linear_glu(const void* x, const void* w, const void* bias, void* y, int64_t M,
+                       int64_t N, int64_t K, int glu_kind, int dtype, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * FP8 (e4m3) weights with f32 scales (per output channel, or one per tensor).
  * The reference simulates FP8 in f32 (crates/sketchpad-core/src/quantization.rs:422-615);

@@ -40,6 +40,9 @@ SIGNATURES = {
                                  _i64, _i64p, _i64p, _i64p, _i64p, _int, _int, _int, _f, _vp]),
     "sp_flash_attn_fwd_wait_test": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int,
                                            _i64, _vp]),
+    "sp_bf16_linear": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "sp_bf16_linear_gated": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "sp_bf16_linear_glu": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp]),
     "sp_groupnorm_act_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64p, _i64, _int]),
     "sp_groupnorm_act_output_strides": (_int, [_i64, _i64, _i64, _i64, _i64p, _i64p]),
     "sp_model_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),

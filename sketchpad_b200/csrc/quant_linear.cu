@@ -34,7 +34,10 @@ constexpr int kWRawBytes = kQBN * kQBK;     // 16 KB
 constexpr int kScBytes = 2 * kQBN * 2;      // 1 KB: two k-blocks x 256 rows of f16
 constexpr int kWCvtBytes = kQBN * kQBK * 2; // 32 KB
 
-enum WFormat : int { W_Q8_0 = 0, W_FP8 = 1, W_Q4K = 2, W_Q2K = 3, W_Q3K = 4 };
+// W_BF16: plain bf16 weights (the UNet's projections and feed-forward), loaded by TMA straight
+// into the UMMA K-major 128B-swizzled layout -- no decode stage; the decoder warps only run the
+// epilogue, and each stage holds x and W tiles of 32 KB each.
+enum WFormat : int { W_Q8_0 = 0, W_FP8 = 1, W_Q4K = 2, W_Q2K = 3, W_Q3K = 4, W_BF16 = 5 };
 
 // K-quant formats: one 4-bit quant per value (32 bytes per row of a k-tile), f32 factors a, b
 // per sub-block of kSub values; w = a * (q - kOff) - b.
@@ -56,6 +59,17 @@ struct QlSmem {
   static constexpr int kSc = kWRaw + kRawStages * kWRawBytes;
   static constexpr int kWCvt = kSc + kRawStages * kScBytes;
   static constexpr int kBar = kWCvt + kCvtStages * kWCvtBytes;
+  static constexpr int kNumBars = 2 * kRawStages + 2 * kCvtStages + 1 + 1;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kAlloc = kMisc + 16 + 1024;
+};
+
+// W_BF16: kRawStages stages of {x tile, bf16 W tile} (192 KB)
+struct QlSmemBf16 {
+  static constexpr int kStage = kXBytes + kWCvtBytes;
+  static constexpr int kX = 0;
+  static constexpr int kW = kXBytes;
+  static constexpr int kBar = kRawStages * kStage;
   static constexpr int kNumBars = 2 * kRawStages + 2 * kCvtStages + 1 + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kAlloc = kMisc + 16 + 1024;
@@ -253,7 +267,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     qlinear_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                    const __grid_constant__ CUtensorMap tms, const __grid_constant__ CUtensorMap tmb,
                    const QlParams p) {
-  using L = QlSmem;
+  using L = typename std::conditional<WF == W_BF16, QlSmemBf16, QlSmem>::type;
   using KF = KqFmt<WF>;
   // K-quants: a raw stage holds the nibble tile, then factor arrays a and b
   static_assert(KF::kQBytes + 2 * KF::kFactorBytes <= kWRawBytes, "k-quant raw stage");
@@ -277,10 +291,12 @@ __global__ void __launch_bounds__(kQThreads, 1)
   const int kbase = (int)blockIdx.z * p.kt_per_split;
   const int ktiles = min((int)(p.K / kQBK) - kbase, p.kt_per_split);
 
+  constexpr bool kBf16 = WF == W_BF16;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRawStages; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], 1 + kQDecoders);  // MMA commit (x consumed) + decoders (raw W)
+      // MMA commit (x consumed) + decoders (raw W); bf16 weights: the MMA commit alone
+      mbar_init(&raw_empty[s], kBf16 ? 1 : 1 + kQDecoders);
     }
     for (int s = 0; s < kCvtStages; ++s) {
       mbar_init(&cvt_full[s], kQDecoders);
@@ -307,26 +323,34 @@ __global__ void __launch_bounds__(kQThreads, 1)
       if constexpr (WF == W_Q8_0 || KF::kIsK) tma_prefetch_desc(&tms);
       if constexpr (KF::kIsK) tma_prefetch_desc(&tmb);
       constexpr uint32_t kTx =
-          kXBytes + (KF::kIsK ? KF::kQBytes + 2 * KF::kFactorBytes
-                              : kWRawBytes + (WF == W_Q8_0 ? kScBytes : 0));
+          kBf16 ? kXBytes + kWCvtBytes
+                : kXBytes + (KF::kIsK ? KF::kQBytes + 2 * KF::kFactorBytes
+                                      : kWRawBytes + (WF == W_Q8_0 ? kScBytes : 0));
       int issued = 0;
       for (int kt = 0; kt < ktiles; ++kt) {
         const int st = kt % kRawStages;
         const uint32_t ph = (kt / kRawStages) & 1;
         if (kt >= kRawStages && !mbar_wait(&raw_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) break;
         mbar_arrive_expect_tx(&raw_full[st], kTx);
-        tma_load_2d(smem + L::kX + st * kXBytes, &tmx, &raw_full[st], (kbase + kt) * kQBK, m0);
+        if constexpr (kBf16) {
+          uint8_t* stage = smem + st * QlSmemBf16::kStage;
+          tma_load_2d(stage + QlSmemBf16::kX, &tmx, &raw_full[st], (kbase + kt) * kQBK, m0);
+          tma_load_2d(stage + QlSmemBf16::kW, &tmw, &raw_full[st], (kbase + kt) * kQBK, n0);
+          issued = kt + 1;
+          continue;
+        }
+        tma_load_2d(smem + QlSmem::kX + st * kXBytes, &tmx, &raw_full[st], (kbase + kt) * kQBK, m0);
         if constexpr (KF::kIsK) {
-          uint8_t* rw = smem + L::kWRaw + st * kWRawBytes;
+          uint8_t* rw = smem + QlSmem::kWRaw + st * kWRawBytes;
           tma_load_2d(rw, &tmw, &raw_full[st], (kbase + kt) * (kQBK / 2), n0);
           tma_load_2d(rw + KF::kQBytes, &tms, &raw_full[st], n0, (kbase + kt) * KF::kFactorRows);
           tma_load_2d(rw + KF::kQBytes + KF::kFactorBytes, &tmb, &raw_full[st], n0,
                       (kbase + kt) * KF::kFactorRows);
         } else {
-          tma_load_2d(smem + L::kWRaw + st * kWRawBytes, &tmw, &raw_full[st], (kbase + kt) * kQBK, n0);
+          tma_load_2d(smem + QlSmem::kWRaw + st * kWRawBytes, &tmw, &raw_full[st], (kbase + kt) * kQBK, n0);
         }
         if constexpr (WF == W_Q8_0)
-          tma_load_2d(smem + L::kSc + st * kScBytes, &tms, &raw_full[st], n0, (kbase + kt) * (kQBK / 32));
+          tma_load_2d(smem + QlSmem::kSc + st * kScBytes, &tms, &raw_full[st], n0, (kbase + kt) * (kQBK / 32));
         issued = kt + 1;
       }
       if (*abort_flag)
@@ -340,13 +364,20 @@ __global__ void __launch_bounds__(kQThreads, 1)
       for (int kt = 0; kt < ktiles; ++kt) {
         const int rs = kt % kRawStages, cs = kt % kCvtStages;
         if (!mbar_wait(&raw_full[rs], (kt / kRawStages) & 1, abort_flag, WD_MMA_WAIT) ||
-            !mbar_wait(&cvt_full[cs], (kt / kCvtStages) & 1, abort_flag, WD_MMA_WAIT)) {
+            (!kBf16 &&
+             !mbar_wait(&cvt_full[cs], (kt / kCvtStages) & 1, abort_flag, WD_MMA_WAIT))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t xa = smem_u32(smem + L::kX + rs * kXBytes);
-        const uint32_t wb = smem_u32(smem + L::kWCvt + cs * kWCvtBytes);
+        uint32_t xa, wb;
+        if constexpr (kBf16) {
+          xa = smem_u32(smem + rs * QlSmemBf16::kStage + QlSmemBf16::kX);
+          wb = smem_u32(smem + rs * QlSmemBf16::kStage + QlSmemBf16::kW);
+        } else {
+          xa = smem_u32(smem + QlSmem::kX + rs * kXBytes);
+          wb = smem_u32(smem + QlSmem::kWCvt + cs * kWCvtBytes);
+        }
 #pragma unroll
         for (int kk = 0; kk < kQBK / 16; ++kk) {
           const uint64_t b = make_smem_desc(wb + kk * 32, 16, 1024, LAYOUT_SW128);
@@ -357,7 +388,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
                   b, idesc, acc);
         }
         umma_commit(&raw_empty[rs]);
-        umma_commit(&cvt_empty[cs]);
+        if constexpr (!kBf16) umma_commit(&cvt_empty[cs]);
       }
       if (ok) umma_commit(acc_full);
       umma_commit(drain);
@@ -367,7 +398,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     // ------------------------------------------------------------ decoders
     const int t = threadIdx.x - kQFirstDecoderWarp * 32;  // 0..255
     bool ok = true;
-    for (int kt = 0; kt < ktiles; ++kt) {
+    for (int kt = 0; kt < (kBf16 ? 0 : ktiles); ++kt) {
       const int rs = kt % kRawStages, cs = kt % kCvtStages;
       if (!mbar_wait(&raw_full[rs], (kt / kRawStages) & 1, abort_flag, WD_CONVERT_WAIT)) {
         ok = false;
@@ -378,9 +409,9 @@ __global__ void __launch_bounds__(kQThreads, 1)
         ok = false;
         break;
       }
-      const uint8_t* raw = smem + L::kWRaw + rs * kWRawBytes;
-      const __half* sc = reinterpret_cast<const __half*>(smem + L::kSc + rs * kScBytes);
-      uint8_t* cvt = smem + L::kWCvt + cs * kWCvtBytes;
+      const uint8_t* raw = smem + QlSmem::kWRaw + rs * kWRawBytes;
+      const __half* sc = reinterpret_cast<const __half*>(smem + QlSmem::kSc + rs * kScBytes);
+      uint8_t* cvt = smem + QlSmem::kWCvt + cs * kWCvtBytes;
 #pragma unroll 2
       for (int it = 0; it < (kQBN * 4) / kQDecoders; ++it) {
         const int task = t + it * kQDecoders;
@@ -516,6 +547,14 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
     if (int rc = encode_tiled(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.kq_b, fdims, fstrides,
                               fbox, CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
+  } else if (WF == W_BF16) {
+    // bf16 W [N, K]: 64 x 256 boxes with the 128B swizzle, the MMA's K-major B layout
+    const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
+    const uint64_t strides[1] = {(uint64_t)p.K * 2};
+    const uint32_t box[2] = {kQBK, kQBN};
+    if (int rc = encode_tiled(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w8, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
   } else {
     const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
     const uint64_t strides[1] = {(uint64_t)p.K};
@@ -534,10 +573,12 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
       return rc;
   }
   auto kern = qlinear_kernel<WF>;
-  static_assert(QlSmem::kAlloc <= 232448, "quantized linear smem budget");
+  static_assert(QlSmem::kAlloc <= 232448 && QlSmemBf16::kAlloc <= 232448,
+                "quantized linear smem budget");
+  constexpr int kSmem = WF == W_BF16 ? QlSmemBf16::kAlloc : QlSmem::kAlloc;
   static unsigned long long attr_set = 0;
   if (first_time_on_device(&attr_set)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, QlSmem::kAlloc);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) {
       __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
       return set_error(SP_ERR_LAUNCH, "quantized linear: smem attribute failed: %s", cudaGetErrorString(e));
@@ -584,7 +625,7 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
   q.ws = static_cast<float*>(ws);
   q.splits = splits;
   dim3 grid((unsigned)tiles_m, (unsigned)tiles_n, (unsigned)splits);
-  kern<<<grid, kQThreads, QlSmem::kAlloc, s>>>(mx, mw, ms, mb, q);
+  kern<<<grid, kQThreads, kSmem, s>>>(mx, mw, ms, mb, q);
   if (splits > 1) {
     const int64_t groups = p.M * (p.N / 8);
     const unsigned rblocks = (unsigned)std::min<int64_t>((groups + 255) / 256, 8LL * sms);
@@ -629,7 +670,8 @@ int ql_entry(const char* what, const void* x, const void* w, const void* q8_scal
   clear_error();
   const bool have_scales = WF == W_Q8_0 ? q8_scale != nullptr
                            : WF == W_FP8 ? fp8_scale != nullptr
-                                         : (kq_a != nullptr && kq_b != nullptr);
+                           : WF == W_BF16 ? true
+                                          : (kq_a != nullptr && kq_b != nullptr);
   if (!x || !w || !have_scales || !y)
     return set_error(SP_ERR_INVALID_ARG, "%s: null pointer", what);
   if (KqFmt<WF>::kIsK && K % 256)
@@ -781,6 +823,27 @@ int sp_fp8_linear_rope(const void* x, const void* w_e4m3, const float* scale, in
       sp::roped(ldy, rope_cos_sin, rope_positions, rope_cols, head_dim, pos_offset, pos_div,
                 pos_mod),
       stream);
+}
+
+int sp_bf16_linear(const void* x, const void* w, const void* bias, void* y, int64_t M, int64_t N,
+                   int64_t K, int dtype, void* stream) {
+  return sp::ql_entry<sp::W_BF16>("bf16 linear", x, w, nullptr, nullptr, 0, bias, y, M, N, K,
+                                  dtype, sp::QlEpilogue{}, stream);
+}
+
+int sp_bf16_linear_gated(const void* x, const void* w, const void* bias, const void* gate,
+                         const void* residual, void* y, int64_t M, int64_t N, int64_t K,
+                         int dtype, void* stream) {
+  return sp::ql_entry<sp::W_BF16>("bf16 linear", x, w, nullptr, nullptr, 0, bias, y, M, N, K,
+                                  dtype, sp::gated(gate, residual), stream);
+}
+
+int sp_bf16_linear_glu(const void* x, const void* w, const void* bias, void* y, int64_t M,
+                       int64_t N, int64_t K, int glu_kind, int dtype, void* stream) {
+  sp::QlEpilogue e;
+  e.glu = glu_kind < 0 ? SP_GLU_SWIGLU + 1 : glu_kind;
+  return sp::ql_entry<sp::W_BF16>("bf16 linear", x, w, nullptr, nullptr, 0, bias, y, M, N, K,
+                                  dtype, e, stream);
 }
 
 }  // extern "C"
