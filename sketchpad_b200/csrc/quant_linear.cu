@@ -609,6 +609,14 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
         splits = sp;
       }
   }
+  // no stream-ordered scratch inside a CUDA-graph capture (a captured pool allocation would
+  // tie the graph to this pool): one split there
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (splits > 1 && (cudaStreamIsCapturing(s, &cap) != cudaSuccess ||
+                     cap != cudaStreamCaptureStatusNone)) {
+    cudaGetLastError();
+    splits = 1;
+  }
   void* ws = nullptr;
   if (splits > 1) {
     q.kt_per_split = (ktotal + splits - 1) / splits;

@@ -23,15 +23,18 @@ class Bf16Linear:
     """weight [out_features, in_features] bf16 (torch / GGUF row order; burn stores [in, out]
     and computes x @ W, the same product), optional bias [out_features]."""
 
-    def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor] = None):
+    def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                 dtype: torch.dtype = torch.bfloat16):
+        """dtype: the stored weight type; the GPU kernel takes bf16 (another dtype only serves
+        host-side stand-ins of the kernel, e.g. wiring tests)."""
         if weight.dim() != 2:
             raise ValueError("weight must be [out_features, in_features]")
-        self.weight = weight.to(torch.bfloat16).contiguous()
+        self.weight = weight.to(dtype).contiguous()
         self.out_features, self.in_features = self.weight.shape
         if self.in_features % 64 or self.out_features % 16:
             raise ValueError("in_features must be a multiple of 64 and out_features of 16")
         self.bias = None if bias is None else bias.reshape(-1).to(self.weight.device,
-                                                                  torch.bfloat16).contiguous()
+                                                                  dtype).contiguous()
 
     @classmethod
     def from_in_out(cls, w_kn: torch.Tensor, bias: Optional[torch.Tensor] = None) -> "Bf16Linear":
@@ -43,11 +46,12 @@ class Bf16Linear:
         """One layer whose rows interleave two halves (first j, second j): its `glu` forward
         gives lo * gelu(hi) / silu(lo) * hi without storing the [M, 2F] product."""
         b = None
+        dt = first.weight.dtype
         if first.bias is not None or second.bias is not None:
             z = lambda l: l.bias if l.bias is not None else torch.zeros(  # noqa: E731
-                l.out_features, dtype=torch.bfloat16, device=l.weight.device)
+                l.out_features, dtype=dt, device=l.weight.device)
             b = interleave_rows(z(first), z(second))
-        return cls(interleave_rows(first.weight, second.weight), b)
+        return cls(interleave_rows(first.weight, second.weight), b, dt)
 
     def forward(self, input: torch.Tensor, out: Optional[torch.Tensor] = None,
                 gate: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,

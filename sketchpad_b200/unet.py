@@ -33,6 +33,8 @@ from .groupnorm_silu import GroupNormSiLuOptions, groupnorm, groupnorm_silu
 from .glu import geglu
 from .residual import add_bias_residual
 from .layernorm import layer_norm
+from .linear import Bf16Linear
+from .quantized_matmul import GLU_GEGLU
 
 
 @dataclass(frozen=True)
@@ -323,19 +325,50 @@ class UNetB200:
                 self.p[st + ".proj_out.obias"] = (self.p[st + ".proj_out.bias"].float() +
                                                   acc @ wm).to(dtype)
         self.freqs = torch.from_numpy(timestep_freqs(cfg.model_channels)).to(self.device)
+        # every dense GEMM of the step on the library's tcgen05 kernel (bf16 weights [out,
+        # in], bias / in-place residual / GEGLU epilogues); torch matmuls elsewhere
+        self.sp_gemm = self.device.type == "cuda" and dtype == torch.bfloat16
+        self._lins: Dict[tuple, Bf16Linear] = {}
         self.kernel_launches = 0
         self.attn_events: list | None = None  # (start, end, flops) when timing attention
         self.attn_events_external = False     # record as graph nodes during a capture
 
     # -- ops ---------------------------------------------------------------------------------
+    def _gemm(self, wname, bname=None, glu=False):
+        """The Bf16Linear of weight p[wname] ([in, out], burn's layout) and bias p[bname];
+        glu: the layer's output columns [value | gate] as one row-interleaved GEGLU layer."""
+        key = (wname, bname, glu)
+        lin = self._lins.get(key)
+        if lin is None:
+            w = self.p[wname].t()
+            b = self.p.get(bname) if bname else None
+            if glu:
+                f = w.shape[0] // 2
+                lin = Bf16Linear.glu(Bf16Linear(w[:f], None if b is None else b[:f], self.dtype),
+                                     Bf16Linear(w[f:], None if b is None else b[f:], self.dtype))
+            else:
+                lin = Bf16Linear(w, b, self.dtype)
+            self._lins[key] = lin
+        return lin
+
     def _lin(self, x, name, bias=True, wkey=".weight", bkey=".bias"):
         w = self.p[name + wkey]
         b = self.p.get(name + bkey) if bias else None
+        if self.sp_gemm:
+            self.kernel_launches += 1
+            return self._gemm(name + wkey, (name + bkey) if b is not None else None).forward(x)
         if b is None:
             return torch.matmul(x, w)
         lead = x.shape[:-1]
         y = torch.addmm(b, x.reshape(-1, x.shape[-1]), w)  # bias fused into the GEMM epilogue
         return y.view(*lead, w.shape[1])
+
+    def _mm(self, x, wname):
+        """x @ p[wname] (no bias)."""
+        if self.sp_gemm:
+            self.kernel_launches += 1
+            return self._gemm(wname).forward(x)
+        return torch.matmul(x, self.p[wname])
 
     def _conv(self, x, name, stride=1, bias=True):
         w = self.p[name + ".weight"]
@@ -391,20 +424,24 @@ class UNetB200:
         b, s, _ = x.shape
         H, D = cfg.num_heads, cfg.head_dim
         if ctx is None:
-            qkv = torch.matmul(x, self.p[p + ".qkv"]).view(b, s, 3, H, D)
+            qkv = self._mm(x, p + ".qkv").view(b, s, 3, H, D)
             q, k, v = qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2), qkv[:, :, 2].transpose(1, 2)
         else:
-            q = torch.matmul(x, self.p[p + ".to_q.weight"]).view(b, s, H, D).transpose(1, 2)
+            q = self._mm(x, p + ".to_q.weight").view(b, s, H, D).transpose(1, 2)
             c = ctx.shape[1]
-            kv = torch.matmul(ctx, self.p[p + ".kv"]).view(b, c, 2, H, D)
+            kv = self._mm(ctx, p + ".kv").view(b, c, 2, H, D)
             k, v = kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2)
         o = torch.empty((b, s, H, D), dtype=x.dtype, device=x.device)
         self._attention(q, k, v, o.transpose(1, 2))  # written straight into [b, s, h, d]
         self._accumulate(resid, o.view(b * s, H * D), p + ".to_out")
 
     def _accumulate(self, resid, x2d, name):
-        """resid += x2d @ W (no bias; cuBLAS accumulates into resid in place)."""
+        """resid += x2d @ W (no bias), accumulated into resid in place by the GEMM epilogue."""
         r2d = resid.view(-1, resid.shape[-1])
+        if self.sp_gemm:
+            self.kernel_launches += 1
+            self._gemm(name + ".weight").forward(x2d, out=r2d, residual=r2d)
+            return
         torch.addmm(r2d, x2d, self.p[name + ".weight"], out=r2d)
 
     def _st(self, x, ctx, p):
@@ -419,9 +456,25 @@ class UNetB200:
             tb = f"{p}.tb{d}"
             self._xattn(self._ln(y, tb + ".norm1"), tb + ".attn1", None, y)
             self._xattn(self._ln(y, tb + ".norm2"), tb + ".attn2", ctx, y)
-            hdn = self._lin(self._ln(y, tb + ".norm3"), tb + ".ff.net_0")
+            xn = self._ln(y, tb + ".norm3")
+            if self.sp_gemm:  # GEGLU in the first FF GEMM's epilogue: no [M, 2F] product
+                self.kernel_launches += 1
+                g = self._gemm(tb + ".ff.net_0.weight", tb + ".ff.net_0.bias", glu=True)
+                hid = g.forward(xn, glu=GLU_GEGLU)
+            else:
+                self.kernel_launches += 1
+                hid = geglu(self._lin(xn, tb + ".ff.net_0"))
+            self._accumulate(y, hid.view(b * h * w, -1), tb + ".ff.net_2")
+        if self.sp_gemm:
+            # proj_out with its folded bias and the block's residual in the epilogue; NHWC
+            # memory is [b*h*w, c] rows for the input, the residual and the output alike
             self.kernel_launches += 1
-            self._accumulate(y, geglu(hdn).view(b * h * w, -1), tb + ".ff.net_2")
+            out = torch.empty((b, c, h, w), dtype=residual.dtype, device=residual.device,
+                              memory_format=torch.channels_last)
+            self._gemm(p + ".proj_out.wmat", p + ".proj_out.obias").forward(
+                y, out=out.permute(0, 2, 3, 1).view(b * h * w, c),
+                residual=residual.permute(0, 2, 3, 1).reshape(b * h * w, c))
+            return out
         yo = torch.matmul(y, self.p[p + ".proj_out.wmat"])  # [b, h*w, c] == NHWC memory
         self.kernel_launches += 1
         return add_bias_residual(yo.view(b, h, w, c).permute(0, 3, 1, 2),

@@ -27,7 +27,29 @@ def _ln(x, w, b, eps, unbiased, out=None, add=None):
     return (xf - xf.mean(-1, keepdim=True)) / torch.sqrt(xf.var(-1, keepdim=True, unbiased=unbiased) + eps) * w + b
 
 
-def test_unet_harness_wiring_matches_oracle(monkeypatch):
+def _bf16lin_forward(self, x, out=None, gate=None, residual=None, glu=None):
+    # Bf16Linear's epilogues in f32 torch: x W^T + b, then the row-interleaved GLU or
+    # residual + gate * (...), written into `out` when given
+    y = x.reshape(-1, self.in_features).float() @ self.weight.float().t()
+    if self.bias is not None:
+        y = y + self.bias.float()
+    if glu is not None:
+        y = y[:, 0::2] * F.gelu(y[:, 1::2])
+    else:
+        if gate is not None:
+            y = y * gate.float().reshape(-1)
+        if residual is not None:
+            y = y + residual.float().reshape(y.shape)
+    y = y.reshape(*x.shape[:-1], y.shape[-1])
+    return out.copy_(y.reshape(out.shape)) if out is not None else y
+
+
+@pytest.mark.parametrize("sp_gemm", [False, True])
+def test_unet_harness_wiring_matches_oracle(monkeypatch, sp_gemm):
+    # sp_gemm: the dense GEMMs through Bf16Linear and its epilogues (bias, in-place residual,
+    # GEGLU over row-interleaved weights, proj_out's folded bias + residual), as on the GPU
+    import sketchpad_b200.linear as LIN
+    monkeypatch.setattr(LIN.Bf16Linear, "forward", _bf16lin_forward)
     monkeypatch.setattr(U, "groupnorm_silu",
                         lambda x, w, b, opt, out=None, add=None: _gn(x, w, b, True, add))
     monkeypatch.setattr(U, "groupnorm", lambda x, w, b, opt, out=None: _gn(x, w, b, False))
@@ -43,6 +65,7 @@ def test_unet_harness_wiring_matches_oracle(monkeypatch):
     ctx = rng.standard_normal((2, 77, 768), dtype=np.float32)
     t = np.array([999.0, 999.0], np.float32)
     net = U.UNetB200(P, device="cpu", dtype=torch.float32)
+    net.sp_gemm = sp_gemm
     with torch.inference_mode():
         y = net(torch.from_numpy(x), torch.from_numpy(t), torch.from_numpy(ctx)).numpy()
     ref = OracleUNet(P)(x, t, ctx)
