@@ -43,7 +43,7 @@ enum WFormat : int { W_Q8_0 = 0, W_FP8 = 1, W_Q4K = 2, W_Q2K = 3, W_Q3K = 4, W_B
 // per sub-block of kSub values; w = a * (q - kOff) - b.
 template <int WF>
 struct KqFmt {
-  static constexpr bool kIsK = WF >= W_Q4K;
+  static constexpr bool kIsK = WF >= W_Q4K && WF <= W_Q3K;
   enum : int {
     kSub = WF == W_Q4K ? 32 : 16,
     kOff = WF == W_Q3K ? 4 : 0,
