@@ -3,10 +3,10 @@
 linears: bias, in-place residual accumulation (residual + gate * (x W^T + b)) and the
 GEGLU / SwiGLU gate over row-interleaved weights.
 
-The UNet harness uses it for every projection and feed-forward GEMM of the SD1.x step -- the
-burn Linear layers of crates/sketchpad-unet/src/blocks.rs:213-231, :292-305, :370-410,
-:446-458 -- so the step's matrix products run on this repository's kernels (the
-convolutions stay on cuDNN).
+UNetB200(gemm="sp") runs every projection and feed-forward GEMM of the SD1.x step on it --
+the burn Linear layers of crates/sketchpad-unet/src/blocks.rs:213-231, :292-305, :370-410,
+:446-458 (the step's default stays cuBLAS: the 256 x 256 tiles underfill the SMs on those
+small-K products).
 """
 from __future__ import annotations
 

@@ -265,7 +265,11 @@ class UNetB200:
     """The denoise step on the GPU: bf16 activations, sm_100a kernels on the hot path."""
 
     def __init__(self, params: Dict[str, np.ndarray], cfg: UNetConfig = UNetConfig(),
-                 device="cuda", dtype=torch.bfloat16):
+                 device="cuda", dtype=torch.bfloat16, gemm: str = "cublas"):
+        """gemm: "cublas" (torch matmuls) or "sp" (every dense GEMM on this library's tcgen05
+        kernel with fused epilogues; on B200 the 4.26 ms step took 6.70 ms that way -- the
+        kernel's 256 x 256 tiles leave most SMs idle on the step's K = 320 .. 1280,
+        N = 320 .. 2560 products -- so cuBLAS is the default)."""
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         self.specs, self.program = unet_plan(cfg)
         if self.device.type == "cuda":
@@ -325,9 +329,11 @@ class UNetB200:
                 self.p[st + ".proj_out.obias"] = (self.p[st + ".proj_out.bias"].float() +
                                                   acc @ wm).to(dtype)
         self.freqs = torch.from_numpy(timestep_freqs(cfg.model_channels)).to(self.device)
-        # every dense GEMM of the step on the library's tcgen05 kernel (bf16 weights [out,
-        # in], bias / in-place residual / GEGLU epilogues); torch matmuls elsewhere
-        self.sp_gemm = self.device.type == "cuda" and dtype == torch.bfloat16
+        # gemm == "sp": every dense GEMM on the library's tcgen05 kernel (bf16 weights [out,
+        # in], bias / in-place residual / GEGLU epilogues)
+        if gemm not in ("cublas", "sp"):
+            raise ValueError("gemm must be 'cublas' or 'sp'")
+        self.sp_gemm = gemm == "sp" and self.device.type == "cuda" and dtype == torch.bfloat16
         self._lins: Dict[tuple, Bf16Linear] = {}
         self.kernel_launches = 0
         self.attn_events: list | None = None  # (start, end, flops) when timing attention

@@ -21,12 +21,14 @@ def params():
     return make_unet_params(seed=0)
 
 
-def test_unet_step_matches_oracle(params):
+@pytest.mark.parametrize("gemm", ["cublas", "sp"])
+def test_unet_step_matches_oracle(params, gemm):
+    # gemm="sp": the step's dense GEMMs on this library's tcgen05 kernel (Bf16Linear)
     rng = np.random.default_rng(1)
     x = rng.standard_normal((2, 4, 64, 64), dtype=np.float32)
     ctx = rng.standard_normal((2, 77, 768), dtype=np.float32)
     t = np.array([999.0, 999.0], np.float32)
-    net = UNetB200(params)
+    net = UNetB200(params, gemm=gemm)
     with torch.inference_mode():
         y = net(torch.from_numpy(x).cuda(), torch.from_numpy(t).cuda(), torch.from_numpy(ctx).cuda())
     torch.cuda.synchronize()

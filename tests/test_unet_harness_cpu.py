@@ -65,7 +65,7 @@ def test_unet_harness_wiring_matches_oracle(monkeypatch, sp_gemm):
     ctx = rng.standard_normal((2, 77, 768), dtype=np.float32)
     t = np.array([999.0, 999.0], np.float32)
     net = U.UNetB200(P, device="cpu", dtype=torch.float32)
-    net.sp_gemm = sp_gemm
+    net.sp_gemm = sp_gemm  # the "sp" GEMM path's wiring, on the CPU stand-in above
     with torch.inference_mode():
         y = net(torch.from_numpy(x), torch.from_numpy(t), torch.from_numpy(ctx)).numpy()
     ref = OracleUNet(P)(x, t, ctx)
