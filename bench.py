@@ -576,9 +576,9 @@ def _case_denoise_loop(torch, kind, steps):
     return (lambda: loop(lat, cu, cc)), steps * unet_flops()["total"], "flop"
 
 
-def _case_unet_step(torch):
+def _case_unet_step(torch, gemm="cublas"):
     from sketchpad_b200.unet import UNetB200, make_unet_params, unet_flops
-    net = UNetB200(make_unet_params(device="cuda", seed=0), device="cuda")
+    net = UNetB200(make_unet_params(device="cuda", seed=0), device="cuda", gemm=gemm)
     g = torch.Generator(device="cuda").manual_seed(1)
     x = torch.randn(2, 4, 64, 64, device="cuda", generator=g)
     ctx = torch.randn(2, 77, 768, device="cuda", generator=g)
@@ -645,6 +645,7 @@ def _case_wan_step(torch):
 
 CASES = {
     "unet_step_eager": _case_unet_step,
+    "unet_step_eager_sp_gemm": lambda t: _case_unet_step(t, "sp"),
     "sd1x_ddim_loop_20": lambda t: _case_denoise_loop(t, "ddim", 20),
     "sd1x_dpmpp2m_loop_20": lambda t: _case_denoise_loop(t, "dpmpp_2m", 20),
     "flux_double_4096x512": lambda t: _case_flux_block(t, False),

@@ -142,7 +142,8 @@ int parse_gguf(ModelFile& f) {
     r.dims = rev;
     uint64_t elems = 1;
     for (int64_t d : r.dims) {
-      if (d <= 0) return set_error(SP_ERR_SHAPE, "GGUF tensor '%s': bad dimension", r.name.c_str());
+      if (d <= 0 || (uint64_t)d > (1ull << 40) || elems > (1ull << 40) / (uint64_t)d)
+        return set_error(SP_ERR_SHAPE, "GGUF tensor '%s': bad dimension", r.name.c_str());
       elems *= (uint64_t)d;
     }
     if (elems % (uint64_t)be) return set_error(SP_ERR_SHAPE, "GGUF tensor '%s': %llu elements are "
@@ -157,8 +158,11 @@ int parse_gguf(ModelFile& f) {
   const uint64_t base = (c.pos + 31) & ~uint64_t(31);
   for (size_t i = 0; i < f.tensors.size(); ++i) {
     TensorRec& r = f.tensors[i];
+    if (base > f.size || rel[i] > f.size - base)
+      return set_error(SP_ERR_SHAPE, "GGUF tensor '%s' starts past the end of the file",
+                       r.name.c_str());
     r.offset = base + rel[i];
-    if (r.offset > f.size || r.nbytes > f.size - r.offset)
+    if (r.nbytes > f.size - r.offset)
       return set_error(SP_ERR_SHAPE, "GGUF tensor '%s' runs past the end of the file",
                        r.name.c_str());
   }
@@ -207,9 +211,17 @@ struct JsonReader {
           case 'r': ch = '\r'; break;
           case 'b': ch = '\b'; break;
           case 'f': ch = '\f'; break;
-          case 'u': {  // keep \uXXXX as UTF-8 for code points < 0x800 (names are ASCII)
+          case 'u': {  // \uXXXX as UTF-8 (tensor names are ASCII in practice)
             if (n - i < 4) { ok = false; return out; }
-            const unsigned cp = (unsigned)std::stoul(std::string(s + i, 4), nullptr, 16);
+            unsigned cp = 0;
+            for (int h = 0; h < 4; ++h) {  // no exceptions may leave this library
+              const char d = s[i + h];
+              const int v = d >= '0' && d <= '9' ? d - '0'
+                            : d >= 'a' && d <= 'f' ? d - 'a' + 10
+                            : d >= 'A' && d <= 'F' ? d - 'A' + 10 : -1;
+              if (v < 0) { ok = false; return out; }
+              cp = cp * 16 + (unsigned)v;
+            }
             i += 4;
             if (cp < 0x80) { out += (char)cp; }
             else if (cp < 0x800) { out += (char)(0xC0 | (cp >> 6)); out += (char)(0x80 | (cp & 0x3F)); }
@@ -330,13 +342,20 @@ int parse_safetensors(ModelFile& f) {
     uint64_t elems = 1;
     if (sh->arr.size() > 8)
       return set_error(SP_ERR_SHAPE, "safetensors tensor '%s': rank above 8", r.name.c_str());
+    auto whole = [](const Json& v) {  // a non-negative integer JSON number below 2^53
+      return v.kind == Json::Num && v.num >= 0 && v.num < 9007199254740992.0 &&
+             v.num == (double)(uint64_t)v.num;
+    };
     for (const Json& d : sh->arr) {
-      if (d.kind != Json::Num || d.num < 0) return set_error(SP_ERR_SHAPE, "bad shape");
+      if (!whole(d) || d.num > (double)(1ull << 40) || elems > (1ull << 40) / ((uint64_t)d.num + 1))
+        return set_error(SP_ERR_SHAPE, "safetensors tensor '%s': bad shape", r.name.c_str());
       r.dims.push_back((int64_t)d.num);
       elems *= (uint64_t)d.num;
     }
+    if (!whole(off->arr[0]) || !whole(off->arr[1]))
+      return set_error(SP_ERR_SHAPE, "safetensors tensor '%s': bad data_offsets", r.name.c_str());
     const uint64_t b = (uint64_t)off->arr[0].num, e = (uint64_t)off->arr[1].num;
-    if (e < b || e - b != elems * (uint64_t)es || base + e > f.size)
+    if (e < b || e - b != elems * (uint64_t)es || e > f.size - base)
       return set_error(SP_ERR_SHAPE, "safetensors tensor '%s': offsets [%llu, %llu) do not match "
                        "its shape or the file", r.name.c_str(), (unsigned long long)b,
                        (unsigned long long)e);
@@ -376,7 +395,12 @@ int sp_model_open(const char* path, void** file_out) {
   uint32_t magic = 0;
   if (f->size >= 4) std::memcpy(&magic, f->map, 4);
   f->container = magic == 0x46554747u ? SP_CONTAINER_GGUF : SP_CONTAINER_SAFETENSORS;
-  const int rc = f->container == SP_CONTAINER_GGUF ? parse_gguf(*f) : parse_safetensors(*f);
+  int rc;
+  try {  // nothing may throw across the C ABI (allocation failure on a hostile header)
+    rc = f->container == SP_CONTAINER_GGUF ? parse_gguf(*f) : parse_safetensors(*f);
+  } catch (...) {
+    rc = set_error(SP_ERR_INVALID_ARG, "'%s' could not be parsed", path);
+  }
   if (rc != SP_OK) {
     delete f;
     return rc;
