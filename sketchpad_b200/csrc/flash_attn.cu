@@ -361,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(r[q][c]));
         mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
-      const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl2;
+      const float m_tile = mx == -INFINITY ? -INFINITY : __fmul_rn(mx, sl2);
       const float m_new = fmaxf(m_run, m_tile);
       bool rescale = false;
       float m_use = m_run;
@@ -394,23 +394,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // exp2 (MUFU), row sum, 16-bit P (column c holds keys 2c, 2c+1); -inf scores of
       // masked tiles give exactly 0.  x = s * scale - m_ref is one fused multiply-add while
-      // m_ref is the ROUNDED product max * scale, so the row maximum's x can exceed 0 by half
-      // an ulp of m_ref: harmless for ordinary logits, but past |m_ref| ~ 2^24 that is more
-      // than 1, and with logits of 1e13 and up (activations in the millions) ex2 overflows to
-      // inf.  Rows with such a reference clamp x at 0 (their maximum's true value).
+      // m_ref is the ROUNDED product max * scale, so the row maximum's x is off by up to half
+      // an ulp of m_ref either way: harmless for ordinary logits, but past |m_ref| ~ 2^24 that
+      // is more than 1 -- with logits of 1e11 and up (activations in the millions) ex2
+      // overflows to inf or the maximum's P underflows to 0.  Warps with such a reference
+      // form x = fl(s * scale) - m_ref from separately rounded operations: exactly 0 for the
+      // maximum (rounded like m_ref), <= 0 for every other key.
       float rs0 = 0.f, rs1 = 0.f;
       uint32_t pk[4][16];
-      auto exps = [&](auto clamp) {
-        constexpr bool kClamp = decltype(clamp)::value;
+      auto exps = [&](auto exact) {
+        constexpr bool kExact = decltype(exact)::value;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
 #pragma unroll
           for (int u = 0; u < 16; ++u) {
-            float x0 = fmaf(__uint_as_float(r[q][2 * u]), sl2, -m_ref);
-            float x1 = fmaf(__uint_as_float(r[q][2 * u + 1]), sl2, -m_ref);
-            if constexpr (kClamp) {
-              x0 = fminf(x0, 0.f);
-              x1 = fminf(x1, 0.f);
+            float x0, x1;
+            if constexpr (kExact) {
+              x0 = __fsub_rn(__fmul_rn(__uint_as_float(r[q][2 * u]), sl2), m_ref);
+              x1 = __fsub_rn(__fmul_rn(__uint_as_float(r[q][2 * u + 1]), sl2), m_ref);
+            } else {
+              x0 = fmaf(__uint_as_float(r[q][2 * u]), sl2, -m_ref);
+              x1 = fmaf(__uint_as_float(r[q][2 * u + 1]), sl2, -m_ref);
             }
             const float e0 = ex2_approx(x0), e1 = ex2_approx(x1);
             rs0 += e0;
