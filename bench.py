@@ -671,6 +671,9 @@ CASES = {
     "q4_k_4608x12288x3072": lambda t: _case_kquant(t, "Q4K", 4608, 12288, 3072),
     "q8_0_4608x12288x3072": lambda t: _case_q8(t, 4608, 12288, 3072),
     "fp8_8192x13824x5120": lambda t: _case_fp8(t, 8192, 13824, 5120),
+    # the Wan block's widest GEMMs at 75,600 tokens: fused q/k/v and the feed-forward down
+    "fp8_75600x15360x5120": lambda t: _case_fp8(t, 75600, 15360, 5120),
+    "fp8_75600x5120x13824": lambda t: _case_fp8(t, 75600, 5120, 13824),
 }
 
 

@@ -94,7 +94,7 @@ struct QlParams {
   const float2* rope;             // [positions, head_dim / 2] or null
   int64_t rope_off, rope_div, rope_mod;
   int rope_cols, rope_half;
-  // split-K (grid.z = splits > 1): CTA z sums k-tiles [z * kt_per_split, ...) and writes its
+  // split-K (grid.y = splits > 1): CTA z sums k-tiles [z * kt_per_split, ...) and writes its
   // raw f32 partial to ws[z][M][N]; a reduce pass sums them in order and runs the epilogue
   float* ws;
   int splits, kt_per_split;
@@ -105,7 +105,25 @@ struct QlParams {
   // y's element type for the plain / rope epilogue: 0 bf16, 1 f16 (the attention inputs of
   // long-sequence DiTs, where f16's 3 extra mantissa bits shrink the logit error 8x)
   int y_f16;
+  // tile raster: grid.x walks tiles_m x tiles_n in groups of `group` tiles along one axis
+  // (raster_n 0: groups of m-tiles, m fastest inside a group, so the group's x rows stay in
+  // L2 while W streams past them; 1: groups of n-tiles, n fastest, W held and x streamed)
+  int tiles_m, tiles_n, group, raster_n;
 };
+
+// (m-tile, n-tile) of linear tile t under the grouped raster above
+__device__ __forceinline__ void ql_tile_of(const QlParams& p, int t, int& mt, int& nt) {
+  const int outer = p.raster_n ? p.tiles_n : p.tiles_m;  // grouped axis
+  const int inner = p.raster_n ? p.tiles_m : p.tiles_n;
+  const int per_group = p.group * inner;
+  const int g = t / per_group;
+  const int first = g * p.group;
+  const int width = min(outer - first, p.group);
+  const int r = t - g * per_group;
+  const int a = first + r % width, b = r / width;
+  mt = p.raster_n ? b : a;
+  nt = p.raster_n ? a : b;
+}
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
@@ -285,10 +303,12 @@ __global__ void __launch_bounds__(kQThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kQBM;
-  const int n0 = blockIdx.y * kQBN;
+  int mtile, ntile;
+  ql_tile_of(p, (int)blockIdx.x, mtile, ntile);
+  const int m0 = mtile * kQBM;
+  const int n0 = ntile * kQBN;
   // this CTA's k-tiles (all of them without split-K); kt below counts from 0
-  const int kbase = (int)blockIdx.z * p.kt_per_split;
+  const int kbase = (int)blockIdx.y * p.kt_per_split;
   const int ktiles = min((int)(p.K / kQBK) - kbase, p.kt_per_split);
 
   constexpr bool kBf16 = WF == W_BF16;
@@ -475,7 +495,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
         const int64_t nb = n0 + c;
         if (nb >= p.N) continue;
         if (p.splits > 1) {  // raw partial sums; the reduce pass applies the epilogue
-          float* wdst = p.ws + ((int64_t)blockIdx.z * p.M + m) * p.N + nb;
+          float* wdst = p.ws + ((int64_t)blockIdx.y * p.M + m) * p.N + nb;
 #pragma unroll
           for (int g = 0; g < 32; g += 8) {
             if (nb + g >= p.N) break;  // N % 16 == 0, so groups of 8 are whole
@@ -507,6 +527,52 @@ __global__ void __launch_bounds__(kQThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+// Bytes of one weight row of K values as the kernel reads them (values + scales / factors).
+template <int WF>
+double ql_w_row_bytes(int64_t K) {
+  switch (WF) {
+    case W_Q8_0: return K * (1.0 + 2.0 / 32);  // int8 + an f16 scale per 32
+    case W_Q4K: return K * (0.5 + 8.0 / 32);   // nibbles + f32 (a, b) per 32
+    case W_Q2K:
+    case W_Q3K: return K * (0.5 + 8.0 / 16);   // nibbles + f32 (a, b) per 16
+    case W_BF16: return K * 2.0;
+    default: return (double)K;                 // e4m3
+  }
+}
+
+#ifndef SP_QL_HOLD_MB
+#define SP_QL_HOLD_MB 40
+#endif
+
+// Grouped tile raster.  The x row-tiles and W column-tiles a wave of CTAs touches come from
+// HBM once if they stay in L2 until their last reader; the plain m-fastest order walks all of x
+// for each W column, so a large x (75,600 x 5120 bf16 = 774 MB for a video DiT) is re-read once
+// per N tile.  Grouping g tiles of one operand, with the other operand's tiles innermost, holds
+// that group (g x tile bytes) in L2 while the other operand streams past it once per group:
+//   groups of m-tiles: traffic = X + W * ceil(tiles_m / g)
+//   groups of n-tiles: traffic = W + X * ceil(tiles_n / g)
+// The orientation with the smaller modelled traffic wins, g as large as the hold budget allows
+// (then evened out over the passes it implies).
+template <int WF>
+void ql_raster(QlParams& q, int tiles_m, int tiles_n) {
+  const double hold = SP_QL_HOLD_MB * 1048576.0;
+  const double xt = (double)kQBM * q.K * 2, wt = (double)kQBN * ql_w_row_bytes<WF>(q.K);
+  const double X = xt * tiles_m, W = wt * tiles_n;
+  auto plan = [&](int tiles, double tile_bytes, int& g) {
+    g = std::max(1, std::min(tiles, (int)(hold / tile_bytes)));
+    const int passes = (tiles + g - 1) / g;
+    g = (tiles + passes - 1) / passes;
+    return passes;
+  };
+  int gm, gn;
+  const double tm = X + W * plan(tiles_m, xt, gm);
+  const double tn = W + X * plan(tiles_n, wt, gn);
+  q.tiles_m = tiles_m;
+  q.tiles_n = tiles_n;
+  q.raster_n = tn < tm ? 1 : 0;
+  q.group = q.raster_n ? gn : gm;
 }
 
 template <int WF>
@@ -632,7 +698,8 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
   }
   q.ws = static_cast<float*>(ws);
   q.splits = splits;
-  dim3 grid((unsigned)tiles_m, (unsigned)tiles_n, (unsigned)splits);
+  ql_raster<WF>(q, tiles_m, tiles_n);
+  dim3 grid((unsigned)tiles, (unsigned)splits);
   kern<<<grid, kQThreads, kSmem, s>>>(mx, mw, ms, mb, q);
   if (splits > 1) {
     const int64_t groups = p.M * (p.N / 8);
