@@ -94,10 +94,12 @@ int sp_flash_attn_fwd_wait_test(const void* q, const void* k, const void* v, voi
  *   gamma, beta [C]; x, y, gamma, beta all of `dtype` (SP_F32, SP_F16, SP_BF16).
  *   act: SP_ACT_SILU (groupnorm_silu) or SP_ACT_NONE (groupnorm).
  *   Returns SP_ERR_SHAPE when C % groups != 0 (the reference panics there).
- * workspace: channels-last inputs, other strided inputs and NCHW groups larger than one
- *   thread-block cluster can hold on chip use two-kernel paths that need device workspace;
- *   sp_groupnorm_act_workspace_size() returns its size, or 0 when x and y are 16-byte aligned
- *   and the single-pass NCHW path applies (workspace may then be NULL).
+ * workspace: NCHW groups of 256 KB and more take the streaming path, which keeps per-slice
+ *   statistics in device workspace (16 bytes per 32 KB slice plus 4 bytes per group, zeroed
+ *   by the call itself); channels-last and other strided inputs use two-kernel paths that
+ *   need workspace too.  sp_groupnorm_act_workspace_size() returns its size, or 0 when x and
+ *   y are 16-byte aligned and the single-pass on-chip NCHW path applies (workspace may then
+ *   be NULL).  Workspace must be 16-byte aligned and not in use by another call in flight.
  * ------------------------------------------------------------------------------------ */
 size_t sp_groupnorm_act_workspace_size(int64_t B, int64_t C, int64_t H, int64_t W,
                                        const int64_t x_strides[4], int64_t groups, int dtype);

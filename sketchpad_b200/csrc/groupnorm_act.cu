@@ -6,15 +6,22 @@
 // Replaces the reference's two-kernel GPU path (groupnorm_silu.rs:64-211), whose statistics
 // kernel runs one thread per (batch, group).
 //
-// Fast path (contiguous x): ONE read and ONE write of HBM.  A (batch, group) is split over a
+// Fast path (contiguous x, groups below 256 KB): ONE read and ONE write of HBM.  A (batch,
+// group) is split over a
 // thread-block cluster of CS CTAs (CS <= 16); each CTA keeps its slice in registers (16-byte
 // vector loads), the cluster reduces the sum and then the centred sum of squares through
 // distributed shared memory, and every CTA normalises its slice straight from registers.
 //
-// General path (strided x, or a group larger than a 16-CTA cluster holds): two kernels.
-// Pass 1 writes per-chunk (count, mean, M2) partials to a caller workspace; pass 2 merges
-// its group's partials (Chan et al.'s pairwise update) and normalises (x is read twice).
+// Streaming path (contiguous x, groups of 256 KB and more): a persistent grid of slice units
+// (statistics of a slice, then normalisation of it once its group's statistics are known);
+// x is read once from HBM and once more from L2, y written once.  Described at
+// gn_slice_kernel.
+//
+// General path (strided x): two kernels.  Pass 1 writes per-chunk (count, mean, M2) partials
+// to a caller workspace; pass 2 merges its group's partials (Chan et al.'s pairwise update)
+// and normalises (x is read twice).
 #include <algorithm>
+#include <type_traits>
 
 #include <cooperative_groups.h>
 
@@ -84,9 +91,18 @@ __device__ __forceinline__ uint4 pack(const float* f) {
     u.z = __float_as_uint(f[2]);
     u.w = __float_as_uint(f[3]);
   } else {
-    T* h = reinterpret_cast<T*>(&u);
+    // two lanes per conversion (cvt.rn.{f16x2,bf16x2}.f32), same rounding as one at a time
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) h[i] = from_f32<T>(f[i]);
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (std::is_same<T, __half>::value) {
+        const __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      } else {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+    }
   }
   return u;
 }
@@ -125,7 +141,6 @@ __device__ __forceinline__ float block_sum(float v, float* scratch /* >= 32 floa
 }
 
 struct GnParams {
-  int resident;  // streaming path: the slice stays in shared memory between the passes
   const void* x;
   const void* gamma;
   const void* beta;
@@ -226,33 +241,36 @@ __global__ void __launch_bounds__(kGnThreads, 2) gn_cluster_kernel(GnParams p) {
 }
 
 // ---------------------------------------------------------------------------------------
-// Streaming path for large contiguous groups (hundreds of KB and up).  Holding such a group
-// in registers takes a 16-CTA cluster per group, few of which fit on the GPU at once, and
-// each serialises load -> reduce -> store.  Here a persistent cluster of CS CTAs owns a
-// sequence of (batch, group)s; each CTA owns one contiguous slice of every group.
-//   warp 8 (producers): bulk-copies the slice into shared memory twice per group: lane 0
-//     through ring A from HBM (L2 evict-last), lane 1 through ring B from L2 (evict-first);
-//     each runs ahead across groups as far as its ring allows.
-//   warps 0-7 (consumers): pass 1 forms per-thread (count, mean, M2) of clamp(x) from sums
-//     shifted by the thread's first value, and max |x|; the partials merge (Chan et al.)
-//     over the warps, then every CTA pushes its partial into every cluster peer's shared
-//     memory and arrives on the peer's mbarrier; each CTA merges the CS partials in rank
-//     order (so all agree on mean and rstd) and tabulates gamma_c * rstd, beta_c for the
-//     group's channels.  Pass 2 normalises, applies the affine map and SiLU (packed f32x2
-//     arithmetic, and no clamps when max |x| and the affine bound show none can bite), and
-//     stores.
-// HBM sees one read and one write of x.
+// Streaming path for large contiguous groups (hundreds of KB and up): a persistent,
+// cooperatively launched grid walks one fixed sequence of slice units.  A group is cut into
+// S slices of kSlBytes.  Unit (pass 0, g, s) reads slice s of group g from HBM once and writes
+// its (count, mean, M2, max |x|) partial to global memory; unit (pass 1, g, s) merges the S
+// partials of g in slice order (so every slice of a group gets the same mean and rstd),
+// re-reads the slice (from L2) and writes the normalised, activated output.  The sequence
+// interleaves pass 0 of group t with pass 1 of group t - L:
+//   * a pass-1 unit depends only on units earlier in the sequence, and every CTA is resident
+//     (cooperative launch) and takes its units in sequence order, so each of its waits ends;
+//   * with L about two grid-widths of units, the partials are normally complete before a
+//     pass-1 unit starts, and the L groups in between (~20 MB) still sit in L2;
+//   * units are small and equal, so every CTA gets the same share of the work whatever the
+//     number of groups (a CTA per group, or a cluster per group, leaves the last wave ragged).
+// Unit k of CTA c is sequence entry c + k * gridDim.x.
+//   warp 8, lane 0 (producer): bulk-copies the CTA's next units into a kSlStages ring.
+//   warps 0-7 (consumers): pass 0 forms per-thread (count, mean, M2) of clamp(x) from sums
+//     shifted by the thread's first value, and max |x|, merged (Chan et al.) over the warps;
+//     pass 1 normalises, applies the affine map and SiLU (packed f32x2 arithmetic, and no
+//     clamps when max |x| and the affine bound show none can bite), and stores.
+// HBM sees one read and one write of x, plus 16 bytes of partial per slice.
 // ---------------------------------------------------------------------------------------
-constexpr int kGrConsumers = 256;
-constexpr int kGrThreads = kGrConsumers + 32;
-constexpr int kGrChunk = 32768;  // bytes per ring stage
-// Two rings: A carries pass-1 chunks (from HBM), B pass-2 chunks (from L2), so the HBM
-// stream of the next group's pass 1 never waits behind the current group's pass 2.
-constexpr int kGrStagesA = 2;
-constexpr int kGrStagesB = 1;
-constexpr int kGrStages = kGrStagesA + kGrStagesB;  // 96 KB: two CTAs per SM
-constexpr int kGrMaxCluster = 16;
-constexpr int kGrMaxCg = 1024;   // channels per group the shared affine table holds
+constexpr int kSlConsumers = 256;                 // warps 0-7
+constexpr int kSlProducerWarp = kSlConsumers / 32;  // warp 8
+constexpr int kSlPublisherWarp = kSlProducerWarp + 1;
+constexpr int kSlStatsWarp = kSlProducerWarp + 2;
+constexpr int kSlThreads = kSlConsumers + 3 * 32;
+constexpr int kSlEmptyCount = kSlConsumers / 32 + 2;  // consumer warps, publisher, stats
+constexpr int kSlBytes = 32768;  // one slice unit
+constexpr int kSlStages = 3;     // 96 KB: two CTAs per SM
+constexpr int kSlMaxCg = 1024;   // channels per group the shared affine table holds
 
 struct Welford {
   float n, mean, m2;
@@ -316,229 +334,314 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
-__device__ __forceinline__ uint32_t map_rank(const void* p, int rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-  return r;
+// pass-0 partials: published with a release add on the group's counter, read after an
+// acquire load of it
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-
-__device__ __forceinline__ void arrive_cluster(uint32_t bar_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_addr)
-               : "memory");
-}
-
-// bounded wait with cluster-scope acquire (the arrivals come from peer CTAs)
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
-                                                  volatile int* abort) {
+// Bounded mbarrier wait that parks the warp (try_wait with a suspend-time hint) instead of
+// spinning: the streaming kernel's helper warps wait most of the time, and spinning would
+// take issue slots from the consumer warps on the same scheduler.
+__device__ __forceinline__ bool sl_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                        int code) {
   const long long t0 = clock64();
-  uint32_t spins = 0;
   while (true) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
         : "memory");
     if (ok) return true;
-    if ((++spins & 255u) == 0) {
-      if (*abort) return false;
-      if (clock64() - t0 > kWaitBudgetCycles) {
-        atomicCAS(&g_watchdog, 0, WD_CLUSTER_WAIT);
-        *abort = 1;
-        return false;
-      }
+    if (abort && *abort) return false;
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      atomicCAS(&g_watchdog, 0, code);
+      if (abort) *abort = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ bool sl_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                             int code) {
+  return __all_sync(0xffffffffu, sl_wait(bar, parity, abort, code));
+}
+
+// Bounded wait until *ready >= want (set by other CTAs of the same launch).
+__device__ __forceinline__ bool wait_ready(const unsigned* ready, unsigned want,
+                                           volatile int* abort) {
+  if (ld_acquire(ready) >= want) return true;
+  const long long t0 = clock64();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire(ready) >= want) return true;
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      atomicCAS(&g_watchdog, 0, WD_FLAG_WAIT);
+      *abort = 1;
+      return false;
     }
   }
 }
 
-__device__ __forceinline__ void consumer_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kGrConsumers) : "memory");
+struct GnSliceParams {
+  const void* x;
+  const void* gamma;
+  const void* beta;
+  void* y;
+  int64_t C, HW, G, cg;  // channels, H*W, groups, channels per group
+  int64_t n;             // elements per group = cg * HW
+  int64_t BG;            // batch * groups
+  int64_t S, L;          // slices per group; pass-1 lag in groups (1 <= L <= BG)
+  unsigned* ready;       // [BG] pass-0 slices finished (zero before the launch)
+  float4* part;          // [BG][S] (count, mean, M2, max |x|)
+  float eps;
+  int act;
+};
+
+struct SlUnit {
+  int pass;
+  int64_t g, s;
+};
+
+// Sequence entry u: L*S pass-0 units of groups [0, L); then per t in [L, BG) the S pass-0
+// units of group t followed by the S pass-1 units of group t - L; then the pass-1 units of
+// groups [BG - L, BG).
+__device__ __forceinline__ SlUnit sl_unit(const GnSliceParams& p, int64_t u) {
+  const int64_t S = p.S, L = p.L, head = L * S, mid = 2 * S * (p.BG - L);
+  SlUnit r;
+  if (u < head) {
+    r.pass = 0;
+    r.g = u / S;
+    r.s = u - r.g * S;
+  } else if (u < head + mid) {
+    const int64_t v = u - head, t = L + v / (2 * S), w = v - (t - L) * 2 * S;
+    r.pass = w < S ? 0 : 1;
+    r.g = w < S ? t : t - L;
+    r.s = w < S ? w : w - S;
+  } else {
+    const int64_t v = u - head - mid;
+    r.pass = 1;
+    r.g = p.BG - L + v / S;
+    r.s = v % S;
+  }
+  return r;
 }
 
-// grid = (n_clusters * CS), cluster = (CS, 1, 1), kGrThreads threads, dynamic smem =
-// kGrStages * kGrChunk (+ alignment).  x, y contiguous NCHW, HW % VE == 0, 16-B aligned.
-// p.chunk_vecs = vectors per CTA slice.
+// grid = resident CTAs (cooperative), kSlThreads threads, dynamic smem kSlStages * kSlBytes
+// (+ alignment).  x, y contiguous NCHW, HW % VE == 0, 16-B aligned.
+//
+// Per ring stage st, for the unit k the stage holds (k % kSlStages == st):
+//   full[st]       the slice landed (producer's bulk copy)
+//   empty[st]      the 8 consumer warps, the publisher and the statistics warp are done
+//                  with it (kSlEmptyCount)
+//   part_full[st]  pass 0: the 8 consumer warps wrote their partials to wpart[st]
+//   stat_full[st]  pass 1: the statistics warp wrote the group's stats to gstat[st]
+// part_full and stat_full complete once per pass-0 (pass-1) unit of the stage, so their
+// waiters track the phase parity per stage.  Every role that waits on full[st] also arrives on
+// empty[st] for every unit: the producer cannot refill a stage before each of them has seen
+// the unit, so none of them can be a whole ring cycle ahead of or behind a barrier's phase
+// (a parity wait would then match the wrong phase).
 template <typename T>
-__global__ void __launch_bounds__(kGrThreads, 2) gn_ring_kernel(GnParams p, int64_t BG) {
+__global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p) {
   constexpr int VE = VecTraits<T>::kElems;
-  constexpr int kCWarps = kGrConsumers / 32;
-  extern __shared__ uint8_t gr_smem_raw[];
-  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gr_smem_raw) + 127) &
+  constexpr int kCWarps = kSlConsumers / 32;
+  constexpr int64_t kSv = kSlBytes / 16;  // 16-byte vectors per slice
+  extern __shared__ uint8_t sl_smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sl_smem_raw) + 127) &
                                              ~uintptr_t(127));
-  __shared__ uint64_t full[kGrStages], empty[kGrStages], stats_bar[2];  // A stages first
-  // partials (n, mean, M2, max|x|) pushed by every rank, per parity
-  __shared__ float slot[2][kGrMaxCluster][4];
-  __shared__ Welford wpart[kCWarps];
-  __shared__ float wamax[kCWarps];
-  __shared__ float2 aff[kGrMaxCg];  // this group's (gamma_c * rstd, beta_c)
-  __shared__ float gb_max[2];       // max |gamma|, max |beta| over all channels
+  __shared__ uint64_t full[kSlStages], empty[kSlStages], part_full[kSlStages],
+      stat_full[kSlStages];
+  __shared__ float4 wpart[kSlStages][kCWarps];  // (count, mean, M2, max |x|) per consumer warp
+  __shared__ float4 gstat[kSlStages];           // (mean, rstd, max |x|, no_clamp)
   __shared__ int abort_flag_s;
   volatile int* abort_flag = &abort_flag_s;
-
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = (int)cluster.block_rank();
-  const int cs = (int)cluster.num_blocks();
-  const int64_t cid = blockIdx.x / cs, ncl = gridDim.x / cs;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t total = 2 * p.BG * p.S;
+  const int64_t nvec = p.n / VE;
+  const T* gam = static_cast<const T*>(p.gamma);
+  const T* bet = static_cast<const T*>(p.beta);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kGrStages; ++i) {
+    for (int i = 0; i < kSlStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kCWarps);
+      mbar_init(&empty[i], kSlEmptyCount);
+      mbar_init(&part_full[i], kCWarps);
+      mbar_init(&stat_full[i], 1);
     }
-    mbar_init(&stats_bar[0], cs);
-    mbar_init(&stats_bar[1], cs);
     abort_flag_s = 0;
     fence_mbar_init();
   }
-  // peers arrive on these barriers: they must be initialised cluster-wide first
-  cluster.sync();
+  __syncthreads();
 
-  // n < 2^31 on this path: slice indices fit 32 bits
-  const int nvec = (int)(p.n / VE);
-  const int v0 = min(nvec, rank * (int)p.chunk_vecs);
-  const int v1 = min(nvec, v0 + (int)p.chunk_vecs);
-  const uint32_t slice_bytes = (uint32_t)(v1 - v0) * 16u;
-  const uint32_t nchunks = (slice_bytes + kGrChunk - 1) / kGrChunk;
-  // the whole slice fits the stages: load it once per group, both passes read it
-  const bool resident = p.resident != 0;
-
-  if (warp == kCWarps) {
-    // ------------------------------------------------------------------ producers
-    // lane 0 feeds ring A (pass 1, HBM, L2 evict-last); lane 1 feeds ring B (pass 2, the
-    // same bytes again from L2, evict-first).  Each runs ahead as far as its ring allows.
-    if (resident && lane == 0) {
-      // resident: chunk c of every group lives in stage c and is read by both passes; the
-      // stage is refilled once the consumers have finished pass 2 of the previous group
-      const uint64_t pol = l2_policy(false);
-      int it = 0;
-      bool ok = true;
-      for (int64_t bg = cid; ok && bg < BG; bg += ncl, ++it) {
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(static_cast<const T*>(p.x) + bg * p.n) +
-                             (size_t)v0 * 16;
-        for (uint32_t c = 0; c < nchunks; ++c) {
-          if (it > 0 && !mbar_wait(&empty[c], (it - 1) & 1, abort_flag, WD_TMA_WAIT)) {
-            ok = false;
-            break;
-          }
-          const uint32_t bytes = min((uint32_t)kGrChunk, slice_bytes - c * kGrChunk);
-          mbar_arrive_expect_tx(&full[c], bytes);
-          bulk_load(ring + c * kGrChunk, src + (size_t)c * kGrChunk, bytes, &full[c], pol);
-        }
+  if (warp == kSlProducerWarp) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t keep = l2_policy(true), drop = l2_policy(false);
+      uint32_t k = 0;  // units issued
+      for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
+        const uint32_t st = k % kSlStages;
+        if (k >= kSlStages &&
+            !sl_wait(&empty[st], ((k / kSlStages) - 1) & 1, abort_flag, WD_TMA_WAIT))
+          break;
+        const SlUnit un = sl_unit(p, u);
+        const int64_t v0 = un.s * kSv;
+        const uint32_t bytes = (uint32_t)((min(nvec, v0 + kSv) - v0) * 16);
+        const uint8_t* src =
+            reinterpret_cast<const uint8_t*>(static_cast<const T*>(p.x) + un.g * p.n) + v0 * 16;
+        mbar_arrive_expect_tx(&full[st], bytes);
+        // pass-0 bytes are read again by the group's pass-1 units: keep them in L2
+        bulk_load(ring + st * kSlBytes, src, bytes, &full[st], un.pass == 0 ? keep : drop);
       }
-      if (!ok)  // let the copies in flight land before the CTA can exit (bounded)
-        for (uint32_t c = 0; c < nchunks; ++c) mbar_wait(&full[c], (it & 1), nullptr, WD_TMA_WAIT);
-    } else if (!resident && lane < 2) {
-      const int pass = lane;
-      const uint32_t nst = pass == 0 ? kGrStagesA : kGrStagesB;
-      const uint32_t base = pass == 0 ? 0 : kGrStagesA;
-      const uint64_t pol = l2_policy(pass == 0);
-      uint32_t k = 0;
-      bool ok = true;
-      for (int64_t bg = cid; ok && bg < BG; bg += ncl) {
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(static_cast<const T*>(p.x) + bg * p.n) +
-                             (size_t)v0 * 16;
-        for (uint32_t c = 0; c < nchunks; ++c, ++k) {
-          const uint32_t st = base + k % nst, ph = (k / nst) & 1;
-          if (k >= nst && !mbar_wait(&empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) {
-            ok = false;
-            break;
-          }
-          const uint32_t bytes = min((uint32_t)kGrChunk, slice_bytes - c * kGrChunk);
-          mbar_arrive_expect_tx(&full[st], bytes);
-          bulk_load(ring + st * kGrChunk, src + (size_t)c * kGrChunk, bytes, &full[st], pol);
-        }
-      }
-      if (!ok) {
-        // let the copies in flight land before the CTA can exit (bounded)
-        for (uint32_t j = k > nst ? k - nst : 0; j < k; ++j)
-          mbar_wait(&full[base + j % nst], (j / nst) & 1, nullptr, WD_TMA_WAIT);
-      }
+      // no copy may still be landing when the CTA exits (the consumers may have left early
+      // on an expired wait): wait for the last ones issued (bounded)
+      for (uint32_t j = k > kSlStages ? k - kSlStages : 0; j < k; ++j)
+        sl_wait(&full[j % kSlStages], (j / kSlStages) & 1, nullptr, WD_TMA_WAIT);
     }
-  } else {
-    // ------------------------------------------------------------------ consumers
-    // A failed (expired) wait sets the shared abort flag before it returns.  Warps never
-    // leave the group loop on their own: they skip work once `ok` is false and leave
-    // together right after a named barrier, where every consumer sees the flag.
-    const T* gam = static_cast<const T*>(p.gamma);
-    const T* bet = static_cast<const T*>(p.beta);
-    // max |gamma|, max |beta| over all channels: bounds the affine output of a group
-    {
-      float gm = 0.f, bm = 0.f;
-      for (int64_t c = threadIdx.x; c < p.C; c += kGrConsumers) {
-        gm = fmaxf(gm, fabsf(to_f32(gam[c])));
-        bm = fmaxf(bm, fabsf(to_f32(bet[c])));
+    return;
+  }
+
+  if (warp == kSlPublisherWarp) {
+    // ------------------------------------------------------------------ publisher
+    // pass 0: merge the 8 warp partials in warp order, publish the slice's partial, release
+    // the group's counter.  Every unit: its arrival on empty[st] (after full[st], so it can
+    // never count toward the stage's previous phase).
+    uint32_t k = 0, pph = 0;  // pph: per-stage part_full parity
+    for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
+      const uint32_t st = k % kSlStages;
+      if (!sl_wait_warp(&full[st], (k / kSlStages) & 1, abort_flag, WD_CONVERT_WAIT)) break;
+      const SlUnit un = sl_unit(p, u);
+      if (un.pass == 0) {
+        if (!sl_wait_warp(&part_full[st], (pph >> st) & 1, abort_flag, WD_CONVERT_WAIT)) break;
+        pph ^= 1u << st;
+        if (lane == 0) {
+          const float4 a = wpart[st][0];
+          Welford t{a.x, a.y, a.z};
+          float am = a.w;
+          for (int i = 1; i < kCWarps; ++i) {
+            const float4 b = wpart[st][i];
+            t = welford_merge(t, Welford{b.x, b.y, b.z});
+            am = fmaxf(am, b.w);
+          }
+          p.part[un.g * p.S + un.s] = make_float4(t.n, t.mean, t.m2, am);
+          red_release_add(p.ready + un.g, 1u);
+        }
+        __syncwarp();
       }
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    return;
+  }
+
+  if (warp == kSlStatsWarp) {
+    // ------------------------------------------------------------------ statistics
+    // pass 1: once the unit's slice has landed (so ahead of the consumers, which are still on
+    // earlier units), wait for the group's S partials, merge them (lane j takes partials j,
+    // j + 32, ... in order, then a fixed xor tree), and hand (mean, rstd, max |x|, no_clamp)
+    // to the consumers.
+    float gm = 0.f, bm = 0.f;  // max |gamma|, max |beta| over all channels
+    for (int64_t c = lane; c < p.C; c += 32) {
+      gm = fmaxf(gm, fabsf(to_f32(gam[c])));
+      bm = fmaxf(bm, fabsf(to_f32(bet[c])));
+    }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
-        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
-      }
-      if (lane == 0) wpart[warp] = Welford{gm, bm, 0.f};
-      consumer_sync();
-      if (threadIdx.x == 0) {
-        for (int i = 1; i < kCWarps; ++i) {
-          gm = fmaxf(gm, wpart[i].n);
-          bm = fmaxf(bm, wpart[i].mean);
-        }
-        gb_max[0] = fmaxf(gm, wpart[0].n);
-        gb_max[1] = fmaxf(bm, wpart[0].mean);
-      }
-      consumer_sync();
+    for (int o = 16; o > 0; o >>= 1) {
+      gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
     }
-    const float gmax = gb_max[0], bmax = gb_max[1];
-    const uint32_t vpc = (uint32_t)(p.HW / VE);  // vectors per channel
-    const float inv_vpc = 1.0f / (float)vpc;
-    uint32_t ka = 0, kb = 0;  // chunks taken from ring A / ring B
-    int it = 0;
-    bool ok = true;  // warp-uniform
-    for (int64_t bg = cid; bg < BG; bg += ncl, ++it) {
-      const int64_t g = bg % p.G;
-      uint4* yv = reinterpret_cast<uint4*>(static_cast<T*>(p.y) + bg * p.n) + v0;
+    uint32_t k = 0;
+    for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
+      const uint32_t st = k % kSlStages;
+      // unit k's slice landed: the stage's previous unit is done, gstat[st] no longer read
+      if (!sl_wait_warp(&full[st], (k / kSlStages) & 1, abort_flag, WD_CONVERT_WAIT)) break;
+      const SlUnit un = sl_unit(p, u);
+      if (un.pass == 1) {
+        if (!__all_sync(0xffffffffu, wait_ready(p.ready + un.g, (unsigned)p.S, abort_flag)))
+          break;
+        const float4* gp = p.part + un.g * p.S;
+        Welford t{0.f, 0.f, 0.f};
+        float am = 0.f;
+        for (int64_t j = lane; j < p.S; j += 32) {
+          const float4 q = gp[j];
+          t = welford_merge(t, Welford{q.x, q.y, q.z});
+          am = fmaxf(am, q.w);
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          Welford b{__shfl_xor_sync(0xffffffffu, t.n, o),
+                    __shfl_xor_sync(0xffffffffu, t.mean, o),
+                    __shfl_xor_sync(0xffffffffu, t.m2, o)};
+          // fixed operand order (lower lane first) so both lanes of a pair agree
+          t = (lane & o) ? welford_merge(b, t) : welford_merge(t, b);
+          am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        }
+        if (lane == 0) {
+          const float rstd = rsqrtf(t.m2 / t.n + p.eps);
+          // no clamp can bite when |x| <= 65000 and |(x - mean) * w + b| <= 65000 for all x, c
+          const bool no_clamp = am <= kClamp && (am + fabsf(t.mean)) * gm * rstd + bm <= kClamp;
+          gstat[st] = make_float4(t.mean, rstd, am, no_clamp ? 1.f : 0.f);
+          mbar_arrive(&stat_full[st]);  // release: gstat is visible to the waiters
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    return;
+  }
 
-      // ---- pass 1: statistics of clamp(x) and max |x|
+  // ------------------------------------------------------------------ consumers
+  // Waits that expire set the shared abort flag; every later wait then returns false at once
+  // and the warps leave the unit loop.
+  const uint32_t vpc = (uint32_t)(p.HW / VE);  // vectors per channel
+  // kSlConsumers vectors = vstep_q channels + vstep_r vectors
+  const uint32_t vstep_q = kSlConsumers / vpc, vstep_r = kSlConsumers % vpc;
+  uint32_t k = 0, sph = 0;  // sph: per-stage stat_full parity
+  for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
+    const uint32_t st = k % kSlStages, ph = (k / kSlStages) & 1;
+    const SlUnit un = sl_unit(p, u);
+    const int64_t v0 = un.s * kSv;
+    const uint32_t cv = (uint32_t)(min(nvec, v0 + kSv) - v0);
+    const uint4* sv = reinterpret_cast<const uint4*>(ring + st * kSlBytes);
+    if (un.pass == 0) {
+      // ---- pass 0: statistics of clamp(x) and max |x| over the slice
+      if (!sl_wait_warp(&full[st], ph, abort_flag, WD_CONVERT_WAIT)) break;
       const uint64_t zero2 = f2(0.f, 0.f);
       uint64_t sh2 = zero2, s1 = zero2, s2 = zero2;
       float amax = 0.f, cnt = 0.f;
       bool first = true;
-      for (uint32_t c = 0; ok && c < nchunks; ++c, ++ka) {
-        const uint32_t st = resident ? c : ka % kGrStagesA;
-        const uint32_t ph = resident ? (uint32_t)(it & 1) : (ka / kGrStagesA) & 1;
-        if (!mbar_wait_warp(&full[st], ph, abort_flag, WD_CONVERT_WAIT)) {
-          ok = false;
-          break;
-        }
-        const uint32_t cv = min((uint32_t)kGrChunk, slice_bytes - c * kGrChunk) / 16u;
-        const uint4* sv = reinterpret_cast<const uint4*>(ring + st * kGrChunk);
-        for (uint32_t i = threadIdx.x; i < cv; i += kGrConsumers) {
-          float f[VE];
-          unpack<T>(sv[i], f);
+#pragma unroll 2
+      for (uint32_t i = threadIdx.x; i < cv; i += kSlConsumers) {
+        float f[VE];
+        unpack<T>(sv[i], f);
+        float vm = fabsf(f[0]);
 #pragma unroll
-          for (int e = 0; e < VE; ++e) {
-            amax = fmaxf(amax, fabsf(f[e]));
-            f[e] = clamp65k(f[e]);
-          }
-          if (first) {
-            sh2 = f2(f[0], f[0]);
-            first = false;
-          }
+        for (int e = 1; e < VE; ++e) vm = fmaxf(vm, fabsf(f[e]));
+        amax = fmaxf(amax, vm);
+        if (vm > kClamp) {  // clamp(x) differs from x only above the bound
 #pragma unroll
-          for (int e = 0; e < VE; e += 2) {
-            const uint64_t d = f2_sub(f2(f[e], f[e + 1]), sh2);
-            s1 = f2_add(s1, d);
-            s2 = f2_fma(d, d, s2);
-          }
-          cnt += (float)VE;
+          for (int e = 0; e < VE; ++e) f[e] = clamp65k(f[e]);
         }
-        __syncwarp();
-        if (lane == 0 && !resident) mbar_arrive(&empty[st]);
+        if (first) {
+          sh2 = f2(f[0], f[0]);
+          first = false;
+        }
+#pragma unroll
+        for (int e = 0; e < VE; e += 2) {
+          const uint64_t d = f2_sub(f2(f[e], f[e + 1]), sh2);
+          s1 = f2_add(s1, d);
+          s2 = f2_fma(d, d, s2);
+        }
+        cnt += (float)VE;
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
       Welford w{cnt, 0.f, 0.f};
       if (cnt > 0.f) {
         float a, b, shift, dummy;
@@ -559,103 +662,71 @@ __global__ void __launch_bounds__(kGrThreads, 2) gn_ring_kernel(GnParams p, int6
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       }
       if (lane == 0) {
-        wpart[warp] = w;
-        wamax[warp] = amax;
+        wpart[st][warp] = make_float4(w.n, w.mean, w.m2, amax);
+        mbar_arrive(&part_full[st]);
       }
-      consumer_sync();
-      if (*abort_flag) break;  // uniform across the consumer warps
-      const int par = it & 1;
-      if (threadIdx.x == 0) {
-        Welford t = wpart[0];
-        float am = wamax[0];
-        for (int i = 1; i < kCWarps; ++i) {
-          t = welford_merge(t, wpart[i]);
-          am = fmaxf(am, wamax[i]);
-        }
-        // push the partial into every rank's slot[par][rank], then arrive there
-        for (int r = 0; r < cs; ++r) {
-          const uint32_t a = map_rank(&slot[par][rank][0], r);
-          st_cluster_f32(a, t.n);
-          st_cluster_f32(a + 4, t.mean);
-          st_cluster_f32(a + 8, t.m2);
-          st_cluster_f32(a + 12, am);
-          arrive_cluster(map_rank(&stats_bar[par], r));
-        }
-      }
-      __syncwarp();
-      ok = __all_sync(0xffffffffu, mbar_wait_cluster(&stats_bar[par], (it >> 1) & 1, abort_flag));
-      float mean = 0.f, rstd = 0.f, gamax = 0.f;
-      if (ok) {
-        Welford t{slot[par][0][0], slot[par][0][1], slot[par][0][2]};
-        gamax = slot[par][0][3];
-        for (int r = 1; r < cs; ++r) {
-          t = welford_merge(t, Welford{slot[par][r][0], slot[par][r][1], slot[par][r][2]});
-          gamax = fmaxf(gamax, slot[par][r][3]);
-        }
-        mean = t.mean;
-        rstd = rsqrtf(t.m2 / t.n + p.eps);
-        for (int c = threadIdx.x; c < (int)p.cg; c += kGrConsumers)
-          aff[c] = make_float2(to_f32(gam[g * p.cg + c]) * rstd, to_f32(bet[g * p.cg + c]));
-      }
-      consumer_sync();
-      if (!ok) continue;  // leaves at the next named barrier (or at the end)
-      // no clamp can bite when |x| <= 65000 and |(x - mean) * w + b| <= 65000 for all x, c
-      const bool no_clamp =
-          gamax <= kClamp && (gamax + fabsf(mean)) * gmax * rstd + bmax <= kClamp;
-      const uint64_t mean2 = f2(mean, mean);
-      const uint64_t half2 = f2(0.5f, 0.5f);
+      continue;
+    }
 
-      // ---- pass 2: normalise, affine, activation, store
-      for (uint32_t c = 0; c < nchunks; ++c, ++kb) {
-        const uint32_t st = resident ? c : kGrStagesA + kb % kGrStagesB;
-        const uint32_t ph = (kb / kGrStagesB) & 1;
-        // resident: the chunk is still in its stage from pass 1
-        if (!resident && !mbar_wait_warp(&full[st], ph, abort_flag, WD_CONVERT_WAIT)) {
-          ok = false;
-          break;
-        }
-        const uint32_t c0 = c * (kGrChunk / 16);  // first vector of this chunk in the slice
-        const uint32_t cv = min((uint32_t)kGrChunk, slice_bytes - c * kGrChunk) / 16u;
-        const uint4* sv = reinterpret_cast<const uint4*>(ring + st * kGrChunk);
-        for (uint32_t i = threadIdx.x; i < cv; i += kGrConsumers) {
-          float f[VE];
-          unpack<T>(sv[i], f);
-          // channel of this vector: vi / vpc via a float estimate and one correction step
-          const uint32_t vi = (uint32_t)v0 + c0 + i;
-          uint32_t q = __float2uint_rz((float)vi * inv_vpc);
-          const int32_t rem = (int32_t)(vi - q * vpc);
-          q = rem < 0 ? q - 1 : (rem >= (int32_t)vpc ? q + 1 : q);
-          const float2 ab = aff[q];
-          const uint64_t w2 = f2(ab.x, ab.x), b2 = f2(ab.y, ab.y);
-          if (no_clamp) {
+    // ---- pass 1: normalise, affine, activation, store
+    if (!sl_wait_warp(&stat_full[st], (sph >> st) & 1, abort_flag, WD_CONVERT_WAIT)) break;
+    sph ^= 1u << st;
+    const float4 gs = gstat[st];
+    const float mean = gs.x, rstd = gs.y;
+    const bool no_clamp = gs.w != 0.f;
+    if (!sl_wait_warp(&full[st], ph, abort_flag, WD_CONVERT_WAIT)) break;
+    const uint64_t mean2 = f2(mean, mean);
+    const bool silu = p.act == SP_ACT_SILU;
+    // SiLU as y = h + h * tanh(h) with h = v / 2 (= v * sigmoid(v)): the 1/2 folds into the
+    // affine map, exactly (a power of two)
+    const float hs = silu ? 0.5f : 1.0f;
+    const T* gam_g = gam + (un.g % p.G) * p.cg;  // this group's channels
+    const T* bet_g = bet + (un.g % p.G) * p.cg;
+    uint4* yv = reinterpret_cast<uint4*>(static_cast<T*>(p.y) + un.g * p.n) + v0;
+    // channel of the thread's vector v0 + i, tracked as (q, rem) = divmod(v0 + i, vpc) and
+    // stepped by kSlConsumers vectors per iteration; gamma, beta reloaded when it changes
+    uint32_t q = ((uint32_t)v0 + threadIdx.x) / vpc;
+    uint32_t rem = ((uint32_t)v0 + threadIdx.x) - q * vpc;
+    uint32_t qc = 0xffffffffu;
+    float wc = 0.f, bc = 0.f;
+    uint64_t w2 = 0, b2 = 0;
+#pragma unroll 2
+    for (uint32_t i = threadIdx.x; i < cv; i += kSlConsumers) {
+      if (q != qc) {
+        qc = q;
+        wc = to_f32(__ldg(gam_g + q)) * rstd;
+        bc = to_f32(__ldg(bet_g + q));
+        w2 = f2(hs * wc, hs * wc);
+        b2 = f2(hs * bc, hs * bc);
+      }
+      float f[VE];
+      unpack<T>(sv[i], f);
+      if (no_clamp) {
 #pragma unroll
-            for (int e = 0; e < VE; e += 2) {
-              uint64_t v = f2_fma(f2_sub(f2(f[e], f[e + 1]), mean2), w2, b2);
-              if (p.act == SP_ACT_SILU) {
-                float t0, t1;
-                f2_split(f2_mul(v, half2), t0, t1);
-                const uint64_t sg = f2_fma(f2(tanh_approx(t0), tanh_approx(t1)), half2, half2);
-                v = f2_mul(v, sg);
-              }
-              f2_split(v, f[e], f[e + 1]);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < VE; ++e)
-              f[e] = apply_act((clamp65k(f[e]) - mean) * ab.x + ab.y, p.act);
+        for (int e = 0; e < VE; e += 2) {
+          uint64_t h = f2_fma(f2_sub(f2(f[e], f[e + 1]), mean2), w2, b2);
+          if (silu) {
+            float h0, h1;
+            f2_split(h, h0, h1);
+            h = f2_fma(h, f2(tanh_approx(h0), tanh_approx(h1)), h);
           }
-          yv[c0 + i] = pack<T>(f);
+          f2_split(h, f[e], f[e + 1]);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < VE; ++e) f[e] = apply_act((clamp65k(f[e]) - mean) * wc + bc, p.act);
+      }
+      yv[i] = pack<T>(f);
+      rem += vstep_r;
+      q += vstep_q;
+      if (rem >= vpc) {
+        rem -= vpc;
+        ++q;
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
   }
-  // no CTA may leave while a peer could still push into its shared memory (the barrier is
-  // warp-aligned: reconverge the producer warp and any consumer lanes first)
-  __syncwarp();
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------------------
@@ -751,8 +822,7 @@ constexpr int64_t kGeneralChunk = 16384;
 
 struct GnPlan {
   bool cluster_path;
-  bool stream_path;  // persistent streaming clusters (large groups)
-  bool resident;     // streaming path with the whole slice held in shared memory
+  bool stream_path;  // persistent slice-unit grid (large groups)
   int cs;      // cluster size
   int vpt;     // vectors per thread
   int64_t chunk_vecs;
@@ -771,17 +841,8 @@ GnPlan plan_gn(int64_t B, int64_t G, int64_t cg, int64_t n, bool contiguous, boo
   const int max_vpt = vec_elems == 4 ? 16 : 8;
   const int64_t group_bytes = n * (16 / vec_elems);
   if (contiguous && vec_ok && n < (1LL << 31) && group_bytes >= kStreamMinGroupBytes &&
-      cg <= kGrMaxCg) {
-    // two CTAs per SM; the smallest cluster (>= 2) that still gives every CTA slot a slice
-    // (measured on B200: larger slices per CTA beat keeping fewer groups in flight, and
-    // clusters grown just to shrink slices into shared memory ran slower)
-    int cs = 2;
-    while (cs < 8 && B * G * cs < (2LL * num_sms() * 7) / 8) cs *= 2;  // 16: measured slower
-    // when the slice fits the stages: one HBM read, both passes from shared memory
-    pl.resident = (nvec + cs - 1) / cs * 16 <= (int64_t)kGrStages * kGrChunk;
+      cg <= kSlMaxCg) {
     pl.stream_path = true;
-    pl.cs = cs;
-    pl.chunk_vecs = (nvec + cs - 1) / cs;
     return pl;
   }
   if (contiguous && vec_ok && n < (1LL << 31)) {
@@ -863,54 +924,66 @@ int launch_cluster_vpt(const GnParams& p, int cs, int vpt, int64_t BG, cudaStrea
   }
 }
 
-constexpr int kGrSmem = kGrStages * kGrChunk + 128;
+constexpr int kSlSmem = kSlStages * kSlBytes + 128;
+
+// Streaming-path workspace: the [BG] ready counters (padded to 16 bytes), then the [BG][S]
+// partials.
+int64_t sl_slices(int64_t n, int es) { return (n * es + kSlBytes - 1) / kSlBytes; }
+size_t sl_ready_bytes(int64_t BG) { return ((size_t)BG * 4 + 15) & ~size_t(15); }
+size_t sl_workspace_bytes(int64_t BG, int64_t S) {
+  return sl_ready_bytes(BG) + (size_t)BG * (size_t)S * 16;
+}
 
 template <typename T>
-int launch_stream(const GnParams& p, int cs, int64_t BG, cudaStream_t stream) {
-  auto kern = gn_ring_kernel<T>;
+int launch_slices(GnSliceParams p, void* ws, cudaStream_t stream) {
+  auto kern = gn_slice_kernel<T>;
   static unsigned long long attr_set = 0;
   if (first_time_on_device(&attr_set)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGrSmem);
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSlSmem);
     if (e != cudaSuccess) {
       __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
       return set_error(SP_ERR_LAUNCH, "groupnorm: kernel attribute failed: %s",
                        cudaGetErrorString(e));
     }
   }
+  // resident CTAs per SM, found once per device: the grid is exactly the resident set
+  // (cooperative launch), so every CTA a pass-1 unit waits on is running
+  static int per_sm[64] = {};
+  const int dev = current_device();
+  int r = (dev >= 0 && dev < 64) ? __atomic_load_n(&per_sm[dev], __ATOMIC_ACQUIRE) : 0;
+  if (r <= 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, kern, kSlThreads, kSlSmem) !=
+            cudaSuccess ||
+        r <= 0) {
+      cudaGetLastError();
+      return set_error(SP_ERR_LAUNCH, "groupnorm: occupancy query failed");
+    }
+    if (dev >= 0 && dev < 64) __atomic_store_n(&per_sm[dev], r, __ATOMIC_RELEASE);
+  }
+  const int64_t units = 2 * p.BG * p.S;
+  const int64_t grid = std::min<int64_t>((int64_t)r * num_sms(), units);
+  // four grid-widths of units between a slice's pass 0 and its pass 1
+  p.L = std::min<int64_t>(p.BG, std::max<int64_t>(1, (2 * grid + p.S - 1) / p.S));
+  p.ready = static_cast<unsigned*>(ws);
+  p.part = reinterpret_cast<float4*>(static_cast<uint8_t*>(ws) + sl_ready_bytes(p.BG));
+  cudaError_t e = cudaMemsetAsync(p.ready, 0, (size_t)p.BG * 4, stream);
+  if (e != cudaSuccess)
+    return set_error(SP_ERR_LAUNCH, "groupnorm: counter reset failed: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)cs;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(kGrThreads, 1, 1);
-  cfg.dynamicSmemBytes = kGrSmem;
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(kSlThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSlSmem;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  // as many clusters as can be resident at once (each loops over groups), found once per
-  // device and cluster size
-  static int resident[64][5] = {};
-  const int dev = current_device();
-  int lg = 0;
-  while ((1 << lg) < cs) ++lg;
-  int ncl = (dev >= 0 && dev < 64) ? __atomic_load_n(&resident[dev][lg], __ATOMIC_ACQUIRE) : 0;
-  if (ncl <= 0) {
-    cfg.gridDim = dim3((unsigned)(cs * (2 * num_sms() / cs)), 1, 1);
-    if (cudaOccupancyMaxActiveClusters(&ncl, kern, &cfg) != cudaSuccess || ncl <= 0) {
-      cudaGetLastError();
-      ncl = 2 * num_sms() / cs;
-    }
-    if (dev >= 0 && dev < 64) __atomic_store_n(&resident[dev][lg], ncl, __ATOMIC_RELEASE);
-  }
-  const int64_t nclusters = std::min<int64_t>(ncl, BG);
-  cfg.gridDim = dim3((unsigned)(nclusters * cs), 1, 1);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, BG);
+  e = cudaLaunchKernelEx(&cfg, kern, p);
   if (e != cudaSuccess)
-    return set_error(SP_ERR_LAUNCH, "groupnorm stream launch (cs=%d) failed: %s", cs,
-                     cudaGetErrorString(e));
+    return set_error(SP_ERR_LAUNCH, "groupnorm slice launch (grid %lld) failed: %s",
+                     (long long)grid, cudaGetErrorString(e));
   return SP_OK;
 }
 
@@ -974,7 +1047,9 @@ size_t sp_groupnorm_act_workspace_size(int64_t B, int64_t C, int64_t H, int64_t 
   const int vec = 16 / es;
   const sp::GnPlan pl = sp::plan_gn(B, groups, C / groups, C / groups * H * W, contiguous,
                                     contiguous && (H * W) % vec == 0, vec);
-  return (pl.cluster_path || pl.stream_path) ? 0 : sp::general_workspace_bytes(B, C, H, W, groups);
+  if (pl.stream_path)
+    return sp::sl_workspace_bytes(B * groups, sp::sl_slices(C / groups * H * W, es));
+  return pl.cluster_path ? 0 : sp::general_workspace_bytes(B, C, H, W, groups);
 }
 
 int sp_groupnorm_act_output_strides(int64_t B, int64_t C, int64_t H, int64_t W,
@@ -1022,16 +1097,24 @@ int sp_groupnorm_act(const void* x, const void* gamma, const void* beta, void* y
   const GnPlan pl = plan_gn(B, groups, cg, n, contiguous, vec_ok, vec_elems);
 
   if (pl.stream_path) {
-    GnParams p{pl.resident ? 1 : 0, x, gamma, beta, y, C, HW, groups, cg, n, pl.chunk_vecs, eps,
-               act};
+    const int64_t S = sl_slices(n, es);
+    const size_t need = sl_workspace_bytes(B * groups, S);
+    if (!workspace || workspace_bytes < need)
+      return set_error(SP_ERR_WORKSPACE,
+                       "groupnorm: this shape takes the streaming path and needs %zu bytes of "
+                       "workspace (got %zu)",
+                       need, workspace_bytes);
+    if (!aligned(workspace, 16)) return set_error(SP_ERR_ALIGN, "groupnorm: workspace misaligned");
+    GnSliceParams p{x, gamma, beta, y, C, HW, groups, cg, n, B * groups, S, 1, nullptr, nullptr,
+                    eps, act};
     switch (dtype) {
-      case SP_F32: return launch_stream<float>(p, pl.cs, B * groups, s);
-      case SP_F16: return launch_stream<__half>(p, pl.cs, B * groups, s);
-      default: return launch_stream<__nv_bfloat16>(p, pl.cs, B * groups, s);
+      case SP_F32: return launch_slices<float>(p, workspace, s);
+      case SP_F16: return launch_slices<__half>(p, workspace, s);
+      default: return launch_slices<__nv_bfloat16>(p, workspace, s);
     }
   }
   if (pl.cluster_path) {
-    GnParams p{0, x, gamma, beta, y, C, HW, groups, cg, n, pl.chunk_vecs, eps, act};
+    GnParams p{x, gamma, beta, y, C, HW, groups, cg, n, pl.chunk_vecs, eps, act};
     switch (dtype) {
       case SP_F32: return launch_cluster_vpt<float>(p, pl.cs, pl.vpt, B * groups, s);
       case SP_F16: return launch_cluster_vpt<__half>(p, pl.cs, pl.vpt, B * groups, s);

@@ -23,6 +23,7 @@ enum WatchdogCode : int {
   WD_EPILOGUE_WAIT = 4,
   WD_CONVERT_WAIT = 5,
   WD_CLUSTER_WAIT = 6,
+  WD_FLAG_WAIT = 7,  // a flag that other CTAs of the same launch set
 };
 
 // Budget for one wait, in SM clock cycles (~2 s at the 1.965 GHz boost clock, longer at
