@@ -7,10 +7,10 @@
 // kernel runs one thread per (batch, group).
 //
 // Fast path (contiguous x, groups below 256 KB): ONE read and ONE write of HBM.  A (batch,
-// group) is split over a
-// thread-block cluster of CS CTAs (CS <= 16); each CTA keeps its slice in registers (16-byte
-// vector loads), the cluster reduces the sum and then the centred sum of squares through
-// distributed shared memory, and every CTA normalises its slice straight from registers.
+// group) is split over a thread-block cluster of CS CTAs (CS <= 16); each CTA keeps its slice
+// in registers (16-byte vector loads), the cluster reduces the sum and then the centred sum
+// of squares through distributed shared memory, and every CTA normalises its slice straight
+// from registers.
 //
 // Streaming path (contiguous x, groups of 256 KB and more): a persistent grid of slice units
 // (statistics of a slice, then normalisation of it once its group's statistics are known);
