@@ -146,6 +146,7 @@ extern "C" {
         b: *const c_float, bias: *const c_void, y: *mut c_void, m: i64, n: i64, k: i64,
         dtype: c_int, stream: *mut c_void
     ) -> c_int;
+    pub fn sp_quant_linear_set_pairing(mode: c_int) -> c_int;
     pub fn sp_q8_0_linear(
         x: *const c_void, q: *const c_void, scale: *const c_void, bias: *const c_void,
         y: *mut c_void, m: i64, n: i64, k: i64, dtype: c_int, stream: *mut c_void

@@ -207,6 +207,14 @@ int sp_kquant_linear(int fmt, const void* x, const void* qpack, const float* a, 
                      const void* bias, void* y, int64_t M, int64_t N, int64_t K, int dtype,
                      void* stream);
 
+/* Tile mode of the quantized linears (Q8_0, FP8, K-quants; no reference counterpart), for the
+ * whole process: 0 (default) = one CTA per 256 x 256 tile; 1 = two-CTA clusters per 512 x 256
+ * tile (tcgen05.mma.cta_group::2) whenever M > 256, which halves each SM's decode work and
+ * weight-operand shared-memory reads.  Both give bit-identical results; on B200 the paired
+ * mode measured no faster, because the mainloop is bound by TMA latency, so it stays opt-in.
+ * Returns the previous mode; SP_ERR_INVALID_ARG for another value. */
+int sp_quant_linear_set_pairing(int mode);
+
 /* y[M,N] = x[M,K] . dequant(W)[N,K]^T (+ bias[N]); the dequantization happens inside the
  * GEMM mainloop (replaces GpuQuantizedLinear::forward, quantized_matmul.rs:752-766).
  * x, y, bias: SP_BF16.  K % 64 == 0, N % 16 == 0.  bias may be NULL.  x, q, scale and y

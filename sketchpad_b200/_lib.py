@@ -88,6 +88,7 @@ SIGNATURES = {
     "sp_kquant_dequant": (_int, [_int, _vp, _vp, _vp, _i64, _i64, _vp, _int, _vp]),
     "sp_kquant_linear": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "sp_q8_0_linear_glu": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp]),
+    "sp_quant_linear_set_pairing": (_int, [_int]),
     "sp_fp8_linear_glu": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _int,
                                  _vp]),
     "sp_q8_0_linear_rope": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64,

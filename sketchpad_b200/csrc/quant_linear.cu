@@ -28,7 +28,6 @@ namespace {
 
 constexpr int kQBM = 256, kQHalf = 128, kQBN = 256, kQBK = 64;
 constexpr int kQThreads = 640, kQDecoders = 512, kQFirstDecoderWarp = 4;
-constexpr int kRawStages = 3, kCvtStages = 2;
 constexpr int kXBytes = kQBM * kQBK * 2;    // 32 KB
 constexpr int kWRawBytes = kQBN * kQBK;     // 16 KB
 constexpr int kScBytes = 2 * kQBN * 2;      // 1 KB: two k-blocks x 256 rows of f16
@@ -41,37 +40,64 @@ enum WFormat : int { W_Q8_0 = 0, W_FP8 = 1, W_Q4K = 2, W_Q2K = 3, W_Q3K = 4, W_B
 
 // K-quant formats: one 4-bit quant per value (32 bytes per row of a k-tile), f32 factors a, b
 // per sub-block of kSub values; w = a * (q - kOff) - b.
-template <int WF>
+// ROWS: weight rows of a CTA's tile.
+template <int WF, int ROWS = kQBN>
 struct KqFmt {
   static constexpr bool kIsK = WF >= W_Q4K && WF <= W_Q3K;
   enum : int {
     kSub = WF == W_Q4K ? 32 : 16,
     kOff = WF == W_Q3K ? 4 : 0,
     kFactorRows = kQBK / kSub,              // sub-blocks per k-tile
-    kQBytes = kQBN * kQBK / 2,              // 8 KB of nibbles
-    kFactorBytes = kFactorRows * kQBN * 4,  // one factor array
+    kQBytes = ROWS * kQBK / 2,              // nibbles (8 KB for 256 rows)
+    kFactorBytes = kFactorRows * ROWS * 4,  // one factor array
   };
 };
 
-struct QlSmem {
-  static constexpr int kX = 0;
-  static constexpr int kWRaw = kX + kRawStages * kXBytes;
-  static constexpr int kSc = kWRaw + kRawStages * kWRawBytes;
-  static constexpr int kWCvt = kSc + kRawStages * kScBytes;
-  static constexpr int kBar = kWCvt + kCvtStages * kWCvtBytes;
-  static constexpr int kNumBars = 2 * kRawStages + 2 * kCvtStages + 1 + 1;
-  static constexpr int kMisc = kBar + kNumBars * 8;
-  static constexpr int kAlloc = kMisc + 16 + 1024;
+// Paired mode (PAIR): a cluster of two CTAs computes a 512 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256 per instruction, 128 rows from each CTA's x tile).  The
+// instruction takes B's 256 columns from both CTAs' shared memory, 128 each, and leaves each
+// CTA's 128 rows x all 256 columns in its own TMEM.  So each CTA loads its own 256 x rows as
+// in unpaired mode but decodes only 128 of the 256 weight rows: half the decode work and half
+// the B-operand shared-memory reads per SM, the stream that limits the unpaired kernel.
+//
+// Three rings: x tiles (consumed by the MMA), raw 8-bit weights with their scales or factors
+// (consumed by the decoders), decoded weights (consumed by the MMA).  The raw-weight ring is
+// released by the decoders alone, so weight loads run ahead of the MMA by the whole ring
+// instead of waiting for the MMA that shares a stage with them: measured, a shared x + W
+// ring made the loop TMA latency -> decode -> MMA -> release the bound (~1,530 SM cycles per
+// k-tile against 1,024 of tensor work).
+template <bool PAIR>
+struct QlGeom {
+  static constexpr int kWRows = PAIR ? kQBN / 2 : kQBN;  // weight rows this CTA decodes
+  static constexpr int kXSt = PAIR ? 4 : 3;               // x stages
+  static constexpr int kWSt = PAIR ? 4 : 3;               // raw-weight stages
+  static constexpr int kCvt = PAIR ? 3 : 2;               // decoded-weight stages
+  static constexpr int kWRawB = kWRows * kQBK;            // 8-bit weights of a k-tile
+  static constexpr int kScB = 2 * kWRows * 2;             // Q8_0: two k-blocks of f16 scales
+  static constexpr int kWStage = kWRawB + kScB;           // raw weights, then the scales
+  static constexpr int kWCvtB = kWRows * kQBK * 2;        // decoded bf16 weights
+  static constexpr int kNumBars = 2 * (kXSt + kWSt + kCvt) + 2;
 };
 
-// W_BF16: kRawStages stages of {x tile, bf16 W tile} (192 KB)
+template <bool PAIR>
+struct QlSmemT {
+  using G = QlGeom<PAIR>;
+  static constexpr int kX = 0;
+  static constexpr int kWRaw = kX + G::kXSt * kXBytes;
+  static constexpr int kWCvt = kWRaw + G::kWSt * G::kWStage;
+  static constexpr int kBar = kWCvt + G::kCvt * G::kWCvtB;
+  static constexpr int kMisc = kBar + G::kNumBars * 8;
+  static constexpr int kAlloc = kMisc + 16 + 1024;
+};
+using QlSmem = QlSmemT<false>;
+
+// W_BF16: the x ring's stages hold {x tile, bf16 W tile} (3 x 64 KB); no decode
 struct QlSmemBf16 {
   static constexpr int kStage = kXBytes + kWCvtBytes;
   static constexpr int kX = 0;
   static constexpr int kW = kXBytes;
-  static constexpr int kBar = kRawStages * kStage;
-  static constexpr int kNumBars = 2 * kRawStages + 2 * kCvtStages + 1 + 1;
-  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kBar = QlGeom<false>::kXSt * kStage;
+  static constexpr int kMisc = kBar + QlGeom<false>::kNumBars * 8;
   static constexpr int kAlloc = kMisc + 16 + 1024;
 };
 
@@ -280,46 +306,148 @@ __global__ void __launch_bounds__(256) ql_splitk_reduce_kernel(const QlParams p)
   }
 }
 
-template <int WF>
+// Shared-memory barrier helpers of the paired mode: a peer CTA's barrier is addressed through
+// the cluster window (mapa), arrivals from the peer are released at cluster scope, and the
+// leader acquires them at cluster scope.
+__device__ __forceinline__ uint32_t ql_cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t ql_peer_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void ql_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ void ql_store_remote(uint32_t cluster_addr, int v) {
+  asm volatile("st.relaxed.cluster.shared::cluster.s32 [%0], %1;" ::"r"(cluster_addr), "r"(v)
+               : "memory");
+}
+// Bounded wait that acquires at cluster scope (arrivals made by the peer CTA).
+__device__ __forceinline__ bool ql_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                volatile int* abort, int code) {
+  const long long t0 = clock64();
+  uint32_t spins = 0;
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((++spins & 255u) == 0) {
+      if (*abort) return false;
+      if (clock64() - t0 > kWaitBudgetCycles) {
+        atomicCAS(&g_watchdog, 0, code);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void ql_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// tcgen05 forms of the pair (cta_group::2): TMEM allocation by one warp in each CTA, MMA issued
+// by the leader, commits arriving on a barrier of either CTA (cluster address)
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          cluster_addr)
+      : "memory");
+}
+
+template <int WF, bool PAIR>
 __global__ void __launch_bounds__(kQThreads, 1)
     qlinear_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                    const __grid_constant__ CUtensorMap tms, const __grid_constant__ CUtensorMap tmb,
                    const QlParams p) {
-  using L = typename std::conditional<WF == W_BF16, QlSmemBf16, QlSmem>::type;
-  using KF = KqFmt<WF>;
+  static_assert(!(PAIR && WF == W_BF16), "bf16 weights run unpaired");
+  using G = QlGeom<PAIR>;
+  using L = typename std::conditional<WF == W_BF16, QlSmemBf16, QlSmemT<PAIR>>::type;
+  using LQ = QlSmemT<PAIR>;  // stage offsets of the decoded formats
+  using KF = KqFmt<WF, G::kWRows>;
+  constexpr int kXSt = G::kXSt, kWSt = G::kWSt, kCvtSt = G::kCvt;
+  constexpr int kWR = G::kWRows;                    // weight rows this CTA loads and decodes
+  constexpr int kDecWarps = kQDecoders / 32;
   // K-quants: a raw stage holds the nibble tile, then factor arrays a and b
-  static_assert(KF::kQBytes + 2 * KF::kFactorBytes <= kWRawBytes, "k-quant raw stage");
+  static_assert(KF::kQBytes + 2 * KF::kFactorBytes <= G::kWRawB, "k-quant raw stage");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  uint64_t* raw_full = bars;
-  uint64_t* raw_empty = raw_full + kRawStages;
-  uint64_t* cvt_full = raw_empty + kRawStages;
-  uint64_t* cvt_empty = cvt_full + kCvtStages;
-  uint64_t* acc_full = cvt_empty + kCvtStages;
+  uint64_t* x_full = bars;                // x tile (bf16 weights: and the W tile) landed
+  uint64_t* x_empty = x_full + kXSt;      // the MMA read it
+  uint64_t* w_full = x_empty + kXSt;      // raw weights (+ scales / factors) landed
+  uint64_t* w_empty = w_full + kWSt;      // the decoder warps read them
+  uint64_t* cvt_full = w_empty + kWSt;    // decoded weights written
+  uint64_t* cvt_empty = cvt_full + kCvtSt;  // the MMA read them
+  uint64_t* acc_full = cvt_empty + kCvtSt;
   uint64_t* drain = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // pair: rank 0 (the leader) issues the MMAs of both CTAs
+  const uint32_t rank = PAIR ? ql_cluster_rank() : 0u;
+  const uint32_t peer = rank ^ 1u;
   int mtile, ntile;
-  ql_tile_of(p, (int)blockIdx.x, mtile, ntile);
-  const int m0 = mtile * kQBM;
-  const int n0 = ntile * kQBN;
+  ql_tile_of(p, PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x, mtile, ntile);
+  const int m0 = mtile * (PAIR ? 2 * kQBM : kQBM) + (int)rank * kQBM;  // this CTA's x rows
+  const int n0 = ntile * kQBN;                                         // the tile's columns
+  const int nw0 = n0 + (int)rank * kWR;                                // this CTA's W rows
   // this CTA's k-tiles (all of them without split-K); kt below counts from 0
   const int kbase = (int)blockIdx.y * p.kt_per_split;
   const int ktiles = min((int)(p.K / kQBK) - kbase, p.kt_per_split);
+  // an expired wait stops this CTA and, paired, its peer (whose waits would else run out too)
+  auto fail = [&]() {
+    *abort_flag = 1;
+    if constexpr (PAIR) ql_store_remote(ql_peer_addr((const void*)abort_flag, peer), 1);
+  };
 
   constexpr bool kBf16 = WF == W_BF16;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kRawStages; ++s) {
-      mbar_init(&raw_full[s], 1);
-      // MMA commit (x consumed) + decoders (raw W); bf16 weights: the MMA commit alone
-      mbar_init(&raw_empty[s], kBf16 ? 1 : 1 + kQDecoders);
+    for (int s = 0; s < kXSt; ++s) {
+      mbar_init(&x_full[s], 1);
+      mbar_init(&x_empty[s], 1);  // MMA commit
     }
-    for (int s = 0; s < kCvtStages; ++s) {
-      mbar_init(&cvt_full[s], kQDecoders);
+    for (int s = 0; s < kWSt; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], kDecWarps);
+    }
+    for (int s = 0; s < kCvtSt; ++s) {
+      // this CTA's decoder warps; the leader's also takes the peer's forwarded arrival
+      mbar_init(&cvt_full[s], PAIR && rank == 0 ? kDecWarps + 1 : kDecWarps);
       mbar_init(&cvt_empty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -328,112 +456,180 @@ __global__ void __launch_bounds__(kQThreads, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  // paired: the peer's barriers, abort flag and TMEM must exist before either CTA uses them
+  if constexpr (PAIR) ql_cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ------------------------------------------------------------ x producer
     if (lane == 0) {
       tma_prefetch_desc(&tmx);
       tma_prefetch_desc(&tmw);
       if constexpr (WF == W_Q8_0 || KF::kIsK) tma_prefetch_desc(&tms);
       if constexpr (KF::kIsK) tma_prefetch_desc(&tmb);
-      constexpr uint32_t kTx =
-          kBf16 ? kXBytes + kWCvtBytes
-                : kXBytes + (KF::kIsK ? KF::kQBytes + 2 * KF::kFactorBytes
-                                      : kWRawBytes + (WF == W_Q8_0 ? kScBytes : 0));
+      constexpr uint32_t kTx = kBf16 ? kXBytes + kWCvtBytes : kXBytes;
       int issued = 0;
       for (int kt = 0; kt < ktiles; ++kt) {
-        const int st = kt % kRawStages;
-        const uint32_t ph = (kt / kRawStages) & 1;
-        if (kt >= kRawStages && !mbar_wait(&raw_empty[st], ph ^ 1, abort_flag, WD_TMA_WAIT)) break;
-        mbar_arrive_expect_tx(&raw_full[st], kTx);
+        const int st = kt % kXSt;
+        if (kt >= kXSt &&
+            !mbar_wait(&x_empty[st], ((kt / kXSt) - 1) & 1, abort_flag, WD_TMA_WAIT)) {
+          fail();
+          break;
+        }
+        mbar_arrive_expect_tx(&x_full[st], kTx);
         if constexpr (kBf16) {
           uint8_t* stage = smem + st * QlSmemBf16::kStage;
-          tma_load_2d(stage + QlSmemBf16::kX, &tmx, &raw_full[st], (kbase + kt) * kQBK, m0);
-          tma_load_2d(stage + QlSmemBf16::kW, &tmw, &raw_full[st], (kbase + kt) * kQBK, n0);
-          issued = kt + 1;
-          continue;
-        }
-        tma_load_2d(smem + QlSmem::kX + st * kXBytes, &tmx, &raw_full[st], (kbase + kt) * kQBK, m0);
-        if constexpr (KF::kIsK) {
-          uint8_t* rw = smem + QlSmem::kWRaw + st * kWRawBytes;
-          tma_load_2d(rw, &tmw, &raw_full[st], (kbase + kt) * (kQBK / 2), n0);
-          tma_load_2d(rw + KF::kQBytes, &tms, &raw_full[st], n0, (kbase + kt) * KF::kFactorRows);
-          tma_load_2d(rw + KF::kQBytes + KF::kFactorBytes, &tmb, &raw_full[st], n0,
-                      (kbase + kt) * KF::kFactorRows);
+          tma_load_2d(stage + QlSmemBf16::kX, &tmx, &x_full[st], (kbase + kt) * kQBK, m0);
+          tma_load_2d(stage + QlSmemBf16::kW, &tmw, &x_full[st], (kbase + kt) * kQBK, n0);
         } else {
-          tma_load_2d(smem + QlSmem::kWRaw + st * kWRawBytes, &tmw, &raw_full[st], (kbase + kt) * kQBK, n0);
+          tma_load_2d(smem + LQ::kX + st * kXBytes, &tmx, &x_full[st], (kbase + kt) * kQBK, m0);
         }
-        if constexpr (WF == W_Q8_0)
-          tma_load_2d(smem + QlSmem::kSc + st * kScBytes, &tms, &raw_full[st], n0, (kbase + kt) * (kQBK / 32));
         issued = kt + 1;
       }
-      if (*abort_flag)
-        for (int kt = max(0, issued - kRawStages); kt < issued; ++kt)
-          mbar_wait(&raw_full[kt % kRawStages], (kt / kRawStages) & 1, nullptr, WD_TMA_WAIT);
+      if (*abort_flag)  // let the copies in flight land before the CTA can exit (bounded)
+        for (int kt = max(0, issued - kXSt); kt < issued; ++kt)
+          mbar_wait(&x_full[kt % kXSt], (kt / kXSt) & 1, nullptr, WD_TMA_WAIT);
+    }
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ weight producer
+    if (lane == 0 && !kBf16) {
+      constexpr uint32_t kTx = KF::kIsK ? KF::kQBytes + 2 * KF::kFactorBytes
+                                        : G::kWRawB + (WF == W_Q8_0 ? G::kScB : 0);
+      int issued = 0;
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int st = kt % kWSt;
+        if (kt >= kWSt &&
+            !mbar_wait(&w_empty[st], ((kt / kWSt) - 1) & 1, abort_flag, WD_TMA_WAIT)) {
+          fail();
+          break;
+        }
+        mbar_arrive_expect_tx(&w_full[st], kTx);
+        uint8_t* rw = smem + LQ::kWRaw + st * G::kWStage;
+        if constexpr (KF::kIsK) {
+          tma_load_2d(rw, &tmw, &w_full[st], (kbase + kt) * (kQBK / 2), nw0);
+          tma_load_2d(rw + KF::kQBytes, &tms, &w_full[st], nw0, (kbase + kt) * KF::kFactorRows);
+          tma_load_2d(rw + KF::kQBytes + KF::kFactorBytes, &tmb, &w_full[st], nw0,
+                      (kbase + kt) * KF::kFactorRows);
+        } else {
+          tma_load_2d(rw, &tmw, &w_full[st], (kbase + kt) * kQBK, nw0);
+          if constexpr (WF == W_Q8_0)
+            tma_load_2d(rw + G::kWRawB, &tms, &w_full[st], nw0, (kbase + kt) * (kQBK / 32));
+        }
+        issued = kt + 1;
+      }
+      if (*abort_flag)  // let the copies in flight land before the CTA can exit (bounded)
+        for (int kt = max(0, issued - kWSt); kt < issued; ++kt)
+          mbar_wait(&w_full[kt % kWSt], (kt / kWSt) & 1, nullptr, WD_TMA_WAIT);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_f16(kQHalf, kQBN, 1u, 0, 0);
+    // ------------------------------------------------------------ MMA (the leader, paired)
+    if (lane == 0 && rank == 0) {
+      // paired: M = 256 per instruction (this CTA's 128 rows of a half, then the peer's)
+      const uint32_t idesc = make_idesc_f16(PAIR ? 2 * kQHalf : kQHalf, kQBN, 1u, 0, 0);
       bool ok = true;
       for (int kt = 0; kt < ktiles; ++kt) {
-        const int rs = kt % kRawStages, cs = kt % kCvtStages;
-        if (!mbar_wait(&raw_full[rs], (kt / kRawStages) & 1, abort_flag, WD_MMA_WAIT) ||
-            (!kBf16 &&
-             !mbar_wait(&cvt_full[cs], (kt / kCvtStages) & 1, abort_flag, WD_MMA_WAIT))) {
+        const int xs = kt % kXSt, cs = kt % kCvtSt;
+        bool got = mbar_wait(&x_full[xs], (kt / kXSt) & 1, abort_flag, WD_MMA_WAIT);
+        // paired: the peer's x tile and decoded stage are forwarded here by its warp 2
+        if (got && !kBf16)
+          got = PAIR ? ql_wait_cluster(&cvt_full[cs], (kt / kCvtSt) & 1, abort_flag, WD_MMA_WAIT)
+                     : mbar_wait(&cvt_full[cs], (kt / kCvtSt) & 1, abort_flag, WD_MMA_WAIT);
+        if (!got) {
+          fail();
           ok = false;
           break;
         }
         tc_fence_after();
         uint32_t xa, wb;
         if constexpr (kBf16) {
-          xa = smem_u32(smem + rs * QlSmemBf16::kStage + QlSmemBf16::kX);
-          wb = smem_u32(smem + rs * QlSmemBf16::kStage + QlSmemBf16::kW);
+          xa = smem_u32(smem + xs * QlSmemBf16::kStage + QlSmemBf16::kX);
+          wb = smem_u32(smem + xs * QlSmemBf16::kStage + QlSmemBf16::kW);
         } else {
-          xa = smem_u32(smem + QlSmem::kX + rs * kXBytes);
-          wb = smem_u32(smem + QlSmem::kWCvt + cs * kWCvtBytes);
+          xa = smem_u32(smem + LQ::kX + xs * kXBytes);
+          wb = smem_u32(smem + LQ::kWCvt + cs * G::kWCvtB);
         }
 #pragma unroll
         for (int kk = 0; kk < kQBK / 16; ++kk) {
           const uint64_t b = make_smem_desc(wb + kk * 32, 16, 1024, LAYOUT_SW128);
           const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
           // rows 0..127 and 128..255 of the x tile (16 KB apart, whole swizzle atoms)
-          umma_ss(tmem, make_smem_desc(xa + kk * 32, 16, 1024, LAYOUT_SW128), b, idesc, acc);
-          umma_ss(tmem + kQBN, make_smem_desc(xa + kQHalf * 128 + kk * 32, 16, 1024, LAYOUT_SW128),
-                  b, idesc, acc);
+          const uint64_t a0 = make_smem_desc(xa + kk * 32, 16, 1024, LAYOUT_SW128);
+          const uint64_t a1 = make_smem_desc(xa + kQHalf * 128 + kk * 32, 16, 1024, LAYOUT_SW128);
+          if constexpr (PAIR) {
+            umma_ss_pair(tmem, a0, b, idesc, acc);
+            umma_ss_pair(tmem + kQBN, a1, b, idesc, acc);
+          } else {
+            umma_ss(tmem, a0, b, idesc, acc);
+            umma_ss(tmem + kQBN, a1, b, idesc, acc);
+          }
         }
-        umma_commit(&raw_empty[rs]);
-        if constexpr (!kBf16) umma_commit(&cvt_empty[cs]);
+        if constexpr (PAIR) {
+          umma_commit_pair(smem_u32(&x_empty[xs]));
+          umma_commit_pair(ql_peer_addr(&x_empty[xs], peer));
+          umma_commit_pair(smem_u32(&cvt_empty[cs]));
+          umma_commit_pair(ql_peer_addr(&cvt_empty[cs], peer));
+        } else {
+          umma_commit(&x_empty[xs]);
+          if constexpr (!kBf16) umma_commit(&cvt_empty[cs]);
+        }
       }
-      if (ok) umma_commit(acc_full);
-      umma_commit(drain);
+      if constexpr (PAIR) {
+        if (ok) {
+          umma_commit_pair(smem_u32(acc_full));
+          umma_commit_pair(ql_peer_addr(acc_full, peer));
+        }
+        umma_commit_pair(smem_u32(drain));
+      } else {
+        if (ok) umma_commit(acc_full);
+        umma_commit(drain);
+      }
       mbar_wait(drain, 0, nullptr, WD_MMA_WAIT);
+    }
+  } else if (PAIR && warp == 2) {
+    // paired, peer only: once this CTA's x tile has landed and its decoder warps have
+    // written the stage, tell the leader with ONE cluster-scope release arrival (one per
+    // decoder warp would put a cluster-wide fence on every decoder warp's path)
+    if (lane == 0 && rank != 0 && !kBf16) {
+      const uint32_t leader_cvt_full = ql_peer_addr(cvt_full, 0u);
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int xs = kt % kXSt, cs = kt % kCvtSt;
+        if (!mbar_wait(&x_full[xs], (kt / kXSt) & 1, abort_flag, WD_CONVERT_WAIT) ||
+            !mbar_wait(&cvt_full[cs], (kt / kCvtSt) & 1, abort_flag, WD_CONVERT_WAIT)) {
+          fail();
+          break;
+        }
+        ql_arrive_remote(leader_cvt_full + (uint32_t)(cs * 8));
+      }
     }
   } else if (warp >= kQFirstDecoderWarp) {
     // ------------------------------------------------------------ decoders
-    const int t = threadIdx.x - kQFirstDecoderWarp * 32;  // 0..255
+    const int t = threadIdx.x - kQFirstDecoderWarp * 32;  // 0..511
     bool ok = true;
     for (int kt = 0; kt < (kBf16 ? 0 : ktiles); ++kt) {
-      const int rs = kt % kRawStages, cs = kt % kCvtStages;
-      if (!mbar_wait(&raw_full[rs], (kt / kRawStages) & 1, abort_flag, WD_CONVERT_WAIT)) {
+      const int ws = kt % kWSt, cs = kt % kCvtSt;
+      // warp-uniform waits: the warp arrives once per stage, after __syncwarp
+      if (!mbar_wait_warp(&w_full[ws], (kt / kWSt) & 1, abort_flag, WD_CONVERT_WAIT) ||
+          (kt >= kCvtSt && !mbar_wait_warp(&cvt_empty[cs], ((kt / kCvtSt) - 1) & 1, abort_flag,
+                                           WD_CONVERT_WAIT))) {
+        fail();
         ok = false;
         break;
       }
-      if (kt >= kCvtStages &&
-          !mbar_wait(&cvt_empty[cs], ((kt / kCvtStages) - 1) & 1, abort_flag, WD_CONVERT_WAIT)) {
-        ok = false;
-        break;
-      }
-      const uint8_t* raw = smem + QlSmem::kWRaw + rs * kWRawBytes;
-      const __half* sc = reinterpret_cast<const __half*>(smem + QlSmem::kSc + rs * kScBytes);
-      uint8_t* cvt = smem + QlSmem::kWCvt + cs * kWCvtBytes;
+      const uint8_t* raw = smem + LQ::kWRaw + ws * G::kWStage;
+      const __half* sc = reinterpret_cast<const __half*>(raw + G::kWRawB);
+      uint8_t* cvt = smem + LQ::kWCvt + cs * G::kWCvtB;
 #pragma unroll 2
-      for (int it = 0; it < (kQBN * 4) / kQDecoders; ++it) {
+      for (int it = 0; it < (kWR * 4) / kQDecoders; ++it) {
         const int task = t + it * kQDecoders;
         const int row = task >> 2, ch = task & 3;  // 16 weights: k = 16*ch .. 16*ch+15
         uint32_t o[8];
@@ -442,25 +638,25 @@ __global__ void __launch_bounds__(kQThreads, 1)
           const uint2 w = *reinterpret_cast<const uint2*>(raw + row * 32 + ch * 8);
           const float* fa = reinterpret_cast<const float*>(raw + KF::kQBytes);
           const int sb = (ch * 16) / KF::kSub;
-          const float a = fa[sb * kQBN + row];
-          const float b = fa[KF::kFactorRows * kQBN + sb * kQBN + row];
+          const float a = fa[sb * kWR + row];
+          const float b = fa[KF::kFactorRows * kWR + sb * kWR + row];
           k4x8_to_bf16(w.x, a, b, KF::kOff, o[0], o[1], o[2], o[3]);
           k4x8_to_bf16(w.y, a, b, KF::kOff, o[4], o[5], o[6], o[7]);
         } else {
-        const uint4 w = *reinterpret_cast<const uint4*>(raw + row * 64 + ch * 16);
-        if constexpr (WF == W_Q8_0) {
-          // rows past N read TMA zero fill: scale 0, weights 0
-          const float s = __half2float(sc[(ch >> 1) * kQBN + row]);
-          q8x4_to_bf16(w.x, s, o[0], o[1]);
-          q8x4_to_bf16(w.y, s, o[2], o[3]);
-          q8x4_to_bf16(w.z, s, o[4], o[5]);
-          q8x4_to_bf16(w.w, s, o[6], o[7]);
-        } else {
-          e4m3x4_to_bf16(w.x, o[0], o[1]);
-          e4m3x4_to_bf16(w.y, o[2], o[3]);
-          e4m3x4_to_bf16(w.z, o[4], o[5]);
-          e4m3x4_to_bf16(w.w, o[6], o[7]);
-        }
+          const uint4 w = *reinterpret_cast<const uint4*>(raw + row * 64 + ch * 16);
+          if constexpr (WF == W_Q8_0) {
+            // rows past N read TMA zero fill: scale 0, weights 0
+            const float s = __half2float(sc[(ch >> 1) * kWR + row]);
+            q8x4_to_bf16(w.x, s, o[0], o[1]);
+            q8x4_to_bf16(w.y, s, o[2], o[3]);
+            q8x4_to_bf16(w.z, s, o[4], o[5]);
+            q8x4_to_bf16(w.w, s, o[6], o[7]);
+          } else {
+            e4m3x4_to_bf16(w.x, o[0], o[1]);
+            e4m3x4_to_bf16(w.y, o[2], o[3]);
+            e4m3x4_to_bf16(w.z, o[4], o[5]);
+            e4m3x4_to_bf16(w.w, o[6], o[7]);
+          }
         }
         // bf16 row of 64 = eight 16-byte chunks; this task fills chunks 2*ch and 2*ch+1
         uint8_t* rowp = cvt + row * 128;
@@ -469,9 +665,13 @@ __global__ void __launch_bounds__(kQThreads, 1)
         *reinterpret_cast<uint4*>(rowp + (((2 * ch + 1) ^ (row & 7)) << 4)) =
             make_uint4(o[4], o[5], o[6], o[7]);
       }
+      // every lane's writes -> async proxy, then one arrival per warp
       fence_proxy_async_smem();
-      mbar_arrive(&raw_empty[rs]);
-      mbar_arrive(&cvt_full[cs]);
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&w_empty[ws]);
+        mbar_arrive(&cvt_full[cs]);  // paired peer: forwarded to the leader by warp 2
+      }
     }
 
     // ------------------------------------------------------------ epilogue
@@ -521,13 +721,18 @@ __global__ void __launch_bounds__(kQThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  // paired: no CTA leaves (or frees TMEM) while the leader's MMAs may still read its shared
+  // memory or write its TMEM, or while a peer arrival may still target its barriers
+  if constexpr (PAIR) ql_cluster_sync(); else __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem, 512); else tmem_dealloc(tmem, 512);
   }
 }
+
+// sp_quant_linear_set_pairing: 0 unpaired tiles (default), 1 paired when M > 256
+int g_ql_pairing = 0;
 
 // Bytes of one weight row of K values as the kernel reads them (values + scales / factors).
 template <int WF>
@@ -556,9 +761,9 @@ double ql_w_row_bytes(int64_t K) {
 // The orientation with the smaller modelled traffic wins, g as large as the hold budget allows
 // (then evened out over the passes it implies).
 template <int WF>
-void ql_raster(QlParams& q, int tiles_m, int tiles_n) {
+void ql_raster(QlParams& q, int tiles_m, int tiles_n, int m_rows) {
   const double hold = SP_QL_HOLD_MB * 1048576.0;
-  const double xt = (double)kQBM * q.K * 2, wt = (double)kQBN * ql_w_row_bytes<WF>(q.K);
+  const double xt = (double)m_rows * q.K * 2, wt = (double)kQBN * ql_w_row_bytes<WF>(q.K);
   const double X = xt * tiles_m, W = wt * tiles_n;
   auto plan = [&](int tiles, double tile_bytes, int& g) {
     g = std::max(1, std::min(tiles, (int)(hold / tile_bytes)));
@@ -584,6 +789,10 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
   using KF = KqFmt<WF>;
   if (KF::kIsK && (!aligned(p.kq_a, 16) || !aligned(p.kq_b, 16)))
     return set_error(SP_ERR_ALIGN, "quantized linear: k-quant factors must be 16-byte aligned");
+  // Paired (2-CTA) tiles, when enabled, whenever x has more than one 256-row tile: the
+  // pair's CTA count is the unpaired count rounded up to even.
+  const bool pair = WF != W_BF16 && p.M > kQBM && __atomic_load_n(&g_ql_pairing, __ATOMIC_RELAXED);
+  const uint32_t wrows = pair ? kQBN / 2 : kQBN;  // weight rows per CTA (TMA box height)
   CUtensorMap mx, mw, ms, mb;
   std::memset(&ms, 0, sizeof(ms));
   std::memset(&mb, 0, sizeof(mb));
@@ -596,17 +805,17 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
       return rc;
   }
   if (KF::kIsK) {
-    // nibbles [N, K/2] bytes: a k-tile of 64 values is 32 bytes of each of 256 rows
+    // nibbles [N, K/2] bytes: a k-tile of 64 values is 32 bytes of each of the CTA's rows
     const uint64_t dims[2] = {(uint64_t)(p.K / 2), (uint64_t)p.N};
     const uint64_t strides[1] = {(uint64_t)(p.K / 2)};
-    const uint32_t box[2] = {kQBK / 2, kQBN};
+    const uint32_t box[2] = {kQBK / 2, wrows};
     if (int rc = encode_tiled(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w8, dims, strides, box,
                               CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
-    // factors a, b [K/sub, N] f32: one box = the k-tile's sub-blocks x 256 rows
+    // factors a, b [K/sub, N] f32: one box = the k-tile's sub-blocks x the CTA's rows
     const uint64_t fdims[2] = {(uint64_t)p.N, (uint64_t)(p.K / KF::kSub)};
     const uint64_t fstrides[1] = {(uint64_t)p.N * 4};
-    const uint32_t fbox[2] = {kQBN, (uint32_t)KF::kFactorRows};
+    const uint32_t fbox[2] = {wrows, (uint32_t)KF::kFactorRows};
     if (int rc = encode_tiled(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.kq_a, fdims, fstrides,
                               fbox, CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
@@ -624,48 +833,57 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
   } else {
     const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
     const uint64_t strides[1] = {(uint64_t)p.K};
-    const uint32_t box[2] = {kQBK, kQBN};
+    const uint32_t box[2] = {kQBK, wrows};
     if (int rc = encode_tiled(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w8, dims, strides, box,
                               CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
   }
   if (WF == W_Q8_0) {
-    // scales [K/32, N] f16: one box = the 2 k-blocks of a k-tile x 256 rows
+    // scales [K/32, N] f16: one box = the 2 k-blocks of a k-tile x the CTA's rows
     const uint64_t dims[2] = {(uint64_t)p.N, (uint64_t)(p.K / 32)};
     const uint64_t strides[1] = {(uint64_t)p.N * 2};
-    const uint32_t box[2] = {kQBN, kQBK / 32};
+    const uint32_t box[2] = {wrows, kQBK / 32};
     if (int rc = encode_tiled(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.q8_scale, dims, strides,
                               box, CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
   }
-  auto kern = qlinear_kernel<WF>;
-  static_assert(QlSmem::kAlloc <= 232448 && QlSmemBf16::kAlloc <= 232448,
+  static_assert(QlSmem::kAlloc <= 232448 && QlSmemT<true>::kAlloc <= 232448 &&
+                    QlSmemBf16::kAlloc <= 232448,
                 "quantized linear smem budget");
-  constexpr int kSmem = WF == W_BF16 ? QlSmemBf16::kAlloc : QlSmem::kAlloc;
-  static unsigned long long attr_set = 0;
-  if (first_time_on_device(&attr_set)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  constexpr int kSmem1 = WF == W_BF16 ? QlSmemBf16::kAlloc : QlSmem::kAlloc;
+  constexpr int kSmem2 = QlSmemT<true>::kAlloc;
+  auto kern1 = qlinear_kernel<WF, false>;
+  auto kern2 = qlinear_kernel<WF, WF != W_BF16>;  // (bf16 weights never pair)
+  static unsigned long long attr_set[2] = {0, 0};
+  if (first_time_on_device(&attr_set[pair])) {
+    cudaError_t e = pair ? cudaFuncSetAttribute(kern2, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                kSmem2)
+                         : cudaFuncSetAttribute(kern1, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                kSmem1);
     if (e != cudaSuccess) {
-      __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
+      __atomic_fetch_and(&attr_set[pair], ~(1ull << current_device()), __ATOMIC_ACQ_REL);
       return set_error(SP_ERR_LAUNCH, "quantized linear: smem attribute failed: %s", cudaGetErrorString(e));
     }
   }
-  const int tiles_m = (int)((p.M + kQBM - 1) / kQBM), tiles_n = (int)((p.N + kQBN - 1) / kQBN);
+  // a paired tile is 512 x rows (two CTAs of 256), an unpaired one 256
+  const int m_rows = pair ? 2 * kQBM : kQBM, cta_per_tile = pair ? 2 : 1;
+  const int tiles_m = (int)((p.M + m_rows - 1) / m_rows), tiles_n = (int)((p.N + kQBN - 1) / kQBN);
   // Split-K when the tile grid leaves most SMs idle (the text-stream and modulation GEMMs of
   // the DiT blocks): each split's CTAs write f32 partials to stream-ordered scratch, and one
   // reduce pass sums them in a fixed order and runs the epilogue.  Scratch that cannot be had
   // means no split.
   QlParams q = p;
   const int ktotal = (int)(p.K / kQBK), tiles = tiles_m * tiles_n, sms = num_sms();
+  const int units = tiles * cta_per_tile;  // CTAs per split
   int splits = 1;
-  if (2 * tiles <= sms && ktotal >= 8) {
-    splits = std::min(std::min(8, sms / tiles), ktotal / 4);
+  if (2 * units <= sms && ktotal >= 8) {
+    splits = std::min(std::min(8, sms / units), ktotal / 4);
   } else if (ktotal >= 128) {
     // long K with a badly quantised last wave (e.g. 192 tiles on 148 SMs: 65 % busy): split
     // 2-4 ways when that fills the waves better; the f32 partials (S x M x N x 4 bytes, written
     // and read once) cost little next to K >= 8192 of MMA work
     auto eff = [&](int sp) {
-      const int ctas = tiles * sp;
+      const int ctas = units * sp;
       return (double)ctas / ((double)((ctas + sms - 1) / sms) * sms);
     };
     double best = eff(1);
@@ -698,9 +916,29 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
   }
   q.ws = static_cast<float*>(ws);
   q.splits = splits;
-  ql_raster<WF>(q, tiles_m, tiles_n);
-  dim3 grid((unsigned)tiles, (unsigned)splits);
-  kern<<<grid, kQThreads, kSmem, s>>>(mx, mw, ms, mb, q);
+  ql_raster<WF>(q, tiles_m, tiles_n, m_rows);
+  if (pair) {
+    // clusters of two consecutive CTAs along x: CTA 2t is tile t's leader, 2t + 1 its peer
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)units, (unsigned)splits, 1);
+    cfg.blockDim = dim3(kQThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmem2;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern2, mx, mw, ms, mb, q);
+    if (e != cudaSuccess)
+      return set_error(SP_ERR_LAUNCH, "quantized linear: paired launch failed: %s",
+                       cudaGetErrorString(e));
+  } else {
+    dim3 grid((unsigned)units, (unsigned)splits);
+    kern1<<<grid, kQThreads, kSmem1, s>>>(mx, mw, ms, mb, q);
+  }
   if (splits > 1) {
     const int64_t groups = p.M * (p.N / 8);
     const unsigned rblocks = (unsigned)std::min<int64_t>((groups + 255) / 256, 8LL * sms);
@@ -864,6 +1102,13 @@ int sp_q8_0_linear_glu(const void* x, const void* q, const void* scale, const vo
   e.glu = glu_kind < 0 ? SP_GLU_SWIGLU + 1 : glu_kind;  // negative kinds are rejected
   return sp::ql_entry<sp::W_Q8_0>("q8_0 linear", x, q, scale, nullptr, 0, bias, y, M, N, K, dtype,
                                   e, stream);
+}
+
+int sp_quant_linear_set_pairing(int mode) {
+  sp::clear_error();
+  if (mode != 0 && mode != 1)
+    return sp::set_error(SP_ERR_INVALID_ARG, "quantized linear pairing: mode must be 0 or 1");
+  return __atomic_exchange_n(&sp::g_ql_pairing, mode, __ATOMIC_RELAXED);
 }
 
 int sp_fp8_linear_glu(const void* x, const void* w_e4m3, const float* scale, int64_t nscale,

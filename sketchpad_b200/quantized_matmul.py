@@ -284,6 +284,16 @@ class GpuQuantizedLinear:
     __call__ = forward
 
 
+def set_tile_pairing(enabled: bool) -> bool:
+    """Process-wide tile mode of the quantized linears (sp_quant_linear_set_pairing): True runs
+    two-CTA clusters per 512 x 256 tile (tcgen05.mma.cta_group::2) when M > 256; False (the
+    default) one CTA per 256 x 256 tile.  Results are bit-identical.  Returns the old mode."""
+    rc = _lib.load().sp_quant_linear_set_pairing(1 if enabled else 0)
+    if rc < 0:
+        raise _lib.SketchpadError("sp_quant_linear_set_pairing", rc, _lib.load().sp_last_error().decode())
+    return bool(rc)
+
+
 def q8_0_quantize_reference(w: np.ndarray) -> bytes:
     """GGUF Q8_0 encoder for building test/bench weights (ggml's scheme: per 32 values,
     d = absmax/127 stored as f16, q = round(v/d)).  Used only to make synthetic inputs."""
@@ -327,6 +337,6 @@ def make_q8_0_synthetic(out_features: int, in_features: int, seed: int = 0) -> b
     return blocks.tobytes()
 
 
-__all__ = ["GpuQuantType", "GpuQuantizedLinear", "dequantize_q8_0", "repack_q8_0",
+__all__ = ["GpuQuantType", "GpuQuantizedLinear", "dequantize_q8_0", "repack_q8_0", "set_tile_pairing",
            "repack_q8_0_host", "q8_0_quantize_reference", "make_q8_0_synthetic",
            "repack_kquant_host", "dequantize_kquant", "make_kquant_synthetic"]

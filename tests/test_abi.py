@@ -109,3 +109,11 @@ def test_nccl_unique_id_on_the_host():
         return
     assert rc == 0 and L.sp_nccl_unique_id(b, n) == 0
     assert a.raw != bytes(n) and a.raw != b.raw
+
+
+def test_quant_linear_pairing_mode_switch_on_the_host():
+    L = _lib.load()
+    assert L.sp_quant_linear_set_pairing(2) == -1  # SP_ERR_INVALID_ARG
+    old = L.sp_quant_linear_set_pairing(1)
+    assert old in (0, 1)
+    assert L.sp_quant_linear_set_pairing(old) == 1

@@ -417,3 +417,36 @@ def test_fp8_linear_glu_epilogue():
     lo = oracle.linear_nt(to_np(x[rows]), to_np(la.weight.dequantize()))
     hi = oracle.linear_nt(to_np(x[rows]), to_np(lb.weight.dequantize()))
     assert rel_err(to_np(y[rows]), oracle.activation(lo, "silu") * hi) < TOL_HALF
+
+
+@pytest.mark.parametrize("fmt", ["Q8_0", "FP8", "Q4K", "Q2K", "Q3K"])
+@pytest.mark.parametrize("M,N,K", [(600, 272, 512), (1024, 768, 512), (300, 160, 256)])
+def test_paired_tiles_bit_identical_to_unpaired(fmt, M, N, K):
+    # sp_quant_linear_set_pairing(1): two-CTA clusters per 512 x 256 tile (cta_group::2 MMA);
+    # ragged M (a peer CTA past the last row) and N (a peer's weight rows past N) included;
+    # the f32 accumulation order per output is unchanged, so the bytes must match
+    from sketchpad_b200.quantized_matmul import (make_kquant_synthetic, set_tile_pairing)
+    g = torch.Generator(device="cpu").manual_seed(M + N)
+    bias = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16).cuda()
+    if fmt == "FP8":
+        w = torch.randn(N, K, generator=g) * 0.02
+        lin = Fp8Linear.from_weight(w.cuda(), bias, Fp8Config.e4m3().with_per_channel(True))
+    elif fmt == "Q8_0":
+        lin = GpuQuantizedLinear.from_bytes(make_q8_0_synthetic(N, K, seed=M), GpuQuantType.Q8_0,
+                                            N, K, bias=bias)
+    else:
+        qt = GpuQuantType[fmt]
+        lin = GpuQuantizedLinear.from_bytes(make_kquant_synthetic(qt, N, K, seed=M), qt, N, K,
+                                            bias=bias)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    old = set_tile_pairing(False)
+    try:
+        y0 = lin.forward(x)
+        set_tile_pairing(True)
+        y1 = lin.forward(x)
+        torch.cuda.synchronize()
+    finally:
+        set_tile_pairing(old)
+    assert torch.equal(y0, y1)
+
+
