@@ -303,11 +303,6 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
 __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
@@ -408,29 +403,31 @@ struct GnSliceParams {
 
 struct SlUnit {
   int pass;
-  int64_t g, s;
+  uint32_t g, s;
 };
 
 // Sequence entry u: L*S pass-0 units of groups [0, L); then per t in [L, BG) the S pass-0
 // units of group t followed by the S pass-1 units of group t - L; then the pass-1 units of
-// groups [BG - L, BG).
-__device__ __forceinline__ SlUnit sl_unit(const GnSliceParams& p, int64_t u) {
-  const int64_t S = p.S, L = p.L, head = L * S, mid = 2 * S * (p.BG - L);
+// groups [BG - L, BG).  The launcher keeps 2 * BG * S below 2^31, so 32-bit arithmetic
+// suffices (a 64-bit division is a long subroutine, and every role decodes every unit).
+__device__ __forceinline__ SlUnit sl_unit(const GnSliceParams& p, uint32_t u) {
+  const uint32_t S = (uint32_t)p.S, L = (uint32_t)p.L, BG = (uint32_t)p.BG;
+  const uint32_t head = L * S, mid = 2 * S * (BG - L);
   SlUnit r;
   if (u < head) {
     r.pass = 0;
     r.g = u / S;
     r.s = u - r.g * S;
   } else if (u < head + mid) {
-    const int64_t v = u - head, t = L + v / (2 * S), w = v - (t - L) * 2 * S;
+    const uint32_t v = u - head, t = v / (2 * S), w = v - t * 2 * S;
     r.pass = w < S ? 0 : 1;
-    r.g = w < S ? t : t - L;
+    r.g = w < S ? L + t : t;
     r.s = w < S ? w : w - S;
   } else {
-    const int64_t v = u - head - mid;
+    const uint32_t v = u - head - mid, q = v / S;
     r.pass = 1;
-    r.g = p.BG - L + v / S;
-    r.s = v % S;
+    r.g = BG - L + q;
+    r.s = v - q * S;
   }
   return r;
 }
@@ -454,17 +451,20 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
   constexpr int VE = VecTraits<T>::kElems;
   constexpr int kCWarps = kSlConsumers / 32;
   constexpr int64_t kSv = kSlBytes / 16;  // 16-byte vectors per slice
+  constexpr int kIt = (int)(kSv / kSlConsumers);  // vectors per consumer thread per slice
+  static_assert(kSv % kSlConsumers == 0, "slice vectors per consumer");
   extern __shared__ uint8_t sl_smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sl_smem_raw) + 127) &
                                              ~uintptr_t(127));
   __shared__ uint64_t full[kSlStages], empty[kSlStages], part_full[kSlStages],
       stat_full[kSlStages];
-  __shared__ float4 wpart[kSlStages][kCWarps];  // (count, mean, M2, max |x|) per consumer warp
+  // per consumer warp: (sum of x - shift, sum of (x - shift)^2, max |x|, unused)
+  __shared__ float4 wpart[kSlStages][kCWarps];
   __shared__ float4 gstat[kSlStages];           // (mean, rstd, max |x|, no_clamp)
   __shared__ int abort_flag_s;
   volatile int* abort_flag = &abort_flag_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t total = 2 * p.BG * p.S;
+  const uint32_t total = (uint32_t)(2 * p.BG * p.S);
   const int64_t nvec = p.n / VE;
   const T* gam = static_cast<const T*>(p.gamma);
   const T* bet = static_cast<const T*>(p.beta);
@@ -486,7 +486,7 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
     if (lane == 0) {
       const uint64_t keep = l2_policy(true), drop = l2_policy(false);
       uint32_t k = 0;  // units issued
-      for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
+      for (uint32_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
         const uint32_t st = k % kSlStages;
         if (k >= kSlStages &&
             !sl_wait(&empty[st], ((k / kSlStages) - 1) & 1, abort_flag, WD_TMA_WAIT))
@@ -514,7 +514,7 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
     // the group's counter.  Every unit: its arrival on empty[st] (after full[st], so it can
     // never count toward the stage's previous phase).
     uint32_t k = 0, pph = 0;  // pph: per-stage part_full parity
-    for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
+    for (uint32_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
       const uint32_t st = k % kSlStages;
       if (!sl_wait_warp(&full[st], (k / kSlStages) & 1, abort_flag, WD_CONVERT_WAIT)) break;
       const SlUnit un = sl_unit(p, u);
@@ -522,15 +522,22 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
         if (!sl_wait_warp(&part_full[st], (pph >> st) & 1, abort_flag, WD_CONVERT_WAIT)) break;
         pph ^= 1u << st;
         if (lane == 0) {
-          const float4 a = wpart[st][0];
-          Welford t{a.x, a.y, a.z};
-          float am = a.w;
-          for (int i = 1; i < kCWarps; ++i) {
+          // the consumer warps' shifted sums, in warp order; the shift is the slice's first
+          // element (clamped), as the consumers took it
+          float t1 = 0.f, t2 = 0.f, am = 0.f;
+          for (int i = 0; i < kCWarps; ++i) {
             const float4 b = wpart[st][i];
-            t = welford_merge(t, Welford{b.x, b.y, b.z});
-            am = fmaxf(am, b.w);
+            t1 += b.x;
+            t2 += b.y;
+            am = fmaxf(am, b.z);
           }
-          p.part[un.g * p.S + un.s] = make_float4(t.n, t.mean, t.m2, am);
+          float f0[VE];
+          unpack<T>(*reinterpret_cast<const uint4*>(ring + st * kSlBytes), f0);
+          const int64_t v0 = (int64_t)un.s * kSv;
+          const float cnt = (float)((min(nvec, v0 + kSv) - v0) * VE);
+          const float m = t1 / cnt;
+          p.part[un.g * p.S + un.s] =
+              make_float4(cnt, clamp65k(f0[0]) + m, fmaxf(t2 - t1 * m, 0.f), am);
           red_release_add(p.ready + un.g, 1u);
         }
         __syncwarp();
@@ -557,7 +564,7 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
       bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
     }
     uint32_t k = 0;
-    for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
+    for (uint32_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
       const uint32_t st = k % kSlStages;
       // unit k's slice landed: the stage's previous unit is done, gstat[st] no longer read
       if (!sl_wait_warp(&full[st], (k / kSlStages) & 1, abort_flag, WD_CONVERT_WAIT)) break;
@@ -602,67 +609,65 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
   const uint32_t vpc = (uint32_t)(p.HW / VE);  // vectors per channel
   // kSlConsumers vectors = vstep_q channels + vstep_r vectors
   const uint32_t vstep_q = kSlConsumers / vpc, vstep_r = kSlConsumers % vpc;
+  // slices start at multiples of kSv vectors: when that divides the channel length, no
+  // slice straddles two channels
+  const bool one_channel = vpc % (uint32_t)kSv == 0;
   uint32_t k = 0, sph = 0;  // sph: per-stage stat_full parity
-  for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
+  for (uint32_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
     const uint32_t st = k % kSlStages, ph = (k / kSlStages) & 1;
     const SlUnit un = sl_unit(p, u);
     const int64_t v0 = un.s * kSv;
     const uint32_t cv = (uint32_t)(min(nvec, v0 + kSv) - v0);
     const uint4* sv = reinterpret_cast<const uint4*>(ring + st * kSlBytes);
     if (un.pass == 0) {
-      // ---- pass 0: statistics of clamp(x) and max |x| over the slice
+      // ---- pass 0: statistics of clamp(x) and max |x| over the slice.  Sums of x - shift
+      // about one value common to the whole slice (its first element), so that the threads'
+      // partials combine by plain addition; the publisher turns the slice's sums into
+      // (count, mean, M2).
       if (!sl_wait_warp(&full[st], ph, abort_flag, WD_CONVERT_WAIT)) break;
-      const uint64_t zero2 = f2(0.f, 0.f);
-      uint64_t sh2 = zero2, s1 = zero2, s2 = zero2;
-      float amax = 0.f, cnt = 0.f;
-      bool first = true;
-#pragma unroll 2
-      for (uint32_t i = threadIdx.x; i < cv; i += kSlConsumers) {
-        float f[VE];
-        unpack<T>(sv[i], f);
-        float vm = fabsf(f[0]);
+      float f0[VE];
+      unpack<T>(sv[0], f0);
+      const float shift = clamp65k(f0[0]);
+      const uint64_t sh2 = f2(shift, shift);
+      uint64_t s1 = f2(0.f, 0.f), s2 = s1;
+      float amax = 0.f;
 #pragma unroll
-        for (int e = 1; e < VE; ++e) vm = fmaxf(vm, fabsf(f[e]));
-        amax = fmaxf(amax, vm);
-        if (vm > kClamp) {  // clamp(x) differs from x only above the bound
+      for (int it = 0; it < kIt; ++it) {
+        const uint32_t i = threadIdx.x + it * kSlConsumers;
+        if (i < cv) {
+          float f[VE];
+          unpack<T>(sv[i], f);
+          float vm = fabsf(f[0]);
 #pragma unroll
-          for (int e = 0; e < VE; ++e) f[e] = clamp65k(f[e]);
-        }
-        if (first) {
-          sh2 = f2(f[0], f[0]);
-          first = false;
-        }
+          for (int e = 1; e < VE; ++e) vm = fmaxf(vm, fabsf(f[e]));
+          amax = fmaxf(amax, vm);
+          if (vm > kClamp) {  // clamp(x) differs from x only above the bound
 #pragma unroll
-        for (int e = 0; e < VE; e += 2) {
-          const uint64_t d = f2_sub(f2(f[e], f[e + 1]), sh2);
-          s1 = f2_add(s1, d);
-          s2 = f2_fma(d, d, s2);
+            for (int e = 0; e < VE; ++e) f[e] = clamp65k(f[e]);
+          }
+#pragma unroll
+          for (int e = 0; e < VE; e += 2) {
+            const uint64_t d = f2_sub(f2(f[e], f[e + 1]), sh2);
+            s1 = f2_add(s1, d);
+            s2 = f2_fma(d, d, s2);
+          }
         }
-        cnt += (float)VE;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
-      Welford w{cnt, 0.f, 0.f};
-      if (cnt > 0.f) {
-        float a, b, shift, dummy;
-        f2_split(s1, a, b);
-        const float t1 = a + b;
-        f2_split(s2, a, b);
-        const float t2 = a + b;
-        f2_split(sh2, shift, dummy);
-        const float m = t1 / cnt;
-        w.mean = shift + m;
-        w.m2 = fmaxf(t2 - t1 * m, 0.f);
-      }
+      float a, b;
+      f2_split(s1, a, b);
+      float t1 = a + b;
+      f2_split(s2, a, b);
+      float t2 = a + b;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
-        Welford b{__shfl_xor_sync(0xffffffffu, w.n, o), __shfl_xor_sync(0xffffffffu, w.mean, o),
-                  __shfl_xor_sync(0xffffffffu, w.m2, o)};
-        w = welford_merge(w, b);
+        t1 += __shfl_xor_sync(0xffffffffu, t1, o);
+        t2 += __shfl_xor_sync(0xffffffffu, t2, o);
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       }
       if (lane == 0) {
-        wpart[st][warp] = make_float4(w.n, w.mean, w.m2, amax);
+        wpart[st][warp] = make_float4(t1, t2, amax, 0.f);
         mbar_arrive(&part_full[st]);
       }
       continue;
@@ -683,22 +688,9 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
     const T* gam_g = gam + (un.g % p.G) * p.cg;  // this group's channels
     const T* bet_g = bet + (un.g % p.G) * p.cg;
     uint4* yv = reinterpret_cast<uint4*>(static_cast<T*>(p.y) + un.g * p.n) + v0;
-    // channel of the thread's vector v0 + i, tracked as (q, rem) = divmod(v0 + i, vpc) and
-    // stepped by kSlConsumers vectors per iteration; gamma, beta reloaded when it changes
-    uint32_t q = ((uint32_t)v0 + threadIdx.x) / vpc;
-    uint32_t rem = ((uint32_t)v0 + threadIdx.x) - q * vpc;
-    uint32_t qc = 0xffffffffu;
-    float wc = 0.f, bc = 0.f;
-    uint64_t w2 = 0, b2 = 0;
-#pragma unroll 2
-    for (uint32_t i = threadIdx.x; i < cv; i += kSlConsumers) {
-      if (q != qc) {
-        qc = q;
-        wc = to_f32(__ldg(gam_g + q)) * rstd;
-        bc = to_f32(__ldg(bet_g + q));
-        w2 = f2(hs * wc, hs * wc);
-        b2 = f2(hs * bc, hs * bc);
-      }
+    // normalise vector i of the slice with channel factors (wc, bc) (w2, b2 = the halved
+    // factors for the packed SiLU form) and store it
+    auto apply_store = [&](uint32_t i, float wc, float bc, uint64_t w2, uint64_t b2) {
       float f[VE];
       unpack<T>(sv[i], f);
       if (no_clamp) {
@@ -717,11 +709,41 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
         for (int e = 0; e < VE; ++e) f[e] = apply_act((clamp65k(f[e]) - mean) * wc + bc, p.act);
       }
       yv[i] = pack<T>(f);
-      rem += vstep_r;
-      q += vstep_q;
-      if (rem >= vpc) {
-        rem -= vpc;
-        ++q;
+    };
+    if (one_channel) {
+      // the slice lies inside one channel: one (gamma, beta) for the whole unit
+      const uint32_t q = (uint32_t)v0 / vpc;
+      const float wc = to_f32(__ldg(gam_g + q)) * rstd, bc = to_f32(__ldg(bet_g + q));
+      const uint64_t w2 = f2(hs * wc, hs * wc), b2 = f2(hs * bc, hs * bc);
+#pragma unroll
+      for (int it = 0; it < kIt; ++it) {
+        const uint32_t i = threadIdx.x + it * kSlConsumers;
+        if (i < cv) apply_store(i, wc, bc, w2, b2);
+      }
+    } else {
+      // channel of the thread's vector v0 + i, tracked as (q, rem) = divmod(v0 + i, vpc) and
+      // stepped by kSlConsumers vectors per iteration; gamma, beta reloaded when it changes
+      uint32_t q = ((uint32_t)v0 + threadIdx.x) / vpc;
+      uint32_t rem = ((uint32_t)v0 + threadIdx.x) - q * vpc;
+      uint32_t qc = 0xffffffffu;
+      float wc = 0.f, bc = 0.f;
+      uint64_t w2 = 0, b2 = 0;
+#pragma unroll 2
+      for (uint32_t i = threadIdx.x; i < cv; i += kSlConsumers) {
+        if (q != qc) {
+          qc = q;
+          wc = to_f32(__ldg(gam_g + q)) * rstd;
+          bc = to_f32(__ldg(bet_g + q));
+          w2 = f2(hs * wc, hs * wc);
+          b2 = f2(hs * bc, hs * bc);
+        }
+        apply_store(i, wc, bc, w2, b2);
+        rem += vstep_r;
+        q += vstep_q;
+        if (rem >= vpc) {
+          rem -= vpc;
+          ++q;
+        }
       }
     }
     __syncwarp();
@@ -840,8 +862,10 @@ GnPlan plan_gn(int64_t B, int64_t G, int64_t cg, int64_t n, bool contiguous, boo
   // stay within the 128 registers that two resident CTAs per SM allow.
   const int max_vpt = vec_elems == 4 ? 16 : 8;
   const int64_t group_bytes = n * (16 / vec_elems);
+  // slice units are numbered in 32 bits by the streaming kernel
+  const int64_t stream_units = 2 * B * G * ((group_bytes + kSlBytes - 1) / kSlBytes);
   if (contiguous && vec_ok && n < (1LL << 31) && group_bytes >= kStreamMinGroupBytes &&
-      cg <= kSlMaxCg) {
+      cg <= kSlMaxCg && stream_units < (1LL << 31)) {
     pl.stream_path = true;
     return pl;
   }
