@@ -267,7 +267,8 @@ constexpr int kSlProducerWarp = kSlConsumers / 32;  // warp 8
 constexpr int kSlPublisherWarp = kSlProducerWarp + 1;
 constexpr int kSlStatsWarp = kSlProducerWarp + 2;
 constexpr int kSlThreads = kSlConsumers + 3 * 32;
-constexpr int kSlEmptyCount = kSlConsumers / 32 + 2;  // consumer warps, publisher, stats
+constexpr int kSlEmptyCount = kSlConsumers / 32 + 1;  // consumer warps, publisher
+constexpr int kStatSlots = 8;  // pass-1 statistics the statistics warp may prepare ahead
 constexpr int kSlBytes = 32768;  // one slice unit
 constexpr int kSlStages = 3;     // 96 KB: two CTAs per SM
 constexpr int kSlMaxCg = 1024;   // channels per group the shared affine table holds
@@ -437,15 +438,18 @@ __device__ __forceinline__ SlUnit sl_unit(const GnSliceParams& p, uint32_t u) {
 //
 // Per ring stage st, for the unit k the stage holds (k % kSlStages == st):
 //   full[st]       the slice landed (producer's bulk copy)
-//   empty[st]      the 8 consumer warps, the publisher and the statistics warp are done
-//                  with it (kSlEmptyCount)
+//   empty[st]      the 8 consumer warps and the publisher are done with it (kSlEmptyCount)
 //   part_full[st]  pass 0: the 8 consumer warps wrote their partials to wpart[st]
-//   stat_full[st]  pass 1: the statistics warp wrote the group's stats to gstat[st]
-// part_full and stat_full complete once per pass-0 (pass-1) unit of the stage, so their
-// waiters track the phase parity per stage.  Every role that waits on full[st] also arrives on
-// empty[st] for every unit: the producer cannot refill a stage before each of them has seen
-// the unit, so none of them can be a whole ring cycle ahead of or behind a barrier's phase
-// (a parity wait would then match the wrong phase).
+// and per statistics slot (the CTA's i-th pass-1 unit uses slot i % kStatSlots):
+//   stat_full[i]   the statistics warp wrote the group's stats to gstat[i] (and the channel
+//                  factors to gaff[i])
+//   stat_empty[i]  the 8 consumer warps have read them
+// part_full completes once per pass-0 unit of the stage, so its waiters track the phase
+// parity per stage.  The consumers and the publisher arrive on empty[st] for every unit, and
+// the producer waits for the stage's previous unit to be released before it starts unit k;
+// the statistics warp waits for a slot's previous use to be read before it refills it.  So
+// no role can be a whole ring (or slot) cycle ahead of or behind a barrier's phase (a parity
+// wait would then match the wrong phase).
 template <typename T>
 __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p) {
   constexpr int VE = VecTraits<T>::kElems;
@@ -456,11 +460,13 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
   extern __shared__ uint8_t sl_smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sl_smem_raw) + 127) &
                                              ~uintptr_t(127));
-  __shared__ uint64_t full[kSlStages], empty[kSlStages], part_full[kSlStages],
-      stat_full[kSlStages];
+  __shared__ uint64_t full[kSlStages], empty[kSlStages], part_full[kSlStages];
+  __shared__ uint64_t stat_full[kStatSlots], stat_empty[kStatSlots];
   // per consumer warp: (sum of x - shift, sum of (x - shift)^2, max |x|, unused)
   __shared__ float4 wpart[kSlStages][kCWarps];
-  __shared__ float4 gstat[kSlStages];           // (mean, rstd, max |x|, no_clamp)
+  __shared__ float4 gstat[kStatSlots];  // (mean, rstd, max |x|, no_clamp)
+  // (gamma[c] * rstd, beta[c]) of the unit's channel when the slice lies in one channel
+  __shared__ float2 gaff[kStatSlots];
   __shared__ int abort_flag_s;
   volatile int* abort_flag = &abort_flag_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -468,13 +474,20 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
   const int64_t nvec = p.n / VE;
   const T* gam = static_cast<const T*>(p.gamma);
   const T* bet = static_cast<const T*>(p.beta);
+  const uint32_t vpc = (uint32_t)(p.HW / VE);  // vectors per channel
+  // slices start at multiples of kSv vectors: when that divides the channel length, no
+  // slice straddles two channels
+  const bool one_channel = vpc % (uint32_t)kSv == 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSlStages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kSlEmptyCount);
       mbar_init(&part_full[i], kCWarps);
+    }
+    for (int i = 0; i < kStatSlots; ++i) {
       mbar_init(&stat_full[i], 1);
+      mbar_init(&stat_empty[i], kCWarps);
     }
     abort_flag_s = 0;
     fence_mbar_init();
@@ -510,9 +523,10 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
 
   if (warp == kSlPublisherWarp) {
     // ------------------------------------------------------------------ publisher
-    // pass 0: merge the 8 warp partials in warp order, publish the slice's partial, release
-    // the group's counter.  Every unit: its arrival on empty[st] (after full[st], so it can
-    // never count toward the stage's previous phase).
+    // pass 0: merge the 8 warp partials in warp order into the slice's partial, release the
+    // stage, publish the partial and count it on the group's counter.  Every unit: one
+    // arrival on empty[st], after full[st] (so it can never count toward the stage's previous
+    // phase).
     uint32_t k = 0, pph = 0;  // pph: per-stage part_full parity
     for (uint32_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
       const uint32_t st = k % kSlStages;
@@ -533,6 +547,7 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
           }
           float f0[VE];
           unpack<T>(*reinterpret_cast<const uint4*>(ring + st * kSlBytes), f0);
+          mbar_arrive(&empty[st]);  // the stage is no longer read
           const int64_t v0 = (int64_t)un.s * kSv;
           const float cnt = (float)((min(nvec, v0 + kSv) - v0) * VE);
           const float m = t1 / cnt;
@@ -541,19 +556,21 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
           red_release_add(p.ready + un.g, 1u);
         }
         __syncwarp();
+      } else if (lane == 0) {
+        mbar_arrive(&empty[st]);
       }
-      if (lane == 0) mbar_arrive(&empty[st]);
     }
     return;
   }
 
   if (warp == kSlStatsWarp) {
     // ------------------------------------------------------------------ statistics
-    // pass 1: once the unit's slice has landed (so ahead of the consumers, which are still on
-    // earlier units), wait for the group's S partials, merge them (lane j takes partials j,
-    // j + 32, ... in order, then a fixed xor tree), and hand (mean, rstd, max |x|, no_clamp)
-    // to the consumers.
-    float gm = 0.f, bm = 0.f;  // max |gamma|, max |beta| over all channels
+    // pass 1, up to kStatSlots units ahead of the consumers: wait for the group's S partials,
+    // merge them (lane j takes partials j, j + 32, ... in order, then a fixed xor tree), and
+    // hand (mean, rstd, max |x|, no_clamp) and, for a slice inside one channel,
+    // (gamma[c] * rstd, beta[c]) to the consumers through slot i % kStatSlots of the CTA's
+    // i-th pass-1 unit.
+    float gm = 0.f, bm = 0.f;  // max |gamma|, max |beta| over all channels (for no_clamp)
     for (int64_t c = lane; c < p.C; c += 32) {
       gm = fmaxf(gm, fabsf(to_f32(gam[c])));
       bm = fmaxf(bm, fabsf(to_f32(bet[c])));
@@ -563,42 +580,46 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
       gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
       bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
     }
-    uint32_t k = 0;
-    for (uint32_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
-      const uint32_t st = k % kSlStages;
-      // unit k's slice landed: the stage's previous unit is done, gstat[st] no longer read
-      if (!sl_wait_warp(&full[st], (k / kSlStages) & 1, abort_flag, WD_CONVERT_WAIT)) break;
+    uint32_t i = 0;  // pass-1 units handled
+    for (uint32_t u = blockIdx.x; u < total; u += gridDim.x) {
       const SlUnit un = sl_unit(p, u);
-      if (un.pass == 1) {
-        if (!__all_sync(0xffffffffu, wait_ready(p.ready + un.g, (unsigned)p.S, abort_flag)))
-          break;
-        const float4* gp = p.part + un.g * p.S;
-        Welford t{0.f, 0.f, 0.f};
-        float am = 0.f;
-        for (int64_t j = lane; j < p.S; j += 32) {
-          const float4 q = gp[j];
-          t = welford_merge(t, Welford{q.x, q.y, q.z});
-          am = fmaxf(am, q.w);
-        }
+      if (un.pass != 1) continue;
+      const uint32_t slot = i % kStatSlots;
+      if (i >= kStatSlots && !sl_wait_warp(&stat_empty[slot], ((i / kStatSlots) - 1) & 1,
+                                           abort_flag, WD_CONVERT_WAIT))
+        break;
+      if (!__all_sync(0xffffffffu, wait_ready(p.ready + un.g, (unsigned)p.S, abort_flag)))
+        break;
+      const float4* gp = p.part + un.g * p.S;
+      Welford t{0.f, 0.f, 0.f};
+      float am = 0.f;
+      for (int64_t j = lane; j < p.S; j += 32) {
+        const float4 q = gp[j];
+        t = welford_merge(t, Welford{q.x, q.y, q.z});
+        am = fmaxf(am, q.w);
+      }
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          Welford b{__shfl_xor_sync(0xffffffffu, t.n, o),
-                    __shfl_xor_sync(0xffffffffu, t.mean, o),
-                    __shfl_xor_sync(0xffffffffu, t.m2, o)};
-          // fixed operand order (lower lane first) so both lanes of a pair agree
-          t = (lane & o) ? welford_merge(b, t) : welford_merge(t, b);
-          am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+      for (int o = 1; o < 32; o <<= 1) {
+        Welford b{__shfl_xor_sync(0xffffffffu, t.n, o), __shfl_xor_sync(0xffffffffu, t.mean, o),
+                  __shfl_xor_sync(0xffffffffu, t.m2, o)};
+        // fixed operand order (lower lane first) so both lanes of a pair agree
+        t = (lane & o) ? welford_merge(b, t) : welford_merge(t, b);
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+      }
+      if (lane == 0) {
+        const float rstd = rsqrtf(t.m2 / t.n + p.eps);
+        // no clamp can bite when |x| <= 65000 and |(x - mean) * w + b| <= 65000 for all x, c
+        const bool no_clamp = am <= kClamp && (am + fabsf(t.mean)) * gm * rstd + bm <= kClamp;
+        gstat[slot] = make_float4(t.mean, rstd, am, no_clamp ? 1.f : 0.f);
+        if (one_channel) {
+          const uint32_t q = un.s * (uint32_t)kSv / vpc;
+          const int64_t c = (int64_t)(un.g % p.G) * p.cg + q;
+          gaff[slot] = make_float2(to_f32(gam[c]) * rstd, to_f32(bet[c]));
         }
-        if (lane == 0) {
-          const float rstd = rsqrtf(t.m2 / t.n + p.eps);
-          // no clamp can bite when |x| <= 65000 and |(x - mean) * w + b| <= 65000 for all x, c
-          const bool no_clamp = am <= kClamp && (am + fabsf(t.mean)) * gm * rstd + bm <= kClamp;
-          gstat[st] = make_float4(t.mean, rstd, am, no_clamp ? 1.f : 0.f);
-          mbar_arrive(&stat_full[st]);  // release: gstat is visible to the waiters
-        }
+        mbar_arrive(&stat_full[slot]);  // release: gstat / gaff are visible to the waiters
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
+      ++i;
     }
     return;
   }
@@ -606,13 +627,9 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
   // ------------------------------------------------------------------ consumers
   // Waits that expire set the shared abort flag; every later wait then returns false at once
   // and the warps leave the unit loop.
-  const uint32_t vpc = (uint32_t)(p.HW / VE);  // vectors per channel
   // kSlConsumers vectors = vstep_q channels + vstep_r vectors
   const uint32_t vstep_q = kSlConsumers / vpc, vstep_r = kSlConsumers % vpc;
-  // slices start at multiples of kSv vectors: when that divides the channel length, no
-  // slice straddles two channels
-  const bool one_channel = vpc % (uint32_t)kSv == 0;
-  uint32_t k = 0, sph = 0;  // sph: per-stage stat_full parity
+  uint32_t k = 0, i1 = 0;  // i1: pass-1 units handled (statistics slot i1 % kStatSlots)
   for (uint32_t u = blockIdx.x; u < total; u += gridDim.x, ++k) {
     const uint32_t st = k % kSlStages, ph = (k / kSlStages) & 1;
     const SlUnit un = sl_unit(p, u);
@@ -674,9 +691,14 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
     }
 
     // ---- pass 1: normalise, affine, activation, store
-    if (!sl_wait_warp(&stat_full[st], (sph >> st) & 1, abort_flag, WD_CONVERT_WAIT)) break;
-    sph ^= 1u << st;
-    const float4 gs = gstat[st];
+    const uint32_t slot = i1 % kStatSlots;
+    if (!sl_wait_warp(&stat_full[slot], (i1 / kStatSlots) & 1, abort_flag, WD_CONVERT_WAIT))
+      break;
+    ++i1;
+    const float4 gs = gstat[slot];
+    const float2 af = gaff[slot];  // published by the same arrival
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&stat_empty[slot]);  // the slot may be refilled
     const float mean = gs.x, rstd = gs.y;
     const bool no_clamp = gs.w != 0.f;
     if (!sl_wait_warp(&full[st], ph, abort_flag, WD_CONVERT_WAIT)) break;
@@ -711,9 +733,9 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
       yv[i] = pack<T>(f);
     };
     if (one_channel) {
-      // the slice lies inside one channel: one (gamma, beta) for the whole unit
-      const uint32_t q = (uint32_t)v0 / vpc;
-      const float wc = to_f32(__ldg(gam_g + q)) * rstd, bc = to_f32(__ldg(bet_g + q));
+      // the slice lies inside one channel: one (gamma * rstd, beta) for the whole unit,
+      // prepared by the statistics warp
+      const float wc = af.x, bc = af.y;
       const uint64_t w2 = f2(hs * wc, hs * wc), b2 = f2(hs * bc, hs * bc);
 #pragma unroll
       for (int it = 0; it < kIt; ++it) {
