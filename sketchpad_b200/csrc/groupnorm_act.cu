@@ -115,6 +115,35 @@ __device__ __forceinline__ float tanh_approx(float x) {
   return y;
 }
 
+// Two 16-bit lanes (f16x2 / bf16x2 by T): round a pair of f32 values, tanh, fused h*t + h.
+template <typename T>
+__device__ __forceinline__ uint32_t cvt2_16(float lo, float hi) {
+  uint32_t r;
+  if constexpr (std::is_same<T, __half>::value)
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  else
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ uint32_t tanh2_16(uint32_t x) {
+  uint32_t r;
+  if constexpr (std::is_same<T, __half>::value)
+    asm("tanh.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
+  else
+    asm("tanh.approx.bf16x2 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ uint32_t fma2_16(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  if constexpr (std::is_same<T, __half>::value)
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  else
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
 // SiLU as x * sigmoid(x) with sigmoid(x) = 0.5 * tanh(x / 2) + 0.5: one MUFU op per element
 // instead of an exponential plus an IEEE division (tanh.approx: ~2^-11 relative error).
 __device__ __forceinline__ float apply_act(float v, int act) {
@@ -715,6 +744,23 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
     auto apply_store = [&](uint32_t i, float wc, float bc, uint64_t w2, uint64_t b2) {
       float f[VE];
       unpack<T>(sv[i], f);
+      if constexpr (sizeof(T) == 2) {
+        if (no_clamp && silu) {
+          // 16-bit output: h = v / 2 rounded to the output type, then tanh and h * t + h on
+          // packed 16-bit pairs (one MUFU op per two elements); the rounding of h is below
+          // the output's own
+          uint32_t w[VE / 2];
+#pragma unroll
+          for (int e = 0; e < VE; e += 2) {
+            float h0, h1;
+            f2_split(f2_fma(f2_sub(f2(f[e], f[e + 1]), mean2), w2, b2), h0, h1);
+            const uint32_t h16 = cvt2_16<T>(h0, h1);
+            w[e / 2] = fma2_16<T>(h16, tanh2_16<T>(h16), h16);
+          }
+          yv[i] = make_uint4(w[0], w[1], w[2], w[3]);
+          return;
+        }
+      }
       if (no_clamp) {
 #pragma unroll
         for (int e = 0; e < VE; e += 2) {

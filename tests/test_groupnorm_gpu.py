@@ -78,6 +78,20 @@ def test_groupnorm_ragged_and_general_paths(shape, groups):
     assert rel_err(to_np(y), ref) < TOL_F32
 
 
+@pytest.mark.parametrize("shape,groups", [((2, 512, 128, 128), 32), ((1, 48, 100, 100), 3)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_groupnorm_silu_streaming_path_16bit(shape, groups, dtype):
+    # 512 KB and 320 KB 16-bit groups take the streaming path: slices inside one channel
+    # (128 x 128) and slices straddling channels (100 x 100); SiLU on packed 16-bit pairs
+    x, g, b = make(shape, seed=6)
+    xt = torch.from_numpy(x).cuda().to(dtype)
+    gg, bb = torch.from_numpy(g).to(dtype), torch.from_numpy(b).to(dtype)
+    ref = oracle.groupnorm_act(to_np(xt), to_np(gg), to_np(bb), groups, 1e-5, silu=True,
+                               dtype=dt(dtype))
+    y = groupnorm_silu(xt, gg.cuda(), bb.cuda(), GroupNormSiLuOptions(groups, 1e-5))
+    assert rel_err(to_np(y), ref) < TOL_HALF
+
+
 @pytest.mark.parametrize("shape,groups,offset", [((1, 48, 100, 100), 3, 1000.0),
                                                  ((3, 64, 64, 64), 2, -300.0)])
 def test_groupnorm_streaming_path_offset_mean(shape, groups, offset):
