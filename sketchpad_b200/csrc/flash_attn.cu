@@ -8,16 +8,13 @@
 // One CTA = two 128-query tiles (T0, T1) of one (batch, head); 384 threads = 3 warpgroups:
 //   warps 0..3  softmax + epilogue of T0, warps 4..7 of T1
 //   warp 8      TMA producer: both Q tiles once, then K/V tiles of 128 keys (STAGES ring).
-//   warp 9      TMEM owner and MMA issuer (one elected lane), per key tile j:
+//   warp 9      TMEM owner + MMA issuer (one elected lane), per key tile j:
 //                 S_t = Q_t K_j^T   (M=128, N=128, K=D padded to 16; f32 in TMEM)
 //                 O_t += P_t V_j    (M=128, N=Dv padded to 64, K=128; P_t read from TMEM)
 //               so the tensor core works on one tile while the other tile's softmax runs.
 //               Dv > 64 (P aliases S): S_0(0) S_1(0) | PV_0(j) S_0(j+1) PV_1(j) S_1(j+1) | ...
-//               Dv <= 64 (P has its own columns): one issuer per tile (warp 9 for T0, warp
-//               10 for T1); S_t(j+1) is issued as soon as the softmax has loaded S_t(j) into
-//               registers (s_free barrier), then PV_t(j).  The two softmax warpgroups then
-//               take turns at their exponentials (turn barriers): the MUFU phase of one tile
-//               overlaps the loads, row maximum and P stores of the other.
+//               Dv <= 64 (P has its own columns): S_t(j+1) is issued as soon as the softmax
+//               has loaded S_t(j) into registers (s_free barrier), then PV_0(j), PV_1(j).
 //   softmax:    one query row per thread (= TMEM lane): tcgen05.ld S, mask, exp2, write P
 //               (16-bit, 2 per column) back to
 //               TMEM with tcgen05.st; O is rescaled in TMEM only when the row max grows by
@@ -43,8 +40,7 @@ constexpr int kBM = 128;            // queries per tile (two tiles per CTA)
 constexpr int kBN = 128;            // keys per KV tile
 constexpr int kBox = 16384;         // bytes of one 128 x 64 16-bit box
 // Three whole warpgroups: registers are reserved per warpgroup, so 320 threads would cost
-// as much as 384; warp 10 issues T1's MMAs in the Dv <= 64 schedule, warp 11 has no role.
-// 168 registers per thread.
+// as much as 384; warps 10 and 11 have no role.  168 registers per thread.
 constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -80,8 +76,8 @@ struct FaSmem {
   static constexpr int kV = kK + STAGES * NBQ * kBox;
   static constexpr int kBar = kV + STAGES * NBV * kBox;
   // barriers: q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2],
-  // o_done[2], s_free[2], drain, turn[2]
-  static constexpr int kNumBars = 1 + 4 * STAGES + 2 + 2 + 2 + 2 + 1 + 2;
+  // o_done[2], s_free[2], drain
+  static constexpr int kNumBars = 1 + 4 * STAGES + 2 + 2 + 2 + 2 + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;  // tmem base + abort flag
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-B alignment of the base
@@ -117,14 +113,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_done = p_full + 2;
   uint64_t* s_free = o_done + 2;
   uint64_t* drain = s_free + 2;
-  // turn[t]: the softmax of tile t may run its exponentials (the two warpgroups alternate)
-  uint64_t* turn = drain + 1;
   // Dv <= 64: P has its own TMEM columns, so S_t(j+1) is issued as soon as the softmax has
   // loaded S_t(j) (s_free) instead of after PV_t(j): the MMA round trip leaves the softmax's
   // critical path, and the softmax waits for PV_t(j-1) (o_done) only before writing P.
   constexpr bool kEarlyQK = NBV == 1;
-  // MMA issuing threads: one per query tile with the early-S schedule, one for both otherwise
-  const int kIssuers = kEarlyQK ? (p.single ? 1 : 2) : 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
 
@@ -146,9 +138,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(q_full, 1);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], kIssuers);  // one commit per issuing thread
+      mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], kIssuers);
+      mbar_init(&v_empty[s], 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
@@ -156,9 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&o_done[t], 1);
       mbar_init(&s_free[t], 128);
     }
-    mbar_init(drain, kIssuers);
-    mbar_init(&turn[0], 128);
-    mbar_init(&turn[1], 128);
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -209,74 +199,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait(&v_full[j % STAGES], (j / STAGES) & 1, nullptr, WD_TMA_WAIT, p.wait_budget);
       }
     }
-  } else if (kEarlyQK && (warp == 9 || (warp == 10 && ntq == 2))) {
-    // ------------------------------------------------------------------ MMA issuers (Dv <= 64)
-    // One issuing thread per query tile (warp 9: tile 0, warp 10: tile 1), so neither tile's
-    // products wait behind the other tile's softmax.  A commit covers the MMAs its own thread
-    // issued, so the K/V stage barriers count one commit per tile.
-    if (lane == 0) {
-      const int t = warp - 9;
-      const uint32_t ab = p.in_f16 ? 0u : 1u;
-      const uint32_t idesc_qk = make_idesc_f16(kBM, kBN, ab, 0, 0);
-      const uint32_t idesc_pv = make_idesc_f16(kBM, (uint32_t)p.dv_pad, ab, 0, 1);
-      const uint32_t qb = smem_u32(smem + L::kQ) + t * NBQ * kBox;
-      const uint32_t tm = tmem + t * 256;
-      const int qk_steps = p.dqk_pad / 16;
-
-      // S_t = Q_t K_j^T
-      auto issue_qk = [&](int j) {
-        const uint32_t k_base = smem_u32(smem + L::kK + (j % STAGES) * NBQ * kBox);
-        for (int kk = 0; kk < qk_steps; ++kk) {
-          const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-          const uint64_t a = make_smem_desc(qb + off, 16, 1024, LAYOUT_SW128);
-          const uint64_t bd = make_smem_desc(k_base + off, 16, 1024, LAYOUT_SW128);
-          umma_ss(tm + TM::kS, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[t]);
-      };
-      // O_t += P_t V_j, P_t from TMEM (8 columns per 16 keys)
-      auto issue_pv = [&](int j) {
-        const uint32_t v_base = smem_u32(smem + L::kV + (j % STAGES) * NBV * kBox);
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bd = make_smem_desc(v_base + kk * 16 * 128, kBox, 1024, LAYOUT_SW128);
-          umma_ts(tm + TM::kO, tm + TM::kP + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&o_done[t]);
-      };
-
-      bool ok = mbar_wait(q_full, 0, abort_flag, WD_MMA_WAIT, p.wait_budget) &&
-                (n_tiles == 0 || mbar_wait(&k_full[0], 0, abort_flag, WD_MMA_WAIT, p.wait_budget));
-      tc_fence_after();
-      if (ok && n_tiles > 0) {
-        issue_qk(0);
-        umma_commit(&k_empty[0]);
-      }
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int st = j % STAGES;
-        const bool more = j + 1 < n_tiles;
-        const int st1 = (j + 1) % STAGES;
-        // S_t(j+1) as soon as the softmax holds S_t(j) in registers, then PV_t(j)
-        if (more) {
-          if (!mbar_wait(&k_full[st1], ((j + 1) / STAGES) & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
-          if (!mbar_wait(&s_free[t], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
-          tc_fence_after();
-          issue_qk(j + 1);
-          umma_commit(&k_empty[st1]);
-        }
-        if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
-        if (!mbar_wait(&p_full[t], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
-        tc_fence_after();
-        issue_pv(j);
-        umma_commit(&v_empty[st]);
-      }
-      // Drain: every MMA issued above (by both issuers) has completed once both commits of
-      // this barrier have arrived.
-      umma_commit(drain);
-      mbar_wait(drain, 0, nullptr, WD_MMA_WAIT, p.wait_budget);
-    }
-  } else if (!kEarlyQK && warp == 9) {
-    // ------------------------------------------------------------------ MMA issuer (Dv > 64)
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t ab = p.in_f16 ? 0u : 1u;
       const uint32_t idesc_qk = make_idesc_f16(kBM, kBN, ab, 0, 0);
@@ -320,6 +244,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = j % STAGES;
         const bool more = j + 1 < n_tiles;
         const int st1 = (j + 1) % STAGES;
+        if constexpr (kEarlyQK) {
+          if (more) {
+            if (!mbar_wait(&k_full[st1], ((j + 1) / STAGES) & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
+            if (!mbar_wait(&s_free[0], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
+            tc_fence_after();
+            issue_qk(0, j + 1);
+            if (ntq == 2) {
+              if (!mbar_wait(&s_free[1], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
+              tc_fence_after();
+              issue_qk(1, j + 1);
+            }
+            umma_commit(&k_empty[st1]);
+          }
+          if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
+          if (!mbar_wait(&p_full[0], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
+          tc_fence_after();
+          issue_pv(0, j);
+          if (ntq == 2) {
+            if (!mbar_wait(&p_full[1], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
+            tc_fence_after();
+            issue_pv(1, j);
+          }
+          umma_commit(&v_empty[st]);
+          continue;
+        }
         if (!mbar_wait(&v_full[st], (j / STAGES) & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
         if (!mbar_wait(&p_full[0], j & 1, abort_flag, WD_MMA_WAIT, p.wait_budget)) break;
         tc_fence_after();
@@ -354,13 +303,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;  // running max in log2 units, running row sum
     bool ok = true;
-    // Two query tiles, early-S schedule: the warpgroups take turns at the exponentials
-    // (turn[t]), so that one tile's MUFU phase overlaps the other's TMEM loads, row maximum,
-    // P stores and waits instead of both contending for the MUFU at the same time (measured:
-    // (2,8,4096,40) 134 -> 124 us; with P aliasing S the turns made D = 128 slower).  Tile 0
-    // goes first.
-    const bool pingpong = kEarlyQK && ntq == 2;
-    if (pingpong && t == 1) mbar_arrive(&turn[0]);
 
     for (int j = 0; j < n_tiles; ++j) {
       if (!mbar_wait_warp(&s_full[t], j & 1, abort_flag, WD_SOFTMAX_WAIT, p.wait_budget)) {
@@ -482,16 +424,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (!kEarlyQK) tmem_st16(lane_addr + TM::kP + q * 16, pk[q]);
         }
       };
-      if (pingpong &&
-          !mbar_wait_warp(&turn[t], j & 1, abort_flag, WD_SOFTMAX_WAIT, p.wait_budget)) {
-        ok = false;
-        break;
-      }
       if (__any_sync(0xffffffffu, fabsf(m_ref) > 1.0e6f))
         exps(std::true_type{});
       else
         exps(std::false_type{});
-      if (pingpong) mbar_arrive(&turn[t ^ 1]);
       if constexpr (kEarlyQK) {
         // PV_t(j-1) must be done before P_t is rewritten and O rescaled
         if (j >= 1 && !mbar_wait_warp(&o_done[t], (j - 1) & 1, abort_flag, WD_SOFTMAX_WAIT, p.wait_budget)) {
