@@ -272,10 +272,11 @@ __global__ void __launch_bounds__(kGnThreads, 2) gn_cluster_kernel(GnParams p) {
 // ---------------------------------------------------------------------------------------
 // Streaming path for large contiguous groups (hundreds of KB and up): a persistent,
 // cooperatively launched grid walks one fixed sequence of slice units.  A group is cut into
-// S slices of kSlBytes.  Unit (pass 0, g, s) reads slice s of group g from HBM once and writes
-// its (count, mean, M2, max |x|) partial to global memory; unit (pass 1, g, s) merges the S
-// partials of g in slice order (so every slice of a group gets the same mean and rstd),
-// re-reads the slice (from L2) and writes the normalised, activated output.  The sequence
+// S slices of SlCfg::kBytes.  Unit (pass 0, g, s) reads slice s of group g from HBM once and
+// writes its (count, mean, M2, max |x|) partial to global memory; unit (pass 1, g, s) takes
+// the group's statistics merged from the S partials in slice order (so every slice of a group
+// gets the same mean and rstd), re-reads the slice (from L2) and writes the normalised,
+// activated output.  The sequence
 // interleaves pass 0 of group t with pass 1 of group t - L:
 //   * a pass-1 unit depends only on units earlier in the sequence, and every CTA is resident
 //     (cooperative launch) and takes its units in sequence order, so each of its waits ends;
@@ -284,23 +285,42 @@ __global__ void __launch_bounds__(kGnThreads, 2) gn_cluster_kernel(GnParams p) {
 //   * units are small and equal, so every CTA gets the same share of the work whatever the
 //     number of groups (a CTA per group, or a cluster per group, leaves the last wave ragged).
 // Unit k of CTA c is sequence entry c + k * gridDim.x.
-//   warp 8, lane 0 (producer): bulk-copies the CTA's next units into a kSlStages ring.
-//   warps 0-7 (consumers): pass 0 forms per-thread (count, mean, M2) of clamp(x) from sums
-//     shifted by the thread's first value, and max |x|, merged (Chan et al.) over the warps;
-//     pass 1 normalises, applies the affine map and SiLU (packed f32x2 arithmetic, and no
-//     clamps when max |x| and the affine bound show none can bite), and stores.
+//   consumer warps (8 or 16): pass 0 forms sums of clamp(x) - shift and its square about the
+//     slice's first value, and max |x|, added over the warps; pass 1 normalises, applies the
+//     affine map and SiLU (packed f32x2 arithmetic, and no clamps when max |x| and the affine
+//     bound show none can bite), and stores.
+//   next warp, lane 0 (producer): bulk-copies the CTA's next units into the ring of stages.
+//   publisher warp: a slice's partial from the warps' sums; statistics warp: the group's
+//     statistics for pass-1 units (both described at the kernel).
 // HBM sees one read and one write of x, plus 16 bytes of partial per slice.
 // ---------------------------------------------------------------------------------------
-constexpr int kSlConsumers = 256;                 // warps 0-7
-constexpr int kSlProducerWarp = kSlConsumers / 32;  // warp 8
-constexpr int kSlPublisherWarp = kSlProducerWarp + 1;
-constexpr int kSlStatsWarp = kSlProducerWarp + 2;
-constexpr int kSlThreads = kSlConsumers + 3 * 32;
-constexpr int kSlEmptyCount = kSlConsumers / 32 + 1;  // consumer warps, publisher
+// Slice-unit configuration per element size, measured on B200 at (8,512,128,128) (CUDA
+// events, same box): f32 48 KB units in 2 stages with 8 consumer warps, two CTAs per SM
+// (106 us; 32 KB x 3: 110, 64 KB x 3 with 16 warps and one CTA per SM: 118); 16-bit 64 KB
+// units in 3 stages with 16 consumer warps, one CTA per SM (75 us; 32 KB x 3: 78).  Smaller
+// units lose to their per-unit waits (16 KB x 6: 198 / 100 us).
+template <int ES>
+struct SlCfg;
+template <>
+struct SlCfg<4> {
+  static constexpr int kConsumers = 256, kBytes = 49152, kStages = 2, kMinBlocks = 2;
+};
+template <>
+struct SlCfg<2> {
+  static constexpr int kConsumers = 512, kBytes = 65536, kStages = 3, kMinBlocks = 1;
+};
+template <typename T>
+struct SlRoles {
+  using C = SlCfg<(int)sizeof(T)>;
+  static constexpr int kProducerWarp = C::kConsumers / 32;  // after the consumer warps
+  static constexpr int kPublisherWarp = kProducerWarp + 1;
+  static constexpr int kStatsWarp = kProducerWarp + 2;
+  static constexpr int kThreads = C::kConsumers + 3 * 32;
+  static constexpr int kEmptyCount = C::kConsumers / 32 + 1;  // consumer warps, publisher
+  static constexpr int kSmem = C::kStages * C::kBytes + 128;
+};
+inline int64_t sl_unit_bytes(int es) { return es == 4 ? SlCfg<4>::kBytes : SlCfg<2>::kBytes; }
 constexpr int kStatSlots = 8;  // pass-1 statistics the statistics warp may prepare ahead
-constexpr int kSlBytes = 32768;  // one slice unit
-constexpr int kSlStages = 3;     // 96 KB: two CTAs per SM
-constexpr int kSlMaxCg = 1024;   // channels per group the shared affine table holds
 
 struct Welford {
   float n, mean, m2;
@@ -462,17 +482,17 @@ __device__ __forceinline__ SlUnit sl_unit(const GnSliceParams& p, uint32_t u) {
   return r;
 }
 
-// grid = resident CTAs (cooperative), kSlThreads threads, dynamic smem kSlStages * kSlBytes
-// (+ alignment).  x, y contiguous NCHW, HW % VE == 0, 16-B aligned.
+// grid = resident CTAs (cooperative), SlRoles::kThreads threads, dynamic smem SlRoles::kSmem
+// (the ring of stages, + alignment).  x, y contiguous NCHW, HW % VE == 0, 16-B aligned.
 //
 // Per ring stage st, for the unit k the stage holds (k % kSlStages == st):
 //   full[st]       the slice landed (producer's bulk copy)
-//   empty[st]      the 8 consumer warps and the publisher are done with it (kSlEmptyCount)
-//   part_full[st]  pass 0: the 8 consumer warps wrote their partials to wpart[st]
+//   empty[st]      the consumer warps and the publisher are done with it
+//   part_full[st]  pass 0: the consumer warps wrote their partials to wpart[st]
 // and per statistics slot (the CTA's i-th pass-1 unit uses slot i % kStatSlots):
 //   stat_full[i]   the statistics warp wrote the group's stats to gstat[i] (and the channel
 //                  factors to gaff[i])
-//   stat_empty[i]  the 8 consumer warps have read them
+//   stat_empty[i]  the consumer warps have read them
 // part_full completes once per pass-0 unit of the stage, so its waiters track the phase
 // parity per stage.  The consumers and the publisher arrive on empty[st] for every unit, and
 // the producer waits for the stage's previous unit to be released before it starts unit k;
@@ -480,7 +500,11 @@ __device__ __forceinline__ SlUnit sl_unit(const GnSliceParams& p, uint32_t u) {
 // no role can be a whole ring (or slot) cycle ahead of or behind a barrier's phase (a parity
 // wait would then match the wrong phase).
 template <typename T>
-__global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p) {
+__global__ void __launch_bounds__(SlRoles<T>::kThreads, SlCfg<(int)sizeof(T)>::kMinBlocks)
+    gn_slice_kernel(GnSliceParams p) {
+  using C = SlCfg<(int)sizeof(T)>;
+  using R = SlRoles<T>;
+  constexpr int kSlConsumers = C::kConsumers, kSlBytes = C::kBytes, kSlStages = C::kStages;
   constexpr int VE = VecTraits<T>::kElems;
   constexpr int kCWarps = kSlConsumers / 32;
   constexpr int64_t kSv = kSlBytes / 16;  // 16-byte vectors per slice
@@ -511,7 +535,7 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSlStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kSlEmptyCount);
+      mbar_init(&empty[i], R::kEmptyCount);
       mbar_init(&part_full[i], kCWarps);
     }
     for (int i = 0; i < kStatSlots; ++i) {
@@ -523,7 +547,7 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
   }
   __syncthreads();
 
-  if (warp == kSlProducerWarp) {
+  if (warp == R::kProducerWarp) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t keep = l2_policy(true), drop = l2_policy(false);
@@ -550,7 +574,7 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
     return;
   }
 
-  if (warp == kSlPublisherWarp) {
+  if (warp == R::kPublisherWarp) {
     // ------------------------------------------------------------------ publisher
     // pass 0: merge the 8 warp partials in warp order into the slice's partial, release the
     // stage, publish the partial and count it on the group's counter.  Every unit: one
@@ -592,7 +616,7 @@ __global__ void __launch_bounds__(kSlThreads, 2) gn_slice_kernel(GnSliceParams p
     return;
   }
 
-  if (warp == kSlStatsWarp) {
+  if (warp == R::kStatsWarp) {
     // ------------------------------------------------------------------ statistics
     // pass 1, up to kStatSlots units ahead of the consumers: wait for the group's S partials,
     // merge them (lane j takes partials j, j + 32, ... in order, then a fixed xor tree), and
@@ -931,9 +955,10 @@ GnPlan plan_gn(int64_t B, int64_t G, int64_t cg, int64_t n, bool contiguous, boo
   const int max_vpt = vec_elems == 4 ? 16 : 8;
   const int64_t group_bytes = n * (16 / vec_elems);
   // slice units are numbered in 32 bits by the streaming kernel
-  const int64_t stream_units = 2 * B * G * ((group_bytes + kSlBytes - 1) / kSlBytes);
+  const int64_t ub = sl_unit_bytes(16 / vec_elems);
+  const int64_t stream_units = 2 * B * G * ((group_bytes + ub - 1) / ub);
   if (contiguous && vec_ok && n < (1LL << 31) && group_bytes >= kStreamMinGroupBytes &&
-      cg <= kSlMaxCg && stream_units < (1LL << 31)) {
+      stream_units < (1LL << 31)) {
     pl.stream_path = true;
     return pl;
   }
@@ -1016,11 +1041,10 @@ int launch_cluster_vpt(const GnParams& p, int cs, int vpt, int64_t BG, cudaStrea
   }
 }
 
-constexpr int kSlSmem = kSlStages * kSlBytes + 128;
 
 // Streaming-path workspace: the [BG] ready counters (padded to 16 bytes), then the [BG][S]
 // partials.
-int64_t sl_slices(int64_t n, int es) { return (n * es + kSlBytes - 1) / kSlBytes; }
+int64_t sl_slices(int64_t n, int es) { return (n * es + sl_unit_bytes(es) - 1) / sl_unit_bytes(es); }
 size_t sl_ready_bytes(int64_t BG) { return ((size_t)BG * 4 + 15) & ~size_t(15); }
 size_t sl_workspace_bytes(int64_t BG, int64_t S) {
   return sl_ready_bytes(BG) + (size_t)BG * (size_t)S * 16;
@@ -1032,7 +1056,7 @@ int launch_slices(GnSliceParams p, void* ws, cudaStream_t stream) {
   static unsigned long long attr_set = 0;
   if (first_time_on_device(&attr_set)) {
     const cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSlSmem);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SlRoles<T>::kSmem);
     if (e != cudaSuccess) {
       __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
       return set_error(SP_ERR_LAUNCH, "groupnorm: kernel attribute failed: %s",
@@ -1045,7 +1069,8 @@ int launch_slices(GnSliceParams p, void* ws, cudaStream_t stream) {
   const int dev = current_device();
   int r = (dev >= 0 && dev < 64) ? __atomic_load_n(&per_sm[dev], __ATOMIC_ACQUIRE) : 0;
   if (r <= 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, kern, kSlThreads, kSlSmem) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, kern, SlRoles<T>::kThreads,
+                                                      SlRoles<T>::kSmem) !=
             cudaSuccess ||
         r <= 0) {
       cudaGetLastError();
@@ -1067,8 +1092,8 @@ int launch_slices(GnSliceParams p, void* ws, cudaStream_t stream) {
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
-  cfg.blockDim = dim3(kSlThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSlSmem;
+  cfg.blockDim = dim3(SlRoles<T>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = SlRoles<T>::kSmem;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
