@@ -590,6 +590,19 @@ def _case_unet_step(torch, gemm="cublas"):
     return step, unet_flops()["total"], "flop"
 
 
+def _case_unet_step_graph(torch, gemm="cublas"):
+    """The bench's captured UNet step (CUDA-graph replay of one CFG-pair step) with the given
+    GEMM backend: "cublas" (torch matmuls) or "sp" (this library's tcgen05 kernels)."""
+    from sketchpad_b200.unet import UNetB200, UNetStepGraph, make_unet_params, unet_flops
+    net = UNetB200(make_unet_params(device="cuda", seed=0), device="cuda", gemm=gemm)
+    graph = UNetStepGraph(net, warmup=2)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    graph.x.copy_(torch.randn(2, 4, 64, 64, device="cuda", generator=g))
+    graph.ctx.copy_(torch.randn(2, 77, 768, device="cuda", generator=g))
+    graph.t.fill_(999.0)
+    return graph.graph.replay, unet_flops()["total"], "flop"
+
+
 def _case_flux_block(torch, single: bool):
     from sketchpad_b200.flux import (FluxConfig, FluxDoubleBlockB200, FluxSingleBlockB200,
                                      flux_step_flops, rope_tables)
@@ -646,6 +659,8 @@ def _case_wan_step(torch):
 CASES = {
     "unet_step_eager": _case_unet_step,
     "unet_step_eager_sp_gemm": lambda t: _case_unet_step(t, "sp"),
+    "unet_step_graph_cublas": lambda t: _case_unet_step_graph(t, "cublas"),
+    "unet_step_graph_sp_gemm": lambda t: _case_unet_step_graph(t, "sp"),
     "sd1x_ddim_loop_20": lambda t: _case_denoise_loop(t, "ddim", 20),
     "sd1x_dpmpp2m_loop_20": lambda t: _case_denoise_loop(t, "dpmpp_2m", 20),
     "flux_double_4096x512": lambda t: _case_flux_block(t, False),

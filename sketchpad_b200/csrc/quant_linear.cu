@@ -731,6 +731,143 @@ __global__ void __launch_bounds__(kQThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// bf16 weights, small products: 128 rows of x x BN weight rows per CTA (the UNet's projection
+// and feed-forward GEMMs: K = 320-5120, M = 128-8192, most of them a few GFLOP, where the
+// 256 x 256 tiles above leave SMs idle and spend most of a CTA's life filling its pipeline).
+// 192 threads: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2-5 the epilogue
+// (warp w reads TMEM lane quarter w % 4); a kSmSt-stage ring of {x tile 128 x 64, W tile BN x
+// 64}, both 128B-swizzled K-major; the f32 accumulator is BN TMEM columns.  Small enough that
+// two CTAs share an SM (BN = 64: 96 KB of shared memory).  The epilogue is the big kernel's
+// (bias, residual, gate, RoPE, GLU, f16 output).
+constexpr int kSmSt = 4;  // ring stages
+constexpr int kSmThreads = 192;
+
+template <int BN>
+struct QlSmallSmem {
+  static constexpr int kA = kQBK * 128 * 2;  // 16 KB x tile
+  static constexpr int kB = kQBK * BN * 2;   // W tile
+  static constexpr int kStage = kA + kB;
+  static constexpr int kBar = kSmSt * kStage;
+  static constexpr int kMisc = kBar + (2 * kSmSt + 1) * 8;
+  static constexpr int kAlloc = kMisc + 16 + 1024;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kSmThreads)
+    qlinear_small_kernel(const __grid_constant__ CUtensorMap tmx,
+                         const __grid_constant__ CUtensorMap tmw, const QlParams p) {
+  using L = QlSmallSmem<BN>;
+  constexpr uint32_t kCols = BN < 32 ? 32 : BN;  // TMEM allocation: a power of two >= 32
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* empty = full + kSmSt;
+  uint64_t* acc_full = empty + kSmSt;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int mtile, ntile;
+  ql_tile_of(p, (int)blockIdx.x, mtile, ntile);
+  const int m0 = mtile * 128, n0 = ntile * BN;
+  const int ktiles = (int)(p.K / kQBK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSmSt; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmx);
+      tma_prefetch_desc(&tmw);
+      int issued = 0;
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int st = kt % kSmSt;
+        if (kt >= kSmSt &&
+            !mbar_wait(&empty[st], ((kt / kSmSt) - 1) & 1, abort_flag, WD_TMA_WAIT))
+          break;
+        uint8_t* stage = smem + st * L::kStage;
+        mbar_arrive_expect_tx(&full[st], L::kStage);
+        tma_load_2d(stage, &tmx, &full[st], kt * kQBK, m0);
+        tma_load_2d(stage + L::kA, &tmw, &full[st], kt * kQBK, n0);
+        issued = kt + 1;
+      }
+      // copies still in flight must land before the CTA can exit (bounded)
+      for (int kt = max(0, issued - kSmSt); kt < issued; ++kt)
+        mbar_wait(&full[kt % kSmSt], (kt / kSmSt) & 1, nullptr, WD_TMA_WAIT);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(128, BN, 1, 0, 0);
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int st = kt % kSmSt;
+        if (!mbar_wait(&full[st], (kt / kSmSt) & 1, abort_flag, WD_MMA_WAIT)) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + st * L::kStage), b = a + L::kA;
+#pragma unroll
+        for (int kk = 0; kk < kQBK / 16; ++kk)
+          umma_ss(tmem, make_smem_desc(a + kk * 32, 16, 1024, LAYOUT_SW128),
+                  make_smem_desc(b + kk * 32, 16, 1024, LAYOUT_SW128), idesc,
+                  (kt > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[st]);  // the stage is free once these MMAs have read it
+      }
+      // the accumulator is final once every MMA above has completed (on an early exit the
+      // epilogue sees the abort flag instead)
+      umma_commit(acc_full);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int64_t m = m0 + quarter * 32 + lane;
+    const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+    if (mbar_wait_warp(acc_full, 0, abort_flag, WD_EPILOGUE_WAIT) && !*abort_flag) {
+      tc_fence_after();
+      const float2* rope_row =
+          p.rope ? p.rope + ((m + p.rope_off) / p.rope_div % p.rope_mod) * p.rope_half : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + c, r);
+        tmem_wait_ld();
+        const int64_t nb = n0 + c;
+        if (m >= p.M || nb >= p.N) continue;
+#pragma unroll
+        for (int g = 0; g < 16; g += 8) {
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[g + e]);
+          ql_finish8<W_BF16>(p, v, m, nb + g, rope_row);  // N % 16 == 0: groups are whole
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kCols);
+  }
+}
+
 // sp_quant_linear_set_pairing: 0 unpaired tiles (default), 1 paired when M > 256
 int g_ql_pairing = 0;
 
@@ -780,6 +917,63 @@ void ql_raster(QlParams& q, int tiles_m, int tiles_n, int m_rows) {
   q.group = q.raster_n ? gn : gm;
 }
 
+// Launch of the small-tile bf16 kernel with BN weight rows per CTA.
+template <int BN>
+int launch_qlinear_small(const void* x, const void* w, const QlParams& p, cudaStream_t s) {
+  using L = QlSmallSmem<BN>;
+  static_assert(L::kAlloc <= 232448, "small bf16 linear smem budget");
+  CUtensorMap mx, mw;
+  {
+    const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.M};
+    const uint64_t strides[1] = {(uint64_t)p.K * 2};
+    const uint32_t box[2] = {kQBK, 128};
+    if (int rc = encode_tiled(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)p.K, (uint64_t)p.N};
+    const uint64_t strides[1] = {(uint64_t)p.K * 2};
+    const uint32_t box[2] = {kQBK, (uint32_t)BN};
+    if (int rc = encode_tiled(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  auto kern = qlinear_small_kernel<BN>;
+  static unsigned long long attr_set = 0;
+  if (first_time_on_device(&attr_set)) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) {
+      __atomic_fetch_and(&attr_set, ~(1ull << current_device()), __ATOMIC_ACQ_REL);
+      return set_error(SP_ERR_LAUNCH, "bf16 linear: smem attribute failed: %s",
+                       cudaGetErrorString(e));
+    }
+  }
+  QlParams q = p;
+  q.ws = nullptr;
+  q.splits = 1;
+  q.kt_per_split = (int)(p.K / kQBK);
+  const int tiles_m = (int)((p.M + 127) / 128), tiles_n = (int)((p.N + BN - 1) / BN);
+  ql_raster<W_BF16>(q, tiles_m, tiles_n, 128);
+  kern<<<(unsigned)(tiles_m * tiles_n), kSmThreads, L::kAlloc, s>>>(mx, mw, q);
+  return check_launch("bf16 linear (small tiles)");
+}
+
+// Weight rows per CTA of the small-tile bf16 kernel for this product, or 0 for the 256 x 256
+// kernel: products whose 256 x 256 grid fills at least two waves with K >= 2048 keep the big
+// tiles; the rest take the widest BN in {256, 128, 64} that divides N and still gives every SM
+// a CTA (else 64).
+int ql_small_bn(const QlParams& p) {
+  const int64_t sms = num_sms();
+  const int64_t big = ((p.M + kQBM - 1) / kQBM) * ((p.N + kQBN - 1) / kQBN);
+  if (big >= 2 * sms && p.K >= 2048) return 0;
+  const int64_t tm = (p.M + 127) / 128;
+  for (int bn : {256, 128, 64})
+    if (p.N % bn == 0 && tm * (p.N / bn) >= sms) return bn;
+  return 64;
+}
+
 template <int WF>
 int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_t s) {
   if (!aligned(x, 16) || !aligned(w8, 16) || !aligned(p.y, 16) ||
@@ -789,6 +983,14 @@ int launch_qlinear(const void* x, const void* w8, const QlParams& p, cudaStream_
   using KF = KqFmt<WF>;
   if (KF::kIsK && (!aligned(p.kq_a, 16) || !aligned(p.kq_b, 16)))
     return set_error(SP_ERR_ALIGN, "quantized linear: k-quant factors must be 16-byte aligned");
+  if constexpr (WF == W_BF16) {
+    switch (ql_small_bn(p)) {
+      case 256: return launch_qlinear_small<256>(x, w8, p, s);
+      case 128: return launch_qlinear_small<128>(x, w8, p, s);
+      case 64: return launch_qlinear_small<64>(x, w8, p, s);
+      default: break;
+    }
+  }
   // Paired (2-CTA) tiles, when enabled, whenever x has more than one 256-row tile: the
   // pair's CTA count is the unpaired count rounded up to even.
   const bool pair = WF != W_BF16 && p.M > kQBM && __atomic_load_n(&g_ql_pairing, __ATOMIC_RELAXED);
