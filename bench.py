@@ -553,6 +553,21 @@ def _case_kquant(torch, name, M, N, K):
     return (lambda: lin.forward(x, out=y)), 2.0 * M * N * K, "flop"
 
 
+def _case_bf16(torch, M, N, K, cublas=False):
+    """One bf16 linear with bias (a UNet projection / feed-forward shape) on this library's
+    tcgen05 GEMM, or on cuBLAS (torch.addmm) for comparison."""
+    from sketchpad_b200.linear import Bf16Linear
+    w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    b = (torch.randn(N, device="cuda") * 0.02).to(torch.bfloat16)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    if cublas:
+        wt = w.t().contiguous()
+        return (lambda: torch.addmm(b, x, wt, out=y)), 2.0 * M * N * K, "flop"
+    lin = Bf16Linear(w, b)
+    return (lambda: lin.forward(x, out=y)), 2.0 * M * N * K, "flop"
+
+
 def _case_fp8(torch, M, N, K):
     from sketchpad_b200.wan import fp8_linear_synthetic
     lin = fp8_linear_synthetic(0, N, K, "cuda", bias=True)
@@ -660,6 +675,12 @@ CASES = {
     "unet_step_eager": _case_unet_step,
     "unet_step_eager_sp_gemm": lambda t: _case_unet_step(t, "sp"),
     "unet_step_graph_cublas": lambda t: _case_unet_step_graph(t, "cublas"),
+    "bf16_8192x320x320": lambda t: _case_bf16(t, 8192, 320, 320),
+    "bf16_8192x320x320_cublas": lambda t: _case_bf16(t, 8192, 320, 320, True),
+    "bf16_8192x2560x320": lambda t: _case_bf16(t, 8192, 2560, 320),
+    "bf16_8192x2560x320_cublas": lambda t: _case_bf16(t, 8192, 2560, 320, True),
+    "bf16_8192x320x1280": lambda t: _case_bf16(t, 8192, 320, 1280),
+    "bf16_8192x320x1280_cublas": lambda t: _case_bf16(t, 8192, 320, 1280, True),
     "unet_step_graph_sp_gemm": lambda t: _case_unet_step_graph(t, "sp"),
     "sd1x_ddim_loop_20": lambda t: _case_denoise_loop(t, "ddim", 20),
     "sd1x_dpmpp2m_loop_20": lambda t: _case_denoise_loop(t, "dpmpp_2m", 20),

@@ -234,14 +234,30 @@ __device__ __forceinline__ float ql_silu(float g) { return g / (1.0f + expf(-g))
 // Epilogue of 8 consecutive accumulator values of row m, columns n .. n+7: FP8 per-channel
 // scale, bias, then either the GLU (4 outputs at column n/2) or optional RoPE, gate and
 // residual, bf16 store.
+// Eight bf16 values a[n .. n+7] as f32: one 16-byte load when the address allows it (n is a
+// multiple of 8 here, so that is when the array itself is 16-byte aligned).
+__device__ __forceinline__ void ql_load8(const __nv_bfloat16* a, int64_t n, float (&o)[8]) {
+  if ((reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(a + n));
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __bfloat162float(h[e]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __bfloat162float(a[n + e]);
+  }
+}
+
 template <int WF>
 __device__ __forceinline__ void ql_finish8(const QlParams& p, float (&v)[8], int64_t m, int64_t n,
                                            const float2* rope_row) {
+  float bv[8];
+  if (p.bias) ql_load8(p.bias, n, bv);
   if (p.glu >= 0) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       if constexpr (WF == W_FP8) v[e] *= p.fp8_scale[p.nscale == 1 ? 0 : n + e];
-      if (p.bias) v[e] += __bfloat162float(p.bias[n + e]);
+      if (p.bias) v[e] += bv[e];
     }
     float o[4];
 #pragma unroll
@@ -258,7 +274,7 @@ __device__ __forceinline__ void ql_finish8(const QlParams& p, float (&v)[8], int
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     if constexpr (WF == W_FP8) v[e] *= p.fp8_scale[p.nscale == 1 ? 0 : n + e];
-    if (p.bias) v[e] += __bfloat162float(p.bias[n + e]);
+    if (p.bias) v[e] += bv[e];
   }
   if (rope_row && n < p.rope_cols) {
     // x*cos + rotate_half(x)*sin, rotate_half([x0, x1]) = [-x1, x0]; 8 | head_dim, so the
@@ -272,9 +288,11 @@ __device__ __forceinline__ void ql_finish8(const QlParams& p, float (&v)[8], int
       v[2 * e + 1] = x1 * t.x + x0 * t.y;
     }
   }
+  float gv[8];
+  if (p.gate) ql_load8(p.gate, n, gv);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    if (p.gate) v[e] *= __bfloat162float(p.gate[n + e]);
+    if (p.gate) v[e] *= gv[e];
     if (p.residual) v[e] += __bfloat162float(re[e]);
   }
   *reinterpret_cast<uint4*>(p.y + m * p.ldy + n) =
@@ -735,29 +753,31 @@ __global__ void __launch_bounds__(kQThreads, 1)
 // bf16 weights, small products: 128 rows of x x BN weight rows per CTA (the UNet's projection
 // and feed-forward GEMMs: K = 320-5120, M = 128-8192, most of them a few GFLOP, where the
 // 256 x 256 tiles above leave SMs idle and spend most of a CTA's life filling its pipeline).
-// 192 threads: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2-5 the epilogue
-// (warp w reads TMEM lane quarter w % 4); a kSmSt-stage ring of {x tile 128 x 64, W tile BN x
-// 64}, both 128B-swizzled K-major; the f32 accumulator is BN TMEM columns.  Small enough that
-// two CTAs share an SM (BN = 64: 96 KB of shared memory).  The epilogue is the big kernel's
-// (bias, residual, gate, RoPE, GLU, f16 output).
-constexpr int kSmSt = 4;  // ring stages
-constexpr int kSmThreads = 192;
+// 320 threads: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2-9 the epilogue
+// (warp w reads TMEM lane quarter w % 4, columns of half (w - 2) / 4); a ring of {x tile 128 x
+// 64, W tile BN x 64}, both 128B-swizzled K-major, of 4 / 3 / 2 stages for BN = 64 / 128 /
+// 256, so that two CTAs share an SM (96 KB of shared memory each) and one CTA's epilogue
+// overlaps the other's loads; the f32 accumulator is BN TMEM columns.  The epilogue is the
+// big kernel's (bias, residual, gate, RoPE, GLU, f16 output).
+constexpr int kSmThreads = 320;
 
 template <int BN>
 struct QlSmallSmem {
+  static constexpr int kSt = BN == 256 ? 2 : BN == 128 ? 3 : 4;  // ring stages
   static constexpr int kA = kQBK * 128 * 2;  // 16 KB x tile
   static constexpr int kB = kQBK * BN * 2;   // W tile
   static constexpr int kStage = kA + kB;
-  static constexpr int kBar = kSmSt * kStage;
-  static constexpr int kMisc = kBar + (2 * kSmSt + 1) * 8;
+  static constexpr int kBar = kSt * kStage;
+  static constexpr int kMisc = kBar + (2 * kSt + 1) * 8;
   static constexpr int kAlloc = kMisc + 16 + 1024;
 };
 
 template <int BN>
-__global__ void __launch_bounds__(kSmThreads)
+__global__ void __launch_bounds__(kSmThreads, 2)
     qlinear_small_kernel(const __grid_constant__ CUtensorMap tmx,
                          const __grid_constant__ CUtensorMap tmw, const QlParams p) {
   using L = QlSmallSmem<BN>;
+  constexpr int kSmSt = L::kSt;
   constexpr uint32_t kCols = BN < 32 ? 32 : BN;  // TMEM allocation: a power of two >= 32
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -834,7 +854,7 @@ __global__ void __launch_bounds__(kSmThreads)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
     const int64_t m = m0 + quarter * 32 + lane;
     const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
     if (mbar_wait_warp(acc_full, 0, abort_flag, WD_EPILOGUE_WAIT) && !*abort_flag) {
@@ -842,7 +862,7 @@ __global__ void __launch_bounds__(kSmThreads)
       const float2* rope_row =
           p.rope ? p.rope + ((m + p.rope_off) / p.rope_div % p.rope_mod) * p.rope_half : nullptr;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
         uint32_t r[16];
         tmem_ld16(taddr + c, r);
         tmem_wait_ld();
