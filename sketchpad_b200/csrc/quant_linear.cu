@@ -231,9 +231,6 @@ __device__ __forceinline__ float ql_gelu_erf(float g) {
 // x * sigmoid(x) with an IEEE division, as the reference's silu
 __device__ __forceinline__ float ql_silu(float g) { return g / (1.0f + expf(-g)); }
 
-// Epilogue of 8 consecutive accumulator values of row m, columns n .. n+7: FP8 per-channel
-// scale, bias, then either the GLU (4 outputs at column n/2) or optional RoPE, gate and
-// residual, bf16 store.
 // Eight bf16 values a[n .. n+7] as f32: one 16-byte load when the address allows it (n is a
 // multiple of 8 here, so that is when the array itself is 16-byte aligned).
 __device__ __forceinline__ void ql_load8(const __nv_bfloat16* a, int64_t n, float (&o)[8]) {
@@ -248,16 +245,17 @@ __device__ __forceinline__ void ql_load8(const __nv_bfloat16* a, int64_t n, floa
   }
 }
 
+// The epilogue of 8 accumulator values with its operands already at hand: bias and gate as f32
+// (null: none), the residual's 8 bf16 values (used when p.residual is set).
 template <int WF>
-__device__ __forceinline__ void ql_finish8(const QlParams& p, float (&v)[8], int64_t m, int64_t n,
-                                           const float2* rope_row) {
-  float bv[8];
-  if (p.bias) ql_load8(p.bias, n, bv);
+__device__ __forceinline__ void ql_finish8_with(const QlParams& p, float (&v)[8], int64_t m,
+                                                int64_t n, const float2* rope_row,
+                                                const float* bv, const float* gv, uint4 rv) {
   if (p.glu >= 0) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       if constexpr (WF == W_FP8) v[e] *= p.fp8_scale[p.nscale == 1 ? 0 : n + e];
-      if (p.bias) v[e] += bv[e];
+      if (bv) v[e] += bv[e];
     }
     float o[4];
 #pragma unroll
@@ -268,13 +266,11 @@ __device__ __forceinline__ void ql_finish8(const QlParams& p, float (&v)[8], int
         make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
     return;
   }
-  uint4 rv = make_uint4(0, 0, 0, 0);
-  if (p.residual) rv = *reinterpret_cast<const uint4*>(p.residual + m * p.ldy + n);
   const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rv);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     if constexpr (WF == W_FP8) v[e] *= p.fp8_scale[p.nscale == 1 ? 0 : n + e];
-    if (p.bias) v[e] += bv[e];
+    if (bv) v[e] += bv[e];
   }
   if (rope_row && n < p.rope_cols) {
     // x*cos + rotate_half(x)*sin, rotate_half([x0, x1]) = [-x1, x0]; 8 | head_dim, so the
@@ -288,11 +284,9 @@ __device__ __forceinline__ void ql_finish8(const QlParams& p, float (&v)[8], int
       v[2 * e + 1] = x1 * t.x + x0 * t.y;
     }
   }
-  float gv[8];
-  if (p.gate) ql_load8(p.gate, n, gv);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    if (p.gate) v[e] *= gv[e];
+    if (gv) v[e] *= gv[e];
     if (p.residual) v[e] += __bfloat162float(re[e]);
   }
   *reinterpret_cast<uint4*>(p.y + m * p.ldy + n) =
@@ -300,6 +294,21 @@ __device__ __forceinline__ void ql_finish8(const QlParams& p, float (&v)[8], int
                            pack_f16x2(v[4], v[5]), pack_f16x2(v[6], v[7]))
               : make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
                            pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+}
+
+// Epilogue of 8 consecutive accumulator values of row m, columns n .. n+7, loading its own
+// operands: FP8 per-channel scale, bias, then either the GLU (4 outputs at column n/2) or
+// optional RoPE, gate and residual, bf16 (or f16) store.
+template <int WF>
+__device__ __forceinline__ void ql_finish8(const QlParams& p, float (&v)[8], int64_t m, int64_t n,
+                                           const float2* rope_row) {
+  float bv[8], gv[8];
+  if (p.bias) ql_load8(p.bias, n, bv);
+  if (p.gate && p.glu < 0) ql_load8(p.gate, n, gv);
+  uint4 rv = make_uint4(0, 0, 0, 0);
+  if (p.residual && p.glu < 0) rv = *reinterpret_cast<const uint4*>(p.residual + m * p.ldy + n);
+  ql_finish8_with<WF>(p, v, m, n, rope_row, p.bias ? bv : nullptr,
+                      p.gate && p.glu < 0 ? gv : nullptr, rv);
 }
 
 // Split-K reduce: out[m, n..n+7] = epilogue(sum over z of ws[z][m][n..n+7]), z in order, one
@@ -787,6 +796,7 @@ __global__ void __launch_bounds__(kSmThreads, 2)
   uint64_t* acc_full = empty + kSmSt;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+  __shared__ float sbias[BN], sgate[BN];  // the tile's bias and gate columns
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int mtile, ntile;
   ql_tile_of(p, (int)blockIdx.x, mtile, ntile);
@@ -854,26 +864,50 @@ __global__ void __launch_bounds__(kSmThreads, 2)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // The tile's bias and gate go to shared memory while the MMAs run (one element per
+    // epilogue thread), and each 32-column step issues its residual loads before it waits for
+    // the TMEM load: the epilogue's global-memory latency is paid once per tile and per step,
+    // not once per 8 columns.
+    const int et = threadIdx.x - 64;  // 0 .. 255
+    for (int c = et; c < BN; c += 256) {
+      const int64_t n = n0 + c;
+      sbias[c] = (p.bias && n < p.N) ? __bfloat162float(p.bias[n]) : 0.f;
+      sgate[c] = (p.gate && n < p.N) ? __bfloat162float(p.gate[n]) : 1.f;
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 epilogue warps
     const int quarter = warp & 3, half = (warp - 2) >> 2;
     const int64_t m = m0 + quarter * 32 + lane;
     const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const bool res = p.residual && p.glu < 0;
     if (mbar_wait_warp(acc_full, 0, abort_flag, WD_EPILOGUE_WAIT) && !*abort_flag) {
       tc_fence_after();
       const float2* rope_row =
           p.rope ? p.rope + ((m + p.rope_off) / p.rope_div % p.rope_mod) * p.rope_half : nullptr;
+      constexpr int kStep = BN / 2 < 32 ? BN / 2 : 32;
 #pragma unroll 1
-      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
-        uint32_t r[16];
-        tmem_ld16(taddr + c, r);
-        tmem_wait_ld();
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kStep) {
+        uint32_t r[32];
+        tmem_ld16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+        if constexpr (kStep == 32) tmem_ld16(taddr + c + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
         const int64_t nb = n0 + c;
-        if (m >= p.M || nb >= p.N) continue;
+        const bool row_ok = m < p.M;
+        uint4 rv[kStep / 8];
 #pragma unroll
-        for (int g = 0; g < 16; g += 8) {
+        for (int g = 0; g < kStep / 8; ++g)
+          rv[g] = (res && row_ok && nb + 8 * g < p.N)
+                      ? *reinterpret_cast<const uint4*>(p.residual + m * p.ldy + nb + 8 * g)
+                      : make_uint4(0, 0, 0, 0);
+        tmem_wait_ld();
+        if (!row_ok) continue;
+#pragma unroll
+        for (int g = 0; g < kStep / 8; ++g) {
+          if (nb + 8 * g >= p.N) break;  // N % 16 == 0: groups of 8 are whole
           float v[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[g + e]);
-          ql_finish8<W_BF16>(p, v, m, nb + g, rope_row);  // N % 16 == 0: groups are whole
+          for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[8 * g + e]);
+          ql_finish8_with<W_BF16>(p, v, m, nb + 8 * g, rope_row,
+                                  p.bias ? &sbias[c + 8 * g] : nullptr,
+                                  p.gate ? &sgate[c + 8 * g] : nullptr, rv[g]);
         }
       }
     }
