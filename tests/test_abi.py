@@ -117,3 +117,18 @@ def test_quant_linear_pairing_mode_switch_on_the_host():
     old = L.sp_quant_linear_set_pairing(1)
     assert old in (0, 1)
     assert L.sp_quant_linear_set_pairing(old) == 1
+
+
+def test_groupnorm_streaming_workspace_size_on_the_host():
+    # contiguous NCHW groups of 256 KB and more take the streaming slice-unit path: the
+    # workspace is one u32 counter per (batch, group), padded to 16 bytes, then a 16-byte
+    # partial per slice unit (48 KB units for f32, 64 KB for 16-bit types)
+    L = _lib.load()
+    B, C, H, W, G = 8, 512, 128, 128, 32
+    st = _lib.i64_array((C * H * W, H * W, W, 1))
+    for dtype, es, unit in ((0, 4, 48 * 1024), (1, 2, 64 * 1024), (2, 2, 64 * 1024)):
+        group_bytes = C // G * H * W * es
+        S = -(-group_bytes // unit)
+        BG = B * G
+        want = ((BG * 4 + 15) // 16) * 16 + BG * S * 16
+        assert L.sp_groupnorm_act_workspace_size(B, C, H, W, st, G, dtype) == want
