@@ -29,8 +29,6 @@ namespace {
 constexpr int kQBM = 256, kQHalf = 128, kQBN = 256, kQBK = 64;
 constexpr int kQThreads = 640, kQDecoders = 512, kQFirstDecoderWarp = 4;
 constexpr int kXBytes = kQBM * kQBK * 2;    // 32 KB
-constexpr int kWRawBytes = kQBN * kQBK;     // 16 KB
-constexpr int kScBytes = 2 * kQBN * 2;      // 1 KB: two k-blocks x 256 rows of f16
 constexpr int kWCvtBytes = kQBN * kQBK * 2; // 32 KB
 
 // W_BF16: plain bf16 weights (the UNet's projections and feed-forward), loaded by TMA straight
